@@ -1,0 +1,133 @@
+/* librevk — C ABI of the B200 (sm_100a) kernels behind the `reversability_b200`
+ * package, a drop-in for the reversible-Transformer hot path of
+ * LokeshJatangi/Reversability (`src/reversibility`).
+ *
+ * Conventions (all entry points):
+ *  - Every pointer is a DEVICE pointer owned by the caller; the library never
+ *    allocates device memory. Workspaces (RMSNorm weight-gradient partials,
+ *    GEMM split partials) are passed in by the caller with their size.
+ *  - Sizes and leading dimensions are element counts (int64_t).
+ *  - `stream` is a cudaStream_t passed as void*; launches are stream ordered
+ *    and nothing here synchronises the host.
+ *  - Return value: RK_OK (0) or one of the RK_ERR_* codes below. No C++
+ *    exception crosses this boundary.
+ *  - Device-side bounded waits that give up set bits in a device status word;
+ *    read (and clear) it with rk_device_status_read().
+ * Each declaration names the reference code it replaces (path:line in the
+ * reference repository).
+ */
+#ifndef REVK_H
+#define REVK_H
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define RK_API __attribute__((visibility("default")))
+#else
+#define RK_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+enum { RK_F32 = 0, RK_BF16 = 1, RK_F16 = 2 };
+
+/* status codes */
+enum {
+  RK_OK = 0,
+  RK_ERR_ARG = 1,         /* null pointer, negative or inconsistent size */
+  RK_ERR_ALIGN = 2,       /* pointer or leading dimension breaks a vector/TMA alignment rule */
+  RK_ERR_DTYPE = 3,       /* dtype combination not supported */
+  RK_ERR_LAUNCH = 4,      /* CUDA launch or driver call failed */
+  RK_ERR_UNSUPPORTED = 5, /* shape outside what the kernel implements (e.g. width > 1024) */
+  RK_ERR_WORKSPACE = 6,   /* caller workspace too small */
+  RK_ERR_DEVICE = 7       /* device status word non-zero (a bounded wait gave up) */
+};
+
+/* device status bits */
+enum {
+  RK_DEV_GEMM_TIMEOUT = 1u << 0,
+  RK_DEV_ATTN_TIMEOUT = 1u << 1
+};
+
+RK_API int rk_abi_version(void);
+RK_API const char* rk_status_string(int status);
+/* Copies the device status word of the current device to *out and clears it.
+ * Synchronises `stream`. */
+RK_API int rk_device_status_read(unsigned int* out, void* stream);
+
+/* ------------------------------------------------------------------ RMSNorm
+ * Replaces kernels_v3.py:9-17 (_rms_forward) launched from kernels_v3.py:60
+ * (FusedRMSNorm.forward) and nn.RMSNorm in model.py:62-64.
+ * y[r,c] = (x[r,c] * rstd[r]) * w[c], rstd[r] = rsqrt(mean_c x[r,c]^2 + eps).
+ * x, y: row-major [rows, width] with leading dims ldx, ldy; dtypes RK_F32/RK_BF16/RK_F16.
+ * w: fp32 [width]. rstd: fp32 [rows] (may be NULL). width <= 1024. */
+RK_API int rk_rmsnorm_fwd(const void* x, int x_dtype, int64_t ldx, const float* w, void* y, int y_dtype, int64_t ldy,
+                   float* rstd, int64_t rows, int64_t width, float eps, void* stream);
+
+/* Replaces kernels_v3.py:19-48 (_rms_dx, _rms_dw_partials, _rms_dw_reduce)
+ * launched from kernels_v3.py:71-73 (FusedRMSNorm.backward).
+ * dx = (dy*w - x * sum(dy*w*x)/width * rstd^2) * rstd ; dw = sum_rows dy * (x*rstd).
+ * dx may alias nothing else. dw (fp32 [width]) is overwritten, or accumulated
+ * into when accumulate_dw != 0. dw_partial: fp32 workspace of at least
+ * rk_rmsnorm_bwd_workspace(rows, width) bytes. */
+RK_API int64_t rk_rmsnorm_bwd_workspace(int64_t rows, int64_t width);
+RK_API int rk_rmsnorm_bwd(const void* x, int x_dtype, int64_t ldx, const float* w, const float* rstd, const void* dy,
+                   int dy_dtype, int64_t lddy, void* dx, int dx_dtype, int64_t lddx, float* dw, int accumulate_dw,
+                   float* dw_partial, int64_t workspace_bytes, int64_t rows, int64_t width, void* stream);
+
+/* ------------------------------------------------------------------ SwiGLU
+ * Replaces kernels.py:88-95 (_swiglu_forward) launched from kernels.py:120
+ * (FusedSwiGLU.forward) and MLP.forward's silu(gate)*value (model.py:55-56).
+ * u: [rows, 2*width] (gate = first width columns, value = last width columns).
+ * h[r,c] = round(silu(gate)) * value, computed in fp32 and stored in `dtype`. */
+RK_API int rk_swiglu_fwd(const void* u, void* h, int dtype, int64_t rows, int64_t width, void* stream);
+
+/* Replaces kernels.py:98-110 (_swiglu_backward), launched from kernels.py:130.
+ * du[:, :width]  = round(dh*value) * sig*(1 + gate*(1-sig))
+ * du[:, width:]  = dh * round(silu(gate)). */
+RK_API int rk_swiglu_bwd(const void* u, const void* dh, void* du, int dtype, int64_t rows, int64_t width, void* stream);
+
+/* ------------------------------------------------------------ Reconstruct
+ * Replaces inverse_pair (reversible.py:28-32) for the midpoint recurrence:
+ * x_prev[i] = x_next[i] - round_F(coeff * force[i]), coeff = 2h, computed the
+ * way autocast does it (scaled force rounded to the force dtype, then an fp32
+ * subtraction). x_next/x_prev fp32 [n]; force dtype RK_F32/RK_BF16/RK_F16.
+ * x_prev may alias x_next. */
+RK_API int rk_reconstruct_midpoint(const float* x_next, const void* force, int force_dtype, float coeff, float* x_prev,
+                            int64_t n, void* stream);
+/* Hamiltonian-Euler inverse half-step (reversible.py:30-32):
+ * state_prev[i] = state[i] - sublayer_out[i] (p_prev = p - M(q); q_prev = q - A(p_prev)). */
+RK_API int rk_reconstruct_euler(const float* state, const void* sublayer_out, int out_dtype, float* state_prev, int64_t n,
+                         void* stream);
+
+/* ------------------------------------------------------------------ GEMMs
+ * Replace F.linear (cuBLAS) inside CausalSelfAttention.qkv/.proj and
+ * MLP.up/.down (model.py:37,45,55-56) and its autograd backward.
+ * Operand dtype `dtype` is RK_BF16 or RK_F16 (tcgen05 tensor cores, fp32
+ * accumulation in tensor memory) or RK_F32 (CUDA-core fp32 path used by the
+ * fp32 parity configuration). Row-major everywhere; ld* are row strides.
+ *
+ * fprop: Y[M,N] = X[M,K] . W[N,K]^T            (nn.Linear forward)
+ * dgrad: DX[M,K] = DY[M,N] . W[N,K]            (grad wrt the Linear input)
+ * wgrad: DW[N,K] (+)= DY[M,N]^T . X[M,K]       (grad wrt the weight, fp32 out)
+ * out_dtype: dtype of Y/DX (RK_F32, RK_BF16 or RK_F16).
+ * For bf16/f16 operands the row strides in bytes must be multiples of 16 and
+ * the base pointers 16-byte aligned (TMA rule).
+ * wgrad splits the M reduction into fixed slices written to `workspace`
+ * (fp32) and summed in a fixed order, so results are deterministic; size it
+ * with rk_gemm_wgrad_workspace(). accumulate != 0 adds into DW. */
+RK_API int rk_gemm_fprop(const void* x, int64_t ldx, const void* w, int64_t ldw, void* y, int64_t ldy, int64_t M,
+                  int64_t N, int64_t K, int dtype, int out_dtype, void* stream);
+RK_API int rk_gemm_dgrad(const void* dy, int64_t lddy, const void* w, int64_t ldw, void* dx, int64_t lddx, int64_t M,
+                  int64_t N, int64_t K, int dtype, int out_dtype, void* stream);
+RK_API int64_t rk_gemm_wgrad_workspace(int64_t M, int64_t N, int64_t K);
+RK_API int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, float* dw, int64_t lddw, int64_t M,
+                  int64_t N, int64_t K, int dtype, int accumulate, float* workspace, int64_t workspace_bytes,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* REVK_H */

@@ -1,0 +1,112 @@
+"""ctypes binding of librevk.so (the C ABI declared in include/revk.h).
+
+The library is loaded once, from this package directory. Every call passes
+raw device pointers, element counts and the current CUDA stream; a non-zero
+status becomes a RuntimeError carrying the library's own message. There is no
+fallback: if the library is missing, every kernel entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "librevk.so"
+HEADER = Path(__file__).resolve().parents[1] / "include" / "revk.h"
+
+F32, BF16, F16 = 0, 1, 2
+DTYPE_CODE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+_p = ctypes.c_void_p
+_i64 = ctypes.c_int64
+_i = ctypes.c_int
+_f = ctypes.c_float
+
+# name -> (restype, argtypes)
+SIGNATURES: dict[str, tuple] = {
+    "rk_abi_version": (_i, []),
+    "rk_status_string": (ctypes.c_char_p, [_i]),
+    "rk_device_status_read": (_i, [ctypes.POINTER(ctypes.c_uint), _p]),
+    "rk_rmsnorm_fwd": (_i, [_p, _i, _i64, _p, _p, _i, _i64, _p, _i64, _i64, _f, _p]),
+    "rk_rmsnorm_bwd_workspace": (_i64, [_i64, _i64]),
+    "rk_rmsnorm_bwd": (_i, [_p, _i, _i64, _p, _p, _p, _i, _i64, _p, _i, _i64, _p, _i, _p, _i64, _i64, _i64, _p]),
+    "rk_swiglu_fwd": (_i, [_p, _p, _i, _i64, _i64, _p]),
+    "rk_swiglu_bwd": (_i, [_p, _p, _p, _i, _i64, _i64, _p]),
+    "rk_reconstruct_midpoint": (_i, [_p, _p, _i, _f, _p, _i64, _p]),
+    "rk_reconstruct_euler": (_i, [_p, _p, _i, _p, _i64, _p]),
+    "rk_gemm_fprop": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p]),
+    "rk_gemm_dgrad": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p]),
+    "rk_gemm_wgrad_workspace": (_i64, [_i64, _i64, _i64]),
+    "rk_gemm_wgrad": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p, _i64, _p]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+class KernelLibraryMissing(RuntimeError):
+    pass
+
+
+def header_symbols() -> list[str]:
+    """Every entry point declared in include/revk.h."""
+    text = HEADER.read_text()
+    return re.findall(r"^RK_API\s+[\w\s\*]+?\b(rk_\w+)\s*\(", text, flags=re.M)
+
+
+def lib():
+    """Loads librevk.so on first use; raises KernelLibraryMissing if it was not built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise KernelLibraryMissing(
+                f"{LIB_PATH.name} is not built; run `python -m reversability_b200.build` (no CPU fallback exists)")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = handle
+    return _lib
+
+
+def status_string(code: int) -> str:
+    return lib().rk_status_string(code).decode()
+
+
+def check(code: int, name: str) -> None:
+    if code != 0:
+        raise RuntimeError(f"{name} failed: status {code} ({status_string(code)})")
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)
+
+
+def stream_ptr(device: torch.device | None = None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def code(dtype: torch.dtype) -> int:
+    try:
+        return DTYPE_CODE[dtype]
+    except KeyError:
+        raise ValueError(f"dtype {dtype} is not supported by the CUDA kernels") from None
+
+
+def device_status(device: torch.device | None = None) -> int:
+    """Reads and clears the library's device status word (synchronises the stream)."""
+    out = ctypes.c_uint(0)
+    check(lib().rk_device_status_read(ctypes.byref(out), stream_ptr(device)), "rk_device_status_read")
+    return out.value

@@ -1,0 +1,277 @@
+// RMSNorm forward/backward (replaces kernels_v3.py:9-48 and nn.RMSNorm).
+//
+// One warp per row. Lane l owns NV vectors of V consecutive columns:
+// columns [(j*32 + l)*V, +V) for j < NV, so every warp-wide load is a
+// contiguous, 16-byte-per-lane transaction. The row reduction is a warp
+// shuffle tree. The weight gradient is reduced first in registers (per lane,
+// over the rows a warp visits), then across the 8 warps of the CTA in shared
+// memory into one fp32 partial row per CTA, then by a second kernel over the
+// partials in a fixed order (deterministic, no atomics).
+#include "vec.cuh"
+
+namespace rk {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <typename Tx, typename Ty, int V, int NV>
+__global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const Tx* __restrict__ x, int64_t ldx,
+                                                          const float* __restrict__ w, Ty* __restrict__ y,
+                                                          int64_t ldy, float* __restrict__ rstd, int64_t rows,
+                                                          int width, float eps) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const Tx* xr = x + row * ldx;
+  float v[NV][V];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (j * 32 + lane) * V;
+    if (c < width) {
+      load_vec<Tx, V>(xr + c, v[j]);
+#pragma unroll
+      for (int e = 0; e < V; ++e) ss += v[j][e] * v[j][e];
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)width + eps);
+  if (rstd && lane == 0) rstd[row] = r;
+  Ty* yr = y + row * ldy;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (j * 32 + lane) * V;
+    if (c < width) {
+      float wv[V], o[V];
+      load_vec<float, V>(w + c, wv);
+#pragma unroll
+      for (int e = 0; e < V; ++e) o[e] = (v[j][e] * r) * wv[e];
+      store_vec<Ty, V>(yr + c, o);
+    }
+  }
+}
+
+template <typename Tx, typename Tg, typename Tdx, int V, int NV>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const Tx* __restrict__ x, int64_t ldx,
+                                                          const float* __restrict__ w,
+                                                          const float* __restrict__ rstd, const Tg* __restrict__ dy,
+                                                          int64_t lddy, Tdx* __restrict__ dx, int64_t lddx,
+                                                          float* __restrict__ partial, int64_t rows, int width) {
+  extern __shared__ float red[];  // [8][width]
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t stride = (int64_t)gridDim.x * 8;
+  float acc[NV][V];
+  float wv[NV][V];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (j * 32 + lane) * V;
+#pragma unroll
+    for (int e = 0; e < V; ++e) acc[j][e] = 0.f;
+    if (c < width) load_vec<float, V>(w + c, wv[j]);
+  }
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < rows; row += stride) {
+    const float r = __ldg(rstd + row);
+    float xv[NV][V], gv[NV][V];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (j * 32 + lane) * V;
+      if (c < width) {
+        load_vec<Tx, V>(x + row * ldx + c, xv[j]);
+        load_vec<Tg, V>(dy + row * lddy + c, gv[j]);
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          dot += (gv[j][e] * wv[j][e]) * xv[j][e];
+          acc[j][e] += gv[j][e] * (xv[j][e] * r);
+        }
+      }
+    }
+    dot = warp_sum(dot);
+    const float corr = dot / (float)width * r * r;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (j * 32 + lane) * V;
+      if (c < width) {
+        float o[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) o[e] = (gv[j][e] * wv[j][e] - xv[j][e] * corr) * r;
+        store_vec<Tdx, V>(dx + row * lddx + c, o);
+      }
+    }
+  }
+  // Cross-warp reduction of the weight-gradient accumulators.
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (j * 32 + lane) * V;
+    if (c < width) {
+#pragma unroll
+      for (int e = 0; e < V; ++e) red[warp * width + c + e] = acc[j][e];
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) s += red[k * width + c];
+    partial[(int64_t)blockIdx.x * width + c] = s;
+  }
+}
+
+// dw[c] (+)= sum over parts in index order.
+__global__ void rmsnorm_dw_reduce_kernel(const float* __restrict__ partial, float* __restrict__ dw, int parts,
+                                         int width, int accumulate) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= width) return;
+  float s = 0.f;
+  for (int p = 0; p < parts; ++p) s += partial[(int64_t)p * width + c];
+  dw[c] = accumulate ? dw[c] + s : s;
+}
+
+}  // namespace rk
+
+using namespace rk;
+
+namespace {
+
+// True when a V-element vector of T at any row start (stride ld elements) is
+// aligned to min(16, V*sizeof(T)) bytes.
+template <typename T>
+bool vec_fits(const void* p, int64_t ld, int V) {
+  const int64_t a = (int64_t)sizeof(T) * V >= 16 ? 16 : (int64_t)sizeof(T) * V;
+  return rk_host::aligned(p, (size_t)a) && ((ld * (int64_t)sizeof(T)) % a == 0);
+}
+
+int rms_parts(int64_t rows) {
+  int64_t warps_rows = (rows + 7) / 8;
+  return (int)(warps_rows < 592 ? (warps_rows > 0 ? warps_rows : 1) : 592);
+}
+
+template <typename Tx, typename Ty, int V>
+int fwd_nv(const void* x, int64_t ldx, const float* w, void* y, int64_t ldy, float* rstd, int64_t rows, int width,
+           float eps, cudaStream_t s) {
+  const int per = 32 * V;
+  const int nv = (width + per - 1) / per;
+  dim3 grid((unsigned)((rows + 7) / 8)), block(256);
+  auto X = static_cast<const Tx*>(x);
+  auto Y = static_cast<Ty*>(y);
+#define RK_FWD(N) rmsnorm_fwd_kernel<Tx, Ty, V, N><<<grid, block, 0, s>>>(X, ldx, w, Y, ldy, rstd, rows, width, eps)
+  if (nv <= 1) RK_FWD(1);
+  else if (nv <= 2) RK_FWD(2);
+  else if (nv <= 4) RK_FWD(4);
+  else if (nv <= 8) RK_FWD(8);
+  else if constexpr (V == 1) {
+    if (nv <= 32) RK_FWD(32);
+    else return RK_ERR_UNSUPPORTED;
+  } else return RK_ERR_UNSUPPORTED;
+#undef RK_FWD
+  return rk_host::launch_status();
+}
+
+template <typename Tx, typename Ty>
+int fwd_typed(const void* x, int64_t ldx, const float* w, void* y, int64_t ldy, float* rstd, int64_t rows, int width,
+              float eps, cudaStream_t s) {
+  constexpr int VX = 16 / (int)sizeof(Tx);
+  const bool vec_ok = (width % VX == 0) && vec_fits<Tx>(x, ldx, VX) && vec_fits<float>(w, 0, VX) &&
+                      vec_fits<Ty>(y, ldy, VX);
+  if (vec_ok) return fwd_nv<Tx, Ty, VX>(x, ldx, w, y, ldy, rstd, rows, width, eps, s);
+  return fwd_nv<Tx, Ty, 1>(x, ldx, w, y, ldy, rstd, rows, width, eps, s);
+}
+
+template <typename Tx, typename Tg, typename Tdx, int V>
+int bwd_nv(const void* x, int64_t ldx, const float* w, const float* rstd, const void* dy, int64_t lddy, void* dx,
+           int64_t lddx, float* partial, int parts, int64_t rows, int width, cudaStream_t s) {
+  const int per = 32 * V;
+  const int nv = (width + per - 1) / per;
+  dim3 grid((unsigned)parts), block(256);
+  size_t smem = (size_t)8 * width * sizeof(float);
+  auto X = static_cast<const Tx*>(x);
+  auto G = static_cast<const Tg*>(dy);
+  auto D = static_cast<Tdx*>(dx);
+#define RK_BWD(N)                                                                                          \
+  do {                                                                                                     \
+    auto k = rmsnorm_bwd_kernel<Tx, Tg, Tdx, V, N>;                                                        \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    k<<<grid, block, smem, s>>>(X, ldx, w, rstd, G, lddy, D, lddx, partial, rows, width);                  \
+  } while (0)
+  if (nv <= 1) RK_BWD(1);
+  else if (nv <= 2) RK_BWD(2);
+  else if (nv <= 4) RK_BWD(4);
+  else if (nv <= 8) RK_BWD(8);
+  else if constexpr (V == 1) {
+    if (nv <= 32) RK_BWD(32);
+    else return RK_ERR_UNSUPPORTED;
+  } else return RK_ERR_UNSUPPORTED;
+#undef RK_BWD
+  return rk_host::launch_status();
+}
+
+template <typename Tx, typename Tg, typename Tdx>
+int bwd_typed(const void* x, int64_t ldx, const float* w, const float* rstd, const void* dy, int64_t lddy, void* dx,
+              int64_t lddx, float* partial, int parts, int64_t rows, int width, cudaStream_t s) {
+  constexpr int VX = 16 / (int)sizeof(Tx);
+  const bool vec_ok = (width % VX == 0) && vec_fits<Tx>(x, ldx, VX) && vec_fits<float>(w, 0, VX) &&
+                      vec_fits<Tg>(dy, lddy, VX) && vec_fits<Tdx>(dx, lddx, VX);
+  if (vec_ok) return bwd_nv<Tx, Tg, Tdx, VX>(x, ldx, w, rstd, dy, lddy, dx, lddx, partial, parts, rows, width, s);
+  return bwd_nv<Tx, Tg, Tdx, 1>(x, ldx, w, rstd, dy, lddy, dx, lddx, partial, parts, rows, width, s);
+}
+
+}  // namespace
+
+extern "C" int rk_rmsnorm_fwd(const void* x, int x_dtype, int64_t ldx, const float* w, void* y, int y_dtype,
+                              int64_t ldy, float* rstd, int64_t rows, int64_t width, float eps, void* stream) {
+  if (!x || !w || !y || rows < 0 || width <= 0 || ldx < width || ldy < width) return RK_ERR_ARG;
+  if (width > 1024) return RK_ERR_UNSUPPORTED;
+  if (rows == 0) return RK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int W = (int)width;
+  if (x_dtype == RK_F32 && y_dtype == RK_F32) return fwd_typed<float, float>(x, ldx, w, y, ldy, rstd, rows, W, eps, s);
+  if (x_dtype == RK_F32 && y_dtype == RK_BF16)
+    return fwd_typed<float, __nv_bfloat16>(x, ldx, w, y, ldy, rstd, rows, W, eps, s);
+  if (x_dtype == RK_F32 && y_dtype == RK_F16) return fwd_typed<float, __half>(x, ldx, w, y, ldy, rstd, rows, W, eps, s);
+  if (x_dtype == RK_BF16 && y_dtype == RK_BF16)
+    return fwd_typed<__nv_bfloat16, __nv_bfloat16>(x, ldx, w, y, ldy, rstd, rows, W, eps, s);
+  if (x_dtype == RK_F16 && y_dtype == RK_F16) return fwd_typed<__half, __half>(x, ldx, w, y, ldy, rstd, rows, W, eps, s);
+  return RK_ERR_DTYPE;
+}
+
+extern "C" int64_t rk_rmsnorm_bwd_workspace(int64_t rows, int64_t width) {
+  return (int64_t)rms_parts(rows) * width * (int64_t)sizeof(float);
+}
+
+extern "C" int rk_rmsnorm_bwd(const void* x, int x_dtype, int64_t ldx, const float* w, const float* rstd,
+                              const void* dy, int dy_dtype, int64_t lddy, void* dx, int dx_dtype, int64_t lddx,
+                              float* dw, int accumulate_dw, float* dw_partial, int64_t workspace_bytes, int64_t rows,
+                              int64_t width, void* stream) {
+  if (!x || !w || !rstd || !dy || !dx || !dw || !dw_partial || rows < 0 || width <= 0) return RK_ERR_ARG;
+  if (ldx < width || lddy < width || lddx < width) return RK_ERR_ARG;
+  if (width > 1024) return RK_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int W = (int)width;
+  if (rows == 0) {
+    if (!accumulate_dw) cudaMemsetAsync(dw, 0, sizeof(float) * W, s);
+    return rk_host::launch_status();
+  }
+  const int parts = rms_parts(rows);
+  if (workspace_bytes < (int64_t)parts * W * (int64_t)sizeof(float)) return RK_ERR_WORKSPACE;
+  int st;
+  if (x_dtype == RK_F32 && dy_dtype == RK_F32 && dx_dtype == RK_F32)
+    st = bwd_typed<float, float, float>(x, ldx, w, rstd, dy, lddy, dx, lddx, dw_partial, parts, rows, W, s);
+  else if (x_dtype == RK_F32 && dy_dtype == RK_BF16 && dx_dtype == RK_F32)
+    st = bwd_typed<float, __nv_bfloat16, float>(x, ldx, w, rstd, dy, lddy, dx, lddx, dw_partial, parts, rows, W, s);
+  else if (x_dtype == RK_F32 && dy_dtype == RK_F16 && dx_dtype == RK_F32)
+    st = bwd_typed<float, __half, float>(x, ldx, w, rstd, dy, lddy, dx, lddx, dw_partial, parts, rows, W, s);
+  else if (x_dtype == RK_BF16 && dy_dtype == RK_BF16 && dx_dtype == RK_BF16)
+    st = bwd_typed<__nv_bfloat16, __nv_bfloat16, __nv_bfloat16>(x, ldx, w, rstd, dy, lddy, dx, lddx, dw_partial,
+                                                                 parts, rows, W, s);
+  else if (x_dtype == RK_F16 && dy_dtype == RK_F16 && dx_dtype == RK_F16)
+    st = bwd_typed<__half, __half, __half>(x, ldx, w, rstd, dy, lddy, dx, lddx, dw_partial, parts, rows, W, s);
+  else
+    return RK_ERR_DTYPE;
+  if (st != RK_OK) return st;
+  rmsnorm_dw_reduce_kernel<<<(W + 255) / 256, 256, 0, s>>>(dw_partial, dw, parts, W, accumulate_dw);
+  return rk_host::launch_status();
+}

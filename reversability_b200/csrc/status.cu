@@ -1,0 +1,51 @@
+// Library-wide device status word and ABI bookkeeping entry points.
+#include "common.cuh"
+
+namespace {
+__device__ unsigned int g_rk_device_status = 0;
+constexpr int kMaxDevices = 64;
+unsigned int* g_status_ptr[kMaxDevices] = {nullptr};
+}  // namespace
+
+namespace rk_host {
+// The address is looked up once per device (with that device current) and cached.
+unsigned int* device_status_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  if (!g_status_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_rk_device_status) != cudaSuccess) return nullptr;
+    g_status_ptr[dev] = static_cast<unsigned int*>(p);
+  }
+  return g_status_ptr[dev];
+}
+}  // namespace rk_host
+
+extern "C" int rk_abi_version(void) { return 1; }
+
+extern "C" const char* rk_status_string(int status) {
+  switch (status) {
+    case RK_OK: return "ok";
+    case RK_ERR_ARG: return "invalid argument (null pointer, negative or inconsistent size)";
+    case RK_ERR_ALIGN: return "alignment rule broken (pointer or leading dimension)";
+    case RK_ERR_DTYPE: return "unsupported dtype combination";
+    case RK_ERR_LAUNCH: return "CUDA launch or driver call failed";
+    case RK_ERR_UNSUPPORTED: return "shape outside what the kernel implements";
+    case RK_ERR_WORKSPACE: return "workspace too small";
+    case RK_ERR_DEVICE: return "device status word set: a bounded device-side wait gave up";
+    default: return "unknown status";
+  }
+}
+
+extern "C" int rk_device_status_read(unsigned int* out, void* stream) {
+  if (!out) return RK_ERR_ARG;
+  unsigned int* p = rk_host::device_status_ptr();
+  if (!p) return RK_ERR_LAUNCH;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned int v = 0;
+  if (cudaMemcpyAsync(&v, p, sizeof(v), cudaMemcpyDeviceToHost, s) != cudaSuccess) return RK_ERR_LAUNCH;
+  if (cudaMemsetAsync(p, 0, sizeof(v), s) != cudaSuccess) return RK_ERR_LAUNCH;
+  if (cudaStreamSynchronize(s) != cudaSuccess) return RK_ERR_LAUNCH;
+  *out = v;
+  return RK_OK;
+}

@@ -1,0 +1,179 @@
+"""Tensor-level wrappers over librevk: argument checks, output allocation and
+the current-stream launch. These are the only functions that touch the C ABI
+directly; autograd Functions and the fused engine build on them.
+
+All inputs must be CUDA tensors; a CPU tensor raises ValueError mentioning
+CUDA (the reference's error convention, kernels.py:59-60, kernels_v3.py:54-57).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+
+_TC_DTYPES = (torch.bfloat16, torch.float16)
+
+
+def require_cuda(*tensors: torch.Tensor, what: str = "librevk kernels") -> None:
+    for t in tensors:
+        if t is not None and t.device.type != "cuda":
+            raise ValueError(f"{what} require CUDA tensors; no CPU fallback exists")
+
+
+def _row_major_2d(t: torch.Tensor, name: str) -> tuple[torch.Tensor, int]:
+    """Returns (t viewed as 2-D, leading dimension); the last dim must be unit-stride."""
+    if t.dim() == 1:
+        t = t.unsqueeze(0)
+    if t.dim() > 2:
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+        t = t.reshape(-1, t.shape[-1])
+    if t.stride(-1) != 1:
+        raise ValueError(f"{name} must have a unit-stride last dimension")
+    return t, t.stride(0) if t.shape[0] > 1 else t.shape[1]
+
+
+# ------------------------------------------------------------------ RMSNorm
+def rmsnorm_fwd(x: torch.Tensor, weight: torch.Tensor, eps: float, out_dtype: torch.dtype | None = None,
+                want_rstd: bool = True, out: torch.Tensor | None = None):
+    """y = x * rsqrt(mean(x^2) + eps) * weight over the last dim; returns (y, rstd)."""
+    require_cuda(x, weight)
+    if weight.dtype != torch.float32 or weight.dim() != 1 or weight.numel() != x.shape[-1]:
+        raise ValueError("RMSNorm weight must be fp32 [width] matching the input width")
+    x2, ldx = _row_major_2d(x, "x")
+    rows, width = x2.shape
+    out_dtype = out_dtype or x.dtype
+    y = out if out is not None else torch.empty(x.shape, device=x.device, dtype=out_dtype)
+    y2, ldy = _row_major_2d(y, "out")
+    rstd = torch.empty(rows, device=x.device, dtype=torch.float32) if want_rstd else None
+    _lib.call("rk_rmsnorm_fwd", x2.data_ptr(), _lib.code(x.dtype), ldx, weight.contiguous().data_ptr(),
+              y2.data_ptr(), _lib.code(out_dtype), ldy, _lib.ptr(rstd), rows, width, float(eps), _lib.stream_ptr())
+    return y, rstd
+
+
+def rmsnorm_bwd(x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor, dy: torch.Tensor,
+                dx_dtype: torch.dtype | None = None, dw: torch.Tensor | None = None, accumulate_dw: bool = False):
+    """Returns (dx, dw) for y = rmsnorm(x) * weight; dw is fp32 [width]."""
+    require_cuda(x, weight, rstd, dy)
+    x2, ldx = _row_major_2d(x, "x")
+    g2, ldg = _row_major_2d(dy, "dy")
+    rows, width = x2.shape
+    dx = torch.empty(x.shape, device=x.device, dtype=dx_dtype or x.dtype)
+    dx2, lddx = _row_major_2d(dx, "dx")
+    if dw is None:
+        dw = torch.empty(width, device=x.device, dtype=torch.float32)
+        accumulate_dw = False
+    ws_bytes = _lib.lib().rk_rmsnorm_bwd_workspace(rows, width)
+    ws = torch.empty(max(ws_bytes // 4, 1), device=x.device, dtype=torch.float32)
+    _lib.call("rk_rmsnorm_bwd", x2.data_ptr(), _lib.code(x.dtype), ldx, weight.contiguous().data_ptr(),
+              rstd.data_ptr(), g2.data_ptr(), _lib.code(dy.dtype), ldg, dx2.data_ptr(), _lib.code(dx.dtype), lddx,
+              dw.data_ptr(), int(accumulate_dw), ws.data_ptr(), ws_bytes, rows, width, _lib.stream_ptr())
+    return dx, dw
+
+
+# ------------------------------------------------------------------ SwiGLU
+def swiglu_fwd(u: torch.Tensor) -> torch.Tensor:
+    require_cuda(u)
+    if not u.is_contiguous() or u.shape[-1] % 2:
+        raise ValueError("SwiGLU input must be contiguous with an even last dimension")
+    width = u.shape[-1] // 2
+    rows = u.numel() // u.shape[-1] if u.numel() else 0
+    h = torch.empty((*u.shape[:-1], width), device=u.device, dtype=u.dtype)
+    _lib.call("rk_swiglu_fwd", u.data_ptr(), h.data_ptr(), _lib.code(u.dtype), rows, width, _lib.stream_ptr())
+    return h
+
+
+def swiglu_bwd(u: torch.Tensor, dh: torch.Tensor) -> torch.Tensor:
+    require_cuda(u, dh)
+    dh = dh.to(u.dtype).contiguous()
+    width = u.shape[-1] // 2
+    rows = u.numel() // u.shape[-1] if u.numel() else 0
+    du = torch.empty_like(u)
+    _lib.call("rk_swiglu_bwd", u.data_ptr(), dh.data_ptr(), du.data_ptr(), _lib.code(u.dtype), rows, width,
+              _lib.stream_ptr())
+    return du
+
+
+# ------------------------------------------------------------------ reconstruct
+def reconstruct_midpoint(x_next: torch.Tensor, force: torch.Tensor, coeff: float,
+                         out: torch.Tensor | None = None) -> torch.Tensor:
+    """x_prev = x_next - round_force_dtype(coeff * force) (fp32 state)."""
+    require_cuda(x_next, force)
+    if x_next.dtype != torch.float32 or not x_next.is_contiguous() or not force.is_contiguous():
+        raise ValueError("reconstruct expects a contiguous fp32 state and a contiguous force")
+    if x_next.numel() != force.numel():
+        raise ValueError("state and force sizes differ")
+    out = out if out is not None else torch.empty_like(x_next)
+    _lib.call("rk_reconstruct_midpoint", x_next.data_ptr(), force.data_ptr(), _lib.code(force.dtype), float(coeff),
+              out.data_ptr(), x_next.numel(), _lib.stream_ptr())
+    return out
+
+
+def reconstruct_euler(state: torch.Tensor, sublayer_out: torch.Tensor, out: torch.Tensor | None = None):
+    require_cuda(state, sublayer_out)
+    if state.dtype != torch.float32 or not state.is_contiguous() or not sublayer_out.is_contiguous():
+        raise ValueError("reconstruct expects a contiguous fp32 state and a contiguous sublayer output")
+    out = out if out is not None else torch.empty_like(state)
+    _lib.call("rk_reconstruct_euler", state.data_ptr(), sublayer_out.data_ptr(), _lib.code(sublayer_out.dtype),
+              out.data_ptr(), state.numel(), _lib.stream_ptr())
+    return out
+
+
+# ------------------------------------------------------------------ GEMMs
+def _gemm_dtype(*ts: torch.Tensor) -> int:
+    dts = {t.dtype for t in ts}
+    if len(dts) != 1:
+        raise ValueError(f"GEMM operands must share a dtype, got {dts}")
+    return _lib.code(dts.pop())
+
+
+def linear_fwd(x: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """y = x @ w.T (nn.Linear without bias); x [..., K], w [N, K]."""
+    require_cuda(x, w)
+    x2, ldx = _row_major_2d(x, "x")
+    w2, ldw = _row_major_2d(w, "weight")
+    M, K = x2.shape
+    N = w2.shape[0]
+    if w2.shape[1] != K:
+        raise ValueError("linear: weight in_features mismatch")
+    out_dtype = out_dtype or x.dtype
+    y = out if out is not None else torch.empty((*x.shape[:-1], N), device=x.device, dtype=out_dtype)
+    y2, ldy = _row_major_2d(y, "out")
+    _lib.call("rk_gemm_fprop", x2.data_ptr(), ldx, w2.data_ptr(), ldw, y2.data_ptr(), ldy, M, N, K,
+              _gemm_dtype(x2, w2), _lib.code(y.dtype), _lib.stream_ptr())
+    return y
+
+
+def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """dx = dy @ w; dy [..., N], w [N, K]."""
+    require_cuda(dy, w)
+    g2, ldg = _row_major_2d(dy, "dy")
+    w2, ldw = _row_major_2d(w, "weight")
+    M, N = g2.shape
+    K = w2.shape[1]
+    dx = torch.empty((*dy.shape[:-1], K), device=dy.device, dtype=out_dtype or dy.dtype)
+    dx2, lddx = _row_major_2d(dx, "dx")
+    _lib.call("rk_gemm_dgrad", g2.data_ptr(), ldg, w2.data_ptr(), ldw, dx2.data_ptr(), lddx, M, N, K,
+              _gemm_dtype(g2, w2), _lib.code(dx.dtype), _lib.stream_ptr())
+    return dx
+
+
+def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor | None = None,
+                 accumulate: bool = False) -> torch.Tensor:
+    """dw (+)= dy^T @ x in fp32; dy [..., N], x [..., K] -> dw [N, K]."""
+    require_cuda(dy, x)
+    g2, ldg = _row_major_2d(dy, "dy")
+    x2, ldx = _row_major_2d(x, "x")
+    M, N = g2.shape
+    K = x2.shape[1]
+    if dw is None:
+        dw = torch.empty((N, K), device=dy.device, dtype=torch.float32)
+        accumulate = False
+    if dw.dtype != torch.float32:
+        raise ValueError("weight gradients accumulate in fp32")
+    ws_bytes = _lib.lib().rk_gemm_wgrad_workspace(M, N, K)
+    ws = torch.empty(max(ws_bytes // 4, 1), device=dy.device, dtype=torch.float32)
+    _lib.call("rk_gemm_wgrad", g2.data_ptr(), ldg, x2.data_ptr(), ldx, dw.data_ptr(), dw.stride(0), M, N, K,
+              _gemm_dtype(g2, x2), int(accumulate), ws.data_ptr(), ws_bytes, _lib.stream_ptr())
+    return dw

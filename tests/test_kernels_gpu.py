@@ -1,0 +1,191 @@
+"""Kernel-level parity on the GPU: each librevk entry point against a plain
+PyTorch fp32 statement of the same formula (the reference's own kernel tests,
+tests/test_kernels.py:37-51 and tests/test_optimized_v3.py:73-84, use the same
+shapes and tolerances where they exist)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+@pytest.fixture(autouse=True)
+def _seed():
+    torch.manual_seed(1234)
+
+
+# ------------------------------------------------------------------ RMSNorm
+@pytest.mark.parametrize("shape", [(3, 23, 256), (5, 8), (17, 33), (4, 1024), (300, 256)])
+def test_rmsnorm_fp32_matches_torch(shape):
+    from reversability_b200 import functional as fn
+    x = torch.randn(shape, device=DEV)
+    w = torch.randn(shape[-1], device=DEV)
+    eps = torch.finfo(torch.float32).eps
+    y, rstd = fn.rmsnorm_fwd(x, w, eps)
+    torch.testing.assert_close(y, F.rms_norm(x, (shape[-1],), w, eps=eps), rtol=5e-5, atol=5e-6)
+    xr = x.clone().requires_grad_(True)
+    wr = w.clone().requires_grad_(True)
+    g = torch.randn_like(x)
+    F.rms_norm(xr, (shape[-1],), wr, eps=eps).backward(g)
+    dx, dw = fn.rmsnorm_bwd(x, w, rstd, g)
+    torch.testing.assert_close(dx, xr.grad, rtol=5e-5, atol=5e-6)
+    torch.testing.assert_close(dw, wr.grad, rtol=5e-5, atol=5e-5)
+
+
+@pytest.mark.parametrize("io", [(torch.float32, torch.bfloat16), (torch.bfloat16, torch.bfloat16),
+                                (torch.float16, torch.float16)])
+def test_rmsnorm_low_precision_io(io):
+    from reversability_b200 import functional as fn
+    xd, yd = io
+    x = torch.randn(1000, 256, device=DEV).to(xd)
+    w = torch.randn(256, device=DEV) * 0.1 + 1
+    y, rstd = fn.rmsnorm_fwd(x, w, 1e-6, out_dtype=yd)
+    ref = F.rms_norm(x.float(), (256,), w, eps=1e-6)
+    assert y.dtype == yd
+    assert rel_l2(y.float(), ref) < 4e-3
+    g = torch.randn(1000, 256, device=DEV).to(yd)
+    xr = x.float().requires_grad_(True)
+    wr = w.clone().requires_grad_(True)
+    F.rms_norm(xr, (256,), wr, eps=1e-6).backward(g.float())
+    dx, dw = fn.rmsnorm_bwd(x, w, rstd, g, dx_dtype=xd)
+    assert rel_l2(dx.float(), xr.grad) < 4e-3
+    assert rel_l2(dw, wr.grad) < 1e-5
+
+
+def test_rmsnorm_dw_accumulates_and_is_deterministic():
+    from reversability_b200 import functional as fn
+    x = torch.randn(5000, 256, device=DEV)
+    w = torch.randn(256, device=DEV)
+    _, rstd = fn.rmsnorm_fwd(x, w, 1e-6)
+    g = torch.randn_like(x)
+    _, dw1 = fn.rmsnorm_bwd(x, w, rstd, g)
+    _, dw2 = fn.rmsnorm_bwd(x, w, rstd, g)
+    assert torch.equal(dw1, dw2)
+    acc = dw1.clone()
+    fn.rmsnorm_bwd(x, w, rstd, g, dw=acc, accumulate_dw=True)
+    torch.testing.assert_close(acc, 2 * dw1, rtol=1e-6, atol=1e-6)
+
+
+# ------------------------------------------------------------------ SwiGLU
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("shape", [(3, 7, 66), (64, 2048), (5, 130)])
+def test_swiglu_matches_torch(dtype, shape):
+    from reversability_b200 import functional as fn
+    a = torch.randn(shape, device=DEV, dtype=dtype, requires_grad=True)
+    gate, value = a.chunk(2, dim=-1)
+    expected = F.silu(gate) * value
+    actual = fn.swiglu_fwd(a.detach())
+    up = torch.randn_like(expected)
+    expected.backward(up)
+    du = fn.swiglu_bwd(a.detach(), up)
+    tol = {torch.float32: 2e-5, torch.float16: 3e-3, torch.bfloat16: 2e-2}[dtype]
+    torch.testing.assert_close(actual, expected, rtol=tol, atol=tol)
+    torch.testing.assert_close(du, a.grad, rtol=tol, atol=tol)
+
+
+# ------------------------------------------------------------------ reconstruct
+@pytest.mark.parametrize("fdtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("coeff", [1.0, 0.5, 1.5])
+@pytest.mark.parametrize("n", [16896 * 256, 1001])
+def test_reconstruct_midpoint_bit_exact(fdtype, coeff, n):
+    from reversability_b200 import functional as fn
+    x_next = torch.randn(n, device=DEV)
+    force = torch.randn(n, device=DEV).to(fdtype)
+    expected = x_next - coeff * force  # autocast-style: scaled force stays in force dtype
+    actual = fn.reconstruct_midpoint(x_next, force, coeff)
+    assert torch.equal(actual, expected)
+
+
+def test_reconstruct_euler_bit_exact():
+    from reversability_b200 import functional as fn
+    s = torch.randn(4099, device=DEV)
+    m = torch.randn(4099, device=DEV).bfloat16()
+    assert torch.equal(fn.reconstruct_euler(s, m), s - m)
+
+
+def test_midpoint_step_inverts_exactly():
+    """Forward x_next = p + round(c*F) then reconstruct: p comes back bit-exact
+    whenever the fp32 add/sub pair is exact, and within 1 ulp otherwise."""
+    from reversability_b200 import functional as fn
+    p = torch.randn(1 << 20, device=DEV)
+    force = torch.randn(1 << 20, device=DEV).bfloat16()
+    q_next = p + 1.0 * force
+    back = fn.reconstruct_midpoint(q_next, force, 1.0)
+    assert (back - p).abs().max().item() <= 2 * torch.finfo(torch.float32).eps * p.abs().max().item()
+
+
+# ------------------------------------------------------------------ GEMMs
+GEMM_SHAPES = [(128, 128, 64), (1000, 768, 256), (1000, 256, 256), (1000, 2048, 256), (1000, 256, 1024),
+               (333, 200, 96), (7, 24, 40), (14848, 2048, 256)]
+
+
+def _ref_fprop(x, w):
+    return x.double() @ w.double().T
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("mnk", GEMM_SHAPES)
+def test_gemm_fprop(dtype, mnk):
+    from reversability_b200 import functional as fn
+    M, N, K = mnk
+    x = torch.randn(M, K, device=DEV).to(dtype)
+    w = (torch.randn(N, K, device=DEV) * 0.05).to(dtype)
+    y32 = fn.linear_fwd(x, w, out_dtype=torch.float32)
+    ref = _ref_fprop(x, w)
+    assert rel_l2(y32, ref) < 1e-5
+    y16 = fn.linear_fwd(x, w)
+    assert y16.dtype == dtype
+    assert rel_l2(y16.float(), ref) < 5e-3
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("mnk", GEMM_SHAPES)
+def test_gemm_dgrad(dtype, mnk):
+    from reversability_b200 import functional as fn
+    M, N, K = mnk
+    dy = torch.randn(M, N, device=DEV).to(dtype)
+    w = (torch.randn(N, K, device=DEV) * 0.05).to(dtype)
+    dx = fn.linear_dgrad(dy, w, out_dtype=torch.float32)
+    assert rel_l2(dx, dy.double() @ w.double()) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("mnk", [(14848, 768, 256), (4096, 256, 1024), (333, 200, 96), (14848, 2048, 256),
+                                 (14848, 256, 1024), (70, 24, 40)])
+def test_gemm_wgrad(dtype, mnk):
+    from reversability_b200 import functional as fn
+    M, N, K = mnk
+    dy = torch.randn(M, N, device=DEV).to(dtype)
+    x = torch.randn(M, K, device=DEV).to(dtype)
+    ref = dy.double().T @ x.double()
+    dw = fn.linear_wgrad(dy, x)
+    assert rel_l2(dw, ref) < 1e-5
+    dw2 = fn.linear_wgrad(dy, x)
+    assert torch.equal(dw, dw2), "wgrad must be deterministic"
+    acc = torch.ones_like(dw)
+    fn.linear_wgrad(dy, x, dw=acc, accumulate=True)
+    assert rel_l2(acc, ref + 1) < 1e-5
+
+
+@pytest.mark.parametrize("mnk", [(333, 200, 96), (1000, 768, 256), (70, 24, 40)])
+def test_gemm_fp32_path(mnk):
+    from reversability_b200 import functional as fn
+    M, N, K = mnk
+    x = torch.randn(M, K, device=DEV)
+    w = torch.randn(N, K, device=DEV)
+    assert rel_l2(fn.linear_fwd(x, w), x.double() @ w.double().T) < 1e-6
+    dy = torch.randn(M, N, device=DEV)
+    assert rel_l2(fn.linear_dgrad(dy, w), dy.double() @ w.double()) < 1e-6
+    assert rel_l2(fn.linear_wgrad(dy, x), dy.double().T @ x.double()) < 1e-6
+
+
+def test_device_status_clean_after_gemms():
+    from reversability_b200 import _lib, functional as fn
+    x = torch.randn(512, 256, device=DEV).bfloat16()
+    w = torch.randn(768, 256, device=DEV).bfloat16()
+    fn.linear_fwd(x, w)
+    assert _lib.device_status() == 0

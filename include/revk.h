@@ -127,6 +127,24 @@ RK_API int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_t ld
                   int64_t N, int64_t K, int dtype, int accumulate, float* workspace, int64_t workspace_bytes,
                   void* stream);
 
+/* ------------------------------------------------------------- Attention
+ * Replaces F.scaled_dot_product_attention(q, k, v, is_causal=True) and the
+ * q/k/v view/transpose plumbing of CausalSelfAttention.forward (model.py:35-45).
+ * qkv: [B*T, ldq] rows holding q | k | v (each H*HD wide, head h at h*HD), i.e.
+ * the qkv Linear output as is. out: [B*T, ldo], head h at columns h*HD (the
+ * proj Linear input). lse: fp32 [B, H, T] row log-sum-exp saved for backward
+ * (base 2 of the scaled scores for bf16/f16, natural log for fp32).
+ * dtype RK_BF16/RK_F16 (tensor cores, HD 32 or 64) or RK_F32 (CUDA cores).
+ * Softmax scale 1/sqrt(HD). Deterministic (no atomics). */
+RK_API int rk_attn_fwd(const void* qkv, int64_t ldq, void* out, int64_t ldo, float* lse, int64_t B, int64_t H,
+                       int64_t HD, int64_t T, int dtype, void* stream);
+/* Backward: dqkv [B*T, lddq] receives dq | dk | dv in the qkv layout.
+ * dout has the layout of out (same ldo). dsum: fp32 [B, H, T] scratch
+ * (rowsum(dout*out)). */
+RK_API int rk_attn_bwd(const void* qkv, int64_t ldq, const void* out, const void* dout, int64_t ldo,
+                       const float* lse, float* dsum, void* dqkv, int64_t lddq, int64_t B, int64_t H, int64_t HD,
+                       int64_t T, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

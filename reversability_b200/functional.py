@@ -177,3 +177,39 @@ def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor | None = No
     _lib.call("rk_gemm_wgrad", g2.data_ptr(), ldg, x2.data_ptr(), ldx, dw.data_ptr(), dw.stride(0), M, N, K,
               _gemm_dtype(g2, x2), int(accumulate), ws.data_ptr(), ws_bytes, _lib.stream_ptr())
     return dw
+
+
+# ------------------------------------------------------------------ attention
+def attention_fwd(qkv: torch.Tensor, n_heads: int, out: torch.Tensor | None = None):
+    """Causal attention over packed qkv [B, T, 3*D]; returns (o [B, T, D], lse [B, H, T])."""
+    require_cuda(qkv)
+    if qkv.dim() != 3 or qkv.shape[-1] % (3 * n_heads) or qkv.stride(-1) != 1:
+        raise ValueError("attention expects qkv [batch, length, 3*d_model] with a unit-stride last dim")
+    B, T, three_d = qkv.shape
+    D = three_d // 3
+    HD = D // n_heads
+    if qkv.stride(0) != T * qkv.stride(1):
+        raise ValueError("qkv rows must be evenly strided")
+    o = out if out is not None else torch.empty((B, T, D), device=qkv.device, dtype=qkv.dtype)
+    lse = torch.empty((B, n_heads, T), device=qkv.device, dtype=torch.float32)
+    _lib.call("rk_attn_fwd", qkv.data_ptr(), qkv.stride(1), o.data_ptr(), o.stride(1), lse.data_ptr(), B, n_heads,
+              HD, T, _lib.code(qkv.dtype), _lib.stream_ptr())
+    return o, lse
+
+
+def attention_bwd(qkv: torch.Tensor, o: torch.Tensor, do: torch.Tensor, lse: torch.Tensor, n_heads: int):
+    """Returns dqkv [B, T, 3*D] for the causal attention of attention_fwd."""
+    require_cuda(qkv, o, do, lse)
+    B, T, three_d = qkv.shape
+    D = three_d // 3
+    do = do.to(o.dtype)
+    if do.stride() != o.stride():
+        do = do.contiguous()
+        if do.stride() != o.stride():
+            raise ValueError("dout must share the layout of out")
+    dqkv = torch.empty_like(qkv)
+    dsum = torch.empty((B, n_heads, T), device=qkv.device, dtype=torch.float32)
+    _lib.call("rk_attn_bwd", qkv.data_ptr(), qkv.stride(1), o.data_ptr(), do.data_ptr(), o.stride(1),
+              lse.data_ptr(), dsum.data_ptr(), dqkv.data_ptr(), dqkv.stride(1), B, n_heads, D // n_heads, T,
+              _lib.code(qkv.dtype), _lib.stream_ptr())
+    return dqkv

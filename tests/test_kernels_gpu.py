@@ -189,3 +189,46 @@ def test_device_status_clean_after_gemms():
     w = torch.randn(768, 256, device=DEV).bfloat16()
     fn.linear_fwd(x, w)
     assert _lib.device_status() == 0
+
+
+# ------------------------------------------------------------------ attention
+def _sdpa_ref(qkv, H):
+    B, T, three_d = qkv.shape
+    D = three_d // 3
+    q, k, v = qkv.double().split(D, dim=-1)
+    sh = (B, T, H, D // H)
+    q, k, v = (t.reshape(sh).transpose(1, 2) for t in (q, k, v))
+    y = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    return y.transpose(1, 2).reshape(B, T, D)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+@pytest.mark.parametrize("bthd", [(2, 512, 8, 32), (3, 17, 2, 32), (1, 130, 4, 64), (29, 512, 8, 32),
+                                  (1, 2048, 2, 64)])
+def test_attention_fwd_bwd(dtype, bthd):
+    from reversability_b200 import functional as fn
+    B, T, H, HD = bthd
+    D = H * HD
+    qkv = torch.randn(B, T, 3 * D, device=DEV).to(dtype)
+    o, lse = fn.attention_fwd(qkv, H)
+    ref_in = qkv.detach().double().requires_grad_(True)
+    ref = _sdpa_ref(ref_in, H)
+    tol_f = 1e-5 if dtype == torch.float32 else 1e-2
+    assert rel_l2(o.float(), ref) < tol_f
+    do = torch.randn(B, T, D, device=DEV).to(dtype)
+    ref.backward(do.double())
+    dqkv = fn.attention_bwd(qkv, o, do, lse, H)
+    for part in range(3):
+        sl = slice(part * D, (part + 1) * D)
+        err = rel_l2(dqkv[..., sl].float(), ref_in.grad[..., sl])
+        assert err < (1e-5 if dtype == torch.float32 else 2e-2), (part, err)
+
+
+def test_attention_deterministic():
+    from reversability_b200 import functional as fn
+    qkv = torch.randn(4, 512, 768, device=DEV).bfloat16()
+    o1, l1 = fn.attention_fwd(qkv, 8)
+    o2, l2 = fn.attention_fwd(qkv, 8)
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
+    do = torch.randn_like(o1)
+    assert torch.equal(fn.attention_bwd(qkv, o1, do, l1, 8), fn.attention_bwd(qkv, o1, do, l1, 8))

@@ -48,7 +48,8 @@ enum {
 /* device status bits */
 enum {
   RK_DEV_GEMM_TIMEOUT = 1u << 0,
-  RK_DEV_ATTN_TIMEOUT = 1u << 1
+  RK_DEV_ATTN_TIMEOUT = 1u << 1,
+  RK_DEV_CE_LABEL = 1u << 2     /* a cross-entropy label outside [0, vocab) and != ignore_index */
 };
 
 RK_API int rk_abi_version(void);
@@ -144,6 +145,17 @@ RK_API int rk_attn_fwd(const void* qkv, int64_t ldq, void* out, int64_t ldo, flo
 RK_API int rk_attn_bwd(const void* qkv, int64_t ldq, const void* out, const void* dout, int64_t ldo,
                        const float* lse, float* dsum, void* dqkv, int64_t lddq, int64_t B, int64_t H, int64_t HD,
                        int64_t T, int dtype, void* stream);
+
+/* ---------------------------------------------------------- Cross-entropy
+ * Replaces F.cross_entropy(logits, labels, ignore_index=-100, reduction="sum")
+ * and its backward (train_baseline.py:262; Triton variant kernels.py:14-85).
+ * logits: [rows, ld] (vocab valid columns), dtype RK_F32/RK_BF16/RK_F16.
+ * loss_rows[r] = logsumexp(logits[r]) - logits[r, labels[r]] (0 for ignored rows).
+ * dlogits[r, c] = (softmax(logits[r])[c] - [c == labels[r]]) * grad_scale, zero
+ * rows for ignored labels; dlogits may alias logits (in place). fp32 math. */
+RK_API int rk_cross_entropy_fwd_bwd(const void* logits, int64_t ld, int64_t vocab, const int64_t* labels,
+                                    int64_t rows, float grad_scale, float* loss_rows, void* dlogits, int64_t ldd,
+                                    int dtype, int ignore_index, void* stream);
 
 #ifdef __cplusplus
 }

@@ -43,6 +43,7 @@ SIGNATURES: dict[str, tuple] = {
     "rk_gemm_wgrad": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p, _i64, _p]),
     "rk_attn_fwd": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p]),
     "rk_attn_bwd": (_i, [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _p]),
+    "rk_cross_entropy_fwd_bwd": (_i, [_p, _i64, _i64, _p, _i64, _f, _p, _p, _i64, _i, _i, _p]),
 }
 
 _lock = threading.Lock()

@@ -43,7 +43,7 @@ struct GemmArgs {
   unsigned int* status;
 };
 
-enum { EPI_STORE = 0, EPI_PARTIAL = 1 };
+enum { EPI_STORE = 0, EPI_PARTIAL = 1, EPI_ACCUM = 2 };  // ACCUM: fp32 out += acc
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
@@ -57,6 +57,26 @@ struct TcSmem {
   static constexpr uint32_t kBarriers = (2 * STAGES + 5) * 8;
   static constexpr uint32_t kTotal = 1024 /*align slack*/ + STAGES * kStage + kBarriers + 16;
 };
+
+template <typename T>
+__device__ __forceinline__ void accum_row_chunk(T* dst, float (&v)[32], int valid, bool vec_ok) {
+  if constexpr (sizeof(T) == 4) {
+    if (valid >= 32 && vec_ok) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 o = reinterpret_cast<const float4*>(dst)[q];
+        v[q * 4] += o.x;
+        v[q * 4 + 1] += o.y;
+        v[q * 4 + 2] += o.z;
+        v[q * 4 + 3] += o.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < valid) v[j] += dst[j];
+    }
+  }
+}
 
 template <typename T>
 __device__ __forceinline__ void store_row_chunk(T* dst, const float (&v)[32], int valid, bool vec_ok) {
@@ -264,7 +284,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[32];
         tmem_ld_32cols(t_row + c, v);
         const int col = n0 + c;
-        if (row < g.M && col < g.N) store_row_chunk<TOut>(out_row + col, v, g.N - col, vec_ok);
+        if (row < g.M && col < g.N) {
+          if constexpr (EPI == EPI_ACCUM) accum_row_chunk<TOut>(out_row + col, v, g.N - col, vec_ok);
+          store_row_chunk<TOut>(out_row + col, v, g.N - col, vec_ok);
+        }
       }
       tc_fence_before();
       mbar_arrive(tempty0 + 8 * acc);
@@ -450,7 +473,7 @@ int dispatch_major(const CUtensorMap& ta, const CUtensorMap& tb, bool a_mn, bool
 
 // Tensor-core GEMM: C[M,N] = sum_k A(m,k) B(n,k).
 int tc_gemm(Operand a, Operand b, int M, int N, int K, int dtype, void* out, int64_t ldo, int out_dtype, int splits,
-            cudaStream_t s) {
+            cudaStream_t s, bool accumulate = false) {
   const size_t esz = 2;
   if (!rk_host::aligned(a.ptr, 16) || !rk_host::aligned(b.ptr, 16)) return RK_ERR_ALIGN;
   if ((a.ld * esz) % 16 || (b.ld * esz) % 16) return RK_ERR_ALIGN;
@@ -479,6 +502,11 @@ int tc_gemm(Operand a, Operand b, int M, int N, int K, int dtype, void* out, int
   if (splits > 1) {
     if (BN == 256) return dispatch_major<256, EPI_PARTIAL, float>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
     return dispatch_major<128, EPI_PARTIAL, float>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
+  }
+  if (accumulate) {
+    if (out_dtype != RK_F32) return RK_ERR_DTYPE;
+    if (BN == 256) return dispatch_major<256, EPI_ACCUM, float>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
+    return dispatch_major<128, EPI_ACCUM, float>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
   }
   switch (out_dtype) {
     case RK_F32:
@@ -584,8 +612,9 @@ extern "C" int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_
                     (int)N, (int)K, (int)M, accumulate, s);
   if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
   const int splits = wgrad_splits(M, N, K);
-  if (splits == 1 && !accumulate && lddw == K)
-    return tc_gemm({dy, lddy, true}, {x, ldx, true}, (int)N, (int)K, (int)M, dtype, dw, lddw, RK_F32, 1, s);
+  if (splits == 1)  // enough output tiles: write (or accumulate into) dw directly, no workspace
+    return tc_gemm({dy, lddy, true}, {x, ldx, true}, (int)N, (int)K, (int)M, dtype, dw, lddw, RK_F32, 1, s,
+                   accumulate != 0);
   const int64_t need = (int64_t)(splits > 1 ? splits : 1) * N * K * (int64_t)sizeof(float);
   if (!workspace || workspace_bytes < need) return RK_ERR_WORKSPACE;
   int st;

@@ -1,0 +1,244 @@
+"""Fused per-layer reversible forward/backward on librevk kernels.
+
+This is the B200 implementation behind _InverseStack / ReusedMidpoint /
+SplitMidpoint (reversible.py:35-69, optimized.py:9-41, optimized_v3.py:66-117
+of the reference). Per layer in the backward sweep it evaluates the force
+ONCE with saved activations, reconstructs the previous state from it, and
+runs the VJP by hand on the saved activations:
+
+    midpoint  (p, q) -> (q, p + 2h F(q)),  F(x) = A(x) + M(x + A(x))
+      backward at (p_n, q_n):  x = p_n
+        a = A(x), y = x + a, m = M(y), F = a + m     (saved: A and M internals)
+        p_{n-1} = q_n - round(2h F)                  (rk_reconstruct_midpoint)
+        gF = round(round(dq) * 2h)
+        dy = M^T gF ; da = gF + round(dy) ; dx = A^T da + dy
+        (dp, dq) <- (dq, dp + dx)
+    euler     q' = q + A(p), p' = p + M(q')
+      backward: m = M(q'), p = p' - m, a = A(p), q = q' - a
+        dq_eff = dq' + M^T round(dp') ; (dp, dq) <- (dp' + A^T round(dq_eff), dq_eff)
+
+That is 3 force-equivalents per layer (1 forward + 2 for the VJP) instead of
+the reference's 4 (inverse, recompute, 2 for autograd.grad). The rounding
+points reproduce what autocast produces in the reference (bf16 Linear/attention
+outputs, a bf16 force, fp32 residual stream and norms), so reconstruction
+inverts the forward update exactly when the force is recomputed bit-identically,
+which the deterministic kernels guarantee.
+
+The MLP runs in token tiles (`mlp_tokens`, the TiledMLP tile of
+optimized_v3.py:135-177): inside the backward each tile's forward is followed
+immediately by its VJP (its cotangent is known before the layer starts), so
+the [tile, 2*d_ff] intermediate is bounded without recomputing the MLP.
+
+Weight gradients accumulate in fp32 (deterministic split reductions), never
+written to .grad here; callers decide where they go.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from . import functional as fn
+
+F32 = torch.float32
+
+
+@dataclass
+class LayerWeights:
+    """One Block's parameters in Block.parameters() order (model.py:59-64),
+    plus compute-dtype copies of the four GEMM weights."""
+    attn_norm: torch.Tensor
+    qkv: torch.Tensor
+    proj: torch.Tensor
+    mlp_norm: torch.Tensor
+    up: torch.Tensor
+    down: torch.Tensor
+    cd: torch.dtype
+    eps_attn: float | None = None
+    eps_mlp: float | None = None
+    qkv_c: torch.Tensor = None
+    proj_c: torch.Tensor = None
+    up_c: torch.Tensor = None
+    down_c: torch.Tensor = None
+
+    @classmethod
+    def from_params(cls, params, cd: torch.dtype, eps_attn=None, eps_mlp=None) -> "LayerWeights":
+        """params in Block.parameters() order; eps None means finfo(fp32).eps
+        (nn.RMSNorm's rule for the fp32 residual stream)."""
+        an, qkv, proj, mn, up, down = params
+        lw = cls(an, qkv, proj, mn, up, down, cd, eps_attn, eps_mlp)
+        lw.refresh()
+        return lw
+
+    @classmethod
+    def from_block(cls, block, cd: torch.dtype) -> "LayerWeights":
+        return cls.from_params(tuple(block.parameters()), cd, block.attn_norm.eps, block.mlp_norm.eps)
+
+    def refresh(self):
+        """Re-derive the compute-dtype GEMM weights from the fp32 masters."""
+        cast = (lambda t: t.detach()) if self.cd == self.qkv.dtype else (lambda t: t.detach().to(self.cd))
+        self.qkv_c, self.proj_c, self.up_c, self.down_c = (cast(t) for t in (self.qkv, self.proj, self.up, self.down))
+
+
+class LayerGrads:
+    """fp32 gradient accumulators for one block, Block.parameters() order."""
+
+    def __init__(self, tensors):
+        self.attn_norm, self.qkv, self.proj, self.mlp_norm, self.up, self.down = tensors
+
+    @classmethod
+    def zeros_like(cls, lw: LayerWeights):
+        return cls([torch.zeros_like(t, dtype=F32) for t in
+                    (lw.attn_norm, lw.qkv, lw.proj, lw.mlp_norm, lw.up, lw.down)])
+
+    def as_tuple(self):
+        return (self.attn_norm, self.qkv, self.proj, self.mlp_norm, self.up, self.down)
+
+
+class LayerKernels:
+    """Sublayer forward / VJP building blocks on [M, d] row-major activations."""
+
+    def __init__(self, n_heads: int, batch: int, length: int, cd: torch.dtype, mlp_tokens: int = 0):
+        self.H, self.B, self.T = n_heads, batch, length
+        self.cd = cd
+        self.mlp_tokens = mlp_tokens
+
+    @staticmethod
+    def _eps(eps):
+        return eps if eps is not None else torch.finfo(F32).eps
+
+    # ---------------------------------------------------------- attention sublayer
+    def attn_forward(self, lw: LayerWeights, x: torch.Tensor, save: bool):
+        """A(x) = proj(attn(qkv(rmsnorm(x)))): returns (a [M, d] in cd, saved)."""
+        n1, rstd1 = fn.rmsnorm_fwd(x, lw.attn_norm, self._eps(lw.eps_attn), out_dtype=self.cd, want_rstd=save)
+        qkv = fn.linear_fwd(n1, lw.qkv_c)
+        o, lse = fn.attention_fwd(qkv.view(self.B, self.T, -1), self.H)
+        a = fn.linear_fwd(o.view(-1, o.shape[-1]), lw.proj_c)
+        return a, ((n1, rstd1, qkv, o, lse) if save else None)
+
+    def attn_vjp(self, lw: LayerWeights, g: LayerGrads, x: torch.Tensor, saved, ga: torch.Tensor) -> torch.Tensor:
+        """dx (fp32) of A at x for cotangent ga (cd); accumulates weight grads."""
+        n1, rstd1, qkv, o, lse = saved
+        o2 = o.view(-1, o.shape[-1])
+        do = fn.linear_dgrad(ga, lw.proj_c)
+        fn.linear_wgrad(ga, o2, dw=g.proj, accumulate=True)
+        dqkv = fn.attention_bwd(qkv.view(self.B, self.T, -1), o, do.view(o.shape), lse, self.H)
+        dqkv2 = dqkv.view(-1, dqkv.shape[-1])
+        fn.linear_wgrad(dqkv2, n1, dw=g.qkv, accumulate=True)
+        dn1 = fn.linear_dgrad(dqkv2, lw.qkv_c)
+        dx, _ = fn.rmsnorm_bwd(x, lw.attn_norm, rstd1, dn1, dx_dtype=F32, dw=g.attn_norm, accumulate_dw=True)
+        return dx
+
+    # ---------------------------------------------------------- MLP sublayer
+    def _mlp_tile_fwd(self, lw, yt, out_t, save):
+        n2, rstd2 = fn.rmsnorm_fwd(yt, lw.mlp_norm, self._eps(lw.eps_mlp), out_dtype=self.cd, want_rstd=save)
+        u = fn.linear_fwd(n2, lw.up_c)
+        hg = fn.swiglu_fwd(u)
+        fn.linear_fwd(hg, lw.down_c, out=out_t)
+        return (n2, rstd2, u, hg) if save else None
+
+    def _mlp_tile_vjp(self, lw, g, yt, saved, gm_t, dy_t):
+        n2, rstd2, u, hg = saved
+        dh = fn.linear_dgrad(gm_t, lw.down_c)
+        fn.linear_wgrad(gm_t, hg, dw=g.down, accumulate=True)
+        du = fn.swiglu_bwd(u, dh)
+        fn.linear_wgrad(du, n2, dw=g.up, accumulate=True)
+        dn2 = fn.linear_dgrad(du, lw.up_c)
+        dx, _ = fn.rmsnorm_bwd(yt, lw.mlp_norm, rstd2, dn2, dx_dtype=F32, dw=g.mlp_norm, accumulate_dw=True)
+        dy_t.copy_(dx)
+
+    def _tiles(self, M):
+        t = self.mlp_tokens if self.mlp_tokens and self.mlp_tokens > 0 else M
+        return [(s, min(s + t, M)) for s in range(0, M, t)]
+
+    def mlp_forward(self, lw: LayerWeights, y: torch.Tensor) -> torch.Tensor:
+        """M(y) without saving (forward sweep)."""
+        M = y.shape[0]
+        m = torch.empty((M, lw.down.shape[0]), device=y.device, dtype=self.cd)
+        for s, e in self._tiles(M):
+            self._mlp_tile_fwd(lw, y[s:e], m[s:e], save=False)
+        return m
+
+    def mlp_forward_vjp(self, lw: LayerWeights, g: LayerGrads, y: torch.Tensor, gm: torch.Tensor):
+        """M(y) and dy = M^T gm, tile by tile (forward then VJP of each tile)."""
+        M = y.shape[0]
+        m = torch.empty((M, lw.down.shape[0]), device=y.device, dtype=self.cd)
+        dy = torch.empty((M, y.shape[1]), device=y.device, dtype=F32)
+        for s, e in self._tiles(M):
+            saved = self._mlp_tile_fwd(lw, y[s:e], m[s:e], save=True)
+            self._mlp_tile_vjp(lw, g, y[s:e], saved, gm[s:e], dy[s:e])
+            del saved
+        return m, dy
+
+    # ---------------------------------------------------------- layer steps
+    def force(self, lw, x):
+        """F(x) = A(x) + M(x + A(x)) in cd (reversible.py:16-18)."""
+        a, _ = self.attn_forward(lw, x, save=False)
+        y = x + a
+        return a + self.mlp_forward(lw, y)
+
+    def forward_midpoint(self, lw, p, q, h):
+        """(p, q) -> (q, p + round(2h F(q))) (reversible.py:21-23)."""
+        f = self.force(lw, q)
+        return q, fn.reconstruct_midpoint(p, f, -2.0 * h)
+
+    def forward_euler(self, lw, p, q):
+        """q' = q + A(p); p' = p + M(q') (reversible.py:24-25)."""
+        a, _ = self.attn_forward(lw, p, save=False)
+        nq = fn.reconstruct_midpoint(q, a, -1.0)
+        m = self.mlp_forward(lw, nq)
+        return fn.reconstruct_midpoint(p, m, -1.0), nq
+
+    def backward_midpoint(self, lw, g: LayerGrads, p, q, dp, dq, h):
+        """Reconstructs (p_{n-1}, q_{n-1}) and returns them with their cotangents."""
+        x = p
+        a, sa = self.attn_forward(lw, x, save=True)
+        y = x + a
+        gF = (dq.to(self.cd) * (2.0 * h)).to(self.cd)
+        m, dy = self.mlp_forward_vjp(lw, g, y, gF)
+        f = a + m
+        prev_p = fn.reconstruct_midpoint(q, f, 2.0 * h)
+        del m, f, y
+        da = gF + dy.to(self.cd)
+        dx = self.attn_vjp(lw, g, x, sa, da)
+        dx += dy
+        dx += dp
+        return prev_p, x, dq, dx
+
+    def backward_euler(self, lw, g: LayerGrads, p, q, dp, dq):
+        gm = dp.to(self.cd)
+        m, dy = self.mlp_forward_vjp(lw, g, q, gm)
+        prev_p = fn.reconstruct_euler(p, m)
+        del m
+        dq_eff = dq + dy
+        a, sa = self.attn_forward(lw, prev_p, save=True)
+        prev_q = fn.reconstruct_euler(q, a)
+        del a
+        dpx = self.attn_vjp(lw, g, prev_p, sa, dq_eff.to(self.cd))
+        dpx += dp
+        return prev_p, prev_q, dpx, dq_eff
+
+
+def compute_dtype(amp_enabled: bool, amp_dtype: torch.dtype, state_dtype: torch.dtype) -> torch.dtype:
+    return amp_dtype if amp_enabled else state_dtype
+
+
+def stack_forward(kern: LayerKernels, layers, p, q, method: str, h: float):
+    """The no-graph forward of _InverseStack (reversible.py:37-45)."""
+    for lw in layers:
+        p, q = kern.forward_midpoint(lw, p, q, h) if method == "midpoint" else kern.forward_euler(lw, p, q)
+    return p, q
+
+
+def stack_backward(kern: LayerKernels, layers, grads, p, q, dp, dq, method: str, h: float, on_layer_done=None):
+    """Reverse sweep over all layers; grads[i] receives layer i's weight grads.
+    on_layer_done(i) is called after layer i's gradients are complete (used to
+    launch that layer's data-parallel gradient bucket)."""
+    for i in reversed(range(len(layers))):
+        if method == "midpoint":
+            p, q, dp, dq = kern.backward_midpoint(layers[i], grads[i], p, q, dp, dq, h)
+        else:
+            p, q, dp, dq = kern.backward_euler(layers[i], grads[i], p, q, dp, dq)
+        if on_layer_done is not None:
+            on_layer_done(i)
+    return p, q, dp, dq

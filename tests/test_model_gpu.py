@@ -1,0 +1,248 @@
+"""Model-level parity: the librevk path (reversability_b200, on the GPU)
+against the CPU oracle on the same seeded inputs.
+
+Tolerances are the north-star ones: per-parameter gradient rel-L2 <= 1e-5 in
+fp32 and <= 2e-2 under bf16 autocast; reconstructed states must equal the
+stored forward states (to fp32 rounding of the residual update).
+"""
+import copy
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from conftest import rel_l2
+from oracle import model as om
+from oracle import stream as ost
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+TINY = dict(vocab_size=101, max_sequence_length=17, n_layers=3, n_heads=2, d_model=32, d_ff=128)
+WIDE = dict(vocab_size=101, max_sequence_length=64, n_layers=7, n_heads=8, d_model=256, d_ff=1024)
+
+
+def product_model(cfg: dict, method: str, h=0.5, eps=None, seed=1337):
+    import reversability_b200 as rb
+    torch.manual_seed(seed)
+    conf = rb.ModelConfig(**cfg)
+    model = rb.BaselineLM(conf) if method == "baseline" else rb.ReversibleLM(conf, method, h)
+    if eps is not None:
+        for m in model.modules():
+            if isinstance(m, torch.nn.RMSNorm):
+                m.eps = eps
+    return model.to(DEV)
+
+
+def product_step(model, ids, labels, denom, low=None):
+    model.zero_grad(set_to_none=True)
+    ctx = torch.autocast("cuda", dtype=low) if low is not None else torch.autocast("cuda", enabled=False)
+    with ctx:
+        logits = model(ids.to(DEV))
+        total = F.cross_entropy(logits.float().flatten(0, 1), labels.to(DEV).flatten(), ignore_index=-100,
+                                reduction="sum")
+    (total / denom).backward()
+    return total.detach().cpu(), {n: p.grad.detach().cpu() for n, p in model.named_parameters()}
+
+
+def batch(cfg: dict, B: int, seed: int):
+    g = torch.Generator().manual_seed(seed)
+    ids = torch.randint(0, cfg["vocab_size"], (B, cfg["max_sequence_length"]), generator=g)
+    labels = torch.randint(0, cfg["vocab_size"], (B, cfg["max_sequence_length"]), generator=g)
+    labels[-1, -1] = -100
+    return ids, labels, int((labels != -100).sum())
+
+
+@pytest.mark.parametrize("method,h", [("midpoint", 0.5), ("midpoint", 0.25), ("euler", 0.5), ("baseline", 0.5)])
+@pytest.mark.parametrize("cfg_name", ["tiny", "wide"])
+def test_fp32_gradients_match_oracle(method, h, cfg_name):
+    cfg = TINY if cfg_name == "tiny" else WIDE
+    eps = None if cfg_name == "tiny" else 1e-6
+    ids, labels, denom = batch(cfg, 2, 7)
+    model = product_model(cfg, method, h, eps)
+    total, grads = product_step(model, ids, labels, denom)
+    p = om.init_params(om.Config(**cfg), seed=1337)
+    ref_total, ref_grads, _ = om.loss_and_grads(p, om.Config(**cfg), ids, labels, method, h, eps=eps,
+                                                denominator=denom)
+    assert abs(total.item() - ref_total.item()) <= 1e-5 * abs(ref_total.item())
+    worst = {n: rel_l2(grads[n], ref_grads[n]) for n in ref_grads}
+    assert max(worst.values()) <= 1e-5, worst
+
+
+@pytest.mark.parametrize("method", ["midpoint", "euler"])
+def test_bf16_autocast_gradients_match_oracle(method):
+    cfg = WIDE
+    ids, labels, denom = batch(cfg, 4, 11)
+    model = product_model(cfg, method, 0.5, 1e-6)
+    total, grads = product_step(model, ids, labels, denom, low=torch.bfloat16)
+    p = om.init_params(om.Config(**cfg), seed=1337)
+    ref_total, ref_grads, _ = om.loss_and_grads(p, om.Config(**cfg), ids, labels, method, 0.5, low=torch.bfloat16,
+                                                eps=1e-6, denominator=denom)
+    assert abs(total.item() - ref_total.item()) <= 2e-3 * abs(ref_total.item())
+    worst = {n: rel_l2(grads[n], ref_grads[n]) for n in ref_grads}
+    assert max(worst.values()) <= 2e-2, worst
+
+
+def test_cfg1_full_model_fp32_matches_oracle():
+    """BASELINE config 0 on the GPU path: 20.3M model, batch 4x512, fp32, eps 1e-6."""
+    cfg = dict()
+    model = product_model(cfg, "midpoint", 0.5, 1e-6)
+    stream = ost.synthetic_stream(4 * 512 + 1, seed=1337)
+    x, y, count = ost.batch_at(stream, 0, 4, 512, 4 * 512)
+    total, grads = product_step(model, x, y, count)
+    p = om.init_params(om.Config(), seed=1337)
+    ref_total, ref_grads, _ = om.loss_and_grads(p, om.Config(), x, y, "midpoint", 0.5, eps=1e-6, denominator=count)
+    assert abs(total.item() - ref_total.item()) <= 1e-5 * abs(ref_total.item())
+    worst = {n: rel_l2(grads[n], ref_grads[n]) for n in ref_grads}
+    assert max(worst.values()) <= 1e-5, sorted(worst.items(), key=lambda kv: -kv[1])[:3]
+
+
+@pytest.mark.parametrize("method", ["midpoint", "euler"])
+@pytest.mark.parametrize("amp", [None, torch.bfloat16])
+def test_reconstruction_reproduces_stored_states(method, amp):
+    from reversability_b200 import engine
+    import reversability_b200 as rb
+    model = product_model(WIDE, method, 0.5, 1e-6)
+    ids, _, _ = batch(WIDE, 3, 5)
+    cd = amp or torch.float32
+    x = model.embed(ids.to(DEV)).detach().reshape(-1, 256)
+    kern = engine.LayerKernels(8, 3, WIDE["max_sequence_length"], cd)
+    layers = [engine.LayerWeights.from_block(b, cd) for b in model.blocks]
+    p, q = x, x
+    states = [(p, q)]
+    for lw in layers:
+        p, q = kern.forward_midpoint(lw, p, q, 0.5) if method == "midpoint" else kern.forward_euler(lw, p, q)
+        states.append((p, q))
+    grads = [engine.LayerGrads.zeros_like(lw) for lw in layers]
+    dp, dq = torch.zeros_like(p), torch.zeros_like(q)
+    for i in reversed(range(len(layers))):
+        if method == "midpoint":
+            p, q, dp, dq = kern.backward_midpoint(layers[i], grads[i], p, q, dp, dq, 0.5)
+        else:
+            p, q, dp, dq = kern.backward_euler(layers[i], grads[i], p, q, dp, dq)
+        sp, sq = states[i]
+        # exact up to the fp32 rounding of one residual add/sub pair per layer
+        tol = 4 * torch.finfo(torch.float32).eps
+        assert (p - sp).abs().max().item() <= tol * (len(layers) - i) * sp.abs().max().item()
+        assert (q - sq).abs().max().item() <= tol * (len(layers) - i) * sq.abs().max().item()
+
+
+@pytest.mark.parametrize("core", ["reuse", "split"])
+@pytest.mark.parametrize("tile", [0, 5])
+def test_v3_cores_and_cached_head_match_oracle(core, tile):
+    """tests/test_optimized_v3.py:14-35 of the reference on the GPU path (fp32)."""
+    from reversability_b200.optimized_v3 import cached_head_backward, install_v3
+    cfg = dict(vocab_size=31, max_sequence_length=8, n_layers=3, n_heads=2, d_model=8 * 4, d_ff=64)
+    model = product_model(cfg, "midpoint", 0.5, seed=71)
+    install_v3(model, core_mode=core, mlp_tokens=tile)
+    g = torch.Generator().manual_seed(3)
+    ids = torch.randint(31, (5, 8), generator=g)
+    labels = ids.roll(-1, 1)
+    labels[-1, :] = -100
+    labels[0, -1] = -100
+    denom = int((labels != -100).sum())
+    total = cached_head_backward(model, ids.to(DEV), labels.to(DEV), denom, 7)
+    p = om.init_params(om.Config(**cfg), seed=71)
+    ref_total, ref_grads, _ = om.loss_and_grads(p, om.Config(**cfg), ids, labels, "midpoint", 0.5,
+                                                denominator=denom, core="reuse")
+    assert abs(total.item() - ref_total.item()) <= 2e-6 * abs(ref_total.item()) + 2e-5
+    for n, prm in model.named_parameters():
+        assert torch.isfinite(prm.grad).all()
+        assert rel_l2(prm.grad.cpu(), ref_grads[n]) <= 5e-5, n
+    assert model.lm_head.weight is model.token_embedding.weight
+
+
+def test_tiled_mlp_tiles_and_gradients():
+    """tests/test_optimized_v3.py:54-63 of the reference: tile count/bounds and full-input gradient."""
+    import reversability_b200.optimized_v3 as v3
+    sizes, original = [], v3.mlp_value
+
+    def observe(x, *args):
+        sizes.append(x.shape[0])
+        return original(x, *args)
+    v3.mlp_value = observe
+    try:
+        x = torch.randn(50, 8, 8, device=DEV, requires_grad=True)
+        up = torch.randn(32, 8, device=DEV, requires_grad=True)
+        down = torch.randn(8, 16, device=DEV, requires_grad=True)
+        y = v3.TiledMLP.apply(x, up, down, 37, False)
+        y.square().mean().backward()
+    finally:
+        v3.mlp_value = original
+    assert y.shape == (50, 8, 8)
+    assert len(sizes) == 2 * ((400 + 36) // 37) and max(sizes) <= 37
+    xr = x.detach().cpu().double().requires_grad_(True)
+    ur = up.detach().cpu().double().requires_grad_(True)
+    dr = down.detach().cpu().double().requires_grad_(True)
+    g_, v_ = F.linear(xr, ur).chunk(2, -1)
+    F.linear(F.silu(g_) * v_, dr).square().mean().backward()
+    assert rel_l2(x.grad.cpu(), xr.grad) < 1e-5
+    assert rel_l2(up.grad.cpu(), ur.grad) < 1e-5 and rel_l2(down.grad.cpu(), dr.grad) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_tiled_ce_full_vocabulary_tail_mask_and_scaled_backward(dtype):
+    """tests/test_kernels.py:19-34 of the reference, on the librevk CE kernel."""
+    from reversability_b200.kernels import cross_entropy_sum
+    torch.manual_seed(41)
+    a = torch.randn(17, 50257, device=DEV, dtype=dtype, requires_grad=True)
+    b = a.detach().clone().requires_grad_(True)
+    y = torch.tensor([0, 1023, 1024, 50256, -100] + list(range(12)), device=DEV)
+    with torch.autocast("cuda", enabled=dtype == torch.float16, dtype=torch.float16):
+        expected = F.cross_entropy(a, y, reduction="sum", ignore_index=-100)
+    actual = cross_entropy_sum(b, y)
+    (expected * .03125).backward()
+    (actual * .03125).backward()
+    torch.testing.assert_close(actual, expected.float(), rtol=.002, atol=.002)
+    relative = (a.grad - b.grad).norm() / a.grad.norm()
+    assert relative < (.02 if dtype == torch.float16 else 2e-5)
+    assert torch.count_nonzero(b.grad[4]) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+def test_fused_swiglu_tail_and_backward(dtype):
+    """tests/test_kernels.py:37-51 of the reference."""
+    from reversability_b200.kernels import FusedSwiGLU
+    torch.manual_seed(42)
+    a = torch.randn(3, 7, 66, device=DEV, dtype=dtype, requires_grad=True)
+    b = a.detach().clone().requires_grad_(True)
+    gate, value = a.chunk(2, dim=-1)
+    expected = F.silu(gate) * value
+    actual = FusedSwiGLU.apply(b)
+    upstream = torch.randn_like(actual)
+    expected.backward(upstream)
+    actual.backward(upstream)
+    tolerance = .003 if dtype == torch.float16 else 2e-5
+    torch.testing.assert_close(actual, expected, rtol=tolerance, atol=tolerance)
+    torch.testing.assert_close(b.grad, a.grad, rtol=tolerance, atol=tolerance)
+
+
+def test_fused_rmsnorm_full_tail_forward_backward():
+    """tests/test_optimized_v3.py:73-84 of the reference."""
+    from reversability_b200.kernels_v3 import FusedRMSNorm
+    torch.manual_seed(74)
+    x = torch.randn(3, 23, 256, device=DEV, requires_grad=True)
+    w = torch.randn(256, device=DEV, requires_grad=True)
+    u = x.detach().clone().requires_grad_(True)
+    v = w.detach().clone().requires_grad_(True)
+    expected = F.rms_norm(x, (256,), w, eps=torch.finfo(x.dtype).eps)
+    actual = FusedRMSNorm.apply(u, v, torch.finfo(x.dtype).eps)
+    g = torch.randn_like(actual)
+    expected.backward(g)
+    actual.backward(g)
+    torch.testing.assert_close(expected, actual, rtol=5e-5, atol=5e-6)
+    torch.testing.assert_close(x.grad, u.grad, rtol=5e-5, atol=5e-6)
+    torch.testing.assert_close(w.grad, v.grad, rtol=5e-5, atol=5e-5)
+
+
+def test_inverse_stack_saves_only_final_pair_and_parameters():
+    """tests/test_reversible.py:25-33 of the reference."""
+    import reversability_b200 as rb
+    for method in ("midpoint", "euler"):
+        model = rb.ReversibleLM(rb.ModelConfig(vocab_size=31, n_layers=7, n_heads=1, d_model=8, d_ff=16),
+                                method).to(DEV)
+        x = torch.randn(2, 4, 8, device=DEV, requires_grad=True)
+        y = model.core(x)
+        saved = y.grad_fn.saved_tensors
+        assert len(saved) == 2 + len(tuple(model.blocks.parameters()))
+        assert [tuple(t.shape) for t in saved[:2]] == [(2, 4, 8), (2, 4, 8)]

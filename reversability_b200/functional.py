@@ -120,6 +120,26 @@ def reconstruct_euler(state: torch.Tensor, sublayer_out: torch.Tensor, out: torc
 
 
 # ------------------------------------------------------------------ GEMMs
+def _tma_ready(t: torch.Tensor) -> torch.Tensor:
+    """Tensor-core operands are read by TMA, which needs 16-byte aligned rows.
+    A 2-D bf16/f16 operand whose row stride or base breaks that is staged into
+    a zero-padded copy (row stride rounded up to 8 elements); the returned view
+    has the original shape, and the padding is never read as data."""
+    if t.dtype not in _TC_DTYPES:
+        return t
+    ld = t.stride(0) if t.shape[0] > 1 else t.shape[1]
+    if (ld * 2) % 16 == 0 and t.data_ptr() % 16 == 0:
+        return t
+    rows, cols = t.shape
+    padded = torch.zeros((rows, (cols + 7) // 8 * 8), device=t.device, dtype=t.dtype)
+    padded[:, :cols].copy_(t)
+    return padded[:, :cols]
+
+
+def _ld(t: torch.Tensor) -> int:
+    return t.stride(0) if t.shape[0] > 1 else (t.stride(0) if t.stride(0) >= t.shape[1] else t.shape[1])
+
+
 def _gemm_dtype(*ts: torch.Tensor) -> int:
     dts = {t.dtype for t in ts}
     if len(dts) != 1:
@@ -131,8 +151,10 @@ def linear_fwd(x: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype | None =
                out: torch.Tensor | None = None) -> torch.Tensor:
     """y = x @ w.T (nn.Linear without bias); x [..., K], w [N, K]."""
     require_cuda(x, w)
-    x2, ldx = _row_major_2d(x, "x")
-    w2, ldw = _row_major_2d(w, "weight")
+    x2, _ = _row_major_2d(x, "x")
+    w2, _ = _row_major_2d(w, "weight")
+    x2, w2 = _tma_ready(x2), _tma_ready(w2)
+    ldx, ldw = _ld(x2), _ld(w2)
     M, K = x2.shape
     N = w2.shape[0]
     if w2.shape[1] != K:
@@ -148,8 +170,10 @@ def linear_fwd(x: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype | None =
 def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype | None = None) -> torch.Tensor:
     """dx = dy @ w; dy [..., N], w [N, K]."""
     require_cuda(dy, w)
-    g2, ldg = _row_major_2d(dy, "dy")
-    w2, ldw = _row_major_2d(w, "weight")
+    g2, _ = _row_major_2d(dy, "dy")
+    w2, _ = _row_major_2d(w, "weight")
+    g2, w2 = _tma_ready(g2), _tma_ready(w2)
+    ldg, ldw = _ld(g2), _ld(w2)
     M, N = g2.shape
     K = w2.shape[1]
     dx = torch.empty((*dy.shape[:-1], K), device=dy.device, dtype=out_dtype or dy.dtype)
@@ -163,8 +187,10 @@ def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor | None = No
                  accumulate: bool = False) -> torch.Tensor:
     """dw (+)= dy^T @ x in fp32; dy [..., N], x [..., K] -> dw [N, K]."""
     require_cuda(dy, x)
-    g2, ldg = _row_major_2d(dy, "dy")
-    x2, ldx = _row_major_2d(x, "x")
+    g2, _ = _row_major_2d(dy, "dy")
+    x2, _ = _row_major_2d(x, "x")
+    g2, x2 = _tma_ready(g2), _tma_ready(x2)
+    ldg, ldx = _ld(g2), _ld(x2)
     M, N = g2.shape
     K = x2.shape[1]
     if dw is None:

@@ -121,10 +121,17 @@ def test_reconstruction_reproduces_stored_states(method, amp):
         else:
             p, q, dp, dq = kern.backward_euler(layers[i], grads[i], p, q, dp, dq)
         sp, sq = states[i]
-        # exact up to the fp32 rounding of one residual add/sub pair per layer
-        tol = 4 * torch.finfo(torch.float32).eps
-        assert (p - sp).abs().max().item() <= tol * (len(layers) - i) * sp.abs().max().item()
-        assert (q - sq).abs().max().item() <= tol * (len(layers) - i) * sq.abs().max().item()
+        if amp is None:
+            # fp32: exact up to the rounding of one residual add/sub pair per layer
+            tol = 4 * torch.finfo(torch.float32).eps * (len(layers) - i)
+            assert (p - sp).abs().max().item() <= tol * sp.abs().max().item()
+            assert (q - sq).abs().max().item() <= tol * sq.abs().max().item()
+        else:
+            # bf16 force: a 1-ulp fp32 reconstruction error in p can move the next
+            # recomputed force by one bf16 ulp, exactly as in the reference; its own
+            # low-precision state gate is atol 5e-3 (validate_reversible.py:28).
+            assert (p - sp).abs().max().item() <= 1e-3
+            assert (q - sq).abs().max().item() <= 1e-3
 
 
 @pytest.mark.parametrize("core", ["reuse", "split"])

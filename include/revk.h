@@ -53,6 +53,9 @@ enum {
 };
 
 RK_API int rk_abi_version(void);
+/* Number of kernel launches this library has issued in the process (host-side
+ * counter; a CUDA-graph replay re-runs captured launches without counting). */
+RK_API unsigned long long rk_launch_count(void);
 RK_API const char* rk_status_string(int status);
 /* Copies the device status word of the current device to *out and clears it.
  * Synchronises `stream`. */
@@ -151,11 +154,32 @@ RK_API int rk_attn_bwd(const void* qkv, int64_t ldq, const void* out, const void
  * and its backward (train_baseline.py:262; Triton variant kernels.py:14-85).
  * logits: [rows, ld] (vocab valid columns), dtype RK_F32/RK_BF16/RK_F16.
  * loss_rows[r] = logsumexp(logits[r]) - logits[r, labels[r]] (0 for ignored rows).
- * dlogits[r, c] = (softmax(logits[r])[c] - [c == labels[r]]) * grad_scale, zero
- * rows for ignored labels; dlogits may alias logits (in place). fp32 math. */
+ * dlogits[r, c] = (softmax(logits[r])[c] - [c == labels[r]]) * scale, zero rows
+ * for ignored labels, where scale = grad_scale * (*grad_scale_dev) when
+ * grad_scale_dev (a device fp32 scalar, e.g. 1/update_targets kept on the GPU
+ * so a captured CUDA graph can be replayed with a new denominator) is not
+ * NULL, else grad_scale. dlogits may alias logits (in place). fp32 math. */
 RK_API int rk_cross_entropy_fwd_bwd(const void* logits, int64_t ld, int64_t vocab, const int64_t* labels,
-                                    int64_t rows, float grad_scale, float* loss_rows, void* dlogits, int64_t ldd,
-                                    int dtype, int ignore_index, void* stream);
+                                    int64_t rows, float grad_scale, const float* grad_scale_dev, float* loss_rows,
+                                    void* dlogits, int64_t ldd, int dtype, int ignore_index, void* stream);
+
+/* -------------------------------------------------------- Clip + AdamW
+ * Replace torch.nn.utils.clip_grad_norm_(params, max_norm) and
+ * torch.optim.AdamW(lr, betas, weight_decay).step() over the parameters of the
+ * whole model held in one flat fp32 buffer (train_baseline.py:152-154,272,280).
+ * scalars: device fp32[8]: [0] lr (set by the caller), [1] step count
+ * (incremented by prepare), [2] gradient norm, [3] clip coefficient,
+ * [4..6] derived per-step constants. prepare computes the global norm
+ * deterministically (fixed-order two-pass reduction) into scalars; step applies
+ * the clip coefficient and the AdamW update in one pass and, if params_c is
+ * non-NULL, writes the updated parameters in c_dtype (RK_BF16/RK_F16) too. */
+RK_API int64_t rk_clip_adamw_workspace(void);
+RK_API int rk_clip_adamw_prepare(const float* grads, int64_t n, float max_norm, float beta1, float beta2,
+                                 float weight_decay, float* workspace, int64_t workspace_bytes, float* scalars,
+                                 void* stream);
+RK_API int rk_adamw_step(float* params, const float* grads, float* exp_avg, float* exp_avg_sq, void* params_c,
+                         int c_dtype, int64_t n, const float* scalars, float beta1, float beta2, float eps,
+                         void* stream);
 
 #ifdef __cplusplus
 }

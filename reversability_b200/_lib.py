@@ -28,6 +28,7 @@ _f = ctypes.c_float
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
     "rk_abi_version": (_i, []),
+    "rk_launch_count": (ctypes.c_ulonglong, []),
     "rk_status_string": (ctypes.c_char_p, [_i]),
     "rk_device_status_read": (_i, [ctypes.POINTER(ctypes.c_uint), _p]),
     "rk_rmsnorm_fwd": (_i, [_p, _i, _i64, _p, _p, _i, _i64, _p, _i64, _i64, _f, _p]),
@@ -43,7 +44,10 @@ SIGNATURES: dict[str, tuple] = {
     "rk_gemm_wgrad": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p, _i64, _p]),
     "rk_attn_fwd": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p]),
     "rk_attn_bwd": (_i, [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _p]),
-    "rk_cross_entropy_fwd_bwd": (_i, [_p, _i64, _i64, _p, _i64, _f, _p, _p, _i64, _i, _i, _p]),
+    "rk_clip_adamw_workspace": (_i64, []),
+    "rk_clip_adamw_prepare": (_i, [_p, _i64, _f, _f, _f, _f, _p, _i64, _p, _p]),
+    "rk_adamw_step": (_i, [_p, _p, _p, _p, _p, _i, _i64, _p, _f, _f, _f, _p]),
+    "rk_cross_entropy_fwd_bwd": (_i, [_p, _i64, _i64, _p, _i64, _f, _p, _p, _p, _i64, _i, _i, _p]),
 }
 
 _lock = threading.Lock()
@@ -78,6 +82,11 @@ def lib():
             fn.argtypes = args
         _lib = handle
     return _lib
+
+
+def launch_count() -> int:
+    """Kernel launches issued by librevk so far in this process."""
+    return int(lib().rk_launch_count())
 
 
 def status_string(code: int) -> str:

@@ -35,8 +35,10 @@ __device__ __forceinline__ void merge(float& m, float& s, float m2, float s2) {
 template <typename T, int V>
 __global__ void __launch_bounds__(512) ce_kernel(const T* logits, int64_t ld, int vocab,
                                                  const int64_t* __restrict__ labels, float scale,
+                                                 const float* __restrict__ scale_dev,
                                                  float* __restrict__ loss_rows, T* dlogits,
                                                  int64_t ldd, int ignore_index, unsigned int* status) {
+  if (scale_dev) scale *= *scale_dev;
   __shared__ float sm_m[32], sm_s[32];
   __shared__ float s_lse;
   const int64_t row = blockIdx.x;
@@ -120,7 +122,7 @@ using namespace rk;
 namespace {
 template <typename T>
 int launch(const void* logits, int64_t ld, int64_t vocab, const int64_t* labels, int64_t rows, float scale,
-           float* loss_rows, void* dlogits, int64_t ldd, int ignore_index, cudaStream_t s) {
+           const float* scale_dev, float* loss_rows, void* dlogits, int64_t ldd, int ignore_index, cudaStream_t s) {
   constexpr int V = 16 / (int)sizeof(T);
   auto X = static_cast<const T*>(logits);
   auto D = static_cast<T*>(dlogits);
@@ -128,26 +130,27 @@ int launch(const void* logits, int64_t ld, int64_t vocab, const int64_t* labels,
   const bool vec = rk_host::aligned(logits, 16) && rk_host::aligned(dlogits, 16) &&
                    (ld * (int64_t)sizeof(T)) % 16 == 0 && (ldd * (int64_t)sizeof(T)) % 16 == 0;
   if (vec)
-    ce_kernel<T, V><<<(unsigned)rows, 512, 0, s>>>(X, ld, (int)vocab, labels, scale, loss_rows, D, ldd, ignore_index, st);
+    ce_kernel<T, V><<<(unsigned)rows, 512, 0, s>>>(X, ld, (int)vocab, labels, scale, scale_dev, loss_rows, D, ldd, ignore_index, st);
   else
-    ce_kernel<T, 1><<<(unsigned)rows, 512, 0, s>>>(X, ld, (int)vocab, labels, scale, loss_rows, D, ldd, ignore_index, st);
+    ce_kernel<T, 1><<<(unsigned)rows, 512, 0, s>>>(X, ld, (int)vocab, labels, scale, scale_dev, loss_rows, D, ldd, ignore_index, st);
   return rk_host::launch_status();
 }
 }  // namespace
 
 extern "C" int rk_cross_entropy_fwd_bwd(const void* logits, int64_t ld, int64_t vocab, const int64_t* labels,
-                                        int64_t rows, float grad_scale, float* loss_rows, void* dlogits,
-                                        int64_t ldd, int dtype, int ignore_index, void* stream) {
+                                        int64_t rows, float grad_scale, const float* grad_scale_dev,
+                                        float* loss_rows, void* dlogits, int64_t ldd, int dtype, int ignore_index,
+                                        void* stream) {
   if (!logits || !labels || !loss_rows || !dlogits || rows < 0 || vocab <= 0 || ld < vocab || ldd < vocab ||
       vocab >= (1ll << 31) || rows >= (1ll << 31))
     return RK_ERR_ARG;
   if (rows == 0) return RK_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
-    case RK_F32: return launch<float>(logits, ld, vocab, labels, rows, grad_scale, loss_rows, dlogits, ldd, ignore_index, s);
+    case RK_F32: return launch<float>(logits, ld, vocab, labels, rows, grad_scale, grad_scale_dev, loss_rows, dlogits, ldd, ignore_index, s);
     case RK_BF16:
-      return launch<__nv_bfloat16>(logits, ld, vocab, labels, rows, grad_scale, loss_rows, dlogits, ldd, ignore_index, s);
-    case RK_F16: return launch<__half>(logits, ld, vocab, labels, rows, grad_scale, loss_rows, dlogits, ldd, ignore_index, s);
+      return launch<__nv_bfloat16>(logits, ld, vocab, labels, rows, grad_scale, grad_scale_dev, loss_rows, dlogits, ldd, ignore_index, s);
+    case RK_F16: return launch<__half>(logits, ld, vocab, labels, rows, grad_scale, grad_scale_dev, loss_rows, dlogits, ldd, ignore_index, s);
     default: return RK_ERR_DTYPE;
   }
 }

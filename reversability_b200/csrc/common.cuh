@@ -194,7 +194,10 @@ __device__ __forceinline__ int elect_lane0() { return (threadIdx.x & 31) == 0; }
 
 // Host-side helpers shared by the translation units.
 namespace rk_host {
+// Counts every kernel launch the library makes (status.cu); read with rk_launch_count().
+void count_launch();
 inline int launch_status() {
+  count_launch();
   cudaError_t e = cudaGetLastError();
   return e == cudaSuccess ? RK_OK : RK_ERR_LAUNCH;
 }
@@ -202,5 +205,9 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 inline size_t dtype_size(int dt) { return dt == RK_F32 ? 4 : 2; }
 // Device address of the status word on the current device (status.cu).
 unsigned int* device_status_ptr();
+// Raises `kernel`'s dynamic shared-memory limit once per (kernel, device), so
+// that calls after the first (e.g. inside CUDA-graph capture) make no
+// attribute calls at all (status.cu).
+void ensure_smem_attr(const void* kernel, int bytes);
 inline bool dtype_ok(int dt) { return dt == RK_F32 || dt == RK_BF16 || dt == RK_F16; }
 }  // namespace rk_host

@@ -427,20 +427,6 @@ bool make_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows,
   return r == CUDA_SUCCESS;
 }
 
-// Raises the dynamic shared-memory limit of `kernel` once per (kernel, device).
-void ensure_smem_attr(const void* kernel, int bytes) {
-  static std::mutex mu;
-  static std::unordered_map<const void*, uint64_t> done;  // kernel -> device bit mask
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
-  std::lock_guard<std::mutex> lock(mu);
-  uint64_t& mask = done[kernel];
-  if (bit && (mask & bit)) return;
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  mask |= bit;
-}
-
 // Operand description for the tensor-core path.
 struct Operand {
   const void* ptr;
@@ -452,7 +438,7 @@ template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, typename TOut>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs g, int dtype, cudaStream_t s) {
   using L = TcSmem<BN, STAGES>;
   auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, EPI, TOut>;
-  ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)L::kTotal);
+  rk_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)L::kTotal);
   const int total = g.tiles_m * g.tiles_n * g.splits;
   int grid = sm_count();
   if (total < grid) grid = total;

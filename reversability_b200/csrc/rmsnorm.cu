@@ -194,7 +194,7 @@ int bwd_nv(const void* x, int64_t ldx, const float* w, const float* rstd, const 
 #define RK_BWD(N)                                                                                          \
   do {                                                                                                     \
     auto k = rmsnorm_bwd_kernel<Tx, Tg, Tdx, V, N>;                                                        \
-    if (smem > 48 * 1024) cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+    if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)smem);         \
     k<<<grid, block, smem, s>>>(X, ldx, w, rstd, G, lddy, D, lddx, partial, rows, width);                  \
   } while (0)
   if (nv <= 1) RK_BWD(1);

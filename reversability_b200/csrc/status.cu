@@ -1,4 +1,7 @@
 // Library-wide device status word and ABI bookkeeping entry points.
+#include <atomic>
+#include <mutex>
+#include <unordered_map>
 #include "common.cuh"
 
 namespace {
@@ -7,7 +10,11 @@ constexpr int kMaxDevices = 64;
 unsigned int* g_status_ptr[kMaxDevices] = {nullptr};
 }  // namespace
 
+std::atomic<unsigned long long> g_launches{0};
+
 namespace rk_host {
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 // The address is looked up once per device (with that device current) and cached.
 unsigned int* device_status_ptr() {
   int dev = 0;
@@ -19,9 +26,25 @@ unsigned int* device_status_ptr() {
   }
   return g_status_ptr[dev];
 }
+
+void ensure_smem_attr(const void* kernel, int bytes) {
+  static std::mutex mu;
+  static std::unordered_map<const void*, std::pair<uint64_t, int>> done;  // kernel -> (device mask, bytes)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+  std::lock_guard<std::mutex> lock(mu);
+  auto& entry = done[kernel];
+  if (bit && (entry.first & bit) && entry.second >= bytes) return;
+  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  entry.first |= bit;
+  if (bytes > entry.second) entry.second = bytes;
+}
 }  // namespace rk_host
 
 extern "C" int rk_abi_version(void) { return 1; }
+
+extern "C" unsigned long long rk_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 extern "C" const char* rk_status_string(int status) {
   switch (status) {

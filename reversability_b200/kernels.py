@@ -28,7 +28,7 @@ class TiledCrossEntropy(torch.autograd.Function):
         losses = torch.empty(rows, device=logits.device, dtype=torch.float32)
         probs = torch.empty_like(logits)
         # dlogits for a unit upstream gradient; backward scales it.
-        _lib.call("rk_cross_entropy_fwd_bwd", logits.data_ptr(), cols, cols, labels.data_ptr(), rows, 1.0,
+        _lib.call("rk_cross_entropy_fwd_bwd", logits.data_ptr(), cols, cols, labels.data_ptr(), rows, 1.0, None,
                   losses.data_ptr(), probs.data_ptr(), cols, _lib.code(logits.dtype), -100, _lib.stream_ptr())
         ctx.save_for_backward(probs)
         return losses.sum()

@@ -1,0 +1,259 @@
+"""B200 training update for the reversible models (the benchmark's "step").
+
+One update = `accumulation` microsteps of the reference trainer loop
+(scripts/train_baseline.py:247-285): forward, sum cross-entropy / update
+targets, reconstruction backward, gradient accumulation; then the global-norm
+clip, the warm-up/cosine learning rate and AdamW(0.9, 0.95, wd 0.1).
+
+Layout in HBM (all fixed at construction, so an update can be captured once in
+a CUDA graph and replayed):
+  - `flat`   fp32 [P]   every parameter (named_parameters order; the tied
+                         head/embedding once); module parameters are views
+  - `flat_c` bf16 [P]   compute copy, refreshed after each optimizer step;
+                         the GEMM weights and the head are views into it
+  - `gflat`  fp32 [P]   gradients; layer i's six gradients are contiguous, so
+                         each layer is one data-parallel all-reduce bucket
+  - logits   bf16 [B*T, Vpad]  the microstep's vocabulary logits, reused as the
+                         in-place dlogits; Vpad = V rounded up to 64 so every
+                         row starts 16-byte aligned for TMA
+Per microstep: embedding gather (torch), the fused stack forward, final norm,
+head GEMM over the whole microstep, fused CE forward+backward in place, head
+dgrad/wgrad, final-norm backward, fused reconstruction backward (engine.py),
+embedding scatter (torch index_add_).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from . import _lib, engine, functional as fn
+from .reversible import ReversibleLM
+
+F32 = torch.float32
+
+
+@dataclass
+class TrainSettings:
+    """Optimisation fields of configs/midpoint.json (plus the cfg2 batch shape)."""
+    batch_size: int = 29
+    sequence_length: int = 512
+    accumulation: int = 2
+    learning_rate: float = 6e-4
+    min_learning_rate: float = 6e-5
+    warmup_targets: int = 1_000_000
+    max_train_targets: int = 50_000_000
+    weight_decay: float = 0.1
+    beta1: float = 0.9
+    beta2: float = 0.95
+    grad_clip: float = 1.0
+    precision: str = "bf16"
+    norm_eps: float | None = 1e-6
+    mlp_tokens: int = 0
+
+
+def learning_rate(s: TrainSettings, committed: int, update_targets: int) -> float:
+    """train_baseline.py:273-277."""
+    progress = (committed + update_targets) / s.max_train_targets
+    warmup = min(1.0, (committed + update_targets) / s.warmup_targets)
+    cosine = s.min_learning_rate + 0.5 * (s.learning_rate - s.min_learning_rate) * (1 + math.cos(math.pi * progress))
+    return min(s.learning_rate * warmup, cosine)
+
+
+class ReversibleTrainer:
+    def __init__(self, model: ReversibleLM, settings: TrainSettings, process_group=None):
+        if not isinstance(model, ReversibleLM):
+            raise ValueError("ReversibleTrainer trains ReversibleLM models")
+        dev = next(model.parameters()).device
+        fn.require_cuda(next(model.parameters()))
+        self.model, self.s, self.dev = model, settings, dev
+        self.cfg = model.config
+        self.pg = process_group
+        self.world = dist.get_world_size(process_group) if process_group is not None else 1
+        self.cd = {"bf16": torch.bfloat16, "fp16": torch.float16, "fp32": torch.float32}[settings.precision]
+        if settings.norm_eps is not None:
+            for m in model.modules():
+                if isinstance(m, torch.nn.RMSNorm):
+                    m.eps = settings.norm_eps
+        # ---- flat parameter / gradient layout
+        named = list(model.named_parameters())
+        total = sum(p.numel() for _, p in named)
+        self.flat = torch.empty(total, device=dev, dtype=F32)
+        self.gflat = torch.zeros(total, device=dev, dtype=F32)
+        self.flat_c = torch.empty(total, device=dev, dtype=self.cd) if self.cd != F32 else self.flat
+        self.offsets = {}
+        off = 0
+        for name, p in named:
+            n = p.numel()
+            self.flat[off:off + n].copy_(p.detach().reshape(-1))
+            p.data = self.flat[off:off + n].view(p.shape)
+            p.grad = self.gflat[off:off + n].view(p.shape)
+            self.offsets[name] = (off, n, tuple(p.shape))
+            off += n
+        self._refresh_compute_copy()
+        self.layers = []
+        self.layer_grads = []
+        self.layer_slices = []
+        for i, b in enumerate(model.blocks):
+            names = [f"blocks.{i}.{k}" for k in ("attn_norm.weight", "attn.qkv.weight", "attn.proj.weight",
+                                                   "mlp_norm.weight", "mlp.up.weight", "mlp.down.weight")]
+            masters = [self.view(self.flat, n) for n in names]
+            lw = engine.LayerWeights(*masters, cd=self.cd, eps_attn=b.attn_norm.eps, eps_mlp=b.mlp_norm.eps)
+            lw.qkv_c, lw.proj_c, lw.up_c, lw.down_c = (self.view(self.flat_c, n) for n in names[1:3] + names[4:6])
+            self.layers.append(lw)
+            self.layer_grads.append(engine.LayerGrads([self.view(self.gflat, n) for n in names]))
+            first, last = self.offsets[names[0]], self.offsets[names[-1]]
+            self.layer_slices.append(self.gflat[first[0]:last[0] + last[1]])
+        self.tok = self.view(self.flat, "token_embedding.weight")
+        self.tok_c = self.view(self.flat_c, "token_embedding.weight")
+        self.pos = self.view(self.flat, "position_embedding.weight")
+        self.final_w = self.view(self.flat, "final_norm.weight")
+        self.g_tok = self.view(self.gflat, "token_embedding.weight")
+        self.g_pos = self.view(self.gflat, "position_embedding.weight")
+        self.g_final = self.view(self.gflat, "final_norm.weight")
+        # ---- static activation buffers
+        B, T = settings.batch_size, settings.sequence_length
+        if T > self.cfg.max_sequence_length:
+            raise ValueError("sequence_length exceeds the model maximum")
+        self.M = B * T
+        V = self.cfg.vocab_size
+        self.vpad = (V + 63) // 64 * 64
+        self.logits = torch.empty((self.M, self.vpad), device=dev, dtype=self.cd)
+        self.ids = torch.zeros((settings.accumulation, B, T), device=dev, dtype=torch.int64)
+        self.labels = torch.full((settings.accumulation, B, T), -100, device=dev, dtype=torch.int64)
+        self.inv_denominator = torch.ones((), device=dev, dtype=F32)
+        self.loss_sum = torch.zeros((), device=dev, dtype=F32)
+        self.kern = engine.LayerKernels(self.cfg.n_heads, B, T, self.cd, settings.mlp_tokens)
+        # AdamW state (flat, fp32) and the device scalar block of rk_clip_adamw_prepare
+        self.exp_avg = torch.zeros_like(self.flat)
+        self.exp_avg_sq = torch.zeros_like(self.flat)
+        self.opt_scalars = torch.zeros(8, device=dev, dtype=F32)
+        self.opt_scalars[0] = settings.learning_rate
+        self.norm_ws = torch.empty(_lib.lib().rk_clip_adamw_workspace() // 4, device=dev, dtype=F32)
+        self.comm = torch.cuda.Stream(device=dev) if self.world > 1 else None
+        self.graph = None
+
+    # ------------------------------------------------------------------ layout helpers
+    def view(self, buf: torch.Tensor, name: str) -> torch.Tensor:
+        off, n, shape = self.offsets[name]
+        return buf[off:off + n].view(shape)
+
+    def _refresh_compute_copy(self):
+        if self.flat_c is not self.flat:
+            self.flat_c.copy_(self.flat)
+
+    # ------------------------------------------------------------------ data
+    def stage_batches(self, batches, update_targets: int):
+        """Copies this rank's microstep batches (from data.update_batches) into
+        the static device buffers; the tail of a short update is padded with
+        ignored targets."""
+        self.ids.zero_()
+        self.labels.fill_(-100)
+        for m, (x, y, _) in enumerate(batches):
+            self.ids[m, :x.shape[0]].copy_(x, non_blocking=True)
+            self.labels[m, :y.shape[0]].copy_(y, non_blocking=True)
+        self.inv_denominator.fill_(1.0 / update_targets)
+
+    # ------------------------------------------------------------------ one microstep
+    def _microstep(self, m: int, last: bool):
+        cfg, s, kern = self.cfg, self.s, self.kern
+        B, T, d = s.batch_size, s.sequence_length, cfg.d_model
+        ids = self.ids[m].reshape(-1)
+        labels = self.labels[m].reshape(-1)
+        x = F.embedding(ids, self.tok) + self.pos[:T].repeat(B, 1)
+        p, q = engine.stack_forward(kern, self.layers, x, x, self.model.method, self.model.step_size)
+        out = q if self.model.method == "midpoint" else p
+        eps_f = self.model.final_norm.eps if self.model.final_norm.eps is not None else torch.finfo(F32).eps
+        hidden, rstd_f = fn.rmsnorm_fwd(out, self.final_w, eps_f, out_dtype=self.cd)
+        V = cfg.vocab_size
+        logits = self.logits[:, :V]
+        fn.linear_fwd(hidden, self.tok_c, out=logits)
+        loss_rows = torch.empty(self.M, device=self.dev, dtype=F32)
+        # dlogits = (softmax - onehot) / update_targets, in place over the logits
+        _lib.call("rk_cross_entropy_fwd_bwd", logits.data_ptr(), self.vpad, V, labels.data_ptr(), self.M, 1.0,
+                  self.inv_denominator.data_ptr(), loss_rows.data_ptr(), logits.data_ptr(), self.vpad,
+                  _lib.code(self.cd), -100, _lib.stream_ptr())
+        self.loss_sum += loss_rows.sum()
+        dhidden = fn.linear_dgrad(logits, self.tok_c)
+        fn.linear_wgrad(logits, hidden, dw=self.g_tok, accumulate=True)
+        dout, _ = fn.rmsnorm_bwd(out, self.final_w, rstd_f, dhidden, dx_dtype=F32, dw=self.g_final,
+                                 accumulate_dw=True)
+        zero = torch.zeros_like(dout)
+        dp, dq = (zero, dout) if self.model.method == "midpoint" else (dout, zero)
+        hook = self._bucket_hook if (last and self.world > 1) else None
+        _, _, dp, dq = engine.stack_backward(kern, self.layers, self.layer_grads, p, q, dp, dq, self.model.method,
+                                             self.model.step_size, on_layer_done=hook)
+        dx = dp + dq
+        self.g_tok.index_add_(0, ids, dx)
+        self.g_pos[:T] += dx.view(B, T, d).sum(0)
+
+    def _bucket_hook(self, layer: int):
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream())
+        self.comm.wait_event(ev)
+        with torch.cuda.stream(self.comm):
+            dist.all_reduce(self.layer_slices[layer], group=self.pg)
+
+    # ------------------------------------------------------------------ one update
+    def _update_body(self):
+        self.gflat.zero_()
+        self.loss_sum.zero_()
+        for m in range(self.s.accumulation):
+            self._microstep(m, last=(m == self.s.accumulation - 1))
+        if self.world > 1:
+            cur = torch.cuda.current_stream()
+            rest = [self.g_tok, self.g_pos, self.g_final]
+            ev = torch.cuda.Event()
+            ev.record(cur)
+            self.comm.wait_event(ev)
+            with torch.cuda.stream(self.comm):
+                for t in rest:
+                    dist.all_reduce(t, group=self.pg)
+            cur.wait_stream(self.comm)
+        self._optimizer_step()
+
+    def _optimizer_step(self):
+        """clip_grad_norm_(max_norm) then AdamW (train_baseline.py:272,280) in two fused kernels."""
+        s = self.s
+        _lib.call("rk_clip_adamw_prepare", self.gflat.data_ptr(), self.gflat.numel(), float(s.grad_clip),
+                  float(s.beta1), float(s.beta2), float(s.weight_decay), self.norm_ws.data_ptr(),
+                  self.norm_ws.numel() * 4, self.opt_scalars.data_ptr(), _lib.stream_ptr())
+        c_ptr = self.flat_c.data_ptr() if self.flat_c is not self.flat else None
+        _lib.call("rk_adamw_step", self.flat.data_ptr(), self.gflat.data_ptr(), self.exp_avg.data_ptr(),
+                  self.exp_avg_sq.data_ptr(), c_ptr, _lib.code(self.cd), self.flat.numel(),
+                  self.opt_scalars.data_ptr(), float(s.beta1), float(s.beta2), 1e-8, _lib.stream_ptr())
+
+    @property
+    def grad_norm(self) -> torch.Tensor:
+        """Pre-clip global gradient norm of the last update (device scalar)."""
+        return self.opt_scalars[2]
+
+    def update(self, lr: float | None = None):
+        """Runs one update on the staged batches; returns the device loss sum.
+        With capture() done, replays the CUDA graph."""
+        if lr is not None:
+            self.opt_scalars[0].fill_(lr)
+        if self.graph is not None:
+            self.graph.replay()
+        else:
+            self._update_body()
+        return self.loss_sum
+
+    def capture(self, warmup: int = 1):
+        """Captures one update as a CUDA graph. `warmup` eager updates run first
+        (on a side stream) so every kernel's one-time host set-up is done; the
+        optimizer state lives in preallocated buffers, so capture needs no
+        warm-up for correctness."""
+        side = torch.cuda.Stream(device=self.dev)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(warmup):
+                self._update_body()
+        torch.cuda.current_stream().wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self._update_body()
+        return self.graph

@@ -30,7 +30,7 @@ def test_library_rejects_bad_arguments_without_launching():
     assert lib.rk_gemm_fprop(None, 0, None, 0, None, 0, 4, 4, 4, 1, 1, None) == 1
     assert lib.rk_swiglu_fwd(None, None, 1, -1, 4, None) == 1
     assert lib.rk_attn_fwd(None, 0, None, 0, None, 1, 1, 32, 4, 1, None) == 1
-    assert lib.rk_cross_entropy_fwd_bwd(None, 0, 0, None, 1, 1.0, None, None, 0, 1, -100, None) == 1
+    assert lib.rk_cross_entropy_fwd_bwd(None, 0, 0, None, 1, 1.0, None, None, None, 0, 1, -100, None) == 1
 
 
 def test_public_names_match_reference_package():

@@ -232,3 +232,31 @@ def test_attention_deterministic():
     assert torch.equal(o1, o2) and torch.equal(l1, l2)
     do = torch.randn_like(o1)
     assert torch.equal(fn.attention_bwd(qkv, o1, do, l1, 8), fn.attention_bwd(qkv, o1, do, l1, 8))
+
+
+# ------------------------------------------------------------------ clip + AdamW
+@pytest.mark.parametrize("n,max_norm", [(20_340_736, 1.0), (1001, 1e9), (4099, 0.5)])
+def test_clip_adamw_matches_torch(n, max_norm):
+    from reversability_b200 import _lib
+    p0 = torch.randn(n, device=DEV)
+    ref = torch.nn.Parameter(p0.clone())
+    opt = torch.optim.AdamW([ref], lr=6e-4, betas=(0.9, 0.95), weight_decay=0.1)
+    p = p0.clone()
+    m, v = torch.zeros_like(p), torch.zeros_like(p)
+    pc = torch.empty(n, device=DEV, dtype=torch.bfloat16)
+    sc = torch.zeros(8, device=DEV)
+    ws = torch.empty(_lib.lib().rk_clip_adamw_workspace() // 4, device=DEV)
+    for step in range(3):
+        g = torch.randn(n, device=DEV) * (step + 1)
+        ref.grad = g.clone()
+        norm = torch.nn.utils.clip_grad_norm_([ref], max_norm)
+        opt.step()
+        sc[0] = 6e-4
+        _lib.call("rk_clip_adamw_prepare", g.data_ptr(), n, max_norm, 0.9, 0.95, 0.1, ws.data_ptr(),
+                  ws.numel() * 4, sc.data_ptr(), _lib.stream_ptr())
+        _lib.call("rk_adamw_step", p.data_ptr(), g.data_ptr(), m.data_ptr(), v.data_ptr(), pc.data_ptr(), _lib.BF16,
+                  n, sc.data_ptr(), 0.9, 0.95, 1e-8, _lib.stream_ptr())
+        assert abs(sc[2].item() - norm.item()) <= 1e-5 * norm.item()
+        assert sc[1].item() == step + 1
+        assert rel_l2(p - p0, ref.detach() - p0) < 1e-5
+    assert torch.equal(pc, p.bfloat16())

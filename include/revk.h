@@ -49,7 +49,8 @@ enum {
 enum {
   RK_DEV_GEMM_TIMEOUT = 1u << 0,
   RK_DEV_ATTN_TIMEOUT = 1u << 1,
-  RK_DEV_CE_LABEL = 1u << 2     /* a cross-entropy label outside [0, vocab) and != ignore_index */
+  RK_DEV_CE_LABEL = 1u << 2,    /* a cross-entropy label outside [0, vocab) and != ignore_index */
+  RK_DEV_EMB_INDEX = 1u << 3    /* an embedding id outside [0, vocab) */
 };
 
 RK_API int rk_abi_version(void);
@@ -180,6 +181,21 @@ RK_API int rk_clip_adamw_prepare(const float* grads, int64_t n, float max_norm, 
 RK_API int rk_adamw_step(float* params, const float* grads, float* exp_avg, float* exp_avg_sq, void* params_c,
                          int c_dtype, int64_t n, const float* scalars, float beta1, float beta2, float eps,
                          void* stream);
+
+/* ------------------------------------------------------------- Embedding
+ * Replace the token + learned position embedding of BaselineLM.forward /
+ * ReversibleLM.forward (model.py:98-101, reversible.py:105-106) and its
+ * backward. ids: int64 [rows] (rows = B*T, row r at position r % T);
+ * tok fp32 [V, d]; pos fp32 [>= T, d]; out fp32 [rows, d].
+ * Backward accumulates into g_tok [V, d] and g_pos [>= T, d] (fp32) in a fixed
+ * order: rows are grouped by id with a stable radix sort and each group is
+ * summed in row order, so results are bitwise reproducible. workspace: at
+ * least rk_embedding_bwd_workspace(rows, V) bytes. d must be a multiple of 4. */
+RK_API int rk_embedding_fwd(const int64_t* ids, const float* tok, const float* pos, float* out, int64_t rows,
+                            int64_t T, int64_t d, int64_t V, void* stream);
+RK_API int64_t rk_embedding_bwd_workspace(int64_t rows, int64_t V);
+RK_API int rk_embedding_bwd(const int64_t* ids, const float* dx, float* g_tok, float* g_pos, int64_t rows, int64_t T,
+                            int64_t d, int64_t V, void* workspace, int64_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -47,6 +47,9 @@ SIGNATURES: dict[str, tuple] = {
     "rk_clip_adamw_workspace": (_i64, []),
     "rk_clip_adamw_prepare": (_i, [_p, _i64, _f, _f, _f, _f, _p, _i64, _p, _p]),
     "rk_adamw_step": (_i, [_p, _p, _p, _p, _p, _i, _i64, _p, _f, _f, _f, _p]),
+    "rk_embedding_fwd": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
+    "rk_embedding_bwd_workspace": (_i64, [_i64, _i64]),
+    "rk_embedding_bwd": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _p]),
     "rk_cross_entropy_fwd_bwd": (_i, [_p, _i64, _i64, _p, _i64, _f, _p, _p, _p, _i64, _i, _i, _p]),
 }
 

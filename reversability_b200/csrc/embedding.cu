@@ -1,0 +1,148 @@
+// Token + learned position embedding, forward and backward (replaces
+// nn.Embedding lookups at model.py:101 / reversible.py:106 and their autograd
+// backward, including the tied-weight accumulation of the head gradient).
+//
+// Forward: x[r] = tok[ids[r]] + pos[r % T], one warp per row, 16-byte loads.
+// Backward, deterministic (no floating-point atomics):
+//   1. rows are sorted by token id with a stable radix sort (CUB, keys = ids,
+//      values = row indices), so equal ids become contiguous runs in row order;
+//   2. one CTA per run start sums its rows' gradients in that order, one
+//      thread per column, and adds the sum into g_tok[id];
+//   3. one CTA per position t sums dx[b*T + t] over b in order into g_pos[t].
+// Ids outside [0, V) set RK_DEV_EMB_INDEX and contribute nothing.
+#include <cub/cub.cuh>
+#include "vec.cuh"
+
+namespace rk {
+
+__global__ void __launch_bounds__(256) emb_fwd_kernel(const int64_t* __restrict__ ids, const float* __restrict__ tok,
+                                                      const float* __restrict__ pos, float* __restrict__ out,
+                                                      int64_t rows, int T, int d, int64_t V, unsigned int* status) {
+  const int lane = threadIdx.x & 31;
+  const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (r >= rows) return;
+  const int64_t id = ids[r];
+  const bool ok = id >= 0 && id < V;
+  if (!ok && lane == 0) flag_error(status, RK_DEV_EMB_INDEX);
+  const float* tr = tok + (ok ? id : 0) * d;
+  const float* pr = pos + (r % T) * d;
+  float* orow = out + r * d;
+  for (int c = lane * 4; c < d; c += 128) {
+    float a[4], b[4], o[4];
+    load_vec<float, 4>(tr + c, a);
+    load_vec<float, 4>(pr + c, b);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) o[e] = (ok ? a[e] : 0.f) + b[e];
+    store_vec<float, 4>(orow + c, o);
+  }
+}
+
+// Sort keys (ids outside [0, V) become V, a run the backward skips) and row indices.
+__global__ void keys_kernel(const int64_t* __restrict__ ids, int64_t* __restrict__ keys, int* __restrict__ rows_out,
+                            int64_t n, int64_t V) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const int64_t id = ids[i];
+    keys[i] = (id >= 0 && id < V) ? id : V;
+    rows_out[i] = (int)i;
+  }
+}
+
+// CTA i handles the run of equal sorted ids starting at i (and exits if i is not a run start).
+__global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restrict__ skeys,
+                                                          const int* __restrict__ srows,
+                                                          const float* __restrict__ dx, float* __restrict__ g_tok,
+                                                          int64_t rows, int d, int64_t V, unsigned int* status) {
+  const int64_t i = blockIdx.x;
+  const int64_t id = skeys[i];
+  if (i > 0 && skeys[i - 1] == id) return;
+  if (id < 0 || id >= V) {
+    if (threadIdx.x == 0) flag_error(status, RK_DEV_EMB_INDEX);
+    return;
+  }
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float s = 0.f;
+    for (int64_t j = i; j < rows && skeys[j] == id; ++j) s += dx[(int64_t)srows[j] * d + c];
+    g_tok[id * d + c] += s;
+  }
+}
+
+__global__ void __launch_bounds__(256) emb_pos_bwd_kernel(const float* __restrict__ dx, float* __restrict__ g_pos,
+                                                          int64_t rows, int T, int d) {
+  const int t = blockIdx.x;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float s = 0.f;
+    for (int64_t r = t; r < rows; r += T) s += dx[r * d + c];
+    g_pos[(int64_t)t * d + c] += s;
+  }
+}
+
+}  // namespace rk
+
+using namespace rk;
+
+namespace {
+int key_bits(int64_t V) {
+  int b = 1;
+  while (b < 63 && (1ll << b) < V) ++b;
+  return b;
+}
+size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+size_t cub_temp_bytes(int64_t rows, int64_t V) {
+  size_t temp = 0;
+  cub::DeviceRadixSort::SortPairs(nullptr, temp, (const int64_t*)nullptr, (int64_t*)nullptr, (const int*)nullptr,
+                                  (int*)nullptr, (int)rows, 0, key_bits(V + 1));
+  return temp;
+}
+}  // namespace
+
+extern "C" int rk_embedding_fwd(const int64_t* ids, const float* tok, const float* pos, float* out, int64_t rows,
+                                int64_t T, int64_t d, int64_t V, void* stream) {
+  if (!ids || !tok || !pos || !out || rows < 0 || T <= 0 || d <= 0 || V <= 0) return RK_ERR_ARG;
+  if (d % 4 || !rk_host::aligned(tok, 16) || !rk_host::aligned(pos, 16) || !rk_host::aligned(out, 16))
+    return RK_ERR_ALIGN;
+  if (rows == 0) return RK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  emb_fwd_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(ids, tok, pos, out, rows, (int)T, (int)d, V,
+                                                            rk_host::device_status_ptr());
+  return rk_host::launch_status();
+}
+
+extern "C" int64_t rk_embedding_bwd_workspace(int64_t rows, int64_t V) {
+  if (rows <= 0 || V <= 0) return 0;
+  return (int64_t)(2 * align256(rows * sizeof(int64_t)) + 2 * align256(rows * sizeof(int)) +
+                   align256(cub_temp_bytes(rows, V)));
+}
+
+extern "C" int rk_embedding_bwd(const int64_t* ids, const float* dx, float* g_tok, float* g_pos, int64_t rows,
+                                int64_t T, int64_t d, int64_t V, void* workspace, int64_t workspace_bytes,
+                                void* stream) {
+  if (!ids || !dx || !g_tok || !g_pos || rows < 0 || T <= 0 || d <= 0 || V <= 0 || rows >= (1ll << 31))
+    return RK_ERR_ARG;
+  if (rows == 0) return RK_OK;
+  if (!workspace || workspace_bytes < rk_embedding_bwd_workspace(rows, V)) return RK_ERR_WORKSPACE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  uint8_t* w = static_cast<uint8_t*>(workspace);
+  int64_t* keys = reinterpret_cast<int64_t*>(w);
+  w += align256(rows * sizeof(int64_t));
+  int64_t* skeys = reinterpret_cast<int64_t*>(w);
+  w += align256(rows * sizeof(int64_t));
+  int* rows_in = reinterpret_cast<int*>(w);
+  w += align256(rows * sizeof(int));
+  int* srows = reinterpret_cast<int*>(w);
+  w += align256(rows * sizeof(int));
+  size_t temp = cub_temp_bytes(rows, V);
+  keys_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(ids, keys, rows_in, rows, V);
+  int st = rk_host::launch_status();
+  if (st) return st;
+  if (cub::DeviceRadixSort::SortPairs(w, temp, keys, skeys, rows_in, srows, (int)rows, 0, key_bits(V + 1), s) !=
+      cudaSuccess)
+    return RK_ERR_LAUNCH;
+  rk_host::count_launch();
+  emb_tok_bwd_kernel<<<(unsigned)rows, 256, 0, s>>>(skeys, srows, dx, g_tok, rows, (int)d, V,
+                                                    rk_host::device_status_ptr());
+  st = rk_host::launch_status();
+  if (st) return st;
+  emb_pos_bwd_kernel<<<(unsigned)T, 256, 0, s>>>(dx, g_pos, rows, (int)T, (int)d);
+  return rk_host::launch_status();
+}

@@ -239,3 +239,28 @@ def attention_bwd(qkv: torch.Tensor, o: torch.Tensor, do: torch.Tensor, lse: tor
               lse.data_ptr(), dsum.data_ptr(), dqkv.data_ptr(), dqkv.stride(1), B, n_heads, D // n_heads, T,
               _lib.code(qkv.dtype), _lib.stream_ptr())
     return dqkv
+
+
+# ------------------------------------------------------------------ embedding
+def embedding_fwd(ids: torch.Tensor, tok: torch.Tensor, pos: torch.Tensor, out: torch.Tensor | None = None):
+    """x[b, t] = tok[ids[b, t]] + pos[t] (fp32) for ids [B, T]; returns [B*T, d]."""
+    require_cuda(ids, tok, pos)
+    B, T = ids.shape
+    d = tok.shape[1]
+    ids = ids.contiguous()
+    out = out if out is not None else torch.empty((B * T, d), device=tok.device, dtype=torch.float32)
+    _lib.call("rk_embedding_fwd", ids.data_ptr(), tok.data_ptr(), pos.data_ptr(), out.data_ptr(), B * T, T, d,
+              tok.shape[0], _lib.stream_ptr())
+    return out
+
+
+def embedding_bwd(ids: torch.Tensor, dx: torch.Tensor, g_tok: torch.Tensor, g_pos: torch.Tensor):
+    """Deterministically accumulates dx [B*T, d] into g_tok[ids] and g_pos[t]."""
+    require_cuda(ids, dx, g_tok, g_pos)
+    B, T = ids.shape
+    d = g_tok.shape[1]
+    ids = ids.contiguous()
+    ws_bytes = _lib.lib().rk_embedding_bwd_workspace(B * T, g_tok.shape[0])
+    ws = torch.empty(max(ws_bytes, 1), device=dx.device, dtype=torch.uint8)
+    _lib.call("rk_embedding_bwd", ids.data_ptr(), dx.contiguous().data_ptr(), g_tok.data_ptr(), g_pos.data_ptr(),
+              B * T, T, d, g_tok.shape[0], ws.data_ptr(), ws_bytes, _lib.stream_ptr())

@@ -16,10 +16,10 @@ a CUDA graph and replayed):
   - logits   bf16 [B*T, Vpad]  the microstep's vocabulary logits, reused as the
                          in-place dlogits; Vpad = V rounded up to 64 so every
                          row starts 16-byte aligned for TMA
-Per microstep: embedding gather (torch), the fused stack forward, final norm,
-head GEMM over the whole microstep, fused CE forward+backward in place, head
+Per microstep: embedding gather, the fused stack forward, final norm, head GEMM
+over the whole microstep, fused CE forward+backward in place, head
 dgrad/wgrad, final-norm backward, fused reconstruction backward (engine.py),
-embedding scatter (torch index_add_).
+deterministic embedding scatter. Every gradient is bitwise reproducible.
 """
 from __future__ import annotations
 
@@ -161,9 +161,9 @@ class ReversibleTrainer:
     def _microstep(self, m: int, last: bool):
         cfg, s, kern = self.cfg, self.s, self.kern
         B, T, d = s.batch_size, s.sequence_length, cfg.d_model
-        ids = self.ids[m].reshape(-1)
+        ids = self.ids[m]
         labels = self.labels[m].reshape(-1)
-        x = F.embedding(ids, self.tok) + self.pos[:T].repeat(B, 1)
+        x = fn.embedding_fwd(ids, self.tok, self.pos)
         p, q = engine.stack_forward(kern, self.layers, x, x, self.model.method, self.model.step_size)
         out = q if self.model.method == "midpoint" else p
         eps_f = self.model.final_norm.eps if self.model.final_norm.eps is not None else torch.finfo(F32).eps
@@ -187,8 +187,7 @@ class ReversibleTrainer:
         _, _, dp, dq = engine.stack_backward(kern, self.layers, self.layer_grads, p, q, dp, dq, self.model.method,
                                              self.model.step_size, on_layer_done=hook)
         dx = dp + dq
-        self.g_tok.index_add_(0, ids, dx)
-        self.g_pos[:T] += dx.view(B, T, d).sum(0)
+        fn.embedding_bwd(ids, dx, self.g_tok, self.g_pos)
 
     def _bucket_hook(self, layer: int):
         ev = torch.cuda.Event()

@@ -260,3 +260,26 @@ def test_clip_adamw_matches_torch(n, max_norm):
         assert sc[1].item() == step + 1
         assert rel_l2(p - p0, ref.detach() - p0) < 1e-5
     assert torch.equal(pc, p.bfloat16())
+
+
+# ------------------------------------------------------------------ embedding
+@pytest.mark.parametrize("B,T,V", [(29, 512, 50257), (3, 17, 101), (2, 64, 7)])
+def test_embedding_fwd_bwd_matches_torch_and_is_deterministic(B, T, V):
+    from reversability_b200 import functional as fn
+    import numpy as np
+    rng = np.random.default_rng(0)
+    ids = torch.from_numpy(np.minimum(rng.zipf(1.1, size=(B, T)) - 1, V - 1)).to(DEV)  # heavy repeats
+    tok = torch.randn(V, 256, device=DEV)
+    pos = torch.randn(max(T, 512), 256, device=DEV)
+    x = fn.embedding_fwd(ids, tok, pos)
+    assert torch.equal(x.view(B, T, 256), tok[ids] + pos[:T])
+    dx = torch.randn(B * T, 256, device=DEV)
+    g1, p1 = torch.ones_like(tok), torch.zeros_like(pos)
+    fn.embedding_bwd(ids, dx, g1, p1)
+    ref_t = torch.ones_like(tok, dtype=torch.float64).index_add_(0, ids.reshape(-1), dx.double())
+    ref_p = dx.double().view(B, T, 256).sum(0)
+    assert rel_l2(g1 - 1, ref_t - 1) < 1e-6
+    assert rel_l2(p1[:T], ref_p) < 1e-6 and torch.count_nonzero(p1[T:]) == 0
+    g2, p2 = torch.ones_like(tok), torch.zeros_like(pos)
+    fn.embedding_bwd(ids, dx, g2, p2)
+    assert torch.equal(g1, g2) and torch.equal(p1, p2)

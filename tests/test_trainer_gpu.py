@@ -74,12 +74,18 @@ def test_bf16_updates_match_oracle(method):
     assert math.sqrt(diff / upd) <= 0.05
 
 
-def test_tiled_mlp_trainer_matches_untiled_bitwise():
-    """The MLP token tile (TiledMLP's knob) changes memory, not results: tiles are
-    independent token ranges and every kernel is deterministic."""
-    a = run_pair("midpoint", "bf16", updates=1, mlp_tokens=0)[0]
-    b = run_pair("midpoint", "bf16", updates=1, mlp_tokens=70)[0]
-    assert torch.equal(a.flat, b.flat)
+def test_tiled_mlp_trainer_matches_untiled():
+    """The MLP token tile (TiledMLP's knob) bounds memory; only the summation
+    order of the MLP weight gradients changes (per-tile partial sums), so the
+    update agrees to fp32 rounding (the reference's fp32 update gate)."""
+    a, ra, oa, before = run_pair("midpoint", "bf16", updates=1, mlp_tokens=0)
+    b, _, ob, _ = run_pair("midpoint", "bf16", updates=1, mlp_tokens=70)
+    assert abs(oa[0][1] - ob[0][1]) <= 1e-5 * oa[0][1]
+    assert oa[0][0] == ob[0][0]  # the forward (and so the loss) is tile-independent
+    init = torch.cat([before[n].reshape(-1) for n in om.parameter_names(om.Config(**WIDE))]).to(DEV)
+    assert rel_l2(a.flat - b.flat + init, a.flat) < 1.0  # sanity: same layout
+    assert math.sqrt(float((a.flat - b.flat).double().square().sum()) /
+                     float((a.flat - init).double().square().sum())) <= 0.01
 
 
 def test_graph_replay_equals_eager_update():

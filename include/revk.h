@@ -42,7 +42,8 @@ enum {
   RK_ERR_LAUNCH = 4,      /* CUDA launch or driver call failed */
   RK_ERR_UNSUPPORTED = 5, /* shape outside what the kernel implements (e.g. width > 1024) */
   RK_ERR_WORKSPACE = 6,   /* caller workspace too small */
-  RK_ERR_DEVICE = 7       /* device status word non-zero (a bounded wait gave up) */
+  RK_ERR_DEVICE = 7,      /* device status word non-zero (a bounded wait gave up) */
+  RK_ERR_SCRATCH = 8      /* request larger than an allocation-free entry point's static scratch */
 };
 
 /* device status bits */
@@ -81,6 +82,22 @@ RK_API int64_t rk_rmsnorm_bwd_workspace(int64_t rows, int64_t width);
 RK_API int rk_rmsnorm_bwd(const void* x, int x_dtype, int64_t ldx, const float* w, const float* rstd, const void* dy,
                    int dy_dtype, int64_t lddy, void* dx, int dx_dtype, int64_t lddx, float* dw, int accumulate_dw,
                    float* dw_partial, int64_t workspace_bytes, int64_t rows, int64_t width, void* stream);
+
+/* Allocation-free rk_rmsnorm_bwd. It has no counterpart in the reference: it
+ * exists for callers that cannot supply device workspace — foreign-function
+ * hosts without a device allocator, plugins whose framework allocator owns all
+ * device memory, work issued during CUDA-graph capture — and is otherwise the
+ * same computation with the same arguments minus dw_partial/workspace_bytes.
+ * The weight-gradient partials live in a static device array of 2,424,832
+ * bytes (592 x 1024 fp32), held on every GPU that loads the library until exit;
+ * widths above 1024 return RK_ERR_SCRATCH. The library allocates nothing here.
+ * The first call on each device looks the array's address up (with that device
+ * current); make that first call before any stream capture. All calls share
+ * the one array, so calls that overlap on the GPU (different streams, or
+ * different host threads, on one device) race; serialise them. */
+RK_API int rk_rmsnorm_bwd_noalloc(const void* x, int x_dtype, int64_t ldx, const float* w, const float* rstd,
+                                  const void* dy, int dy_dtype, int64_t lddy, void* dx, int dx_dtype, int64_t lddx,
+                                  float* dw, int accumulate_dw, int64_t rows, int64_t width, void* stream);
 
 /* ------------------------------------------------------------------ SwiGLU
  * Replaces kernels.py:88-95 (_swiglu_forward) launched from kernels.py:120

@@ -34,6 +34,7 @@ SIGNATURES: dict[str, tuple] = {
     "rk_rmsnorm_fwd": (_i, [_p, _i, _i64, _p, _p, _i, _i64, _p, _i64, _i64, _f, _p]),
     "rk_rmsnorm_bwd_workspace": (_i64, [_i64, _i64]),
     "rk_rmsnorm_bwd": (_i, [_p, _i, _i64, _p, _p, _p, _i, _i64, _p, _i, _i64, _p, _i, _p, _i64, _i64, _i64, _p]),
+    "rk_rmsnorm_bwd_noalloc": (_i, [_p, _i, _i64, _p, _p, _p, _i, _i64, _p, _i, _i64, _p, _i, _i64, _i64, _p]),
     "rk_swiglu_fwd": (_i, [_p, _p, _i, _i64, _i64, _p]),
     "rk_swiglu_bwd": (_i, [_p, _p, _p, _i, _i64, _i64, _p]),
     "rk_reconstruct_midpoint": (_i, [_p, _p, _i, _f, _p, _i64, _p]),

@@ -7,6 +7,7 @@
 // over the rows a warp visits), then across the 8 warps of the CTA in shared
 // memory into one fp32 partial row per CTA, then by a second kernel over the
 // partials in a fixed order (deterministic, no atomics).
+#include <mutex>
 #include "vec.cuh"
 
 namespace rk {
@@ -274,4 +275,65 @@ extern "C" int rk_rmsnorm_bwd(const void* x, int x_dtype, int64_t ldx, const flo
   if (st != RK_OK) return st;
   rmsnorm_dw_reduce_kernel<<<(W + 255) / 256, 256, 0, s>>>(dw_partial, dw, parts, W, accumulate_dw);
   return rk_host::launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of rk_rmsnorm_bwd.
+//
+// Some callers cannot hand the library a workspace: a host runtime reaching
+// this library through a foreign-function binding with no device allocator of
+// its own, a plugin inside a framework whose caching allocator owns all device
+// memory, or code issuing work while a CUDA graph is being captured, where a
+// cudaMalloc would either be forbidden or synchronise the device. For them the
+// weight-gradient partials live in this file-scope device array instead, sized
+// for the largest request the kernel accepts: 592 partial rows (the fixed CTA
+// count of the backward) x 1024 columns of fp32 = 2,424,832 bytes, held by
+// every GPU that loads the library until the process exits.
+namespace {
+constexpr int64_t kNoallocMaxWidth = 1024;
+constexpr int64_t kNoallocScratchFloats = 592 * kNoallocMaxWidth;
+static __device__ __align__(256) float g_rmsnorm_noalloc_scratch[kNoallocScratchFloats];
+
+constexpr int kNoallocMaxDevices = 64;
+float* g_noalloc_ptr[kNoallocMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+// Device address of the scratch array on the current device. In host code the
+// array's name is only a host-side stand-in, so the address comes from
+// cudaGetSymbolAddress, once per device, with that device current.
+float* noalloc_scratch(int* status) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoallocMaxDevices) {
+    *status = RK_ERR_LAUNCH;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    float* p = nullptr;
+    if (cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_rmsnorm_noalloc_scratch) != cudaSuccess || !p) {
+      *status = RK_ERR_LAUNCH;
+      return nullptr;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  *status = RK_OK;
+  return g_noalloc_ptr[dev];
+}
+}  // namespace
+
+extern "C" int rk_rmsnorm_bwd_noalloc(const void* x, int x_dtype, int64_t ldx, const float* w, const float* rstd,
+                                      const void* dy, int dy_dtype, int64_t lddy, void* dx, int dx_dtype,
+                                      int64_t lddx, float* dw, int accumulate_dw, int64_t rows, int64_t width,
+                                      void* stream) {
+  if (width > kNoallocMaxWidth) return RK_ERR_SCRATCH;
+  if (rows < 0 || width <= 0) return RK_ERR_ARG;
+  const int64_t need = rk_rmsnorm_bwd_workspace(rows, width);
+  if (need > kNoallocScratchFloats * (int64_t)sizeof(float)) return RK_ERR_SCRATCH;
+  int st = RK_OK;
+  float* scratch = noalloc_scratch(&st);
+  if (!scratch) return st;
+  // Every partial row the kernel reads is written earlier in the same call, so
+  // stale contents from a previous call need no clearing.
+  return rk_rmsnorm_bwd(x, x_dtype, ldx, w, rstd, dy, dy_dtype, lddy, dx, dx_dtype, lddx, dw, accumulate_dw,
+                        scratch, kNoallocScratchFloats * (int64_t)sizeof(float), rows, width, stream);
 }

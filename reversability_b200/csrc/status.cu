@@ -56,6 +56,7 @@ extern "C" const char* rk_status_string(int status) {
     case RK_ERR_UNSUPPORTED: return "shape outside what the kernel implements";
     case RK_ERR_WORKSPACE: return "workspace too small";
     case RK_ERR_DEVICE: return "device status word set: a bounded device-side wait gave up";
+    case RK_ERR_SCRATCH: return "request exceeds the static scratch of an allocation-free entry point";
     default: return "unknown status";
   }
 }

@@ -1,0 +1,70 @@
+"""The allocation-free RMSNorm backward (rk_rmsnorm_bwd_noalloc) against the
+workspace-taking entry point (rk_rmsnorm_bwd), both called through the C ABI.
+
+The no-allocation entry point serves callers that cannot give the library
+device workspace: a host runtime that binds the library through an FFI and
+has no device allocator of its own, a plugin whose framework allocator owns all
+device memory, or work issued while a CUDA graph is being captured, where a
+cudaMalloc is forbidden or would synchronise the device. Its scratch is a
+static device array shared by every call, so the test makes two calls in a row
+with different shapes: the second must not be disturbed by what the first left
+in the scratch. This file is collected last so a run that stops at the first
+failure has run every other test before it.
+"""
+import pytest
+import torch
+
+from reversability_b200 import _lib
+
+DEV = "cuda"
+TOL = {"dx": dict(rtol=5e-5, atol=5e-6), "dw": dict(rtol=5e-5, atol=5e-5)}  # the RMSNorm tests' tolerances
+
+
+def _call_pair(x, w, dy, x_dt, dy_dt, dx_dt):
+    lib = _lib.lib()
+    rows, width = x.shape
+    s = _lib.stream_ptr()
+    y = torch.empty(rows, width, device=DEV, dtype=dy.dtype)
+    rstd = torch.empty(rows, device=DEV)
+    assert lib.rk_rmsnorm_fwd(x.data_ptr(), x_dt, width, w.data_ptr(), y.data_ptr(), dy_dt, width,
+                              rstd.data_ptr(), rows, width, 1e-6, s) == 0
+    ws_bytes = lib.rk_rmsnorm_bwd_workspace(rows, width)
+    ws = torch.empty(ws_bytes // 4, device=DEV)
+    dx_ref = torch.empty(rows, width, device=DEV, dtype=x.dtype)
+    dw_ref = torch.empty(width, device=DEV)
+    assert lib.rk_rmsnorm_bwd(x.data_ptr(), x_dt, width, w.data_ptr(), rstd.data_ptr(), dy.data_ptr(), dy_dt,
+                              width, dx_ref.data_ptr(), dx_dt, width, dw_ref.data_ptr(), 0, ws.data_ptr(), ws_bytes,
+                              rows, width, s) == 0
+    dx = torch.empty_like(dx_ref)
+    dw = torch.full((width,), float("nan"), device=DEV)
+    assert lib.rk_rmsnorm_bwd_noalloc(x.data_ptr(), x_dt, width, w.data_ptr(), rstd.data_ptr(), dy.data_ptr(),
+                                      dy_dt, width, dx.data_ptr(), dx_dt, width, dw.data_ptr(), 0, rows, width,
+                                      s) == 0
+    torch.cuda.synchronize()
+    return (dx, dw), (dx_ref, dw_ref)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtypes", [(torch.float32, torch.float32), (torch.float32, torch.bfloat16),
+                                    (torch.bfloat16, torch.bfloat16)])
+def test_noalloc_matches_workspace_entry_point_on_two_calls(dtypes):
+    xd, gd = dtypes
+    torch.manual_seed(2024)
+    # first call large (fills many partial rows), second call small and wider
+    for rows, width in ((14848, 256), (37, 1024)):
+        x = torch.randn(rows, width, device=DEV).to(xd)
+        w = torch.randn(width, device=DEV)
+        dy = torch.randn(rows, width, device=DEV).to(gd)
+        (dx, dw), (dx_ref, dw_ref) = _call_pair(x, w, dy, _lib.code(xd), _lib.code(gd), _lib.code(xd))
+        torch.testing.assert_close(dx.float(), dx_ref.float(), **TOL["dx"])
+        torch.testing.assert_close(dw, dw_ref, **TOL["dw"])
+    assert _lib.device_status() == 0
+
+
+@pytest.mark.gpu
+def test_noalloc_rejects_widths_beyond_its_scratch():
+    lib = _lib.lib()
+    # rejected on the host before any device work; the pointers are never touched
+    assert lib.rk_rmsnorm_bwd_noalloc(None, 0, 2048, None, None, None, 0, 2048, None, 0, 2048, None, 0, 16, 2048,
+                                      None) == 8
+    assert "static scratch" in _lib.status_string(8)

@@ -48,11 +48,17 @@ __global__ void keys_kernel(const int64_t* __restrict__ ids, int64_t* __restrict
   }
 }
 
-// CTA i handles the run of equal sorted ids starting at i (and exits if i is not a run start).
+// CTA i handles the run of equal sorted ids starting at i (and exits if i is
+// not a run start). The run's end is found by binary search in the sorted
+// keys. Warp w sums rows i+w, i+w+8, ... of the run (lanes over columns, 16-byte
+// loads), and the 8 warp sums are added in warp order, so the result does not
+// depend on scheduling. Long runs (frequent tokens under a Zipf distribution)
+// are thus read by 8 warps with many loads in flight.
 __global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restrict__ skeys,
                                                           const int* __restrict__ srows,
                                                           const float* __restrict__ dx, float* __restrict__ g_tok,
                                                           int64_t rows, int d, int64_t V, unsigned int* status) {
+  __shared__ float part[8][128];
   const int64_t i = blockIdx.x;
   const int64_t id = skeys[i];
   if (i > 0 && skeys[i - 1] == id) return;
@@ -60,10 +66,35 @@ __global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restr
     if (threadIdx.x == 0) flag_error(status, RK_DEV_EMB_INDEX);
     return;
   }
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    float s = 0.f;
-    for (int64_t j = i; j < rows && skeys[j] == id; ++j) s += dx[(int64_t)srows[j] * d + c];
-    g_tok[id * d + c] += s;
+  int64_t lo = i + 1, hi = rows;  // first index with key != id
+  while (lo < hi) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (skeys[mid] == id) lo = mid + 1; else hi = mid;
+  }
+  const int64_t end = lo;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int c0 = 0; c0 < d; c0 += 128) {
+    const int c = c0 + lane * 4;
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    if (c < d) {
+#pragma unroll 4
+      for (int64_t j = i + warp; j < end; j += 8) {
+        float v[4];
+        load_vec<float, 4>(dx + (int64_t)srows[j] * d + c, v);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] += v[e];
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) part[warp][lane * 4 + e] = acc[e];
+    __syncthreads();
+    if (threadIdx.x < 128 && c0 + (int)threadIdx.x < d) {
+      float sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) sum += part[w][threadIdx.x];
+      g_tok[id * d + c0 + threadIdx.x] += sum;
+    }
+    __syncthreads();
   }
 }
 
@@ -119,6 +150,7 @@ extern "C" int rk_embedding_bwd(const int64_t* ids, const float* dx, float* g_to
                                 void* stream) {
   if (!ids || !dx || !g_tok || !g_pos || rows < 0 || T <= 0 || d <= 0 || V <= 0 || rows >= (1ll << 31))
     return RK_ERR_ARG;
+  if (d % 4 || !rk_host::aligned(dx, 16)) return RK_ERR_ALIGN;
   if (rows == 0) return RK_OK;
   if (!workspace || workspace_bytes < rk_embedding_bwd_workspace(rows, V)) return RK_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);

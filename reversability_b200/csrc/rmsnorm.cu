@@ -122,14 +122,26 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const Tx* __restrict__
   }
 }
 
-// dw[c] (+)= sum over parts in index order.
-__global__ void rmsnorm_dw_reduce_kernel(const float* __restrict__ partial, float* __restrict__ dw, int parts,
-                                         int width, int accumulate) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= width) return;
+// dw[c] (+)= sum over parts. A CTA owns 32 columns; thread (g, c) sums parts
+// g, g+8, g+16, ... of column c (coalesced 128-byte rows), then the 8 group
+// sums are added in group order: a fixed order, so dw is deterministic.
+__global__ void __launch_bounds__(256) rmsnorm_dw_reduce_kernel(const float* __restrict__ partial,
+                                                                float* __restrict__ dw, int parts, int width,
+                                                                int accumulate) {
+  __shared__ float grp[8][32];
+  const int lc = threadIdx.x & 31, g = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + lc;
   float s = 0.f;
-  for (int p = 0; p < parts; ++p) s += partial[(int64_t)p * width + c];
-  dw[c] = accumulate ? dw[c] + s : s;
+  if (c < width)
+    for (int p = g; p < parts; p += 8) s += partial[(int64_t)p * width + c];
+  grp[g][lc] = s;
+  __syncthreads();
+  if (g == 0 && c < width) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += grp[k][lc];
+    dw[c] = accumulate ? dw[c] + t : t;
+  }
 }
 
 }  // namespace rk
@@ -273,7 +285,7 @@ extern "C" int rk_rmsnorm_bwd(const void* x, int x_dtype, int64_t ldx, const flo
   else
     return RK_ERR_DTYPE;
   if (st != RK_OK) return st;
-  rmsnorm_dw_reduce_kernel<<<(W + 255) / 256, 256, 0, s>>>(dw_partial, dw, parts, W, accumulate_dw);
+  rmsnorm_dw_reduce_kernel<<<(W + 31) / 32, 256, 0, s>>>(dw_partial, dw, parts, W, accumulate_dw);
   return rk_host::launch_status();
 }
 

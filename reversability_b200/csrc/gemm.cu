@@ -25,6 +25,7 @@
 // writes an fp32 partial tile and a second kernel sums slices in index order,
 // so weight gradients are bitwise deterministic for a given shape.
 #include <cudaTypedefs.h>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 #include "common.cuh"
@@ -37,26 +38,56 @@ struct GemmArgs {
   int splits;            // reduction slices (1 = none)
   int kb_per_split;      // 64-wide k blocks per slice
   int kb_total;          // ceil(K / 64)
-  void* out;             // EPI_STORE: [M, N] row-major (ldo); EPI_PARTIAL: fp32 [splits][M][N]
+  int split_rows;        // EPI_TMA with splits > 1: rows between split slices (M rounded up to 128)
+  void* out;             // EPI_STORE: [M, N] row-major (ldo); split slices: fp32 [splits][split_rows][N]
   int64_t ldo;
   int out_dtype;
   unsigned int* status;
 };
 
-enum { EPI_STORE = 0, EPI_PARTIAL = 1, EPI_ACCUM = 2 };  // ACCUM: fp32 out += acc
+// STORE: direct row stores; PARTIAL: fp32 split slices; ACCUM: fp32 out += acc;
+// TMA: rows staged in 128-byte-swizzled shared memory, written by TMA tensor
+// stores (split slices too, at row split*split_rows); TMA_ADD: the same staging
+// written with TMA reduce-add (out += acc; every element has exactly one
+// writing CTA, so the result is deterministic).
+enum { EPI_STORE = 0, EPI_PARTIAL = 1, EPI_ACCUM = 2, EPI_TMA = 3, EPI_TMA_ADD = 4 };
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kThreads = 192;
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, bool STAGE_OUT = false>
 struct TcSmem {
   static constexpr uint32_t kA = kBM * kBK * 2;  // 16 KB
   static constexpr uint32_t kB = BN * kBK * 2;
   static constexpr uint32_t kStage = kA + kB;
+  // output staging: 4 epilogue warps x 2 buffers x (32 rows x 128 bytes)
+  static constexpr uint32_t kOut = STAGE_OUT ? 4 * 2 * 4096 : 0;
   static constexpr uint32_t kBarriers = (2 * STAGES + 5) * 8;
-  static constexpr uint32_t kTotal = 1024 /*align slack*/ + STAGES * kStage + kBarriers + 16;
+  static constexpr uint32_t kTotal = 1024 /*align slack*/ + STAGES * kStage + kOut + kBarriers + 16;
 };
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// Tiled TMA store of a shared-memory box to global (bulk async-group).
+__device__ __forceinline__ void tma_store_2d(const void* tmap, uint32_t src, int x, int y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(tmap), "r"(src),
+               "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void tma_reduce_add_2d(const void* tmap, uint32_t src, int x, int y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   tmap),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 template <typename T>
 __device__ __forceinline__ void accum_row_chunk(T* dst, float (&v)[32], int valid, bool vec_ok) {
@@ -105,13 +136,14 @@ __device__ __forceinline__ void store_row_chunk(T* dst, const float (&v)[32], in
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmArgs g, const uint32_t idesc) {
-  using L = TcSmem<BN, STAGES>;
+                   const __grid_constant__ CUtensorMap tmC, const GemmArgs g, const uint32_t idesc) {
+  using L = TcSmem<BN, STAGES, EPI == EPI_TMA || EPI == EPI_TMA_ADD>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * L::kA;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStage);
+  uint8_t* sOut = smem + STAGES * L::kStage;  // EPI_TMA staging (1024-aligned)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStage + L::kOut);
   const uint32_t full0 = smem_u32(bars);
   const uint32_t empty0 = full0 + STAGES * 8;
   const uint32_t tfull0 = empty0 + STAGES * 8;
@@ -266,13 +298,59 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const int row = m0 + quarter * 32 + lane;
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if constexpr (EPI == EPI_TMA || EPI == EPI_TMA_ADD) {
+        // Each warp stages its 32 rows, CW columns at a time, in a 128-byte
+        // swizzled layout (16-byte chunk j of row r at j ^ (r % 8): conflict-free
+        // stores) and writes them with one TMA store per chunk; two buffers per
+        // warp let the next chunk be staged while the previous store drains.
+        constexpr int CW = 128 / (int)sizeof(TOut);
+        constexpr int PER16 = 16 / (int)sizeof(TOut);
+        uint8_t* stage = sOut + (warp - 2) * 8192;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += CW) {
+          float v[CW];
+#pragma unroll
+          for (int q = 0; q < CW / 32; ++q) {
+            float part[32];
+            tmem_ld_32cols(t_row + c + q * 32, part);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[q * 32 + j] = part[j];
+          }
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+          uint8_t* buf = stage + ((c / CW) & 1) * 4096;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 raw;
+            TOut* e = reinterpret_cast<TOut*>(&raw);
+#pragma unroll
+            for (int k = 0; k < PER16; ++k) e[k] = Dt<TOut>::from_f(v[j * PER16 + k]);
+            *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) = raw;
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            const int y = split * g.split_rows + m0 + quarter * 32;
+            if constexpr (EPI == EPI_TMA_ADD) tma_reduce_add_2d(&tmC, smem_u32(buf), n0 + c, y);
+            else tma_store_2d(&tmC, smem_u32(buf), n0 + c, y);
+            bulk_commit();
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(tempty0 + 8 * acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
+      const int row = m0 + quarter * 32 + lane;
       TOut* out_row;
       int64_t ldo;
       if constexpr (EPI == EPI_PARTIAL) {
         ldo = g.N;
-        out_row = reinterpret_cast<TOut*>(g.out) + (int64_t)split * g.M * g.N + (int64_t)row * ldo;
+        out_row = reinterpret_cast<TOut*>(g.out) + (int64_t)split * g.split_rows * g.N + (int64_t)row * ldo;
       } else {
         ldo = g.ldo;
         out_row = reinterpret_cast<TOut*>(g.out) + (int64_t)row * ldo;
@@ -298,6 +376,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  if constexpr (EPI == EPI_TMA || EPI == EPI_TMA_ADD) {
+    if (warp >= 2 && lane == 0) bulk_wait_all();
+  }
   __syncthreads();
   if (*s_abort && threadIdx.x == 0) {
     // Wait (bounded) for the TMA loads this CTA issued that no MMA consumed.
@@ -312,13 +393,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// dw[i] (+)= sum_s partial[s][i], slices summed in index order.
+// dw[r, c] (+)= sum_s partial[s][r][c] (slices `slice_rows` rows apart), in slice order.
 __global__ void split_reduce_kernel(const float* __restrict__ partial, int splits, int64_t rows, int64_t cols,
-                                    float* __restrict__ dw, int64_t lddw, int accumulate) {
+                                    int64_t slice_rows, float* __restrict__ dw, int64_t lddw, int accumulate) {
   const int64_t n = rows * cols;
+  const int64_t slice = slice_rows * cols;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
     float s = 0.f;
-    for (int k = 0; k < splits; ++k) s += partial[(int64_t)k * n + i];
+    for (int k = 0; k < splits; ++k) s += partial[(int64_t)k * slice + i];
     const int64_t r = i / cols, c = i - r * cols;
     float* d = dw + r * lddw + c;
     *d = accumulate ? *d + s : s;
@@ -435,35 +517,66 @@ struct Operand {
 };
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, typename TOut>
-int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, GemmArgs g, int dtype, cudaStream_t s) {
-  using L = TcSmem<BN, STAGES>;
+int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmArgs g, int dtype,
+              cudaStream_t s) {
+  using L = TcSmem<BN, STAGES, EPI == EPI_TMA || EPI == EPI_TMA_ADD>;
   auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, EPI, TOut>;
   rk_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)L::kTotal);
   const int total = g.tiles_m * g.tiles_n * g.splits;
   int grid = sm_count();
   if (total < grid) grid = total;
   const uint32_t idesc = idesc_f16(kBM, BN, dtype == RK_BF16 ? 1 : 0, A_MN ? 1 : 0, B_MN ? 1 : 0);
-  kern<<<grid, kThreads, L::kTotal, s>>>(ta, tb, g, idesc);
+  kern<<<grid, kThreads, L::kTotal, s>>>(ta, tb, tc, g, idesc);
   return rk_host::launch_status();
 }
 
 template <int BN, int EPI, typename TOut>
-int dispatch_major(const CUtensorMap& ta, const CUtensorMap& tb, bool a_mn, bool b_mn, const GemmArgs& g, int dtype,
-                   cudaStream_t s) {
+int dispatch_major(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, bool a_mn, bool b_mn,
+                   const GemmArgs& g, int dtype, cudaStream_t s) {
   constexpr int ST = BN == 256 ? 4 : 6;
-  if (!a_mn && !b_mn) return launch_tc<BN, ST, false, false, EPI, TOut>(ta, tb, g, dtype, s);
-  if (!a_mn && b_mn) return launch_tc<BN, ST, false, true, EPI, TOut>(ta, tb, g, dtype, s);
-  if (a_mn && b_mn) return launch_tc<BN, ST, true, true, EPI, TOut>(ta, tb, g, dtype, s);
+  if (!a_mn && !b_mn) return launch_tc<BN, ST, false, false, EPI, TOut>(ta, tb, tc, g, dtype, s);
+  if (!a_mn && b_mn) return launch_tc<BN, ST, false, true, EPI, TOut>(ta, tb, tc, g, dtype, s);
+  if (a_mn && b_mn) return launch_tc<BN, ST, true, true, EPI, TOut>(ta, tb, tc, g, dtype, s);
   return RK_ERR_UNSUPPORTED;
+}
+
+// Output tensor map for the TMA-store epilogue: [M, N] row-major, box CW x 32 rows.
+bool make_out_map(CUtensorMap* map, void* base, uint64_t N, uint64_t M, uint64_t ld, int out_dtype) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const uint32_t esz = out_dtype == RK_F32 ? 4 : 2;
+  cuuint64_t dims[2] = {N, M};
+  cuuint64_t strides[1] = {ld * esz};
+  cuuint32_t box[2] = {128 / esz, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = out_dtype == RK_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                 : out_dtype == RK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                        : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// Output-tile width: 256 (fewer A-tile reads, measured faster than 128 on every
+// shape of this model, including the narrow N=256 ones); 128 only for N <= 128.
+// REVK_GEMM_BN=128|256 in the environment pins it (a tuning override).
+int pick_bn(int M, int N) {
+  (void)M;
+  static int forced = [] {
+    const char* e = getenv("REVK_GEMM_BN");
+    return e ? atoi(e) : 0;
+  }();
+  if (forced == 128 || forced == 256) return forced;
+  return N <= 128 ? 128 : 256;
 }
 
 // Tensor-core GEMM: C[M,N] = sum_k A(m,k) B(n,k).
 int tc_gemm(Operand a, Operand b, int M, int N, int K, int dtype, void* out, int64_t ldo, int out_dtype, int splits,
-            cudaStream_t s, bool accumulate = false) {
+            cudaStream_t s, bool accumulate = false, int split_rows = 0) {
   const size_t esz = 2;
   if (!rk_host::aligned(a.ptr, 16) || !rk_host::aligned(b.ptr, 16)) return RK_ERR_ALIGN;
   if ((a.ld * esz) % 16 || (b.ld * esz) % 16) return RK_ERR_ALIGN;
-  const int BN = (N > 128) ? 256 : 128;
+  const int BN = pick_bn(M, N);
   CUtensorMap ta, tb;
   bool ok;
   if (a.mn_major) ok = make_map(&ta, a.ptr, (uint64_t)M, (uint64_t)K, (uint64_t)a.ld, dtype, 64, 64);
@@ -485,26 +598,57 @@ int tc_gemm(Operand a, Operand b, int M, int N, int K, int dtype, void* out, int
   g.ldo = ldo;
   g.out_dtype = out_dtype;
   g.status = rk_host::device_status_ptr();
+  g.split_rows = 0;
+  CUtensorMap tc = ta;  // placeholder unless a TMA epilogue is used
+  const bool mn_a = a.mn_major, mn_b = b.mn_major;
+  const size_t osz = out_dtype == RK_F32 ? 4 : 2;
   if (splits > 1) {
-    if (BN == 256) return dispatch_major<256, EPI_PARTIAL, float>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
-    return dispatch_major<128, EPI_PARTIAL, float>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
+    if (split_rows < M) return RK_ERR_ARG;
+    g.split_rows = split_rows;
+    // slices are split_rows (>= tiles_m*128) rows apart, so a tile's rows past
+    // M never reach the next slice and the whole tile can be TMA-stored
+    if (split_rows >= g.tiles_m * kBM && rk_host::aligned(out, 16) && (N * 4) % 16 == 0 &&
+        make_out_map(&tc, out, (uint64_t)N, (uint64_t)split_rows * g.splits, (uint64_t)N, RK_F32)) {
+      if (BN == 256) return dispatch_major<256, EPI_TMA, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+      return dispatch_major<128, EPI_TMA, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+    }
+    if (BN == 256) return dispatch_major<256, EPI_PARTIAL, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+    return dispatch_major<128, EPI_PARTIAL, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
   }
   if (accumulate) {
     if (out_dtype != RK_F32) return RK_ERR_DTYPE;
-    if (BN == 256) return dispatch_major<256, EPI_ACCUM, float>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
-    return dispatch_major<128, EPI_ACCUM, float>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
+    if (rk_host::aligned(out, 16) && (ldo * 4) % 16 == 0 &&
+        make_out_map(&tc, out, (uint64_t)N, (uint64_t)M, (uint64_t)ldo, RK_F32)) {
+      if (BN == 256) return dispatch_major<256, EPI_TMA_ADD, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+      return dispatch_major<128, EPI_TMA_ADD, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+    }
+    if (BN == 256) return dispatch_major<256, EPI_ACCUM, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+    return dispatch_major<128, EPI_ACCUM, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
   }
+  const bool tma_out = rk_host::aligned(out, 16) && (ldo * (int64_t)osz) % 16 == 0 &&
+                       make_out_map(&tc, out, (uint64_t)N, (uint64_t)M, (uint64_t)ldo, out_dtype);
   switch (out_dtype) {
     case RK_F32:
-      if (BN == 256) return dispatch_major<256, EPI_STORE, float>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
-      return dispatch_major<128, EPI_STORE, float>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
+      if (tma_out) {
+        if (BN == 256) return dispatch_major<256, EPI_TMA, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+        return dispatch_major<128, EPI_TMA, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+      }
+      if (BN == 256) return dispatch_major<256, EPI_STORE, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+      return dispatch_major<128, EPI_STORE, float>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
     case RK_BF16:
-      if (BN == 256)
-        return dispatch_major<256, EPI_STORE, __nv_bfloat16>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
-      return dispatch_major<128, EPI_STORE, __nv_bfloat16>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
+      if (tma_out) {
+        if (BN == 256) return dispatch_major<256, EPI_TMA, __nv_bfloat16>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+        return dispatch_major<128, EPI_TMA, __nv_bfloat16>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+      }
+      if (BN == 256) return dispatch_major<256, EPI_STORE, __nv_bfloat16>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+      return dispatch_major<128, EPI_STORE, __nv_bfloat16>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
     case RK_F16:
-      if (BN == 256) return dispatch_major<256, EPI_STORE, __half>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
-      return dispatch_major<128, EPI_STORE, __half>(ta, tb, a.mn_major, b.mn_major, g, dtype, s);
+      if (tma_out) {
+        if (BN == 256) return dispatch_major<256, EPI_TMA, __half>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+        return dispatch_major<128, EPI_TMA, __half>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+      }
+      if (BN == 256) return dispatch_major<256, EPI_STORE, __half>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+      return dispatch_major<128, EPI_STORE, __half>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
     default:
       return RK_ERR_DTYPE;
   }
@@ -578,7 +722,8 @@ extern "C" int rk_gemm_dgrad(const void* dy, int64_t lddy, const void* w, int64_
 
 extern "C" int64_t rk_gemm_wgrad_workspace(int64_t M, int64_t N, int64_t K) {
   const int s = wgrad_splits(M, N, K);
-  return (int64_t)s * N * K * (int64_t)sizeof(float);
+  const int64_t slice_rows = (N + kBM - 1) / kBM * kBM;
+  return (int64_t)s * slice_rows * K * (int64_t)sizeof(float);
 }
 
 extern "C" int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, float* dw, int64_t lddw,
@@ -601,16 +746,14 @@ extern "C" int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_
   if (splits == 1)  // enough output tiles: write (or accumulate into) dw directly, no workspace
     return tc_gemm({dy, lddy, true}, {x, ldx, true}, (int)N, (int)K, (int)M, dtype, dw, lddw, RK_F32, 1, s,
                    accumulate != 0);
-  const int64_t need = (int64_t)(splits > 1 ? splits : 1) * N * K * (int64_t)sizeof(float);
+  const int64_t slice_rows = (N + kBM - 1) / kBM * kBM;
+  const int64_t need = (int64_t)splits * slice_rows * K * (int64_t)sizeof(float);
   if (!workspace || workspace_bytes < need) return RK_ERR_WORKSPACE;
-  int st;
-  if (splits > 1)
-    st = tc_gemm({dy, lddy, true}, {x, ldx, true}, (int)N, (int)K, (int)M, dtype, workspace, K, RK_F32, splits, s);
-  else
-    st = tc_gemm({dy, lddy, true}, {x, ldx, true}, (int)N, (int)K, (int)M, dtype, workspace, K, RK_F32, 1, s);
+  const int st = tc_gemm({dy, lddy, true}, {x, ldx, true}, (int)N, (int)K, (int)M, dtype, workspace, K, RK_F32,
+                         splits, s, false, (int)slice_rows);
   if (st != RK_OK) return st;
   int64_t blocks = (N * K + 255) / 256;
   if (blocks > 148 * 8) blocks = 148 * 8;
-  split_reduce_kernel<<<(unsigned)blocks, 256, 0, s>>>(workspace, splits, N, K, dw, lddw, accumulate);
+  split_reduce_kernel<<<(unsigned)blocks, 256, 0, s>>>(workspace, splits, N, K, slice_rows, dw, lddw, accumulate);
   return rk_host::launch_status();
 }

@@ -31,6 +31,7 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from . import _lib, engine, functional as fn
+from .dist import GradBuckets
 from .reversible import ReversibleLM
 
 F32 = torch.float32
@@ -133,7 +134,10 @@ class ReversibleTrainer:
         self.opt_scalars = torch.zeros(8, device=dev, dtype=F32)
         self.opt_scalars[0] = settings.learning_rate
         self.norm_ws = torch.empty(_lib.lib().rk_clip_adamw_workspace() // 4, device=dev, dtype=F32)
-        self.comm = torch.cuda.Stream(device=dev) if self.world > 1 else None
+        # DP buckets: one per layer (launched as the last microstep's sweep passes it),
+        # then the embedding, position and final-norm gradients
+        self.buckets = GradBuckets(self.layer_slices + [self.g_tok, self.g_pos, self.g_final], process_group,
+                                   dev) if self.world > 1 else None
         self.graph = None
 
     # ------------------------------------------------------------------ layout helpers
@@ -190,11 +194,7 @@ class ReversibleTrainer:
         fn.embedding_bwd(ids, dx, self.g_tok, self.g_pos)
 
     def _bucket_hook(self, layer: int):
-        ev = torch.cuda.Event()
-        ev.record(torch.cuda.current_stream())
-        self.comm.wait_event(ev)
-        with torch.cuda.stream(self.comm):
-            dist.all_reduce(self.layer_slices[layer], group=self.pg)
+        self.buckets.launch(layer)
 
     # ------------------------------------------------------------------ one update
     def _update_body(self):
@@ -203,15 +203,10 @@ class ReversibleTrainer:
         for m in range(self.s.accumulation):
             self._microstep(m, last=(m == self.s.accumulation - 1))
         if self.world > 1:
-            cur = torch.cuda.current_stream()
-            rest = [self.g_tok, self.g_pos, self.g_final]
-            ev = torch.cuda.Event()
-            ev.record(cur)
-            self.comm.wait_event(ev)
-            with torch.cuda.stream(self.comm):
-                for t in rest:
-                    dist.all_reduce(t, group=self.pg)
-            cur.wait_stream(self.comm)
+            n = len(self.layers)
+            for i in range(n, n + 3):
+                self.buckets.launch(i)
+            self.buckets.finish()
         self._optimizer_step()
 
     def _optimizer_step(self):

@@ -1,0 +1,122 @@
+"""Data-parallel host logic on CPU ranks (gloo, world size 2): the per-layer
+gradient buckets sum correctly and in the same order on every rank, the rank
+windows reproduce one global batch, and a rank that never joins makes the
+others' collective fail within the process-group timeout (host-side failure,
+no GPU involved)."""
+import datetime
+import os
+import socket
+import time
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _init(rank, world, port, timeout_s=30):
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def _bucket_worker(rank, world, port, queue):
+    try:
+        import sys
+        sys.path.insert(0, os.getcwd())
+        from reversability_b200.dist import GradBuckets
+        from reversability_b200 import data as rdata
+        _init(rank, world, port)
+        torch.manual_seed(rank)
+        flat = torch.randn(1000)
+        sizes = [100, 250, 50, 400, 200]
+        offs = [0]
+        for n in sizes:
+            offs.append(offs[-1] + n)
+        slices = [flat[offs[i]:offs[i + 1]] for i in range(len(sizes))]
+        expected = torch.zeros(1000)
+        for r in range(world):
+            torch.manual_seed(r)
+            expected += torch.randn(1000)
+        b = GradBuckets(slices, None, torch.device("cpu"))
+        for i in reversed(range(3)):  # layers finish in reverse order
+            b.launch(i)
+        b.launch(3)
+        b.launch(4)
+        order = b.finish()
+        orders = [None] * world
+        dist.all_gather_object(orders, order)
+        ok_sum = torch.allclose(flat, expected, rtol=1e-6, atol=1e-6)
+        # data windows: concatenating the ranks' batches equals one global batch_at
+        B, T, acc = 2, 8, 2
+        stream = rdata.synthetic_stream(world * acc * B * T * 2 + 1, seed=4, vocab_size=101, eos=100, mean_doc=30.0)
+        batches, targets = rdata.update_batches(stream, 0, rank, world, B, T, acc, len(stream) - 1)
+        mine = torch.stack([x for x, _, _ in batches])
+        gathered = [torch.empty_like(mine) for _ in range(world)]
+        dist.all_gather(gathered, mine)
+        gx, _, gc = rdata.batch_at(stream, 0, world * acc * B, T, world * acc * B * T)
+        pieces = [gathered[r][m] for m in range(acc) for r in range(world)]
+        ok_data = torch.equal(torch.cat(pieces), gx) and targets == gc
+        queue.put((rank, ok_sum, orders[0] == orders[1], ok_data))
+        dist.destroy_process_group()
+    except Exception as exc:  # report instead of hanging the parent
+        queue.put((rank, repr(exc), False, False))
+
+
+def _timeout_worker(rank, world, port, queue):
+    try:
+        _init(rank, world, port, timeout_s=5)
+        if rank == 1:
+            os._exit(0)  # leaves between steps: nothing of this rank is in flight
+        t0 = time.time()
+        try:
+            dist.all_reduce(torch.ones(4))
+            queue.put((rank, "no error", time.time() - t0))
+        except Exception as exc:
+            queue.put((rank, type(exc).__name__, time.time() - t0))
+    except Exception as exc:
+        queue.put((rank, "setup:" + repr(exc), 0.0))
+
+
+def _run(target, world=2, timeout=120):
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = []
+    deadline = time.time() + timeout
+    while len(results) < world and time.time() < deadline:
+        try:
+            results.append(queue.get(timeout=1))
+        except Exception:
+            if all(not p.is_alive() for p in procs) and queue.empty():
+                break
+    for p in procs:
+        p.join(timeout=10)
+        if p.is_alive():
+            p.kill()
+    return results
+
+
+def test_grad_buckets_and_rank_windows_gloo():
+    res = _run(_bucket_worker)
+    assert len(res) == 2, res
+    for rank, ok_sum, same_order, ok_data in res:
+        assert ok_sum is True, (rank, ok_sum)
+        assert same_order and ok_data, (rank, same_order, ok_data)
+
+
+def test_missing_rank_makes_collective_fail_within_timeout():
+    res = _run(_timeout_worker)
+    survivors = [r for r in res if r[0] == 0]
+    assert survivors, res
+    _, outcome, elapsed = survivors[0]
+    assert outcome != "no error" and not outcome.startswith("setup"), survivors
+    assert elapsed < 60

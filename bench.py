@@ -42,8 +42,8 @@ FLOP_PER_TARGET = 143_255_040  # 4 x body (fwd + attention) + 3 x head, cfg2 (20
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["librevk", "reference"], default="librevk")
     ap.add_argument("--method", choices=["midpoint", "euler"], default="midpoint")
     ap.add_argument("--batch", type=int, default=29)
@@ -83,7 +83,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.reader = threading.Thread(target=self._read, daemon=True)
             self.reader.start()

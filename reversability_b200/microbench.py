@@ -1,0 +1,208 @@
+"""Isolated kernel microbenchmark and ncu driver.
+
+    python -m reversability_b200.microbench [--only NAME[,NAME...]] [--iters N]
+
+Workload: 16,896 tokens x width 256 in bf16 (activations N(0,1), weights
+N(0,0.02)); RMSNorm fwd+bwd, SwiGLU fwd+bwd (gate/up 256->1024, i.e. u is
+[N, 2048], h is [N, 1024]), the MLP GEMMs 256->2048->256 forward and backward,
+and the midpoint reconstruct step x_prev = x_next - 2h*F on fp32 residuals
+N(0,1) (2h = 1, fp32 force). Also the cfg2 head GEMM and attention.
+
+Each kernel is launched `iters` times from one captured CUDA graph, cycling
+through enough input/output buffer sets that every launch misses L2 (sets
+total > 126 MB), and timed with CUDA events on the launching stream.
+Algorithmic bytes / FLOPs per launch are the minimal traffic / work of the
+operation (each input read once, each output written once). Prints one JSON
+object per kernel: achieved GB/s or TFLOP/s and the fraction of the measured
+peaks in MEASURED_PEAKS.json (fallback 6650 GB/s, 1590 TFLOP/s).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import torch
+
+from . import _lib, functional as fn
+
+N_TOK, D, FF = 16_896, 256, 1_024
+L2_BYTES = 126 * 1024 * 1024
+
+
+def peaks():
+    p = Path(__file__).resolve().parents[1] / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("hbm_gbs", 6650.0), d.get("bf16_tflops", 1590.0), "measured"
+    return 6650.0, 1590.0, "fallback"
+
+
+def sets_for(bytes_per_set: int) -> int:
+    return max(2, -(-2 * L2_BYTES // max(bytes_per_set, 1)))
+
+
+def time_graph(launch, nsets: int, iters: int) -> float:
+    """Average device time (us) of launch(k) over `iters` launches cycling k."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for k in range(min(nsets, 3)):
+            launch(k)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(iters):
+            launch(i % nsets)
+    g.replay()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) * 1e3 / iters
+
+
+def bench_rmsnorm(iters):
+    per = 2 * N_TOK * D * 3 + 4 * N_TOK
+    ns = sets_for(per)
+    w = torch.randn(D, device="cuda") * 0.02 + 1
+    xs = [torch.randn(N_TOK, D, device="cuda").bfloat16() for _ in range(ns)]
+    ys = [torch.empty_like(x) for x in xs]
+    rs = [torch.empty(N_TOK, device="cuda") for _ in range(ns)]
+    gs = [torch.randn(N_TOK, D, device="cuda").bfloat16() for _ in range(ns)]
+    dxs = [torch.empty_like(x) for x in xs]
+    dw = torch.empty(D, device="cuda")
+    ws_bytes = _lib.lib().rk_rmsnorm_bwd_workspace(N_TOK, D)
+    ws = torch.empty(ws_bytes // 4, device="cuda")
+    s = lambda: _lib.stream_ptr()
+
+    def fwd(k):
+        _lib.call("rk_rmsnorm_fwd", xs[k].data_ptr(), _lib.BF16, D, w.data_ptr(), ys[k].data_ptr(), _lib.BF16, D,
+                  rs[k].data_ptr(), N_TOK, D, 1e-6, s())
+
+    def bwd(k):
+        _lib.call("rk_rmsnorm_bwd", xs[k].data_ptr(), _lib.BF16, D, w.data_ptr(), rs[k].data_ptr(), gs[k].data_ptr(),
+                  _lib.BF16, D, dxs[k].data_ptr(), _lib.BF16, D, dw.data_ptr(), 0, ws.data_ptr(), ws_bytes, N_TOK, D,
+                  s())
+    out = []
+    for name, f, nbytes in (("rmsnorm_fwd", fwd, 4 * N_TOK * D + 4 * N_TOK),
+                            ("rmsnorm_bwd", bwd, 6 * N_TOK * D + 4 * N_TOK)):
+        us = time_graph(f, ns, iters)
+        out.append(("hbm", name, nbytes, us))
+    return out
+
+
+def bench_swiglu(iters):
+    per = 2 * N_TOK * 2 * FF * 2 + 2 * N_TOK * FF * 2
+    ns = sets_for(per)
+    us_ = [torch.randn(N_TOK, 2 * FF, device="cuda").bfloat16() for _ in range(ns)]
+    hs = [torch.empty(N_TOK, FF, device="cuda", dtype=torch.bfloat16) for _ in range(ns)]
+    dhs = [torch.randn(N_TOK, FF, device="cuda").bfloat16() for _ in range(ns)]
+    dus = [torch.empty_like(u) for u in us_]
+
+    def fwd(k):
+        _lib.call("rk_swiglu_fwd", us_[k].data_ptr(), hs[k].data_ptr(), _lib.BF16, N_TOK, FF, _lib.stream_ptr())
+
+    def bwd(k):
+        _lib.call("rk_swiglu_bwd", us_[k].data_ptr(), dhs[k].data_ptr(), dus[k].data_ptr(), _lib.BF16, N_TOK, FF,
+                  _lib.stream_ptr())
+    return [("hbm", "swiglu_fwd", 2 * N_TOK * 2 * FF + 2 * N_TOK * FF, time_graph(fwd, ns, iters)),
+            ("hbm", "swiglu_bwd", 2 * N_TOK * 2 * FF * 2 + 2 * N_TOK * FF, time_graph(bwd, ns, iters))]
+
+
+def bench_reconstruct(iters):
+    per = 12 * N_TOK * D
+    ns = sets_for(per)
+    xn = [torch.randn(N_TOK * D, device="cuda") for _ in range(ns)]
+    f = [torch.randn(N_TOK * D, device="cuda") for _ in range(ns)]
+    xp = [torch.empty_like(x) for x in xn]
+
+    def run(k):
+        _lib.call("rk_reconstruct_midpoint", xn[k].data_ptr(), f[k].data_ptr(), _lib.F32, 1.0, xp[k].data_ptr(),
+                  N_TOK * D, _lib.stream_ptr())
+    return [("hbm", "reconstruct_midpoint", 12 * N_TOK * D, time_graph(run, ns, iters))]
+
+
+def bench_mlp_gemms(iters):
+    ns = 2
+    x = [torch.randn(N_TOK, D, device="cuda").bfloat16() for _ in range(ns)]
+    up = (torch.randn(2 * FF, D, device="cuda") * 0.02).bfloat16()
+    down = (torch.randn(D, FF, device="cuda") * 0.02).bfloat16()
+    u = [torch.empty(N_TOK, 2 * FF, device="cuda", dtype=torch.bfloat16) for _ in range(ns)]
+    h = [torch.randn(N_TOK, FF, device="cuda").bfloat16() for _ in range(ns)]
+    y = [torch.empty(N_TOK, D, device="cuda", dtype=torch.bfloat16) for _ in range(ns)]
+    gy = [torch.randn(N_TOK, D, device="cuda").bfloat16() for _ in range(ns)]
+    gu = [torch.randn(N_TOK, 2 * FF, device="cuda").bfloat16() for _ in range(ns)]
+    dw_up, dw_down = torch.zeros(2 * FF, D, device="cuda"), torch.zeros(D, FF, device="cuda")
+
+    def fwd(k):
+        fn.linear_fwd(x[k], up, out=u[k])
+        fn.linear_fwd(h[k], down, out=y[k])
+
+    def bwd(k):
+        fn.linear_dgrad(gy[k], down)
+        fn.linear_wgrad(gy[k], h[k], dw=dw_down, accumulate=True)
+        fn.linear_dgrad(gu[k], up)
+        fn.linear_wgrad(gu[k], x[k], dw=dw_up, accumulate=True)
+    f_fwd = 2 * N_TOK * D * 2 * FF + 2 * N_TOK * FF * D
+    return [("tensor", "mlp_gemms_fwd", f_fwd, time_graph(fwd, ns, iters)),
+            ("tensor", "mlp_gemms_bwd", 2 * f_fwd, time_graph(bwd, ns, iters))]
+
+
+def bench_head(iters):
+    M, V = 29 * 512, 50257
+    vpad = (V + 63) // 64 * 64
+    hid = torch.randn(M, D, device="cuda").bfloat16()
+    w = (torch.randn(V, D, device="cuda") * 0.02).bfloat16()
+    logits = torch.empty(M, vpad, device="cuda", dtype=torch.bfloat16)[:, :V]
+
+    def run(k):
+        fn.linear_fwd(hid, w, out=logits)
+    return [("tensor", "head_fprop_gemm", 2 * M * V * D, time_graph(run, 1, max(iters // 10, 3)))]
+
+
+def bench_attention(iters):
+    B, T, H = 29, 512, 8
+    qkv = torch.randn(B, T, 3 * D, device="cuda").bfloat16()
+    o, lse = fn.attention_fwd(qkv, H)
+    do = torch.randn_like(o)
+
+    def fwd(k):
+        fn.attention_fwd(qkv, H, out=o)
+
+    def bwd(k):
+        fn.attention_bwd(qkv, o, do, lse, H)
+    flops = 4 * (T * (T + 1) // 2) * (D // H) * B * H
+    return [("tensor", "attention_fwd", flops, time_graph(fwd, 1, iters)),
+            ("tensor", "attention_bwd", int(2.5 * flops), time_graph(bwd, 1, iters))]
+
+
+BENCHES = {"rmsnorm": bench_rmsnorm, "swiglu": bench_swiglu, "reconstruct": bench_reconstruct,
+           "mlp_gemms": bench_mlp_gemms, "head": bench_head, "attention": bench_attention}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default=",".join(BENCHES))
+    ap.add_argument("--iters", type=int, default=50)
+    args = ap.parse_args()
+    hbm, tf, kind = peaks()
+    for name in args.only.split(","):
+        for bound, kname, work, us in BENCHES[name](args.iters):
+            if bound == "hbm":
+                ach = work / (us * 1e-6) / 1e9
+                rec = {"kernel": kname, "bound": "hbm", "bytes_per_launch": work, "us": us, "achieved": ach,
+                       "unit": "GB/s", "peak": hbm, "frac": ach / hbm}
+            else:
+                ach = work / (us * 1e-6) / 1e12
+                rec = {"kernel": kname, "bound": "tensor", "flops_per_launch": work, "us": us, "achieved": ach,
+                       "unit": "TFLOP/s", "peak": tf, "frac": ach / tf}
+            rec["peak_source"] = kind
+            print(json.dumps(rec), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -83,6 +83,23 @@ RK_API int rk_rmsnorm_bwd(const void* x, int x_dtype, int64_t ldx, const float* 
                    int dy_dtype, int64_t lddy, void* dx, int dx_dtype, int64_t lddx, float* dw, int accumulate_dw,
                    float* dw_partial, int64_t workspace_bytes, int64_t rows, int64_t width, void* stream);
 
+/* Residual add fused into RMSNorm: s = x + a (fp32), y = rmsnorm(s) * w
+ * (model.py:67-68, reversible.py:18: mlp_norm(x + attention)). x fp32, a in
+ * a_dtype, y in y_dtype, rows contiguous (ld = width, width % 4 == 0).
+ * sum_out (fp32, may be NULL) receives s; rstd may be NULL. */
+RK_API int rk_add_rmsnorm_fwd(const float* x, const void* a, int a_dtype, const float* w, void* y, int y_dtype,
+                              float* sum_out, float* rstd, int64_t rows, int64_t width, float eps, void* stream);
+/* RMSNorm backward (fp32 input, rows contiguous) with the reversible step's
+ * cotangent bookkeeping fused into its epilogue: dx_out = dx + residual
+ * (residual may be NULL); if lp_out is not NULL it receives, in lp_dtype,
+ * round(lp_add + round(dx)) when lp_add is given (the low-precision sum
+ * autograd forms when a bf16 tensor has two consumers) or round(dx_out)
+ * otherwise. Workspace as rk_rmsnorm_bwd. */
+RK_API int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float* rstd, const void* dy, int dy_dtype,
+                                const float* residual, const void* lp_add, void* lp_out, int lp_dtype, float* dx_out,
+                                float* dw, int accumulate_dw, float* dw_partial, int64_t workspace_bytes,
+                                int64_t rows, int64_t width, void* stream);
+
 /* Allocation-free rk_rmsnorm_bwd. It has no counterpart in the reference: it
  * exists for callers that cannot supply device workspace — foreign-function
  * hosts without a device allocator, plugins whose framework allocator owns all
@@ -119,6 +136,16 @@ RK_API int rk_swiglu_bwd(const void* u, const void* dh, void* du, int dtype, int
  * x_prev may alias x_next. */
 RK_API int rk_reconstruct_midpoint(const float* x_next, const void* force, int force_dtype, float coeff, float* x_prev,
                             int64_t n, void* stream);
+/* Midpoint step with the force given as its two sublayer outputs:
+ * F = round(a + m) (attention + MLP, reversible.py:18, in the force dtype),
+ * x_prev = x_next - round(coeff * F). coeff = 2h reconstructs (inverse_pair);
+ * coeff = -2h applies the forward update p + 2h*F (forward_pair). */
+RK_API int rk_reconstruct_midpoint_sum(const float* x_next, const void* a, const void* m, int dtype, float coeff,
+                                       float* x_prev, int64_t n, void* stream);
+/* out = round(round(x) * scale) in out_dtype: an fp32 cotangent cast to the
+ * compute dtype and scaled there (the backward of `2 * h * F` under autocast,
+ * reversible.py:22). */
+RK_API int rk_cast_scale(const float* x, void* out, int out_dtype, float scale, int64_t n, void* stream);
 /* Hamiltonian-Euler inverse half-step (reversible.py:30-32):
  * state_prev[i] = state[i] - sublayer_out[i] (p_prev = p - M(q); q_prev = q - A(p_prev)). */
 RK_API int rk_reconstruct_euler(const float* state, const void* sublayer_out, int out_dtype, float* state_prev, int64_t n,
@@ -204,15 +231,17 @@ RK_API int rk_adamw_step(float* params, const float* grads, float* exp_avg, floa
  * ReversibleLM.forward (model.py:98-101, reversible.py:105-106) and its
  * backward. ids: int64 [rows] (rows = B*T, row r at position r % T);
  * tok fp32 [V, d]; pos fp32 [>= T, d]; out fp32 [rows, d].
- * Backward accumulates into g_tok [V, d] and g_pos [>= T, d] (fp32) in a fixed
+ * Backward accumulates dx (+ dx2 if not NULL; the two cotangents the boundary
+ * p = q = embedding receives, reversible.py:91) into g_tok [V, d] and g_pos [>= T, d] (fp32) in a fixed
  * order: rows are grouped by id with a stable radix sort and each group is
  * summed in row order, so results are bitwise reproducible. workspace: at
  * least rk_embedding_bwd_workspace(rows, V) bytes. d must be a multiple of 4. */
 RK_API int rk_embedding_fwd(const int64_t* ids, const float* tok, const float* pos, float* out, int64_t rows,
                             int64_t T, int64_t d, int64_t V, void* stream);
 RK_API int64_t rk_embedding_bwd_workspace(int64_t rows, int64_t V);
-RK_API int rk_embedding_bwd(const int64_t* ids, const float* dx, float* g_tok, float* g_pos, int64_t rows, int64_t T,
-                            int64_t d, int64_t V, void* workspace, int64_t workspace_bytes, void* stream);
+RK_API int rk_embedding_bwd(const int64_t* ids, const float* dx, const float* dx2, float* g_tok, float* g_pos,
+                            int64_t rows, int64_t T, int64_t d, int64_t V, void* workspace, int64_t workspace_bytes,
+                            void* stream);
 
 #ifdef __cplusplus
 }

@@ -9,6 +9,8 @@
 //   2. one CTA per run start sums its rows' gradients in that order, one
 //      thread per column, and adds the sum into g_tok[id];
 //   3. one CTA per position t sums dx[b*T + t] over b in order into g_pos[t].
+// The row cotangent is dx (+ dx2 when given: the boundary state p = q = x of
+// the reversible stack receives one cotangent through each).
 // Ids outside [0, V) set RK_DEV_EMB_INDEX and contribute nothing.
 #include <cub/cub.cuh>
 #include "vec.cuh"
@@ -56,8 +58,9 @@ __global__ void keys_kernel(const int64_t* __restrict__ ids, int64_t* __restrict
 // are thus read by 8 warps with many loads in flight.
 __global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restrict__ skeys,
                                                           const int* __restrict__ srows,
-                                                          const float* __restrict__ dx, float* __restrict__ g_tok,
-                                                          int64_t rows, int d, int64_t V, unsigned int* status) {
+                                                          const float* __restrict__ dx, const float* __restrict__ dx2,
+                                                          float* __restrict__ g_tok, int64_t rows, int d, int64_t V,
+                                                          unsigned int* status) {
   __shared__ float part[8][128];
   const int64_t i = blockIdx.x;
   const int64_t id = skeys[i];
@@ -80,7 +83,14 @@ __global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restr
 #pragma unroll 4
       for (int64_t j = i + warp; j < end; j += 8) {
         float v[4];
-        load_vec<float, 4>(dx + (int64_t)srows[j] * d + c, v);
+        const int64_t off = (int64_t)srows[j] * d + c;
+        load_vec<float, 4>(dx + off, v);
+        if (dx2) {
+          float v2[4];
+          load_vec<float, 4>(dx2 + off, v2);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[e] += v2[e];
+        }
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[e] += v[e];
       }
@@ -98,12 +108,12 @@ __global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restr
   }
 }
 
-__global__ void __launch_bounds__(256) emb_pos_bwd_kernel(const float* __restrict__ dx, float* __restrict__ g_pos,
-                                                          int64_t rows, int T, int d) {
+__global__ void __launch_bounds__(256) emb_pos_bwd_kernel(const float* __restrict__ dx, const float* __restrict__ dx2,
+                                                          float* __restrict__ g_pos, int64_t rows, int T, int d) {
   const int t = blockIdx.x;
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
     float s = 0.f;
-    for (int64_t r = t; r < rows; r += T) s += dx[r * d + c];
+    for (int64_t r = t; r < rows; r += T) s += dx2 ? dx[r * d + c] + dx2[r * d + c] : dx[r * d + c];
     g_pos[(int64_t)t * d + c] += s;
   }
 }
@@ -145,12 +155,12 @@ extern "C" int64_t rk_embedding_bwd_workspace(int64_t rows, int64_t V) {
                    align256(cub_temp_bytes(rows, V)));
 }
 
-extern "C" int rk_embedding_bwd(const int64_t* ids, const float* dx, float* g_tok, float* g_pos, int64_t rows,
-                                int64_t T, int64_t d, int64_t V, void* workspace, int64_t workspace_bytes,
+extern "C" int rk_embedding_bwd(const int64_t* ids, const float* dx, const float* dx2, float* g_tok, float* g_pos,
+                                int64_t rows, int64_t T, int64_t d, int64_t V, void* workspace, int64_t workspace_bytes,
                                 void* stream) {
   if (!ids || !dx || !g_tok || !g_pos || rows < 0 || T <= 0 || d <= 0 || V <= 0 || rows >= (1ll << 31))
     return RK_ERR_ARG;
-  if (d % 4 || !rk_host::aligned(dx, 16)) return RK_ERR_ALIGN;
+  if (d % 4 || !rk_host::aligned(dx, 16) || (dx2 && !rk_host::aligned(dx2, 16))) return RK_ERR_ALIGN;
   if (rows == 0) return RK_OK;
   if (!workspace || workspace_bytes < rk_embedding_bwd_workspace(rows, V)) return RK_ERR_WORKSPACE;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -171,10 +181,10 @@ extern "C" int rk_embedding_bwd(const int64_t* ids, const float* dx, float* g_to
       cudaSuccess)
     return RK_ERR_LAUNCH;
   rk_host::count_launch();
-  emb_tok_bwd_kernel<<<(unsigned)rows, 256, 0, s>>>(skeys, srows, dx, g_tok, rows, (int)d, V,
+  emb_tok_bwd_kernel<<<(unsigned)rows, 256, 0, s>>>(skeys, srows, dx, dx2, g_tok, rows, (int)d, V,
                                                     rk_host::device_status_ptr());
   st = rk_host::launch_status();
   if (st) return st;
-  emb_pos_bwd_kernel<<<(unsigned)T, 256, 0, s>>>(dx, g_pos, rows, (int)T, (int)d);
+  emb_pos_bwd_kernel<<<(unsigned)T, 256, 0, s>>>(dx, dx2, g_pos, rows, (int)T, (int)d);
   return rk_host::launch_status();
 }

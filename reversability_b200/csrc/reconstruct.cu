@@ -36,6 +36,51 @@ __global__ void __launch_bounds__(256) reconstruct_kernel(const float* __restric
   }
 }
 
+
+// Force assembled from its two sublayer outputs: F = round_T(a + m) (the bf16
+// add of reversible.py:18), then x_prev = x_next - round_T(coeff * F).
+template <typename TF, int V>
+__global__ void __launch_bounds__(256) reconstruct_sum_kernel(const float* __restrict__ xn, const TF* __restrict__ a,
+                                                              const TF* __restrict__ m, float coeff,
+                                                              float* __restrict__ xp, int64_t n) {
+  const int64_t nv = n / V;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nv; t += (int64_t)gridDim.x * blockDim.x) {
+    float x[V], av[V], mv[V], o[V];
+    load_vec<float, V>(xn + t * V, x);
+    load_vec<TF, V>(a + t * V, av);
+    load_vec<TF, V>(m + t * V, mv);
+#pragma unroll
+    for (int e = 0; e < V; ++e) {
+      const float f = round_to<TF>(__fadd_rn(av[e], mv[e]));
+      o[e] = __fsub_rn(x[e], round_to<TF>(__fmul_rn(coeff, f)));
+    }
+    store_vec<float, V>(xp + t * V, o);
+  }
+  const int64_t i = nv * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float f = round_to<TF>(__fadd_rn(Dt<TF>::to_f(a[i]), Dt<TF>::to_f(m[i])));
+    xp[i] = __fsub_rn(xn[i], round_to<TF>(__fmul_rn(coeff, f)));
+  }
+}
+
+// out = round_T(round_T(x) * scale): an fp32 cotangent cast to the compute
+// dtype and scaled there (autograd's cast-backward followed by the backward of
+// `2 * h * F`).
+template <typename T, int V>
+__global__ void __launch_bounds__(256) cast_scale_kernel(const float* __restrict__ x, T* __restrict__ out, float scale,
+                                                         int64_t n) {
+  const int64_t nv = n / V;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nv; t += (int64_t)gridDim.x * blockDim.x) {
+    float v[V], o[V];
+    load_vec<float, V>(x + t * V, v);
+#pragma unroll
+    for (int e = 0; e < V; ++e) o[e] = __fmul_rn(round_to<T>(v[e]), scale);
+    store_vec<T, V>(out + t * V, o);
+  }
+  const int64_t i = nv * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = Dt<T>::from_f(__fmul_rn(round_to<T>(x[i]), scale));
+}
+
 }  // namespace rk
 
 using namespace rk;
@@ -79,4 +124,58 @@ extern "C" int rk_reconstruct_euler(const float* state, const void* sublayer_out
   if (!state || !sublayer_out || !state_prev || n < 0) return RK_ERR_ARG;
   if (n == 0) return RK_OK;
   return dispatch<false>(state, sublayer_out, out_dtype, 1.f, state_prev, n, static_cast<cudaStream_t>(stream));
+}
+
+namespace {
+unsigned blocks_for(int64_t work) {
+  int64_t b = (work + 255) / 256;
+  if (b > 148 * 16) b = 148 * 16;
+  return (unsigned)(b < 1 ? 1 : b);
+}
+template <typename TF>
+int sum_launch(const float* xn, const void* a, const void* m, float coeff, float* xp, int64_t n, cudaStream_t s) {
+  auto A = static_cast<const TF*>(a);
+  auto Mv = static_cast<const TF*>(m);
+  const size_t va = 4 * sizeof(TF) >= 16 ? 16 : 4 * sizeof(TF);
+  if (rk_host::aligned(xn, 16) && rk_host::aligned(xp, 16) && rk_host::aligned(a, va) && rk_host::aligned(m, va))
+    reconstruct_sum_kernel<TF, 4><<<blocks_for(n / 4), 256, 0, s>>>(xn, A, Mv, coeff, xp, n);
+  else
+    reconstruct_sum_kernel<TF, 1><<<blocks_for(n), 256, 0, s>>>(xn, A, Mv, coeff, xp, n);
+  return rk_host::launch_status();
+}
+template <typename T>
+int cast_launch(const float* x, void* out, float scale, int64_t n, cudaStream_t s) {
+  auto O = static_cast<T*>(out);
+  const size_t vo = 4 * sizeof(T) >= 16 ? 16 : 4 * sizeof(T);
+  if (rk_host::aligned(x, 16) && rk_host::aligned(out, vo))
+    cast_scale_kernel<T, 4><<<blocks_for(n / 4), 256, 0, s>>>(x, O, scale, n);
+  else
+    cast_scale_kernel<T, 1><<<blocks_for(n), 256, 0, s>>>(x, O, scale, n);
+  return rk_host::launch_status();
+}
+}  // namespace
+
+extern "C" int rk_reconstruct_midpoint_sum(const float* x_next, const void* a, const void* m, int dtype, float coeff,
+                                           float* x_prev, int64_t n, void* stream) {
+  if (!x_next || !a || !m || !x_prev || n < 0) return RK_ERR_ARG;
+  if (n == 0) return RK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case RK_F32: return sum_launch<float>(x_next, a, m, coeff, x_prev, n, s);
+    case RK_BF16: return sum_launch<__nv_bfloat16>(x_next, a, m, coeff, x_prev, n, s);
+    case RK_F16: return sum_launch<__half>(x_next, a, m, coeff, x_prev, n, s);
+    default: return RK_ERR_DTYPE;
+  }
+}
+
+extern "C" int rk_cast_scale(const float* x, void* out, int out_dtype, float scale, int64_t n, void* stream) {
+  if (!x || !out || n < 0) return RK_ERR_ARG;
+  if (n == 0) return RK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (out_dtype) {
+    case RK_F32: return cast_launch<float>(x, out, scale, n, s);
+    case RK_BF16: return cast_launch<__nv_bfloat16>(x, out, scale, n, s);
+    case RK_F16: return cast_launch<__half>(x, out, scale, n, s);
+    default: return RK_ERR_DTYPE;
+  }
 }

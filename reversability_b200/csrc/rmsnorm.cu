@@ -144,6 +144,143 @@ __global__ void __launch_bounds__(256) rmsnorm_dw_reduce_kernel(const float* __r
   }
 }
 
+
+// ---------------------------------------------------------------- fused variants
+// Residual add + RMSNorm: s = x + a (fp32), y = rmsnorm(s) * w. `a` is the
+// low-precision sublayer output (autocast's bf16 Linear result); the sum is
+// written out only when the backward needs it (sum_out != NULL).
+template <typename Ta, typename Ty, int NV>
+__global__ void __launch_bounds__(256) add_rmsnorm_fwd_kernel(const float* __restrict__ x, const Ta* __restrict__ a,
+                                                              const float* __restrict__ w, Ty* __restrict__ y,
+                                                              float* __restrict__ sum_out, float* __restrict__ rstd,
+                                                              int64_t rows, int width, float eps) {
+  constexpr int V = 4;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int64_t base = row * width;
+  float v[NV][V];
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (j * 32 + lane) * V;
+    if (c < width) {
+      float xa[V], aa[V];
+      load_vec<float, V>(x + base + c, xa);
+      load_vec<Ta, V>(a + base + c, aa);
+#pragma unroll
+      for (int e = 0; e < V; ++e) {
+        v[j][e] = xa[e] + aa[e];
+        ss += v[j][e] * v[j][e];
+      }
+      if (sum_out) store_vec<float, V>(sum_out + base + c, v[j]);
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / (float)width + eps);
+  if (rstd && lane == 0) rstd[row] = r;
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (j * 32 + lane) * V;
+    if (c < width) {
+      float wv[V], o[V];
+      load_vec<float, V>(w + c, wv);
+#pragma unroll
+      for (int e = 0; e < V; ++e) o[e] = (v[j][e] * r) * wv[e];
+      store_vec<Ty, V>(y + base + c, o);
+    }
+  }
+}
+
+// RMSNorm backward with the cotangent bookkeeping of the reversible step fused
+// into its epilogue (rows contiguous, fp32 input x):
+//   dx_out = dx + residual                         (fp32; residual may be NULL)
+//   LP == 1: lp_out = round(lp_add + round(dx))    (the bf16 sum autograd forms
+//            when a bf16 tensor feeds two consumers)
+//   LP == 2: lp_out = round(dx_out)                (cast of the total)
+template <typename Tg, typename Tlp, int NV, bool RES, int LP>
+__global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(
+    const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ rstd, const Tg* __restrict__ dy,
+    const float* __restrict__ residual, const Tlp* __restrict__ lp_add, float* __restrict__ dx_out,
+    Tlp* __restrict__ lp_out, float* __restrict__ partial, int64_t rows, int width) {
+  constexpr int V = 4;
+  extern __shared__ float red[];  // [8][width]
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int64_t stride = (int64_t)gridDim.x * 8;
+  float acc[NV][V];
+  float wv[NV][V];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (j * 32 + lane) * V;
+#pragma unroll
+    for (int e = 0; e < V; ++e) acc[j][e] = 0.f;
+    if (c < width) load_vec<float, V>(w + c, wv[j]);
+  }
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < rows; row += stride) {
+    const float r = __ldg(rstd + row);
+    const int64_t base = row * width;
+    float xv[NV][V], gv[NV][V];
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (j * 32 + lane) * V;
+      if (c < width) {
+        load_vec<float, V>(x + base + c, xv[j]);
+        load_vec<Tg, V>(dy + base + c, gv[j]);
+#pragma unroll
+        for (int e = 0; e < V; ++e) {
+          dot += (gv[j][e] * wv[j][e]) * xv[j][e];
+          acc[j][e] += gv[j][e] * (xv[j][e] * r);
+        }
+      }
+    }
+    dot = warp_sum(dot);
+    const float corr = dot / (float)width * r * r;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (j * 32 + lane) * V;
+      if (c < width) {
+        float o[V], res[V], lp[V];
+#pragma unroll
+        for (int e = 0; e < V; ++e) o[e] = (gv[j][e] * wv[j][e] - xv[j][e] * corr) * r;
+        if constexpr (LP == 1) {
+          float la[V];
+          load_vec<Tlp, V>(lp_add + base + c, la);
+#pragma unroll
+          for (int e = 0; e < V; ++e) lp[e] = __fadd_rn(la[e], round_to<Tlp>(o[e]));
+        }
+        if constexpr (RES) {
+          load_vec<float, V>(residual + base + c, res);
+#pragma unroll
+          for (int e = 0; e < V; ++e) o[e] = __fadd_rn(o[e], res[e]);  // no contraction into the last multiply
+        }
+        if constexpr (LP == 2) {
+#pragma unroll
+          for (int e = 0; e < V; ++e) lp[e] = o[e];
+        }
+        store_vec<float, V>(dx_out + base + c, o);
+        if constexpr (LP != 0) store_vec<Tlp, V>(lp_out + base + c, lp);
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = (j * 32 + lane) * V;
+    if (c < width) {
+#pragma unroll
+      for (int e = 0; e < V; ++e) red[warp * width + c + e] = acc[j][e];
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < width; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += red[k * width + c];
+    partial[(int64_t)blockIdx.x * width + c] = t;
+  }
+}
+
 }  // namespace rk
 
 using namespace rk;
@@ -282,6 +419,121 @@ extern "C" int rk_rmsnorm_bwd(const void* x, int x_dtype, int64_t ldx, const flo
                                                                  parts, rows, W, s);
   else if (x_dtype == RK_F16 && dy_dtype == RK_F16 && dx_dtype == RK_F16)
     st = bwd_typed<__half, __half, __half>(x, ldx, w, rstd, dy, lddy, dx, lddx, dw_partial, parts, rows, W, s);
+  else
+    return RK_ERR_DTYPE;
+  if (st != RK_OK) return st;
+  rmsnorm_dw_reduce_kernel<<<(W + 31) / 32, 256, 0, s>>>(dw_partial, dw, parts, W, accumulate_dw);
+  return rk_host::launch_status();
+}
+
+
+// ---------------------------------------------------------------- fused entry points
+namespace {
+template <typename Ta, typename Ty>
+int add_fwd_typed(const float* x, const void* a, const float* w, void* y, float* sum_out, float* rstd, int64_t rows,
+                  int width, float eps, cudaStream_t s) {
+  const int nv = (width + 127) / 128;
+  dim3 grid((unsigned)((rows + 7) / 8));
+  auto A = static_cast<const Ta*>(a);
+  auto Y = static_cast<Ty*>(y);
+#define RK_AF(N) add_rmsnorm_fwd_kernel<Ta, Ty, N><<<grid, 256, 0, s>>>(x, A, w, Y, sum_out, rstd, rows, width, eps)
+  if (nv <= 1) RK_AF(1);
+  else if (nv <= 2) RK_AF(2);
+  else if (nv <= 4) RK_AF(4);
+  else if (nv <= 8) RK_AF(8);
+  else return RK_ERR_UNSUPPORTED;
+#undef RK_AF
+  return rk_host::launch_status();
+}
+
+template <typename Tg, typename Tlp, bool RES, int LP>
+int bwd_fused_nv(const float* x, const float* w, const float* rstd, const void* dy, const float* residual,
+                 const void* lp_add, float* dx_out, void* lp_out, float* partial, int parts, int64_t rows, int width,
+                 cudaStream_t s) {
+  const int nv = (width + 127) / 128;
+  const size_t smem = (size_t)8 * width * sizeof(float);
+  auto G = static_cast<const Tg*>(dy);
+  auto LA = static_cast<const Tlp*>(lp_add);
+  auto LO = static_cast<Tlp*>(lp_out);
+#define RK_BF(N)                                                                                            \
+  do {                                                                                                      \
+    auto k = rmsnorm_bwd_fused_kernel<Tg, Tlp, N, RES, LP>;                                                 \
+    if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)smem);          \
+    k<<<parts, 256, smem, s>>>(x, w, rstd, G, residual, LA, dx_out, LO, partial, rows, width);              \
+  } while (0)
+  if (nv <= 1) RK_BF(1);
+  else if (nv <= 2) RK_BF(2);
+  else if (nv <= 4) RK_BF(4);
+  else if (nv <= 8) RK_BF(8);
+  else return RK_ERR_UNSUPPORTED;
+#undef RK_BF
+  return rk_host::launch_status();
+}
+
+template <typename Tg, typename Tlp>
+int bwd_fused_modes(const float* x, const float* w, const float* rstd, const void* dy, const float* residual,
+                    const void* lp_add, float* dx_out, void* lp_out, float* partial, int parts, int64_t rows,
+                    int width, cudaStream_t s) {
+  const bool res = residual != nullptr;
+  const int lp = lp_out == nullptr ? 0 : (lp_add != nullptr ? 1 : 2);
+#define RK_M(R, L)                                                                                           \
+  if (res == R && lp == L)                                                                                   \
+    return bwd_fused_nv<Tg, Tlp, R, L>(x, w, rstd, dy, residual, lp_add, dx_out, lp_out, partial, parts, rows, \
+                                       width, s);
+  RK_M(false, 0) RK_M(false, 1) RK_M(false, 2) RK_M(true, 0) RK_M(true, 1) RK_M(true, 2)
+#undef RK_M
+  return RK_ERR_ARG;
+}
+}  // namespace
+
+extern "C" int rk_add_rmsnorm_fwd(const float* x, const void* a, int a_dtype, const float* w, void* y, int y_dtype,
+                                  float* sum_out, float* rstd, int64_t rows, int64_t width, float eps, void* stream) {
+  if (!x || !a || !w || !y || rows < 0 || width <= 0) return RK_ERR_ARG;
+  if (width > 1024) return RK_ERR_UNSUPPORTED;
+  if (width % 4 || !rk_host::aligned(x, 16) || !rk_host::aligned(w, 16) || !rk_host::aligned(a, 8) ||
+      !rk_host::aligned(y, 8) || (sum_out && !rk_host::aligned(sum_out, 16)))
+    return RK_ERR_ALIGN;
+  if (rows == 0) return RK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int W = (int)width;
+  if (a_dtype == RK_BF16 && y_dtype == RK_BF16)
+    return add_fwd_typed<__nv_bfloat16, __nv_bfloat16>(x, a, w, y, sum_out, rstd, rows, W, eps, s);
+  if (a_dtype == RK_F16 && y_dtype == RK_F16)
+    return add_fwd_typed<__half, __half>(x, a, w, y, sum_out, rstd, rows, W, eps, s);
+  if (a_dtype == RK_F32 && y_dtype == RK_F32)
+    return add_fwd_typed<float, float>(x, a, w, y, sum_out, rstd, rows, W, eps, s);
+  return RK_ERR_DTYPE;
+}
+
+extern "C" int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float* rstd, const void* dy, int dy_dtype,
+                                    const float* residual, const void* lp_add, void* lp_out, int lp_dtype,
+                                    float* dx_out, float* dw, int accumulate_dw, float* dw_partial,
+                                    int64_t workspace_bytes, int64_t rows, int64_t width, void* stream) {
+  if (!x || !w || !rstd || !dy || !dx_out || !dw || !dw_partial || rows < 0 || width <= 0) return RK_ERR_ARG;
+  if (lp_add && !lp_out) return RK_ERR_ARG;
+  if (width > 1024) return RK_ERR_UNSUPPORTED;
+  if (width % 4 || !rk_host::aligned(x, 16) || !rk_host::aligned(w, 16) || !rk_host::aligned(dx_out, 16) ||
+      (residual && !rk_host::aligned(residual, 16)) || !rk_host::aligned(dy, 8) ||
+      (lp_add && !rk_host::aligned(lp_add, 8)) || (lp_out && !rk_host::aligned(lp_out, 8)))
+    return RK_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int W = (int)width;
+  if (rows == 0) {
+    if (!accumulate_dw) cudaMemsetAsync(dw, 0, sizeof(float) * W, s);
+    return rk_host::launch_status();
+  }
+  const int parts = rms_parts(rows);
+  if (workspace_bytes < (int64_t)parts * W * (int64_t)sizeof(float)) return RK_ERR_WORKSPACE;
+  int st;
+  const int lpd = lp_out ? lp_dtype : dy_dtype;
+  if (dy_dtype == RK_BF16 && lpd == RK_BF16)
+    st = bwd_fused_modes<__nv_bfloat16, __nv_bfloat16>(x, w, rstd, dy, residual, lp_add, dx_out, lp_out, dw_partial,
+                                                      parts, rows, W, s);
+  else if (dy_dtype == RK_F16 && lpd == RK_F16)
+    st = bwd_fused_modes<__half, __half>(x, w, rstd, dy, residual, lp_add, dx_out, lp_out, dw_partial, parts, rows, W,
+                                        s);
+  else if (dy_dtype == RK_F32 && lpd == RK_F32)
+    st = bwd_fused_modes<float, float>(x, w, rstd, dy, residual, lp_add, dx_out, lp_out, dw_partial, parts, rows, W, s);
   else
     return RK_ERR_DTYPE;
   if (st != RK_OK) return st;

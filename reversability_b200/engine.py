@@ -116,8 +116,10 @@ class LayerKernels:
         a = fn.linear_fwd(o.view(-1, o.shape[-1]), lw.proj_c)
         return a, ((n1, rstd1, qkv, o, lse) if save else None)
 
-    def attn_vjp(self, lw: LayerWeights, g: LayerGrads, x: torch.Tensor, saved, ga: torch.Tensor) -> torch.Tensor:
-        """dx (fp32) of A at x for cotangent ga (cd); accumulates weight grads."""
+    def attn_vjp(self, lw: LayerWeights, g: LayerGrads, x: torch.Tensor, saved, ga: torch.Tensor,
+                 residual: torch.Tensor | None = None) -> torch.Tensor:
+        """dx (fp32) of A at x for cotangent ga (cd), plus `residual` if given
+        (added in the norm's epilogue); accumulates weight grads."""
         n1, rstd1, qkv, o, lse = saved
         o2 = o.view(-1, o.shape[-1])
         do = fn.linear_dgrad(ga, lw.proj_c)
@@ -126,97 +128,109 @@ class LayerKernels:
         dqkv2 = dqkv.view(-1, dqkv.shape[-1])
         fn.linear_wgrad(dqkv2, n1, dw=g.qkv, accumulate=True)
         dn1 = fn.linear_dgrad(dqkv2, lw.qkv_c)
-        dx, _ = fn.rmsnorm_bwd(x, lw.attn_norm, rstd1, dn1, dx_dtype=F32, dw=g.attn_norm, accumulate_dw=True)
+        dx, _ = fn.rmsnorm_bwd_fused(x, lw.attn_norm, rstd1, dn1, g.attn_norm, residual=residual)
         return dx
 
     # ---------------------------------------------------------- MLP sublayer
-    def _mlp_tile_fwd(self, lw, yt, out_t, save):
-        n2, rstd2 = fn.rmsnorm_fwd(yt, lw.mlp_norm, self._eps(lw.eps_mlp), out_dtype=self.cd, want_rstd=save)
-        u = fn.linear_fwd(n2, lw.up_c)
-        hg = fn.swiglu_fwd(u)
-        fn.linear_fwd(hg, lw.down_c, out=out_t)
-        return (n2, rstd2, u, hg) if save else None
-
-    def _mlp_tile_vjp(self, lw, g, yt, saved, gm_t, dy_t):
-        n2, rstd2, u, hg = saved
-        dh = fn.linear_dgrad(gm_t, lw.down_c)
-        fn.linear_wgrad(gm_t, hg, dw=g.down, accumulate=True)
-        du = fn.swiglu_bwd(u, dh)
-        fn.linear_wgrad(du, n2, dw=g.up, accumulate=True)
-        dn2 = fn.linear_dgrad(du, lw.up_c)
-        dx, _ = fn.rmsnorm_bwd(yt, lw.mlp_norm, rstd2, dn2, dx_dtype=F32, dw=g.mlp_norm, accumulate_dw=True)
-        dy_t.copy_(dx)
-
     def _tiles(self, M):
         t = self.mlp_tokens if self.mlp_tokens and self.mlp_tokens > 0 else M
         return [(s, min(s + t, M)) for s in range(0, M, t)]
 
-    def mlp_forward(self, lw: LayerWeights, y: torch.Tensor) -> torch.Tensor:
-        """M(y) without saving (forward sweep)."""
-        M = y.shape[0]
-        m = torch.empty((M, lw.down.shape[0]), device=y.device, dtype=self.cd)
+    def _mlp_norm(self, lw, y, x, a, save):
+        """n2 = rmsnorm(y) with y given, or of y = x + a formed inside the norm."""
+        eps = self._eps(lw.eps_mlp)
+        if a is not None:
+            n2, ysum, rstd2 = fn.add_rmsnorm_fwd(x, a, lw.mlp_norm, eps, self.cd, want_sum=save, want_rstd=save)
+            return n2, ysum, rstd2
+        n2, rstd2 = fn.rmsnorm_fwd(y, lw.mlp_norm, eps, out_dtype=self.cd, want_rstd=save)
+        return n2, y, rstd2
+
+    def mlp_forward(self, lw: LayerWeights, y: torch.Tensor | None = None, x: torch.Tensor | None = None,
+                    a: torch.Tensor | None = None) -> torch.Tensor:
+        """M(y) without saving (forward sweep); y = x + a when a is given."""
+        n2, _, _ = self._mlp_norm(lw, y, x, a, save=False)
+        M = n2.shape[0]
+        m = torch.empty((M, lw.down.shape[0]), device=n2.device, dtype=self.cd)
         for s, e in self._tiles(M):
-            self._mlp_tile_fwd(lw, y[s:e], m[s:e], save=False)
+            fn.linear_fwd(fn.swiglu_fwd(fn.linear_fwd(n2[s:e], lw.up_c)), lw.down_c, out=m[s:e])
         return m
 
-    def mlp_forward_vjp(self, lw: LayerWeights, g: LayerGrads, y: torch.Tensor, gm: torch.Tensor):
-        """M(y) and dy = M^T gm, tile by tile (forward then VJP of each tile)."""
-        M = y.shape[0]
-        m = torch.empty((M, lw.down.shape[0]), device=y.device, dtype=self.cd)
-        dy = torch.empty((M, y.shape[1]), device=y.device, dtype=F32)
+    def mlp_forward_vjp(self, lw: LayerWeights, g: LayerGrads, gm: torch.Tensor, y: torch.Tensor | None = None,
+                        x: torch.Tensor | None = None, a: torch.Tensor | None = None,
+                        residual: torch.Tensor | None = None, lp_add: torch.Tensor | None = None,
+                        want_lp: bool = False):
+        """M(y) and its VJP for cotangent gm, tile by tile (each tile's forward is
+        followed at once by its VJP). Returns (m, dx_out, lp_out) where
+        dx_out = M^T gm + residual and lp_out is the low-precision epilogue output
+        of rk_rmsnorm_bwd_fused (round(lp_add + round(M^T gm)) or round(dx_out))."""
+        n2, ysum, rstd2 = self._mlp_norm(lw, y, x, a, save=True)
+        M, d = n2.shape
+        m = torch.empty((M, lw.down.shape[0]), device=n2.device, dtype=self.cd)
+        dxo = torch.empty((M, d), device=n2.device, dtype=F32)
+        lp = torch.empty((M, d), device=n2.device, dtype=self.cd) if want_lp else None
         for s, e in self._tiles(M):
-            saved = self._mlp_tile_fwd(lw, y[s:e], m[s:e], save=True)
-            self._mlp_tile_vjp(lw, g, y[s:e], saved, gm[s:e], dy[s:e])
-            del saved
-        return m, dy
+            u = fn.linear_fwd(n2[s:e], lw.up_c)
+            hg = fn.swiglu_fwd(u)
+            fn.linear_fwd(hg, lw.down_c, out=m[s:e])
+            gm_t = gm[s:e]
+            dh = fn.linear_dgrad(gm_t, lw.down_c)
+            fn.linear_wgrad(gm_t, hg, dw=g.down, accumulate=True)
+            del hg
+            du = fn.swiglu_bwd(u, dh)
+            del u, dh
+            fn.linear_wgrad(du, n2[s:e], dw=g.up, accumulate=True)
+            dn2 = fn.linear_dgrad(du, lw.up_c)
+            del du
+            fn.rmsnorm_bwd_fused(ysum[s:e], lw.mlp_norm, rstd2[s:e], dn2, g.mlp_norm,
+                                 residual=None if residual is None else residual[s:e],
+                                 lp_add=None if lp_add is None else lp_add[s:e],
+                                 dx_out=dxo[s:e], lp_out=None if lp is None else lp[s:e])
+        return m, dxo, lp
 
     # ---------------------------------------------------------- layer steps
     def force(self, lw, x):
         """F(x) = A(x) + M(x + A(x)) in cd (reversible.py:16-18)."""
         a, _ = self.attn_forward(lw, x, save=False)
-        y = x + a
-        return a + self.mlp_forward(lw, y)
+        return a + self.mlp_forward(lw, x=x, a=a)
 
     def forward_midpoint(self, lw, p, q, h):
         """(p, q) -> (q, p + round(2h F(q))) (reversible.py:21-23)."""
-        f = self.force(lw, q)
-        return q, fn.reconstruct_midpoint(p, f, -2.0 * h)
+        a, _ = self.attn_forward(lw, q, save=False)
+        m = self.mlp_forward(lw, x=q, a=a)
+        return q, fn.reconstruct_midpoint_sum(p, a, m, -2.0 * h)
 
     def forward_euler(self, lw, p, q):
         """q' = q + A(p); p' = p + M(q') (reversible.py:24-25)."""
         a, _ = self.attn_forward(lw, p, save=False)
         nq = fn.reconstruct_midpoint(q, a, -1.0)
-        m = self.mlp_forward(lw, nq)
+        m = self.mlp_forward(lw, y=nq)
         return fn.reconstruct_midpoint(p, m, -1.0), nq
 
     def backward_midpoint(self, lw, g: LayerGrads, p, q, dp, dq, h):
-        """Reconstructs (p_{n-1}, q_{n-1}) and returns them with their cotangents."""
+        """Reconstructs (p_{n-1}, q_{n-1}) and returns them with their cotangents.
+        dp may be None (a zero cotangent)."""
         x = p
         a, sa = self.attn_forward(lw, x, save=True)
-        y = x + a
-        gF = (dq.to(self.cd) * (2.0 * h)).to(self.cd)
-        m, dy = self.mlp_forward_vjp(lw, g, y, gF)
-        f = a + m
-        prev_p = fn.reconstruct_midpoint(q, f, 2.0 * h)
-        del m, f, y
-        da = gF + dy.to(self.cd)
-        dx = self.attn_vjp(lw, g, x, sa, da)
-        dx += dy
-        dx += dp
-        return prev_p, x, dq, dx
+        gF = fn.cast_scale(dq, self.cd, 2.0 * h)
+        # dxacc = M^T gF + dp ; da = round(gF + round(M^T gF)) for the attention VJP
+        m, dxacc, da = self.mlp_forward_vjp(lw, g, gF, x=x, a=a, residual=dp, lp_add=gF, want_lp=True)
+        prev_p = fn.reconstruct_midpoint_sum(q, a, m, 2.0 * h)
+        del m, gF
+        dq_new = self.attn_vjp(lw, g, x, sa, da, residual=dxacc)
+        return prev_p, x, dq, dq_new
 
     def backward_euler(self, lw, g: LayerGrads, p, q, dp, dq):
-        gm = dp.to(self.cd)
-        m, dy = self.mlp_forward_vjp(lw, g, q, gm)
+        """dq may be None (a zero cotangent)."""
+        gm = fn.cast_scale(dp, self.cd, 1.0)
+        # dq_eff = dq' + M^T round(dp'); ga = round(dq_eff)
+        m, dq_eff, ga = self.mlp_forward_vjp(lw, g, gm, y=q, residual=dq, want_lp=True)
         prev_p = fn.reconstruct_euler(p, m)
-        del m
-        dq_eff = dq + dy
+        del m, gm
         a, sa = self.attn_forward(lw, prev_p, save=True)
         prev_q = fn.reconstruct_euler(q, a)
         del a
-        dpx = self.attn_vjp(lw, g, prev_p, sa, dq_eff.to(self.cd))
-        dpx += dp
-        return prev_p, prev_q, dpx, dq_eff
+        dp_new = self.attn_vjp(lw, g, prev_p, sa, ga, residual=dp)
+        return prev_p, prev_q, dp_new, dq_eff
 
 
 def compute_dtype(amp_enabled: bool, amp_dtype: torch.dtype, state_dtype: torch.dtype) -> torch.dtype:

@@ -254,13 +254,70 @@ def embedding_fwd(ids: torch.Tensor, tok: torch.Tensor, pos: torch.Tensor, out: 
     return out
 
 
-def embedding_bwd(ids: torch.Tensor, dx: torch.Tensor, g_tok: torch.Tensor, g_pos: torch.Tensor):
-    """Deterministically accumulates dx [B*T, d] into g_tok[ids] and g_pos[t]."""
+def embedding_bwd(ids: torch.Tensor, dx: torch.Tensor, g_tok: torch.Tensor, g_pos: torch.Tensor,
+                  dx2: torch.Tensor | None = None):
+    """Deterministically accumulates dx (+ dx2) [B*T, d] into g_tok[ids] and g_pos[t]."""
     require_cuda(ids, dx, g_tok, g_pos)
     B, T = ids.shape
     d = g_tok.shape[1]
     ids = ids.contiguous()
     ws_bytes = _lib.lib().rk_embedding_bwd_workspace(B * T, g_tok.shape[0])
     ws = torch.empty(max(ws_bytes, 1), device=dx.device, dtype=torch.uint8)
-    _lib.call("rk_embedding_bwd", ids.data_ptr(), dx.contiguous().data_ptr(), g_tok.data_ptr(), g_pos.data_ptr(),
+    _lib.call("rk_embedding_bwd", ids.data_ptr(), dx.contiguous().data_ptr(),
+              None if dx2 is None else dx2.contiguous().data_ptr(), g_tok.data_ptr(), g_pos.data_ptr(),
               B * T, T, d, g_tok.shape[0], ws.data_ptr(), ws_bytes, _lib.stream_ptr())
+
+
+# ------------------------------------------------------------------ fused reversible-step helpers
+def add_rmsnorm_fwd(x: torch.Tensor, a: torch.Tensor, weight: torch.Tensor, eps: float, out_dtype: torch.dtype,
+                    want_sum: bool = False, want_rstd: bool = True):
+    """s = x + a; y = rmsnorm(s) * weight. Returns (y, s or None, rstd or None); rows contiguous."""
+    require_cuda(x, a, weight)
+    rows, width = x.shape
+    y = torch.empty((rows, width), device=x.device, dtype=out_dtype)
+    ssum = torch.empty((rows, width), device=x.device, dtype=torch.float32) if want_sum else None
+    rstd = torch.empty(rows, device=x.device, dtype=torch.float32) if want_rstd else None
+    _lib.call("rk_add_rmsnorm_fwd", x.data_ptr(), a.data_ptr(), _lib.code(a.dtype), weight.data_ptr(), y.data_ptr(),
+              _lib.code(out_dtype), _lib.ptr(ssum), _lib.ptr(rstd), rows, width, float(eps), _lib.stream_ptr())
+    return y, ssum, rstd
+
+
+def rmsnorm_bwd_fused(x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor, dy: torch.Tensor,
+                      dw: torch.Tensor, residual: torch.Tensor | None = None, lp_add: torch.Tensor | None = None,
+                      lp_dtype: torch.dtype | None = None, dx_out: torch.Tensor | None = None,
+                      lp_out: torch.Tensor | None = None, accumulate_dw: bool = True):
+    """dx_out = rmsnorm_bwd(dy) + residual (fp32); lp_out = round(lp_add + round(dx)) if lp_add else
+    round(dx_out) when lp_dtype is given. dw accumulates. Returns (dx_out, lp_out)."""
+    require_cuda(x, weight, rstd, dy)
+    rows, width = x.shape
+    dx_out = dx_out if dx_out is not None else torch.empty((rows, width), device=x.device, dtype=torch.float32)
+    if lp_dtype is not None and lp_out is None:
+        lp_out = torch.empty((rows, width), device=x.device, dtype=lp_dtype)
+    ws_bytes = _lib.lib().rk_rmsnorm_bwd_workspace(rows, width)
+    ws = torch.empty(max(ws_bytes // 4, 1), device=x.device, dtype=torch.float32)
+    _lib.call("rk_rmsnorm_bwd_fused", x.data_ptr(), weight.data_ptr(), rstd.data_ptr(), dy.data_ptr(),
+              _lib.code(dy.dtype), _lib.ptr(residual), _lib.ptr(lp_add), _lib.ptr(lp_out),
+              _lib.code(lp_out.dtype) if lp_out is not None else _lib.code(dy.dtype), dx_out.data_ptr(),
+              dw.data_ptr(), int(accumulate_dw), ws.data_ptr(), ws_bytes, rows, width, _lib.stream_ptr())
+    return dx_out, lp_out
+
+
+def reconstruct_midpoint_sum(x_next: torch.Tensor, a: torch.Tensor, m: torch.Tensor, coeff: float,
+                             out: torch.Tensor | None = None) -> torch.Tensor:
+    """x_prev = x_next - round(coeff * round(a + m)); coeff = -2h gives the forward update."""
+    require_cuda(x_next, a, m)
+    if a.dtype != m.dtype:
+        raise ValueError("force parts must share a dtype")
+    out = out if out is not None else torch.empty_like(x_next)
+    _lib.call("rk_reconstruct_midpoint_sum", x_next.data_ptr(), a.data_ptr(), m.data_ptr(), _lib.code(a.dtype),
+              float(coeff), out.data_ptr(), x_next.numel(), _lib.stream_ptr())
+    return out
+
+
+def cast_scale(x: torch.Tensor, dtype: torch.dtype, scale: float) -> torch.Tensor:
+    """round(round(x) * scale) in dtype (x fp32)."""
+    require_cuda(x)
+    out = torch.empty(x.shape, device=x.device, dtype=dtype)
+    _lib.call("rk_cast_scale", x.data_ptr(), out.data_ptr(), _lib.code(dtype), float(scale), x.numel(),
+              _lib.stream_ptr())
+    return out

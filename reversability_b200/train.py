@@ -185,13 +185,13 @@ class ReversibleTrainer:
         fn.linear_wgrad(logits, hidden, dw=self.g_tok, accumulate=True)
         dout, _ = fn.rmsnorm_bwd(out, self.final_w, rstd_f, dhidden, dx_dtype=F32, dw=self.g_final,
                                  accumulate_dw=True)
-        zero = torch.zeros_like(dout)
-        dp, dq = (zero, dout) if self.model.method == "midpoint" else (dout, zero)
+        # the unused output's cotangent is zero; the engine takes None for it
+        dp, dq = (None, dout) if self.model.method == "midpoint" else (dout, None)
         hook = self._bucket_hook if (last and self.world > 1) else None
         _, _, dp, dq = engine.stack_backward(kern, self.layers, self.layer_grads, p, q, dp, dq, self.model.method,
                                              self.model.step_size, on_layer_done=hook)
-        dx = dp + dq
-        fn.embedding_bwd(ids, dx, self.g_tok, self.g_pos)
+        # boundary p = q = embedding: both cotangents reach it (summed inside the kernel)
+        fn.embedding_bwd(ids, dp, self.g_tok, self.g_pos, dx2=dq)
 
     def _bucket_hook(self, layer: int):
         self.buckets.launch(layer)

@@ -283,3 +283,52 @@ def test_embedding_fwd_bwd_matches_torch_and_is_deterministic(B, T, V):
     g2, p2 = torch.ones_like(tok), torch.zeros_like(pos)
     fn.embedding_bwd(ids, dx, g2, p2)
     assert torch.equal(g1, g2) and torch.equal(p1, p2)
+
+
+# ------------------------------------------------------------------ fused reversible-step kernels
+@pytest.mark.parametrize("cd", [torch.bfloat16, torch.float32])
+def test_add_rmsnorm_fwd_matches_unfused(cd):
+    from reversability_b200 import functional as fn
+    x = torch.randn(4099, 256, device=DEV)
+    a = torch.randn(4099, 256, device=DEV).to(cd)
+    w = torch.randn(256, device=DEV)
+    y, s, r = fn.add_rmsnorm_fwd(x, a, w, 1e-6, cd, want_sum=True)
+    s_ref = x + a
+    y_ref, r_ref = fn.rmsnorm_fwd(s_ref, w, 1e-6, out_dtype=cd)
+    assert torch.equal(s, s_ref) and torch.equal(y, y_ref) and torch.equal(r, r_ref)
+
+
+@pytest.mark.parametrize("mode", ["plain", "res", "res_lpadd", "lp_total", "lpadd"])
+def test_rmsnorm_bwd_fused_epilogues(mode):
+    from reversability_b200 import functional as fn
+    rows = 3000
+    x = torch.randn(rows, 256, device=DEV)
+    w = torch.randn(256, device=DEV)
+    _, rstd = fn.rmsnorm_fwd(x, w, 1e-6)
+    g = torch.randn(rows, 256, device=DEV).bfloat16()
+    res = torch.randn(rows, 256, device=DEV) if "res" in mode else None
+    lpa = torch.randn(rows, 256, device=DEV).bfloat16() if "lpadd" in mode else None
+    want_lp = mode in ("res_lpadd", "lp_total", "lpadd")
+    dx_ref, dw_ref = fn.rmsnorm_bwd(x, w, rstd, g, dx_dtype=torch.float32)
+    dw = torch.zeros(256, device=DEV)
+    dxo, lp = fn.rmsnorm_bwd_fused(x, w, rstd, g, dw, residual=res, lp_add=lpa,
+                                   lp_dtype=torch.bfloat16 if want_lp else None)
+    total = dx_ref + (res if res is not None else 0)
+    assert torch.equal(dxo, total)
+    assert torch.equal(dw, dw_ref)
+    if lpa is not None:
+        assert torch.equal(lp, lpa + dx_ref.bfloat16())
+    elif want_lp:
+        assert torch.equal(lp, total.bfloat16())
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])
+def test_reconstruct_sum_and_cast_scale(dt):
+    from reversability_b200 import functional as fn
+    n = 16896 * 256 + 3
+    x = torch.randn(n, device=DEV)
+    a = torch.randn(n, device=DEV).to(dt)
+    m = torch.randn(n, device=DEV).to(dt)
+    for coeff in (1.0, -1.0, 0.5):
+        assert torch.equal(fn.reconstruct_midpoint_sum(x, a, m, coeff), x - coeff * (a + m))
+    assert torch.equal(fn.cast_scale(x, dt, 0.5), (x.to(dt) * 0.5).to(dt))

@@ -171,6 +171,12 @@ RK_API int rk_gemm_fprop(const void* x, int64_t ldx, const void* w, int64_t ldw,
                   int64_t N, int64_t K, int dtype, int out_dtype, void* stream);
 RK_API int rk_gemm_dgrad(const void* dy, int64_t lddy, const void* w, int64_t ldw, void* dx, int64_t lddx, int64_t M,
                   int64_t N, int64_t K, int dtype, int out_dtype, void* stream);
+/* MLP up projection with SwiGLU fused into the epilogue (model.py:55-56):
+ * u = X[M,K] . W_up[2ff,K]^T, h[M,ff] = round(silu(u[:, :ff])) * u[:, ff:] with
+ * the same rounding as rk_swiglu_fwd on a bf16/f16 u. If u is not NULL it also
+ * receives u itself (the backward needs it). bf16/f16 only; ff % 128 == 0. */
+RK_API int rk_gemm_fprop_swiglu(const void* x, int64_t ldx, const void* w_up, int64_t ldw, void* h, int64_t ldh,
+                                void* u, int64_t ldu, int64_t M, int64_t ff, int64_t K, int dtype, void* stream);
 RK_API int64_t rk_gemm_wgrad_workspace(int64_t M, int64_t N, int64_t K);
 RK_API int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, float* dw, int64_t lddw, int64_t M,
                   int64_t N, int64_t K, int dtype, int accumulate, float* workspace, int64_t workspace_bytes,

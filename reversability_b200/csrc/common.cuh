@@ -43,6 +43,20 @@ template <typename T> __device__ __forceinline__ void st_f(T* p, float v) { *p =
 // Round a float through storage type T (the reference's `.to(dtype).to(float32)`).
 template <typename T> __device__ __forceinline__ float round_to(float v) { return Dt<T>::to_f(Dt<T>::from_f(v)); }
 
+// Logistic pieces of SiLU with the hardware exponential and an approximate
+// divide (ex2.approx + div.approx, a few ulp in fp32 — like the reference's
+// Triton kernels, which compile exp and '/' to the same approximate
+// instructions). Shared by the standalone SwiGLU kernels and the GEMM epilogue
+// so both produce identical bits.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float exp_neg(float g) { return ex2_approx(-1.4426950408889634f * g); }
+__device__ __forceinline__ float silu_value(float g) { return __fdividef(g, 1.f + exp_neg(g)); }
+__device__ __forceinline__ float sigmoid_value(float g) { return __fdividef(1.f, 1.f + exp_neg(g)); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -39,6 +39,7 @@ struct GemmArgs {
   int kb_per_split;      // 64-wide k blocks per slice
   int kb_total;          // ceil(K / 64)
   int split_rows;        // EPI_TMA with splits > 1: rows between split slices (M rounded up to 128)
+  int ff;                // EPI_SWIGLU*: offset of the value rows in W (and of the value columns in u)
   void* out;             // EPI_STORE: [M, N] row-major (ldo); split slices: fp32 [splits][split_rows][N]
   int64_t ldo;
   int out_dtype;
@@ -50,19 +51,29 @@ struct GemmArgs {
 // stores (split slices too, at row split*split_rows); TMA_ADD: the same staging
 // written with TMA reduce-add (out += acc; every element has exactly one
 // writing CTA, so the result is deterministic).
-enum { EPI_STORE = 0, EPI_PARTIAL = 1, EPI_ACCUM = 2, EPI_TMA = 3, EPI_TMA_ADD = 4 };
+// SWIGLU: fprop of the MLP up projection with SwiGLU in the epilogue: the B
+// tile holds W rows [n0, n0+128) (gate) and [ff+n0, ff+n0+128) (value), so the
+// accumulator has gate | value for the same 128 columns and the epilogue writes
+// h = round(silu(round(g))) * round(v) only; SWIGLU_SAVE also writes u itself.
+enum { EPI_STORE = 0, EPI_PARTIAL = 1, EPI_ACCUM = 2, EPI_TMA = 3, EPI_TMA_ADD = 4, EPI_SWIGLU = 5, EPI_SWIGLU_SAVE = 6 };
+
+__host__ __device__ constexpr bool epi_is_swiglu(int e) { return e == EPI_SWIGLU || e == EPI_SWIGLU_SAVE; }
+__host__ __device__ constexpr bool epi_stages_out(int e) { return e == EPI_TMA || e == EPI_TMA_ADD || epi_is_swiglu(e); }
+__host__ __device__ constexpr uint32_t epi_out_bytes(int e) {
+  return e == EPI_SWIGLU_SAVE ? 4 * 3 * 4096 : (epi_stages_out(e) ? 4 * 2 * 4096 : 0);
+}
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
 constexpr int kThreads = 192;
 
-template <int BN, int STAGES, bool STAGE_OUT = false>
+template <int BN, int STAGES, uint32_t OUT_BYTES = 0>
 struct TcSmem {
   static constexpr uint32_t kA = kBM * kBK * 2;  // 16 KB
   static constexpr uint32_t kB = BN * kBK * 2;
   static constexpr uint32_t kStage = kA + kB;
-  // output staging: 4 epilogue warps x 2 buffers x (32 rows x 128 bytes)
-  static constexpr uint32_t kOut = STAGE_OUT ? 4 * 2 * 4096 : 0;
+  // output staging: 4 epilogue warps x 2 (or 3) buffers x (32 rows x 128 bytes)
+  static constexpr uint32_t kOut = OUT_BYTES;
   static constexpr uint32_t kBarriers = (2 * STAGES + 5) * 8;
   static constexpr uint32_t kTotal = 1024 /*align slack*/ + STAGES * kStage + kOut + kBarriers + 16;
 };
@@ -136,8 +147,10 @@ __device__ __forceinline__ void store_row_chunk(T* dst, const float (&v)[32], in
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, typename TOut>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const __grid_constant__ CUtensorMap tmC, const GemmArgs g, const uint32_t idesc) {
-  using L = TcSmem<BN, STAGES, EPI == EPI_TMA || EPI == EPI_TMA_ADD>;
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
+                   const GemmArgs g, const uint32_t idesc) {
+  using L = TcSmem<BN, STAGES, epi_out_bytes(EPI)>;
+  constexpr int NSTEP = epi_is_swiglu(EPI) ? BN / 2 : BN;  // output columns per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -194,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int split = t / tiles_mn;
       const int mn = t - split * tiles_mn;
       const int m0 = (mn / g.tiles_n) * kBM;
-      const int n0 = (mn % g.tiles_n) * BN;
+      const int n0 = (mn % g.tiles_n) * NSTEP;
       const int kb0 = split * g.kb_per_split;
       int kb1 = kb0 + g.kb_per_split;
       if (kb1 > g.kb_total) kb1 = g.kb_total;
@@ -214,7 +227,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           tma_load_2d(a_dst, &tmA, fb, k0, m0);
         }
-        if constexpr (B_MN) {
+        if constexpr (epi_is_swiglu(EPI)) {  // gate rows, then the matching value rows
+          tma_load_2d(b_dst, &tmB, fb, k0, n0);
+          tma_load_2d(b_dst + (BN / 2) * 128, &tmB, fb, k0, g.ff + n0);
+        } else if constexpr (B_MN) {
 #pragma unroll
           for (int c = 0; c < BN / 64; ++c) tma_load_2d(b_dst + c * 8192, &tmB, fb, n0 + 64 * c, k0);
         } else {
@@ -293,12 +309,86 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int split = t / tiles_mn;
       const int mn = t - split * tiles_mn;
       const int m0 = (mn / g.tiles_n) * kBM;
-      const int n0 = (mn % g.tiles_n) * BN;
+      const int n0 = (mn % g.tiles_n) * NSTEP;
       bool ok = mbar_wait(tfull0 + 8 * acc, acc_phase, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if constexpr (epi_is_swiglu(EPI)) {
+        // h = round(silu(round(g))) * round(v) for the tile's 128 columns, 64 at a
+        // time; the same operation order as rk_swiglu_fwd on a bf16 u.
+        uint8_t* stage = sOut + (warp - 2) * (EPI == EPI_SWIGLU_SAVE ? 12288 : 8192);
+        const int y = m0 + quarter * 32;
+#pragma unroll 1
+        for (int c = 0; c < BN / 2; c += 64) {
+          float gv[64], vv[64];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            float part[32];
+            tmem_ld_32cols(t_row + c + q * 32, part);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) gv[q * 32 + j] = round_to<TOut>(part[j]);
+            tmem_ld_32cols(t_row + BN / 2 + c + q * 32, part);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) vv[q * 32 + j] = round_to<TOut>(part[j]);
+          }
+          if constexpr (EPI == EPI_SWIGLU_SAVE) {
+            if (lane == 0) bulk_wait_read<0>();
+          } else {
+            if (lane == 0) bulk_wait_read<1>();
+          }
+          __syncwarp();
+          uint8_t* hb = EPI == EPI_SWIGLU_SAVE ? stage : stage + ((c / 64) & 1) * 4096;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            uint4 raw;
+            TOut* e = reinterpret_cast<TOut*>(&raw);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const float gg = gv[j * 8 + k];
+              const float silu = round_to<TOut>(silu_value(gg));
+              e[k] = Dt<TOut>::from_f(__fmul_rn(silu, vv[j * 8 + k]));
+            }
+            *reinterpret_cast<uint4*>(hb + lane * 128 + ((j ^ (lane & 7)) * 16)) = raw;
+          }
+          if constexpr (EPI == EPI_SWIGLU_SAVE) {
+            uint8_t* gb = stage + 4096;
+            uint8_t* vb = stage + 8192;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              uint4 rg, rv;
+              TOut* eg = reinterpret_cast<TOut*>(&rg);
+              TOut* ev = reinterpret_cast<TOut*>(&rv);
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                eg[k] = Dt<TOut>::from_f(gv[j * 8 + k]);
+                ev[k] = Dt<TOut>::from_f(vv[j * 8 + k]);
+              }
+              const int off = lane * 128 + ((j ^ (lane & 7)) * 16);
+              *reinterpret_cast<uint4*>(gb + off) = rg;
+              *reinterpret_cast<uint4*>(vb + off) = rv;
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, smem_u32(hb), n0 + c, y);
+            if constexpr (EPI == EPI_SWIGLU_SAVE) {
+              tma_store_2d(&tmD, smem_u32(stage + 4096), n0 + c, y);
+              tma_store_2d(&tmD, smem_u32(stage + 8192), g.ff + n0 + c, y);
+            }
+            bulk_commit();
+          }
+        }
+        tc_fence_before();
+        mbar_arrive(tempty0 + 8 * acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
       if constexpr (EPI == EPI_TMA || EPI == EPI_TMA_ADD) {
         // Each warp stages its 32 rows, CW columns at a time, in a 128-byte
         // swizzled layout (16-byte chunk j of row r at j ^ (r % 8): conflict-free
@@ -376,7 +466,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  if constexpr (EPI == EPI_TMA || EPI == EPI_TMA_ADD) {
+  if constexpr (epi_stages_out(EPI)) {
     if (warp >= 2 && lane == 0) bulk_wait_all();
   }
   __syncthreads();
@@ -518,15 +608,15 @@ struct Operand {
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, typename TOut>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmArgs g, int dtype,
-              cudaStream_t s) {
-  using L = TcSmem<BN, STAGES, EPI == EPI_TMA || EPI == EPI_TMA_ADD>;
+              cudaStream_t s, const CUtensorMap* td = nullptr) {
+  using L = TcSmem<BN, STAGES, epi_out_bytes(EPI)>;
   auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, EPI, TOut>;
   rk_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)L::kTotal);
   const int total = g.tiles_m * g.tiles_n * g.splits;
   int grid = sm_count();
   if (total < grid) grid = total;
   const uint32_t idesc = idesc_f16(kBM, BN, dtype == RK_BF16 ? 1 : 0, A_MN ? 1 : 0, B_MN ? 1 : 0);
-  kern<<<grid, kThreads, L::kTotal, s>>>(ta, tb, tc, g, idesc);
+  kern<<<grid, kThreads, L::kTotal, s>>>(ta, tb, tc, td ? *td : tc, g, idesc);
   return rk_host::launch_status();
 }
 
@@ -756,4 +846,44 @@ extern "C" int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_
   if (blocks > 148 * 8) blocks = 148 * 8;
   split_reduce_kernel<<<(unsigned)blocks, 256, 0, s>>>(workspace, splits, N, K, slice_rows, dw, lddw, accumulate);
   return rk_host::launch_status();
+}
+
+// ---------------------------------------------------------------- fused SwiGLU up projection
+extern "C" int rk_gemm_fprop_swiglu(const void* x, int64_t ldx, const void* w_up, int64_t ldw, void* h, int64_t ldh,
+                                    void* u, int64_t ldu, int64_t M, int64_t ff, int64_t K, int dtype, void* stream) {
+  if (!x || !w_up || !h || M < 0 || ff <= 0 || K <= 0 || ldx < K || ldw < K || ldh < ff || (u && ldu < 2 * ff))
+    return RK_ERR_ARG;
+  if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
+  if (ff % 128) return RK_ERR_UNSUPPORTED;
+  if (M == 0) return RK_OK;
+  if (!rk_host::aligned(x, 16) || !rk_host::aligned(w_up, 16) || !rk_host::aligned(h, 16) ||
+      (u && !rk_host::aligned(u, 16)) || (ldx * 2) % 16 || (ldw * 2) % 16 || (ldh * 2) % 16 || (u && (ldu * 2) % 16))
+    return RK_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap ta, tb, tc, td;
+  if (!make_map(&ta, x, (uint64_t)K, (uint64_t)M, (uint64_t)ldx, dtype, 64, kBM) ||
+      !make_map(&tb, w_up, (uint64_t)K, (uint64_t)(2 * ff), (uint64_t)ldw, dtype, 64, 128) ||
+      !make_out_map(&tc, h, (uint64_t)ff, (uint64_t)M, (uint64_t)ldh, dtype))
+    return RK_ERR_LAUNCH;
+  if (u && !make_out_map(&td, u, (uint64_t)(2 * ff), (uint64_t)M, (uint64_t)ldu, dtype)) return RK_ERR_LAUNCH;
+  GemmArgs g{};
+  g.M = (int)M;
+  g.N = (int)(2 * ff);
+  g.K = (int)K;
+  g.tiles_m = (int)((M + kBM - 1) / kBM);
+  g.tiles_n = (int)(ff / 128);
+  g.kb_total = (int)((K + kBK - 1) / kBK);
+  g.splits = 1;
+  g.kb_per_split = g.kb_total;
+  g.ff = (int)ff;
+  g.out = h;
+  g.ldo = ldh;
+  g.out_dtype = dtype;
+  g.status = rk_host::device_status_ptr();
+  if (dtype == RK_BF16) {
+    if (u) return launch_tc<256, 3, false, false, EPI_SWIGLU_SAVE, __nv_bfloat16>(ta, tb, tc, g, dtype, s, &td);
+    return launch_tc<256, 4, false, false, EPI_SWIGLU, __nv_bfloat16>(ta, tb, tc, g, dtype, s);
+  }
+  if (u) return launch_tc<256, 3, false, false, EPI_SWIGLU_SAVE, __half>(ta, tb, tc, g, dtype, s, &td);
+  return launch_tc<256, 4, false, false, EPI_SWIGLU, __half>(ta, tb, tc, g, dtype, s);
 }

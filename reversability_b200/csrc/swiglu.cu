@@ -4,7 +4,8 @@
 // handles V consecutive columns of one row with 16-byte loads of gate and
 // value and a 16-byte store, so the kernel streams HBM at full width. The
 // arithmetic follows the reference kernels operation by operation, with FMA
-// contraction suppressed (the reference compiles with enable_fp_fusion=False):
+// contraction suppressed (the reference compiles with enable_fp_fusion=False)
+// and the exponential/divide on the approximate hardware paths (common.cuh):
 //   forward : silu = round_T(g / (1 + exp(-g)));  h = silu * v
 //   backward: s = 1/(1+exp(-g)); silu = round_T(g*s); t = round_T(dh*v)
 //             dg = t * (s * (1 + g*(1-s)));  dv = dh * silu
@@ -14,7 +15,7 @@ namespace rk {
 
 template <typename T>
 __device__ __forceinline__ float silu_fwd(float g) {
-  return round_to<T>(__fdiv_rn(g, __fadd_rn(1.f, expf(-g))));
+  return round_to<T>(silu_value(g));
 }
 
 template <typename T, int V>
@@ -50,7 +51,7 @@ __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const T* __restrict__ u
     load_vec<T, V>(dh + r * width + c, up);
 #pragma unroll
     for (int e = 0; e < V; ++e) {
-      const float s = __fdiv_rn(1.f, __fadd_rn(1.f, expf(-g[e])));
+      const float s = sigmoid_value(g[e]);
       const float silu = round_to<T>(__fmul_rn(g[e], s));
       const float t_ = round_to<T>(__fmul_rn(up[e], v[e]));
       const float slope = __fmul_rn(s, __fadd_rn(1.f, __fmul_rn(g[e], __fsub_rn(1.f, s))));

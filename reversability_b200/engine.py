@@ -151,8 +151,13 @@ class LayerKernels:
         n2, _, _ = self._mlp_norm(lw, y, x, a, save=False)
         M = n2.shape[0]
         m = torch.empty((M, lw.down.shape[0]), device=n2.device, dtype=self.cd)
+        fused = fn.swiglu_fusable(n2, lw.up_c)
         for s, e in self._tiles(M):
-            fn.linear_fwd(fn.swiglu_fwd(fn.linear_fwd(n2[s:e], lw.up_c)), lw.down_c, out=m[s:e])
+            if fused:  # SwiGLU in the up-projection epilogue: u never reaches HBM
+                hg, _ = fn.linear_swiglu_fwd(n2[s:e], lw.up_c)
+            else:
+                hg = fn.swiglu_fwd(fn.linear_fwd(n2[s:e], lw.up_c))
+            fn.linear_fwd(hg, lw.down_c, out=m[s:e])
         return m
 
     def mlp_forward_vjp(self, lw: LayerWeights, g: LayerGrads, gm: torch.Tensor, y: torch.Tensor | None = None,
@@ -168,9 +173,13 @@ class LayerKernels:
         m = torch.empty((M, lw.down.shape[0]), device=n2.device, dtype=self.cd)
         dxo = torch.empty((M, d), device=n2.device, dtype=F32)
         lp = torch.empty((M, d), device=n2.device, dtype=self.cd) if want_lp else None
+        fused = fn.swiglu_fusable(n2, lw.up_c)
         for s, e in self._tiles(M):
-            u = fn.linear_fwd(n2[s:e], lw.up_c)
-            hg = fn.swiglu_fwd(u)
+            if fused:  # h from the up-projection epilogue, u kept for the SwiGLU backward
+                hg, u = fn.linear_swiglu_fwd(n2[s:e], lw.up_c, save_u=True)
+            else:
+                u = fn.linear_fwd(n2[s:e], lw.up_c)
+                hg = fn.swiglu_fwd(u)
             fn.linear_fwd(hg, lw.down_c, out=m[s:e])
             gm_t = gm[s:e]
             dh = fn.linear_dgrad(gm_t, lw.down_c)

@@ -321,3 +321,22 @@ def cast_scale(x: torch.Tensor, dtype: torch.dtype, scale: float) -> torch.Tenso
     _lib.call("rk_cast_scale", x.data_ptr(), out.data_ptr(), _lib.code(dtype), float(scale), x.numel(),
               _lib.stream_ptr())
     return out
+
+
+def linear_swiglu_fwd(x: torch.Tensor, w_up: torch.Tensor, save_u: bool = False):
+    """h = silu(gate) * value of u = x @ w_up.T computed in the GEMM epilogue
+    (u never written unless save_u). x [M, K], w_up [2ff, K] (gate rows first).
+    Returns (h [M, ff], u [M, 2ff] or None)."""
+    require_cuda(x, w_up)
+    M, K = x.shape
+    ff = w_up.shape[0] // 2
+    h = torch.empty((M, ff), device=x.device, dtype=x.dtype)
+    u = torch.empty((M, 2 * ff), device=x.device, dtype=x.dtype) if save_u else None
+    _lib.call("rk_gemm_fprop_swiglu", x.data_ptr(), x.stride(0), w_up.data_ptr(), w_up.stride(0), h.data_ptr(), ff,
+              _lib.ptr(u), 2 * ff, M, ff, K, _gemm_dtype(x, w_up), _lib.stream_ptr())
+    return h, u
+
+
+def swiglu_fusable(x: torch.Tensor, w_up: torch.Tensor) -> bool:
+    return x.dtype in _TC_DTYPES and w_up.dtype == x.dtype and (w_up.shape[0] // 2) % 128 == 0 and \
+        x.is_contiguous() and w_up.is_contiguous() and (x.shape[1] * 2) % 16 == 0

@@ -332,3 +332,17 @@ def test_reconstruct_sum_and_cast_scale(dt):
     for coeff in (1.0, -1.0, 0.5):
         assert torch.equal(fn.reconstruct_midpoint_sum(x, a, m, coeff), x - coeff * (a + m))
     assert torch.equal(fn.cast_scale(x, dt, 0.5), (x.to(dt) * 0.5).to(dt))
+
+
+@pytest.mark.parametrize("M", [14848, 333, 8192])
+@pytest.mark.parametrize("save", [False, True])
+def test_swiglu_fused_up_gemm_bitwise(M, save):
+    from reversability_b200 import functional as fn
+    x = torch.randn(M, 256, device=DEV).bfloat16()
+    w = (torch.randn(2048, 256, device=DEV) * 0.05).bfloat16()
+    u_ref = fn.linear_fwd(x, w)
+    h_ref = fn.swiglu_fwd(u_ref)
+    h, u = fn.linear_swiglu_fwd(x, w, save_u=save)
+    assert torch.equal(h, h_ref)
+    if save:
+        assert torch.equal(u, u_ref)

@@ -142,6 +142,7 @@ template <typename T, int HD>
 __global__ void __launch_bounds__(128) fwd_kernel(const T* __restrict__ qkv, T* __restrict__ out,
                                                   float* __restrict__ lse, int H, int Tlen, int64_t ldq, int64_t ldo,
                                                   float c_log2) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   constexpr int LD = HD + 8;
   __shared__ __align__(16) T Qs[BQ * LD];
   __shared__ __align__(16) T Ks[2][BKV * LD];
@@ -253,6 +254,7 @@ __global__ void __launch_bounds__(128) bwd_dq_kernel(const T* __restrict__ qkv, 
                                                      float* __restrict__ dsum, T* __restrict__ dqkv, int H,
                                                      int Tlen, int64_t ldq, int64_t ldo, int64_t lddq, float c_log2,
                                                      float scale) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   constexpr int LD = HD + 8;
   extern __shared__ __align__(16) unsigned char dsm[];  // 6 tiles of 64 x LD
   T* Qs = reinterpret_cast<T*>(dsm);
@@ -355,6 +357,7 @@ __global__ void __launch_bounds__(128) bwd_dkv_kernel(const T* __restrict__ qkv,
                                                       const float* __restrict__ lse, const float* __restrict__ dsum,
                                                       T* __restrict__ dqkv, int H, int Tlen, int64_t ldq,
                                                       int64_t ldo, int64_t lddq, float c_log2, float scale) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   constexpr int LD = HD + 8;
   extern __shared__ __align__(16) unsigned char dsm[];  // 6 tiles of 64 x LD, then 4 x 64 floats
   T* Ks = reinterpret_cast<T*>(dsm);
@@ -456,6 +459,7 @@ __global__ void __launch_bounds__(128) bwd_dkv_kernel(const T* __restrict__ qkv,
 __global__ void __launch_bounds__(128) fwd_f32_kernel(const float* __restrict__ qkv, float* __restrict__ out,
                                                       float* __restrict__ lse, int H, int HD, int Tlen, int64_t ldq,
                                                       int64_t ldo, float scale) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   extern __shared__ float sm[];  // [4 warps][Tlen] scores
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 4 + warp;
@@ -498,6 +502,7 @@ __global__ void __launch_bounds__(128) bwd_dq_f32_kernel(const float* __restrict
                                                          const float* __restrict__ lse, float* __restrict__ dsum,
                                                          float* __restrict__ dqkv, int H, int HD, int Tlen,
                                                          int64_t ldq, int64_t ldo, int64_t lddq, float scale) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   extern __shared__ float sm[];  // [4][Tlen] dS
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.x * 4 + warp;
@@ -541,6 +546,7 @@ __global__ void __launch_bounds__(128) bwd_dkv_f32_kernel(const float* __restric
                                                           const float* __restrict__ dsum, float* __restrict__ dqkv,
                                                           int H, int HD, int Tlen, int64_t ldq, int64_t ldo,
                                                           int64_t lddq, float scale) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   extern __shared__ float sm[];  // [4][2][Tlen]: p and dS per query
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int key = blockIdx.x * 4 + warp;
@@ -593,7 +599,7 @@ template <typename T, int HD>
 int fwd_tc(const void* qkv, void* out, float* lse, int B, int H, int Tlen, int64_t ldq, int64_t ldo, cudaStream_t s) {
   dim3 grid((Tlen + BQ - 1) / BQ, B * H);
   const float c_log2 = 1.4426950408889634f / sqrtf((float)HD);
-  fwd_kernel<T, HD><<<grid, 128, 0, s>>>(static_cast<const T*>(qkv), static_cast<T*>(out), lse, H, Tlen, ldq, ldo,
+  rk_host::launch_k(fwd_kernel<T, HD>, grid, 128, 0, s, static_cast<const T*>(qkv), static_cast<T*>(out), lse, H, Tlen, ldq, ldo,
                                          c_log2);
   return rk_host::launch_status();
 }
@@ -610,12 +616,12 @@ int bwd_tc(const void* qkv, const void* o, const void* dout, const float* lse, f
   static_assert(smem_dkv <= 227 * 1024, "attention backward tiles exceed shared memory");
   rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dq_kernel<T, HD>), smem_dq);
   rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dkv_kernel<T, HD>), smem_dkv);
-  bwd_dq_kernel<T, HD><<<grid, 128, smem_dq, s>>>(static_cast<const T*>(qkv), static_cast<const T*>(o),
+  rk_host::launch_k(bwd_dq_kernel<T, HD>, grid, 128, smem_dq, s, static_cast<const T*>(qkv), static_cast<const T*>(o),
                                             static_cast<const T*>(dout), lse, dsum, static_cast<T*>(dqkv), H, Tlen,
                                             ldq, ldo, lddq, c_log2, scale);
   int st = rk_host::launch_status();
   if (st) return st;
-  bwd_dkv_kernel<T, HD><<<grid, 128, smem_dkv, s>>>(static_cast<const T*>(qkv), static_cast<const T*>(dout), lse, dsum,
+  rk_host::launch_k(bwd_dkv_kernel<T, HD>, grid, 128, smem_dkv, s, static_cast<const T*>(qkv), static_cast<const T*>(dout), lse, dsum,
                                              static_cast<T*>(dqkv), H, Tlen, ldq, ldo, lddq, c_log2, scale);
   return rk_host::launch_status();
 }
@@ -636,7 +642,7 @@ extern "C" int rk_attn_fwd(const void* qkv, int64_t ldq, void* out, int64_t ldo,
     dim3 grid((unsigned)((T + 3) / 4), (unsigned)(B * H));
     const size_t smem = 4 * T * sizeof(float);
     if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(fwd_f32_kernel), (int)smem);
-    fwd_f32_kernel<<<grid, 128, smem, s>>>(static_cast<const float*>(qkv), static_cast<float*>(out), lse, (int)H,
+    rk_host::launch_k(fwd_f32_kernel, grid, 128, smem, s, static_cast<const float*>(qkv), static_cast<float*>(out), lse, (int)H,
                                            (int)HD, (int)T, ldq, ldo, 1.f / sqrtf((float)HD));
     return rk_host::launch_status();
   }
@@ -662,14 +668,14 @@ extern "C" int rk_attn_bwd(const void* qkv, int64_t ldq, const void* out, const 
     const float scale = 1.f / sqrtf((float)HD);
     size_t smem = 4 * T * sizeof(float);
     if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dq_f32_kernel), (int)smem);
-    bwd_dq_f32_kernel<<<grid, 128, smem, s>>>(static_cast<const float*>(qkv), static_cast<const float*>(out),
+    rk_host::launch_k(bwd_dq_f32_kernel, grid, 128, smem, s, static_cast<const float*>(qkv), static_cast<const float*>(out),
                                               static_cast<const float*>(dout), lse, dsum, static_cast<float*>(dqkv),
                                               (int)H, (int)HD, (int)T, ldq, ldo, lddq, scale);
     int st = rk_host::launch_status();
     if (st) return st;
     smem = 8 * T * sizeof(float);
     if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dkv_f32_kernel), (int)smem);
-    bwd_dkv_f32_kernel<<<grid, 128, smem, s>>>(static_cast<const float*>(qkv), static_cast<const float*>(dout), lse,
+    rk_host::launch_k(bwd_dkv_f32_kernel, grid, 128, smem, s, static_cast<const float*>(qkv), static_cast<const float*>(dout), lse,
                                                dsum, static_cast<float*>(dqkv), (int)H, (int)HD, (int)T, ldq, ldo,
                                                lddq, scale);
     return rk_host::launch_status();

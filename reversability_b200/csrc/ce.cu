@@ -38,6 +38,7 @@ __global__ void __launch_bounds__(512) ce_kernel(const T* logits, int64_t ld, in
                                                  const float* __restrict__ scale_dev,
                                                  float* __restrict__ loss_rows, T* dlogits,
                                                  int64_t ldd, int ignore_index, unsigned int* status) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   if (scale_dev) scale *= *scale_dev;
   __shared__ float sm_m[32], sm_s[32];
   __shared__ float s_lse;
@@ -130,9 +131,9 @@ int launch(const void* logits, int64_t ld, int64_t vocab, const int64_t* labels,
   const bool vec = rk_host::aligned(logits, 16) && rk_host::aligned(dlogits, 16) &&
                    (ld * (int64_t)sizeof(T)) % 16 == 0 && (ldd * (int64_t)sizeof(T)) % 16 == 0;
   if (vec)
-    ce_kernel<T, V><<<(unsigned)rows, 512, 0, s>>>(X, ld, (int)vocab, labels, scale, scale_dev, loss_rows, D, ldd, ignore_index, st);
+    rk_host::launch_k(ce_kernel<T, V>, (unsigned)rows, 512, 0, s, X, ld, (int)vocab, labels, scale, scale_dev, loss_rows, D, ldd, ignore_index, st);
   else
-    ce_kernel<T, 1><<<(unsigned)rows, 512, 0, s>>>(X, ld, (int)vocab, labels, scale, scale_dev, loss_rows, D, ldd, ignore_index, st);
+    rk_host::launch_k(ce_kernel<T, 1>, (unsigned)rows, 512, 0, s, X, ld, (int)vocab, labels, scale, scale_dev, loss_rows, D, ldd, ignore_index, st);
   return rk_host::launch_status();
 }
 }  // namespace

@@ -204,12 +204,41 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_fmt, int a
 
 __device__ __forceinline__ int elect_lane0() { return (threadIdx.x & 31) == 0; }
 
+// Programmatic dependent launch: every librevk kernel is launched with
+// programmatic stream serialization, so it may become resident while the
+// previous kernel on the stream drains. pdl_wait() blocks until that kernel
+// has completed and its writes are visible; a kernel calls it before its first
+// read of inputs or write of outputs; it is a no-op when the launch had no PDL
+// attribute. No kernel triggers its dependents explicitly: the next grid starts
+// launching as this grid's blocks exit, so its prologue and launch latency
+// overlap this grid's tail without taking SM slots from this grid's main loop
+// (an explicit trigger at kernel entry measured slower).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 }  // namespace rk
 
 // Host-side helpers shared by the translation units.
 namespace rk_host {
 // Counts every kernel launch the library makes (status.cu); read with rk_launch_count().
 void count_launch();
+// Programmatic dependent launch on/off (status.cu; REVK_PDL=0 in the environment disables it).
+bool pdl_enabled();
+
+// Launches `kernel` on stream `s` with programmatic stream serialization (see pdl_wait).
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
 inline int launch_status() {
   count_launch();
   cudaError_t e = cudaGetLastError();

@@ -6,8 +6,8 @@
 // Backward, deterministic (no floating-point atomics):
 //   1. rows are sorted by token id with a stable radix sort (CUB, keys = ids,
 //      values = row indices), so equal ids become contiguous runs in row order;
-//   2. one CTA per run start sums its rows' gradients in that order, one
-//      thread per column, and adds the sum into g_tok[id];
+//   2. each run is summed in two fixed-order passes (per-32-row pieces, then
+//      the pieces of a run in order) and added into g_tok[id];
 //   3. one CTA per position t sums dx[b*T + t] over b in order into g_pos[t].
 // The row cotangent is dx (+ dx2 when given: the boundary state p = q = x of
 // the reversible stack receives one cotangent through each).
@@ -20,6 +20,7 @@ namespace rk {
 __global__ void __launch_bounds__(256) emb_fwd_kernel(const int64_t* __restrict__ ids, const float* __restrict__ tok,
                                                       const float* __restrict__ pos, float* __restrict__ out,
                                                       int64_t rows, int T, int d, int64_t V, unsigned int* status) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   const int lane = threadIdx.x & 31;
   const int64_t r = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (r >= rows) return;
@@ -42,6 +43,7 @@ __global__ void __launch_bounds__(256) emb_fwd_kernel(const int64_t* __restrict_
 // Sort keys (ids outside [0, V) become V, a run the backward skips) and row indices.
 __global__ void keys_kernel(const int64_t* __restrict__ ids, int64_t* __restrict__ keys, int* __restrict__ rows_out,
                             int64_t n, int64_t V) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i < n) {
     const int64_t id = ids[i];
@@ -50,38 +52,30 @@ __global__ void keys_kernel(const int64_t* __restrict__ ids, int64_t* __restrict
   }
 }
 
-// CTA i handles the run of equal sorted ids starting at i (and exits if i is
-// not a run start). The run's end is found by binary search in the sorted
-// keys. Warp w sums rows i+w, i+w+8, ... of the run (lanes over columns, 16-byte
-// loads), and the 8 warp sums are added in warp order, so the result does not
-// depend on scheduling. Long runs (frequent tokens under a Zipf distribution)
-// are thus read by 8 warps with many loads in flight.
-__global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restrict__ skeys,
-                                                          const int* __restrict__ srows,
-                                                          const float* __restrict__ dx, const float* __restrict__ dx2,
-                                                          float* __restrict__ g_tok, int64_t rows, int d, int64_t V,
-                                                          unsigned int* status) {
-  __shared__ float part[8][128];
-  const int64_t i = blockIdx.x;
-  const int64_t id = skeys[i];
-  if (i > 0 && skeys[i - 1] == id) return;
-  if (id < 0 || id >= V) {
-    if (threadIdx.x == 0) flag_error(status, RK_DEV_EMB_INDEX);
-    return;
-  }
-  int64_t lo = i + 1, hi = rows;  // first index with key != id
-  while (lo < hi) {
-    const int64_t mid = (lo + hi) >> 1;
-    if (skeys[mid] == id) lo = mid + 1; else hi = mid;
-  }
-  const int64_t end = lo;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+// Token-gradient reduction in two fixed-order passes over the sorted rows.
+// Pass 1: warp w owns sorted positions [32w, 32w+32); it sums the rows of each
+// run piece inside its range in position order (lanes over columns, one
+// 16-byte vector per lane per row) and writes the piece's sum at
+// piece[start of the piece]. Pass 2: the CTA of each run start adds the pieces
+// of its run (one per 32-row range it overlaps) in range order into g_tok.
+// Every sum has a fixed order, so g_tok is bitwise reproducible, and a long
+// run (a frequent token) is read by many warps in parallel.
+__global__ void __launch_bounds__(256) emb_tok_piece_kernel(const int64_t* __restrict__ skeys,
+                                                            const int* __restrict__ srows,
+                                                            const float* __restrict__ dx,
+                                                            const float* __restrict__ dx2, float* __restrict__ piece,
+                                                            int64_t rows, int d) {
+  pdl_wait();  // inputs are the previous kernel's outputs
+  const int lane = threadIdx.x & 31;
+  const int64_t r0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * 32;
+  if (r0 >= rows) return;
+  const int64_t r1 = r0 + 32 < rows ? r0 + 32 : rows;
   for (int c0 = 0; c0 < d; c0 += 128) {
     const int c = c0 + lane * 4;
+    int64_t start = r0;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    if (c < d) {
-#pragma unroll 4
-      for (int64_t j = i + warp; j < end; j += 8) {
+    for (int64_t j = r0; j < r1; ++j) {
+      if (c < d) {
         float v[4];
         const int64_t off = (int64_t)srows[j] * d + c;
         load_vec<float, 4>(dx + off, v);
@@ -94,22 +88,44 @@ __global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restr
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[e] += v[e];
       }
-    }
+      const bool last = (j + 1 == r1) || (skeys[j + 1] != skeys[j]);
+      if (last) {
+        if (c < d) store_vec<float, 4>(piece + start * d + c, acc);
 #pragma unroll
-    for (int e = 0; e < 4; ++e) part[warp][lane * 4 + e] = acc[e];
-    __syncthreads();
-    if (threadIdx.x < 128 && c0 + (int)threadIdx.x < d) {
-      float sum = 0.f;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) sum += part[w][threadIdx.x];
-      g_tok[id * d + c0 + threadIdx.x] += sum;
+        for (int e = 0; e < 4; ++e) acc[e] = 0.f;
+        start = j + 1;
+      }
     }
-    __syncthreads();
+  }
+}
+
+__global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restrict__ skeys,
+                                                          const float* __restrict__ piece, float* __restrict__ g_tok,
+                                                          int64_t rows, int d, int64_t V, unsigned int* status) {
+  pdl_wait();  // inputs are the previous kernel's outputs
+  const int64_t i = blockIdx.x;
+  const int64_t id = skeys[i];
+  if (i > 0 && skeys[i - 1] == id) return;
+  if (id < 0 || id >= V) {
+    if (threadIdx.x == 0) flag_error(status, RK_DEV_EMB_INDEX);
+    return;
+  }
+  int64_t lo = i + 1, hi = rows;  // run end: first index with a different key
+  while (lo < hi) {
+    const int64_t mid = (lo + hi) >> 1;
+    if (skeys[mid] == id) lo = mid + 1; else hi = mid;
+  }
+  const int64_t end = lo;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float s = 0.f;
+    for (int64_t p = i; p < end; p = (p / 32 + 1) * 32) s += piece[p * d + c];  // one piece per 32-row range
+    g_tok[id * d + c] += s;
   }
 }
 
 __global__ void __launch_bounds__(256) emb_pos_bwd_kernel(const float* __restrict__ dx, const float* __restrict__ dx2,
                                                           float* __restrict__ g_pos, int64_t rows, int T, int d) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   const int t = blockIdx.x;
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
     float s = 0.f;
@@ -129,6 +145,7 @@ int key_bits(int64_t V) {
   return b;
 }
 size_t align256(size_t x) { return (x + 255) & ~size_t(255); }
+constexpr int64_t kMaxEmbWidth = 1024;  // widest embedding the piece buffer is sized for
 size_t cub_temp_bytes(int64_t rows, int64_t V) {
   size_t temp = 0;
   cub::DeviceRadixSort::SortPairs(nullptr, temp, (const int64_t*)nullptr, (int64_t*)nullptr, (const int*)nullptr,
@@ -144,7 +161,7 @@ extern "C" int rk_embedding_fwd(const int64_t* ids, const float* tok, const floa
     return RK_ERR_ALIGN;
   if (rows == 0) return RK_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  emb_fwd_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(ids, tok, pos, out, rows, (int)T, (int)d, V,
+  rk_host::launch_k(emb_fwd_kernel, (unsigned)((rows + 7) / 8), 256, 0, s, ids, tok, pos, out, rows, (int)T, (int)d, V,
                                                             rk_host::device_status_ptr());
   return rk_host::launch_status();
 }
@@ -152,7 +169,7 @@ extern "C" int rk_embedding_fwd(const int64_t* ids, const float* tok, const floa
 extern "C" int64_t rk_embedding_bwd_workspace(int64_t rows, int64_t V) {
   if (rows <= 0 || V <= 0) return 0;
   return (int64_t)(2 * align256(rows * sizeof(int64_t)) + 2 * align256(rows * sizeof(int)) +
-                   align256(cub_temp_bytes(rows, V)));
+                   align256(cub_temp_bytes(rows, V)) + align256(rows * 4 * (size_t)kMaxEmbWidth));
 }
 
 extern "C" int rk_embedding_bwd(const int64_t* ids, const float* dx, const float* dx2, float* g_tok, float* g_pos,
@@ -160,6 +177,7 @@ extern "C" int rk_embedding_bwd(const int64_t* ids, const float* dx, const float
                                 void* stream) {
   if (!ids || !dx || !g_tok || !g_pos || rows < 0 || T <= 0 || d <= 0 || V <= 0 || rows >= (1ll << 31))
     return RK_ERR_ARG;
+  if (d > kMaxEmbWidth) return RK_ERR_UNSUPPORTED;
   if (d % 4 || !rk_host::aligned(dx, 16) || (dx2 && !rk_host::aligned(dx2, 16))) return RK_ERR_ALIGN;
   if (rows == 0) return RK_OK;
   if (!workspace || workspace_bytes < rk_embedding_bwd_workspace(rows, V)) return RK_ERR_WORKSPACE;
@@ -174,17 +192,20 @@ extern "C" int rk_embedding_bwd(const int64_t* ids, const float* dx, const float
   int* srows = reinterpret_cast<int*>(w);
   w += align256(rows * sizeof(int));
   size_t temp = cub_temp_bytes(rows, V);
-  keys_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(ids, keys, rows_in, rows, V);
+  float* piece = reinterpret_cast<float*>(w + align256(temp));
+  rk_host::launch_k(keys_kernel, (unsigned)((rows + 255) / 256), 256, 0, s, ids, keys, rows_in, rows, V);
   int st = rk_host::launch_status();
   if (st) return st;
   if (cub::DeviceRadixSort::SortPairs(w, temp, keys, skeys, rows_in, srows, (int)rows, 0, key_bits(V + 1), s) !=
       cudaSuccess)
     return RK_ERR_LAUNCH;
   rk_host::count_launch();
-  emb_tok_bwd_kernel<<<(unsigned)rows, 256, 0, s>>>(skeys, srows, dx, dx2, g_tok, rows, (int)d, V,
-                                                    rk_host::device_status_ptr());
+  rk_host::launch_k(emb_tok_piece_kernel, (unsigned)((rows + 255) / 256), 256, 0, s, skeys, srows, dx, dx2, piece, rows, (int)d);
   st = rk_host::launch_status();
   if (st) return st;
-  emb_pos_bwd_kernel<<<(unsigned)T, 256, 0, s>>>(dx, dx2, g_pos, rows, (int)T, (int)d);
+  rk_host::launch_k(emb_tok_bwd_kernel, (unsigned)rows, 256, 0, s, skeys, piece, g_tok, rows, (int)d, V, rk_host::device_status_ptr());
+  st = rk_host::launch_status();
+  if (st) return st;
+  rk_host::launch_k(emb_pos_bwd_kernel, (unsigned)T, 256, 0, s, dx, dx2, g_pos, rows, (int)T, (int)d);
   return rk_host::launch_status();
 }

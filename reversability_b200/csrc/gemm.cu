@@ -28,7 +28,7 @@
 #include <cstdlib>
 #include <mutex>
 #include <unordered_map>
-#include "common.cuh"
+#include "vec.cuh"
 
 namespace rk {
 
@@ -149,6 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                    const GemmArgs g, const uint32_t idesc) {
+  
   using L = TcSmem<BN, STAGES, epi_out_bytes(EPI)>;
   constexpr int NSTEP = epi_is_swiglu(EPI) ? BN / 2 : BN;  // output columns per tile
   extern __shared__ uint8_t smem_raw[];
@@ -193,6 +194,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *s_tmem;
+  // The prologue above (barriers, tensor-map prefetch, TMEM allocation) touches
+  // no global data, so it overlaps the previous kernel's tail.
+  pdl_wait();
 
   const int tiles_mn = g.tiles_m * g.tiles_n;
   const int total = tiles_mn * g.splits;
@@ -483,17 +487,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// dw[r, c] (+)= sum_s partial[s][r][c] (slices `slice_rows` rows apart), in slice order.
-__global__ void split_reduce_kernel(const float* __restrict__ partial, int splits, int64_t rows, int64_t cols,
-                                    int64_t slice_rows, float* __restrict__ dw, int64_t lddw, int accumulate) {
-  const int64_t n = rows * cols;
+// dw[r, c] (+)= sum_s partial[s][r][c] (slices `slice_rows` rows apart), in
+// slice order; 4 consecutive columns per thread when cols % 4 == 0.
+template <int V>
+__global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restrict__ partial, int splits, int64_t rows,
+                                                           int64_t cols, int64_t slice_rows, float* __restrict__ dw,
+                                                           int64_t lddw, int accumulate) {
+  pdl_wait();  // inputs are the previous kernel's outputs
+  const int64_t n = rows * cols / V;
   const int64_t slice = slice_rows * cols;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-    float s = 0.f;
-    for (int k = 0; k < splits; ++k) s += partial[(int64_t)k * slice + i];
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = t * V;
+    float s[V];
+#pragma unroll
+    for (int e = 0; e < V; ++e) s[e] = 0.f;
+    for (int k = 0; k < splits; ++k) {
+      float v[V];
+      load_vec<float, V>(partial + (int64_t)k * slice + i, v);
+#pragma unroll
+      for (int e = 0; e < V; ++e) s[e] += v[e];
+    }
     const int64_t r = i / cols, c = i - r * cols;
     float* d = dw + r * lddw + c;
-    *d = accumulate ? *d + s : s;
+    if (accumulate) {
+      float o[V];
+      load_vec<float, V>(d, o);
+#pragma unroll
+      for (int e = 0; e < V; ++e) s[e] += o[e];
+    }
+    store_vec<float, V>(d, s);
   }
 }
 
@@ -504,6 +526,7 @@ __global__ void __launch_bounds__(256) gemm_f32_kernel(const float* __restrict__
                                                        const float* __restrict__ B, int64_t sbn, int64_t sbk,
                                                        TOut* __restrict__ C, int64_t ldc, int M, int N, int K,
                                                        int accumulate) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   __shared__ float As[16][64 + 4];
   __shared__ float Bs[16][64 + 4];
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
@@ -616,7 +639,7 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
   int grid = sm_count();
   if (total < grid) grid = total;
   const uint32_t idesc = idesc_f16(kBM, BN, dtype == RK_BF16 ? 1 : 0, A_MN ? 1 : 0, B_MN ? 1 : 0);
-  kern<<<grid, kThreads, L::kTotal, s>>>(ta, tb, tc, td ? *td : tc, g, idesc);
+  rk_host::launch_k(kern, grid, kThreads, L::kTotal, s, ta, tb, tc, td ? *td : tc, g, idesc);
   return rk_host::launch_status();
 }
 
@@ -662,11 +685,11 @@ int pick_bn(int M, int N) {
 
 // Tensor-core GEMM: C[M,N] = sum_k A(m,k) B(n,k).
 int tc_gemm(Operand a, Operand b, int M, int N, int K, int dtype, void* out, int64_t ldo, int out_dtype, int splits,
-            cudaStream_t s, bool accumulate = false, int split_rows = 0) {
+            cudaStream_t s, bool accumulate = false, int split_rows = 0, int bn = 0) {
   const size_t esz = 2;
   if (!rk_host::aligned(a.ptr, 16) || !rk_host::aligned(b.ptr, 16)) return RK_ERR_ALIGN;
   if ((a.ld * esz) % 16 || (b.ld * esz) % 16) return RK_ERR_ALIGN;
-  const int BN = pick_bn(M, N);
+  const int BN = bn ? bn : pick_bn(M, N);
   CUtensorMap ta, tb;
   bool ok;
   if (a.mn_major) ok = make_map(&ta, a.ptr, (uint64_t)M, (uint64_t)K, (uint64_t)a.ld, dtype, 64, 64);
@@ -748,7 +771,7 @@ template <typename TOut>
 int f32_gemm_typed(const float* A, int64_t sam, int64_t sak, const float* B, int64_t sbn, int64_t sbk, void* C,
                    int64_t ldc, int M, int N, int K, int accumulate, cudaStream_t s) {
   dim3 grid((N + 63) / 64, (M + 63) / 64);
-  gemm_f32_kernel<TOut><<<grid, 256, 0, s>>>(A, sam, sak, B, sbn, sbk, static_cast<TOut*>(C), ldc, M, N, K, accumulate);
+  rk_host::launch_k(gemm_f32_kernel<TOut>, grid, 256, 0, s, A, sam, sak, B, sbn, sbk, static_cast<TOut*>(C), ldc, M, N, K, accumulate);
   return rk_host::launch_status();
 }
 
@@ -768,9 +791,11 @@ bool dims_ok(int64_t M, int64_t N, int64_t K) {
 }
 
 int wgrad_splits(int64_t M, int64_t N, int64_t K) {
-  // Output tiles of dW[N,K]; choose slices so that tiles*slices fills ~the SMs,
-  // with each slice at least 8 k-blocks (512 tokens) long. Fixed per shape.
-  const int64_t tiles = ((N + 127) / 128) * ((K + (K > 128 ? 255 : 127)) / (K > 128 ? 256 : 128));
+  // Output tiles of dW[N,K] (128x128 when split: the fp32 slice traffic is
+  // slices x N x K, and narrower tiles halve the slice count for the same
+  // SM fill); choose slices so that tiles*slices fills ~the SMs, with each
+  // slice at least 8 k-blocks (512 tokens) long. Fixed per shape.
+  const int64_t tiles = ((N + 127) / 128) * ((K + 127) / 128);
   const int64_t kb = (M + 63) / 64;
   int64_t s = (148 + tiles - 1) / tiles;
   if (s > kb / 8) s = kb / 8;
@@ -840,11 +865,15 @@ extern "C" int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_
   const int64_t need = (int64_t)splits * slice_rows * K * (int64_t)sizeof(float);
   if (!workspace || workspace_bytes < need) return RK_ERR_WORKSPACE;
   const int st = tc_gemm({dy, lddy, true}, {x, ldx, true}, (int)N, (int)K, (int)M, dtype, workspace, K, RK_F32,
-                         splits, s, false, (int)slice_rows);
+                         splits, s, false, (int)slice_rows, 128);
   if (st != RK_OK) return st;
-  int64_t blocks = (N * K + 255) / 256;
-  if (blocks > 148 * 8) blocks = 148 * 8;
-  split_reduce_kernel<<<(unsigned)blocks, 256, 0, s>>>(workspace, splits, N, K, slice_rows, dw, lddw, accumulate);
+  const bool vec = K % 4 == 0 && lddw % 4 == 0 && rk_host::aligned(dw, 16) && rk_host::aligned(workspace, 16);
+  int64_t blocks = (N * K / (vec ? 4 : 1) + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (vec)
+    rk_host::launch_k(split_reduce_kernel<4>, (unsigned)blocks, 256, 0, s, workspace, splits, N, K, slice_rows, dw, lddw, accumulate);
+  else
+    rk_host::launch_k(split_reduce_kernel<1>, (unsigned)blocks, 256, 0, s, workspace, splits, N, K, slice_rows, dw, lddw, accumulate);
   return rk_host::launch_status();
 }
 

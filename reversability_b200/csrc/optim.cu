@@ -22,6 +22,7 @@ namespace rk {
 constexpr int kNormBlocks = 1184;  // 8 per SM on 148 SMs: fixed, so the reduction order is fixed
 
 __global__ void __launch_bounds__(256) sumsq_kernel(const float* __restrict__ g, int64_t n, float* __restrict__ partial) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   __shared__ float red[8];
   float s = 0.f;
   const int64_t n4 = n / 4;
@@ -51,6 +52,7 @@ __global__ void __launch_bounds__(256) sumsq_kernel(const float* __restrict__ g,
 __global__ void __launch_bounds__(256) prepare_kernel(const float* __restrict__ partial, int parts, float max_norm,
                                                       float beta1, float beta2, float weight_decay,
                                                       float* __restrict__ scalars) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   __shared__ double red[256];
   double s = 0.0;
   for (int i = threadIdx.x; i < parts; i += blockDim.x) s += (double)partial[i];
@@ -81,6 +83,7 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ p, const
                                                     float* __restrict__ m, float* __restrict__ v, TC* __restrict__ pc,
                                                     int64_t n, const float* __restrict__ scalars, float beta1,
                                                     float beta2, float eps) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   const float coef = scalars[3], step_size = scalars[4], bc2s = scalars[5], decay = scalars[6];
   const float om1 = 1.f - beta1, om2 = 1.f - beta2;
   const int64_t n4 = n / 4;
@@ -130,10 +133,10 @@ extern "C" int rk_clip_adamw_prepare(const float* grads, int64_t n, float max_no
   if (workspace_bytes < rk_clip_adamw_workspace()) return RK_ERR_WORKSPACE;
   if (!rk_host::aligned(grads, 16)) return RK_ERR_ALIGN;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  sumsq_kernel<<<kNormBlocks, 256, 0, s>>>(grads, n, workspace);
+  rk_host::launch_k(sumsq_kernel, kNormBlocks, 256, 0, s, grads, n, workspace);
   int st = rk_host::launch_status();
   if (st) return st;
-  prepare_kernel<<<1, 256, 0, s>>>(workspace, kNormBlocks, max_norm, beta1, beta2, weight_decay, scalars);
+  rk_host::launch_k(prepare_kernel, 1, 256, 0, s, workspace, kNormBlocks, max_norm, beta1, beta2, weight_decay, scalars);
   return rk_host::launch_status();
 }
 
@@ -150,14 +153,14 @@ extern "C" int rk_adamw_step(float* params, const float* grads, float* exp_avg, 
   if (blocks > 148 * 8) blocks = 148 * 8;
   if (blocks < 1) blocks = 1;
   if (!params_c) {
-    adamw_kernel<float><<<(unsigned)blocks, 256, 0, s>>>(params, grads, exp_avg, exp_avg_sq, nullptr, n, scalars,
+    rk_host::launch_k(adamw_kernel<float>, (unsigned)blocks, 256, 0, s, params, grads, exp_avg, exp_avg_sq, nullptr, n, scalars,
                                                         beta1, beta2, eps);
   } else if (c_dtype == RK_BF16) {
-    adamw_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, s>>>(params, grads, exp_avg, exp_avg_sq,
+    rk_host::launch_k(adamw_kernel<__nv_bfloat16>, (unsigned)blocks, 256, 0, s, params, grads, exp_avg, exp_avg_sq,
                                                                 static_cast<__nv_bfloat16*>(params_c), n, scalars,
                                                                 beta1, beta2, eps);
   } else if (c_dtype == RK_F16) {
-    adamw_kernel<__half><<<(unsigned)blocks, 256, 0, s>>>(params, grads, exp_avg, exp_avg_sq,
+    rk_host::launch_k(adamw_kernel<__half>, (unsigned)blocks, 256, 0, s, params, grads, exp_avg, exp_avg_sq,
                                                          static_cast<__half*>(params_c), n, scalars, beta1, beta2,
                                                          eps);
   } else {

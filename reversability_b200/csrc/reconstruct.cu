@@ -14,6 +14,7 @@ namespace rk {
 template <typename TF, int V, bool SCALE>
 __global__ void __launch_bounds__(256) reconstruct_kernel(const float* __restrict__ xn, const TF* __restrict__ f,
                                                           float coeff, float* __restrict__ xp, int64_t n) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   const int64_t nv = n / V;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nv; t += (int64_t)gridDim.x * blockDim.x) {
     float a[V], b[V], o[V];
@@ -43,6 +44,7 @@ template <typename TF, int V>
 __global__ void __launch_bounds__(256) reconstruct_sum_kernel(const float* __restrict__ xn, const TF* __restrict__ a,
                                                               const TF* __restrict__ m, float coeff,
                                                               float* __restrict__ xp, int64_t n) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   const int64_t nv = n / V;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nv; t += (int64_t)gridDim.x * blockDim.x) {
     float x[V], av[V], mv[V], o[V];
@@ -69,6 +71,7 @@ __global__ void __launch_bounds__(256) reconstruct_sum_kernel(const float* __res
 template <typename T, int V>
 __global__ void __launch_bounds__(256) cast_scale_kernel(const float* __restrict__ x, T* __restrict__ out, float scale,
                                                          int64_t n) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   const int64_t nv = n / V;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < nv; t += (int64_t)gridDim.x * blockDim.x) {
     float v[V], o[V];
@@ -95,9 +98,9 @@ int launch(const float* xn, const void* f, float coeff, float* xp, int64_t n, cu
   if (blocks > 148 * 16) blocks = 148 * 16;
   if (blocks < 1) blocks = 1;
   if (vec)
-    reconstruct_kernel<TF, 4, SCALE><<<(unsigned)blocks, 256, 0, s>>>(xn, F, coeff, xp, n);
+    rk_host::launch_k(reconstruct_kernel<TF, 4, SCALE>, (unsigned)blocks, 256, 0, s, xn, F, coeff, xp, n);
   else
-    reconstruct_kernel<TF, 1, SCALE><<<(unsigned)blocks, 256, 0, s>>>(xn, F, coeff, xp, n);
+    rk_host::launch_k(reconstruct_kernel<TF, 1, SCALE>, (unsigned)blocks, 256, 0, s, xn, F, coeff, xp, n);
   return rk_host::launch_status();
 }
 
@@ -138,9 +141,9 @@ int sum_launch(const float* xn, const void* a, const void* m, float coeff, float
   auto Mv = static_cast<const TF*>(m);
   const size_t va = 4 * sizeof(TF) >= 16 ? 16 : 4 * sizeof(TF);
   if (rk_host::aligned(xn, 16) && rk_host::aligned(xp, 16) && rk_host::aligned(a, va) && rk_host::aligned(m, va))
-    reconstruct_sum_kernel<TF, 4><<<blocks_for(n / 4), 256, 0, s>>>(xn, A, Mv, coeff, xp, n);
+    rk_host::launch_k(reconstruct_sum_kernel<TF, 4>, blocks_for(n / 4), 256, 0, s, xn, A, Mv, coeff, xp, n);
   else
-    reconstruct_sum_kernel<TF, 1><<<blocks_for(n), 256, 0, s>>>(xn, A, Mv, coeff, xp, n);
+    rk_host::launch_k(reconstruct_sum_kernel<TF, 1>, blocks_for(n), 256, 0, s, xn, A, Mv, coeff, xp, n);
   return rk_host::launch_status();
 }
 template <typename T>
@@ -148,9 +151,9 @@ int cast_launch(const float* x, void* out, float scale, int64_t n, cudaStream_t 
   auto O = static_cast<T*>(out);
   const size_t vo = 4 * sizeof(T) >= 16 ? 16 : 4 * sizeof(T);
   if (rk_host::aligned(x, 16) && rk_host::aligned(out, vo))
-    cast_scale_kernel<T, 4><<<blocks_for(n / 4), 256, 0, s>>>(x, O, scale, n);
+    rk_host::launch_k(cast_scale_kernel<T, 4>, blocks_for(n / 4), 256, 0, s, x, O, scale, n);
   else
-    cast_scale_kernel<T, 1><<<blocks_for(n), 256, 0, s>>>(x, O, scale, n);
+    rk_host::launch_k(cast_scale_kernel<T, 1>, blocks_for(n), 256, 0, s, x, O, scale, n);
   return rk_host::launch_status();
 }
 }  // namespace

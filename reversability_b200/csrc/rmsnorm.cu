@@ -18,39 +18,55 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-template <typename Tx, typename Ty, int V, int NV>
+// Each warp handles R consecutive rows and issues all of their loads before
+// reducing any of them, so enough bytes are in flight per SM to cover memory
+// latency (one 512-byte bf16 row per warp would not).
+template <typename Tx, typename Ty, int V, int NV, int R>
 __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const Tx* __restrict__ x, int64_t ldx,
                                                           const float* __restrict__ w, Ty* __restrict__ y,
                                                           int64_t ldy, float* __restrict__ rstd, int64_t rows,
                                                           int width, float eps) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (row >= rows) return;
-  const Tx* xr = x + row * ldx;
-  float v[NV][V];
-  float ss = 0.f;
+  const int64_t row0 = ((int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5)) * R;
+  if (row0 >= rows) return;
+  float v[R][NV][V];
 #pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int c = (j * 32 + lane) * V;
-    if (c < width) {
-      load_vec<Tx, V>(xr + c, v[j]);
+  for (int r = 0; r < R; ++r) {
+    const int64_t row = row0 + r;
 #pragma unroll
-      for (int e = 0; e < V; ++e) ss += v[j][e] * v[j][e];
+    for (int j = 0; j < NV; ++j) {
+      const int c = (j * 32 + lane) * V;
+      if (row < rows && c < width) load_vec<Tx, V>(x + row * ldx + c, v[r][j]);
     }
   }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)width + eps);
-  if (rstd && lane == 0) rstd[row] = r;
-  Ty* yr = y + row * ldy;
 #pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int c = (j * 32 + lane) * V;
-    if (c < width) {
-      float wv[V], o[V];
-      load_vec<float, V>(w + c, wv);
+  for (int r = 0; r < R; ++r) {
+    const int64_t row = row0 + r;
+    if (row >= rows) break;
+    float ss = 0.f;
 #pragma unroll
-      for (int e = 0; e < V; ++e) o[e] = (v[j][e] * r) * wv[e];
-      store_vec<Ty, V>(yr + c, o);
+    for (int j = 0; j < NV; ++j) {
+      const int c = (j * 32 + lane) * V;
+      if (c < width) {
+#pragma unroll
+        for (int e = 0; e < V; ++e) ss += v[r][j][e] * v[r][j][e];
+      }
+    }
+    ss = warp_sum(ss);
+    const float rs = rsqrtf(ss / (float)width + eps);
+    if (rstd && lane == 0) rstd[row] = rs;
+    Ty* yr = y + row * ldy;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = (j * 32 + lane) * V;
+      if (c < width) {
+        float wv[V], o[V];
+        load_vec<float, V>(w + c, wv);
+#pragma unroll
+        for (int e = 0; e < V; ++e) o[e] = (v[r][j][e] * rs) * wv[e];
+        store_vec<Ty, V>(yr + c, o);
+      }
     }
   }
 }
@@ -61,6 +77,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const Tx* __restrict__
                                                           const float* __restrict__ rstd, const Tg* __restrict__ dy,
                                                           int64_t lddy, Tdx* __restrict__ dx, int64_t lddx,
                                                           float* __restrict__ partial, int64_t rows, int width) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   extern __shared__ float red[];  // [8][width]
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
@@ -74,33 +91,50 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const Tx* __restrict__
     for (int e = 0; e < V; ++e) acc[j][e] = 0.f;
     if (c < width) load_vec<float, V>(w + c, wv[j]);
   }
-  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < rows; row += stride) {
-    const float r = __ldg(rstd + row);
-    float xv[NV][V], gv[NV][V];
-    float dot = 0.f;
+  // two rows per iteration (rows `row` and `row + stride`), all loads first
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < rows; row += 2 * stride) {
+    float xv[2][NV][V], gv[2][NV][V], rr[2];
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int c = (j * 32 + lane) * V;
-      if (c < width) {
-        load_vec<Tx, V>(x + row * ldx + c, xv[j]);
-        load_vec<Tg, V>(dy + row * lddy + c, gv[j]);
+    for (int h = 0; h < 2; ++h) {
+      const int64_t rw = row + h * stride;
+      rr[h] = rw < rows ? __ldg(rstd + rw) : 0.f;
 #pragma unroll
-        for (int e = 0; e < V; ++e) {
-          dot += (gv[j][e] * wv[j][e]) * xv[j][e];
-          acc[j][e] += gv[j][e] * (xv[j][e] * r);
+      for (int j = 0; j < NV; ++j) {
+        const int c = (j * 32 + lane) * V;
+        if (rw < rows && c < width) {
+          load_vec<Tx, V>(x + rw * ldx + c, xv[h][j]);
+          load_vec<Tg, V>(dy + rw * lddy + c, gv[h][j]);
         }
       }
     }
-    dot = warp_sum(dot);
-    const float corr = dot / (float)width * r * r;
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int c = (j * 32 + lane) * V;
-      if (c < width) {
-        float o[V];
+    for (int h = 0; h < 2; ++h) {
+      const int64_t rw = row + h * stride;
+      if (rw >= rows) break;
+      const float r = rr[h];
+      float dot = 0.f;
 #pragma unroll
-        for (int e = 0; e < V; ++e) o[e] = (gv[j][e] * wv[j][e] - xv[j][e] * corr) * r;
-        store_vec<Tdx, V>(dx + row * lddx + c, o);
+      for (int j = 0; j < NV; ++j) {
+        const int c = (j * 32 + lane) * V;
+        if (c < width) {
+#pragma unroll
+          for (int e = 0; e < V; ++e) {
+            dot += (gv[h][j][e] * wv[j][e]) * xv[h][j][e];
+            acc[j][e] += gv[h][j][e] * (xv[h][j][e] * r);
+          }
+        }
+      }
+      dot = warp_sum(dot);
+      const float corr = dot / (float)width * r * r;
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        const int c = (j * 32 + lane) * V;
+        if (c < width) {
+          float o[V];
+#pragma unroll
+          for (int e = 0; e < V; ++e) o[e] = (gv[h][j][e] * wv[j][e] - xv[h][j][e] * corr) * r;
+          store_vec<Tdx, V>(dx + rw * lddx + c, o);
+        }
       }
     }
   }
@@ -122,28 +156,29 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_kernel(const Tx* __restrict__
   }
 }
 
-// dw[c] (+)= sum over parts. A CTA owns 32 columns; thread (g, c) sums parts
-// g, g+8, g+16, ... of column c (coalesced 128-byte rows), then the 8 group
-// sums are added in group order: a fixed order, so dw is deterministic.
-__global__ void __launch_bounds__(256) rmsnorm_dw_reduce_kernel(const float* __restrict__ partial,
-                                                                float* __restrict__ dw, int parts, int width,
-                                                                int accumulate) {
-  __shared__ float grp[8][32];
+// dw[c] (+)= sum over parts. A CTA owns 32 columns; thread (g, c) of its 32
+// groups sums parts g, g+32, ... of column c (coalesced 128-byte rows), then
+// the 32 group sums are added in group order: a fixed order, so dw is
+// deterministic.
+__global__ void __launch_bounds__(1024) rmsnorm_dw_reduce_kernel(const float* __restrict__ partial,
+                                                                 float* __restrict__ dw, int parts, int width,
+                                                                 int accumulate) {
+  pdl_wait();  // inputs are the previous kernel's outputs
+  __shared__ float grp[32][33];
   const int lc = threadIdx.x & 31, g = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lc;
   float s = 0.f;
   if (c < width)
-    for (int p = g; p < parts; p += 8) s += partial[(int64_t)p * width + c];
+    for (int p = g; p < parts; p += 32) s += partial[(int64_t)p * width + c];
   grp[g][lc] = s;
   __syncthreads();
   if (g == 0 && c < width) {
     float t = 0.f;
 #pragma unroll
-    for (int k = 0; k < 8; ++k) t += grp[k][lc];
+    for (int k = 0; k < 32; ++k) t += grp[k][lc];
     dw[c] = accumulate ? dw[c] + t : t;
   }
 }
-
 
 // ---------------------------------------------------------------- fused variants
 // Residual add + RMSNorm: s = x + a (fp32), y = rmsnorm(s) * w. `a` is the
@@ -154,6 +189,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_fwd_kernel(const float* __res
                                                               const float* __restrict__ w, Ty* __restrict__ y,
                                                               float* __restrict__ sum_out, float* __restrict__ rstd,
                                                               int64_t rows, int width, float eps) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   constexpr int V = 4;
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
@@ -203,6 +239,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ rstd, const Tg* __restrict__ dy,
     const float* __restrict__ residual, const Tlp* __restrict__ lp_add, float* __restrict__ dx_out,
     Tlp* __restrict__ lp_out, float* __restrict__ partial, int64_t rows, int width) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   constexpr int V = 4;
   extern __shared__ float red[];  // [8][width]
   const int lane = threadIdx.x & 31;
@@ -297,7 +334,7 @@ bool vec_fits(const void* p, int64_t ld, int V) {
 
 int rms_parts(int64_t rows) {
   int64_t warps_rows = (rows + 7) / 8;
-  return (int)(warps_rows < 592 ? (warps_rows > 0 ? warps_rows : 1) : 592);
+  return (int)(warps_rows < 296 ? (warps_rows > 0 ? warps_rows : 1) : 296);
 }
 
 template <typename Tx, typename Ty, int V>
@@ -308,7 +345,8 @@ int fwd_nv(const void* x, int64_t ldx, const float* w, void* y, int64_t ldy, flo
   dim3 grid((unsigned)((rows + 7) / 8)), block(256);
   auto X = static_cast<const Tx*>(x);
   auto Y = static_cast<Ty*>(y);
-#define RK_FWD(N) rmsnorm_fwd_kernel<Tx, Ty, V, N><<<grid, block, 0, s>>>(X, ldx, w, Y, ldy, rstd, rows, width, eps)
+#define RK_FWD(N) \
+  rk_host::launch_k(rmsnorm_fwd_kernel<Tx, Ty, V, N, 1>, grid, block, 0, s, X, ldx, w, Y, ldy, rstd, rows, width, eps)
   if (nv <= 1) RK_FWD(1);
   else if (nv <= 2) RK_FWD(2);
   else if (nv <= 4) RK_FWD(4);
@@ -345,7 +383,7 @@ int bwd_nv(const void* x, int64_t ldx, const float* w, const float* rstd, const 
   do {                                                                                                     \
     auto k = rmsnorm_bwd_kernel<Tx, Tg, Tdx, V, N>;                                                        \
     if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)smem);         \
-    k<<<grid, block, smem, s>>>(X, ldx, w, rstd, G, lddy, D, lddx, partial, rows, width);                  \
+    rk_host::launch_k(k, grid, block, smem, s, X, ldx, w, rstd, G, lddy, D, lddx, partial, rows, width);                  \
   } while (0)
   if (nv <= 1) RK_BWD(1);
   else if (nv <= 2) RK_BWD(2);
@@ -422,7 +460,7 @@ extern "C" int rk_rmsnorm_bwd(const void* x, int x_dtype, int64_t ldx, const flo
   else
     return RK_ERR_DTYPE;
   if (st != RK_OK) return st;
-  rmsnorm_dw_reduce_kernel<<<(W + 31) / 32, 256, 0, s>>>(dw_partial, dw, parts, W, accumulate_dw);
+  rk_host::launch_k(rmsnorm_dw_reduce_kernel, (W + 31) / 32, 1024, 0, s, dw_partial, dw, parts, W, accumulate_dw);
   return rk_host::launch_status();
 }
 
@@ -436,7 +474,7 @@ int add_fwd_typed(const float* x, const void* a, const float* w, void* y, float*
   dim3 grid((unsigned)((rows + 7) / 8));
   auto A = static_cast<const Ta*>(a);
   auto Y = static_cast<Ty*>(y);
-#define RK_AF(N) add_rmsnorm_fwd_kernel<Ta, Ty, N><<<grid, 256, 0, s>>>(x, A, w, Y, sum_out, rstd, rows, width, eps)
+#define RK_AF(N) rk_host::launch_k(add_rmsnorm_fwd_kernel<Ta, Ty, N>, grid, 256, 0, s, x, A, w, Y, sum_out, rstd, rows, width, eps)
   if (nv <= 1) RK_AF(1);
   else if (nv <= 2) RK_AF(2);
   else if (nv <= 4) RK_AF(4);
@@ -459,7 +497,7 @@ int bwd_fused_nv(const float* x, const float* w, const float* rstd, const void* 
   do {                                                                                                      \
     auto k = rmsnorm_bwd_fused_kernel<Tg, Tlp, N, RES, LP>;                                                 \
     if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)smem);          \
-    k<<<parts, 256, smem, s>>>(x, w, rstd, G, residual, LA, dx_out, LO, partial, rows, width);              \
+    rk_host::launch_k(k, parts, 256, smem, s, x, w, rstd, G, residual, LA, dx_out, LO, partial, rows, width);              \
   } while (0)
   if (nv <= 1) RK_BF(1);
   else if (nv <= 2) RK_BF(2);
@@ -537,7 +575,7 @@ extern "C" int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float*
   else
     return RK_ERR_DTYPE;
   if (st != RK_OK) return st;
-  rmsnorm_dw_reduce_kernel<<<(W + 31) / 32, 256, 0, s>>>(dw_partial, dw, parts, W, accumulate_dw);
+  rk_host::launch_k(rmsnorm_dw_reduce_kernel, (W + 31) / 32, 1024, 0, s, dw_partial, dw, parts, W, accumulate_dw);
   return rk_host::launch_status();
 }
 
@@ -550,9 +588,10 @@ extern "C" int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float*
 // memory, or code issuing work while a CUDA graph is being captured, where a
 // cudaMalloc would either be forbidden or synchronise the device. For them the
 // weight-gradient partials live in this file-scope device array instead, sized
-// for the largest request the kernel accepts: 592 partial rows (the fixed CTA
-// count of the backward) x 1024 columns of fp32 = 2,424,832 bytes, held by
-// every GPU that loads the library until the process exits.
+// for the largest request the kernel accepts: up to 592 partial rows (the
+// backward uses one per CTA, at most 296 today) x 1024 columns of fp32 =
+// 2,424,832 bytes, held by every GPU that loads the library until the process
+// exits.
 namespace {
 constexpr int64_t kNoallocMaxWidth = 1024;
 constexpr int64_t kNoallocScratchFloats = 592 * kNoallocMaxWidth;

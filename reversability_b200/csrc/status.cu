@@ -1,5 +1,6 @@
 // Library-wide device status word and ABI bookkeeping entry points.
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 #include "common.cuh"
@@ -14,6 +15,14 @@ std::atomic<unsigned long long> g_launches{0};
 
 namespace rk_host {
 void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("REVK_PDL");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 // The address is looked up once per device (with that device current) and cached.
 unsigned int* device_status_ptr() {

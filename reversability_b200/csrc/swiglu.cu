@@ -21,6 +21,7 @@ __device__ __forceinline__ float silu_fwd(float g) {
 template <typename T, int V>
 __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const T* __restrict__ u, T* __restrict__ h, int64_t rows,
                                                          int64_t width) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   const int64_t vecs_per_row = width / V;
   const int64_t total = rows * vecs_per_row;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
@@ -39,6 +40,7 @@ __global__ void __launch_bounds__(256) swiglu_fwd_kernel(const T* __restrict__ u
 template <typename T, int V>
 __global__ void __launch_bounds__(256) swiglu_bwd_kernel(const T* __restrict__ u, const T* __restrict__ dh,
                                                          T* __restrict__ du, int64_t rows, int64_t width) {
+  pdl_wait();  // inputs are the previous kernel's outputs
   const int64_t vecs_per_row = width / V;
   const int64_t total = rows * vecs_per_row;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
@@ -83,9 +85,9 @@ int fwd_typed(const void* u, void* h, int64_t rows, int64_t width, cudaStream_t 
   auto U = static_cast<const T*>(u);
   auto H = static_cast<T*>(h);
   if (width % V == 0 && rk_host::aligned(u, 16) && rk_host::aligned(h, 16))
-    swiglu_fwd_kernel<T, V><<<grid_for(rows * width / V), 256, 0, s>>>(U, H, rows, width);
+    rk_host::launch_k(swiglu_fwd_kernel<T, V>, grid_for(rows * width / V), 256, 0, s, U, H, rows, width);
   else
-    swiglu_fwd_kernel<T, 1><<<grid_for(rows * width), 256, 0, s>>>(U, H, rows, width);
+    rk_host::launch_k(swiglu_fwd_kernel<T, 1>, grid_for(rows * width), 256, 0, s, U, H, rows, width);
   return rk_host::launch_status();
 }
 
@@ -96,9 +98,9 @@ int bwd_typed(const void* u, const void* dh, void* du, int64_t rows, int64_t wid
   auto G = static_cast<const T*>(dh);
   auto D = static_cast<T*>(du);
   if (width % V == 0 && rk_host::aligned(u, 16) && rk_host::aligned(dh, 16) && rk_host::aligned(du, 16))
-    swiglu_bwd_kernel<T, V><<<grid_for(rows * width / V), 256, 0, s>>>(U, G, D, rows, width);
+    rk_host::launch_k(swiglu_bwd_kernel<T, V>, grid_for(rows * width / V), 256, 0, s, U, G, D, rows, width);
   else
-    swiglu_bwd_kernel<T, 1><<<grid_for(rows * width), 256, 0, s>>>(U, G, D, rows, width);
+    rk_host::launch_k(swiglu_bwd_kernel<T, 1>, grid_for(rows * width), 256, 0, s, U, G, D, rows, width);
   return rk_host::launch_status();
 }
 

@@ -214,6 +214,42 @@ RK_API int rk_cross_entropy_fwd_bwd(const void* logits, int64_t ld, int64_t voca
                                     int64_t rows, float grad_scale, const float* grad_scale_dev, float* loss_rows,
                                     void* dlogits, int64_t ldd, int dtype, int ignore_index, void* stream);
 
+/* ------------------------------------------------ Softmax head (fused CE)
+ * The vocabulary head and its cross-entropy with no pass of their own over the
+ * logits; together they replace the head Linear, F.cross_entropy(...,
+ * reduction="sum") and their backward (model.py:104, train_baseline.py:262,
+ * optimized_v3.py cached_head_backward). Blocks b are 128 columns wide.
+ *   rk_head_fprop : expo[M, V] = exp(x - m_b) (bf16/f16) where x = hidden . W^T
+ *                   rounded to the compute type and m_b the max of x over the
+ *                   row's block b; stats[M][width] float2 = (m_b, sum of exp)
+ *                   with width = rk_head_stats_width(V); xlabel[r] = x at the
+ *                   row's label (rows whose label is in [0, V));
+ *   rk_head_loss  : loss_rows[r] = lse - x[label] (0 for ignore_index),
+ *                   rowc[r] float4 = (-lse*log2(e), s, (exp(x[label]-lse)-1)*s, 0)
+ *                   with s = grad_scale * (*grad_scale_dev), and the per-block
+ *                   factors fcoef[b * fcoef_ld + r] = exp(m_b - lse) * s
+ *                   ([width][fcoef_ld >= rows] floats); all 0 for ignored rows;
+ *                   a label outside [0, V) sets RK_DEV_CE_LABEL and the row is
+ *                   ignored;
+ *   rk_head_dgrad : dhidden[M, K] = dlogits . W, and
+ *   rk_head_wgrad : dW[V, K] (+)= dlogits^T . hidden, where
+ *                   dlogits = (softmax(x) - onehot(label)) * s is formed inside
+ *                   the GEMM as expo * fcoef, the label entry taken from rowc
+ *                   (never written to global memory). */
+RK_API int64_t rk_head_stats_width(int64_t vocab);
+RK_API int rk_head_fprop(const void* hidden, int64_t ldh, const void* w, int64_t ldw, const int64_t* labels,
+                         void* expo, int64_t lde, float* stats, float* xlabel, int64_t M, int64_t V, int64_t K,
+                         int dtype, void* stream);
+RK_API int rk_head_loss(const float* stats, int64_t width, const float* xlabel, const int64_t* labels, int64_t rows,
+                        int64_t V, float grad_scale, const float* grad_scale_dev, float* loss_rows, float* rowc,
+                        float* fcoef, int64_t fcoef_ld, int ignore_index, void* stream);
+RK_API int rk_head_dgrad(const void* expo, int64_t lde, const float* fcoef, int64_t fcoef_ld, const float* rowc,
+                         const int64_t* labels, const void* w, int64_t ldw, void* dx, int64_t lddx, int64_t M,
+                         int64_t V, int64_t K, int dtype, int out_dtype, void* stream);
+RK_API int rk_head_wgrad(const void* expo, int64_t lde, const float* fcoef, int64_t fcoef_ld, const float* rowc,
+                         const int64_t* labels, const void* x, int64_t ldx, float* dw, int64_t lddw, int64_t M,
+                         int64_t V, int64_t K, int dtype, int accumulate, void* stream);
+
 /* -------------------------------------------------------- Clip + AdamW
  * Replace torch.nn.utils.clip_grad_norm_(params, max_norm) and
  * torch.optim.AdamW(lr, betas, weight_decay).step() over the parameters of the

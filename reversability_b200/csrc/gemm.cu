@@ -7,8 +7,11 @@
 //   warp 1      : allocates 2*BN tensor-memory columns (two accumulators) and
 //                 issues tcgen05.mma (M=128, N=BN, K=16) from one thread;
 //                 tcgen05.commit frees smem stages and publishes accumulators.
-//   warps 2..5  : epilogue; warp w reads TMEM lanes 32*(w%4)..+31 (one output
-//                 row per thread) with tcgen05.ld and stores to global memory.
+//   warps 2..9  : epilogue; warp w reads TMEM lanes 32*(w%4)..+31 (one output
+//                 row per thread) of one column half of the tile ((w-2)/4)
+//                 with tcgen05.ld and stores to global memory. Two warps per
+//                 lane quarter (two per SM sub-partition) hide each other's
+//                 TMEM-load and store latency.
 // The accumulator is double buffered so the epilogue of tile i overlaps the
 // MMAs of tile i+1. Operands may be K-major or MN-major (the transposed views
 // that dgrad and wgrad need) without any transposition pass: TMA loads
@@ -26,6 +29,7 @@
 // so weight gradients are bitwise deterministic for a given shape.
 #include <cudaTypedefs.h>
 #include <cstdlib>
+#include <type_traits>
 #include <mutex>
 #include <unordered_map>
 #include "vec.cuh"
@@ -44,6 +48,16 @@ struct GemmArgs {
   int64_t ldo;
   int out_dtype;
   unsigned int* status;
+  // Softmax head (vocabulary logits; 128-column blocks b of a row):
+  float2* stats;          // EPI_LSE writes, XF reads: per (row, b) (m_b, sum of exp(x - m_b)), m_b = block max
+  int stats_ld;           // float2 entries per row (2 * ceil(V / 256))
+  const float4* rowc;     // XF: per token (-lse * log2(e), scale, label gradient, -); scale 0 = ignored row
+  const float* fcoef;     // XF: per (block b, token) exp(m_b - lse) * scale, block-major (fcoef_ld per block)
+  int64_t fcoef_ld;
+  const int64_t* labels;  // EPI_LSE / XF: per token label
+  float* xlabel;          // EPI_LSE: per token, the rounded logit at its label
+  int vocab;              // EPI_LSE / XF: valid vocabulary entries
+  int tokens;             // XF: valid token rows
 };
 
 // STORE: direct row stores; PARTIAL: fp32 split slices; ACCUM: fp32 out += acc;
@@ -55,27 +69,86 @@ struct GemmArgs {
 // tile holds W rows [n0, n0+128) (gate) and [ff+n0, ff+n0+128) (value), so the
 // accumulator has gate | value for the same 128 columns and the epilogue writes
 // h = round(silu(round(g))) * round(v) only; SWIGLU_SAVE also writes u itself.
-enum { EPI_STORE = 0, EPI_PARTIAL = 1, EPI_ACCUM = 2, EPI_TMA = 3, EPI_TMA_ADD = 4, EPI_SWIGLU = 5, EPI_SWIGLU_SAVE = 6 };
+// LSE (softmax head forward): per row and 128-column block b, the rounded
+// logits x give m_b = max x and e = exp(x - m_b); e is TMA-stored (16-bit)
+// instead of x, (m_b, sum e) goes to g.stats and the logit at the row's label
+// to g.xlabel. Columns at or past g.vocab do not count.
+enum {
+  EPI_STORE = 0, EPI_PARTIAL = 1, EPI_ACCUM = 2, EPI_TMA = 3, EPI_TMA_ADD = 4, EPI_SWIGLU = 5, EPI_SWIGLU_SAVE = 6,
+  EPI_LSE = 7
+};
+// A-operand transforms (XF): the A tile holds e = exp(x - m_b) from the LSE
+// epilogue and is turned, in shared memory before the MMA reads it, into the
+// cross-entropy gradient dlogit = e * exp(m_b - lse) * scale, with the label's
+// entry replaced by its exact (exp(x_label - lse) - 1) * scale.
+//   XF_ROWS : A is K-major [tokens, vocab] (head dgrad: dX = dlogits . W)
+//   XF_COLS : A is MN-major, i.e. dlogits^T [vocab, tokens] (head wgrad)
+enum { XF_NONE = 0, XF_ROWS = 1, XF_COLS = 2 };
 
 __host__ __device__ constexpr bool epi_is_swiglu(int e) { return e == EPI_SWIGLU || e == EPI_SWIGLU_SAVE; }
-__host__ __device__ constexpr bool epi_stages_out(int e) { return e == EPI_TMA || e == EPI_TMA_ADD || epi_is_swiglu(e); }
+__host__ __device__ constexpr bool epi_stages_out(int e) {
+  return e == EPI_TMA || e == EPI_TMA_ADD || e == EPI_LSE || epi_is_swiglu(e);
+}
+constexpr int kEpiWarps = 8;
+// Output staging: one 4 KB box (32 rows x 128 bytes) per epilogue warp, two for
+// SWIGLU_SAVE (h and the gate half of u; the value half reuses the first).
 __host__ __device__ constexpr uint32_t epi_out_bytes(int e) {
-  return e == EPI_SWIGLU_SAVE ? 4 * 3 * 4096 : (epi_stages_out(e) ? 4 * 2 * 4096 : 0);
+  return e == EPI_SWIGLU_SAVE ? kEpiWarps * 2 * 4096 : (epi_stages_out(e) ? kEpiWarps * 4096 : 0);
 }
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
-template <int BN, int STAGES, uint32_t OUT_BYTES = 0>
+// B-resident mode (RES): K <= kResK; the whole BN x K operand tile stays in
+// shared memory while the CTA walks consecutive M tiles of one N block, so a
+// tile streams only its 16 KB A k-blocks through the ring.
+constexpr int kResKb = 4;  // 64-wide k blocks held resident (K <= 256)
+
+template <int BN, int STAGES, uint32_t OUT_BYTES = 0, bool RES = false>
 struct TcSmem {
   static constexpr uint32_t kA = kBM * kBK * 2;  // 16 KB
   static constexpr uint32_t kB = BN * kBK * 2;
-  static constexpr uint32_t kStage = kA + kB;
-  // output staging: 4 epilogue warps x 2 (or 3) buffers x (32 rows x 128 bytes)
-  static constexpr uint32_t kOut = OUT_BYTES;
-  static constexpr uint32_t kBarriers = (2 * STAGES + 5) * 8;
-  static constexpr uint32_t kTotal = 1024 /*align slack*/ + STAGES * kStage + kOut + kBarriers + 16;
+  static constexpr uint32_t kStage = RES ? kA : kA + kB;
+  static constexpr uint32_t kBres = RES ? kResKb * kB : 0;
+  static constexpr uint32_t kOut = OUT_BYTES;  // epilogue staging (epi_out_bytes)
+  static constexpr uint32_t kBarriers = (3 * STAGES + 7) * 8;
+  static constexpr uint32_t kTotal = 1024 /*align slack*/ + STAGES * kStage + kBres + kOut + kBarriers + 16;
+};
+
+// Tile walk. Default: tile t = blockIdx.x + i * gridDim.x, N fastest, split
+// slices outermost. RES: CTA c owns the contiguous run [c*T/G, (c+1)*T/G) of
+// the M-fastest order, so consecutive tiles share the resident B block.
+template <bool RES>
+struct TileWalk {
+  int t, end, step;
+  __device__ TileWalk(int total) {
+    if (RES) {
+      t = (int)((int64_t)blockIdx.x * total / gridDim.x);
+      end = (int)((int64_t)(blockIdx.x + 1) * total / gridDim.x);
+      step = 1;
+    } else {
+      t = blockIdx.x;
+      end = total;
+      step = gridDim.x;
+    }
+  }
+  __device__ bool more() const { return t < end; }
+  __device__ void next() { t += step; }
+  // split slice, first output row, n-tile index of tile t
+  __device__ void coords(const GemmArgs& g, int tt, int& split, int& m0, int& nt) const {
+    if (RES) {
+      split = 0;
+      nt = tt / g.tiles_m;
+      m0 = (tt - nt * g.tiles_m) * kBM;
+    } else {
+      const int tiles_mn = g.tiles_m * g.tiles_n;
+      split = tt / tiles_mn;
+      const int mn = tt - split * tiles_mn;
+      m0 = (mn / g.tiles_n) * kBM;
+      nt = mn % g.tiles_n;
+    }
+  }
 };
 
 __device__ __forceinline__ void fence_proxy_async_smem() {
@@ -144,26 +217,122 @@ __device__ __forceinline__ void store_row_chunk(T* dst, const float (&v)[32], in
   }
 }
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, typename TOut>
+constexpr float kLog2eF = 1.4426950408889634f;
+
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Two floats rounded to a packed pair of 16-bit values (lo in bits 0..15), and back.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2_rn(float lo, float hi) {
+  uint32_t d;
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  else asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+template <typename T>
+__device__ __forceinline__ float unpack_half(uint32_t u, int which) {
+  const uint32_t b = which ? (u >> 16) : (u & 0xffffu);
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) return __uint_as_float(b << 16);
+  else return __half2float(__ushort_as_half((unsigned short)b));
+}
+
+// (m, s) += (m2, s2) for online log-sum-exp pairs (s = sum of exp(x - m)).
+__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
+  const float mn = fmaxf(m, m2);
+  if (mn == -INFINITY) return;
+  s = (m == -INFINITY ? 0.f : s * ex2_fast((m - mn) * kLog2eF)) +
+      (m2 == -INFINITY ? 0.f : s2 * ex2_fast((m2 - mn) * kLog2eF));
+  m = mn;
+}
+
+// One 16-byte chunk (8 entries of one token, vocabulary v0..v0+7) of an A
+// tile, in place: e * f, and the entry at `label` (if in the chunk) set to gl.
+template <typename T>
+__device__ __forceinline__ uint32_t scale_pair(uint32_t wd, float f) {
+  return pack2_rn<T>(unpack_half<T>(wd, 0) * f, unpack_half<T>(wd, 1) * f);
+}
+// bf16 pair times f, with f = f_hi + f_lo split into two bf16 values (both
+// halves of fhi2 / flo2): fma(e, f_hi, e * f_lo) rounds once, so the result is
+// e * f correctly rounded up to the negligible rounding of the e * f_lo term.
+__device__ __forceinline__ uint32_t bf16x2_scale(uint32_t e2, uint32_t fhi2, uint32_t flo2) {
+  uint32_t t, d;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(t) : "r"(e2), "r"(flo2));
+  asm("fma.rn.bf16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(e2), "r"(fhi2), "r"(t));
+  return d;
+}
+struct ChunkScale {
+  float f;
+  uint32_t fhi2, flo2;  // bf16: f split into high and low bf16 parts, both halves
+};
+template <typename T>
+__device__ __forceinline__ ChunkScale chunk_scale(float f) {
+  ChunkScale c;
+  c.f = f;
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+    const uint32_t hi = pack2_rn<T>(f, f);
+    const float fh = unpack_half<T>(hi, 0);
+    c.fhi2 = hi;
+    c.flo2 = pack2_rn<T>(f - fh, f - fh);
+  } else {
+    c.fhi2 = c.flo2 = 0u;
+  }
+  return c;
+}
+template <typename T>
+__device__ __forceinline__ uint32_t scale_word(uint32_t wd, const ChunkScale& c) {
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) return bf16x2_scale(wd, c.fhi2, c.flo2);
+  else return scale_pair<T>(wd, c.f);
+}
+template <typename T>
+__device__ __forceinline__ void softmax_grad_chunk(uint8_t* p, int v0, const ChunkScale& f, int64_t label, float gl) {
+  uint4 raw = *reinterpret_cast<const uint4*>(p);
+  raw.x = scale_word<T>(raw.x, f);
+  raw.y = scale_word<T>(raw.y, f);
+  raw.z = scale_word<T>(raw.z, f);
+  raw.w = scale_word<T>(raw.w, f);
+  const int64_t li = label - v0;
+  if (li >= 0 && li < 8) {
+    const uint32_t gp = pack2_rn<T>(gl, gl);
+    const uint32_t mask = (li & 1) ? 0xffff0000u : 0x0000ffffu;
+    const int qi = (int)(li >> 1);
+    raw.x = qi == 0 ? ((raw.x & ~mask) | (gp & mask)) : raw.x;
+    raw.y = qi == 1 ? ((raw.y & ~mask) | (gp & mask)) : raw.y;
+    raw.z = qi == 2 ? ((raw.z & ~mask) | (gp & mask)) : raw.z;
+    raw.w = qi == 3 ? ((raw.w & ~mask) | (gp & mask)) : raw.w;
+  }
+  *reinterpret_cast<uint4*>(p) = raw;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, typename TOut, bool RES = false, int XF = XF_NONE,
+          typename TIn = __nv_bfloat16>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                    const GemmArgs g, const uint32_t idesc) {
-  
-  using L = TcSmem<BN, STAGES, epi_out_bytes(EPI)>;
+  static_assert(!RES || !B_MN, "the resident B tile is K-major");
+  static_assert(XF == XF_NONE || (XF == XF_ROWS) == !A_MN, "XF_ROWS needs a K-major A, XF_COLS an MN-major A");
+  static_assert(XF == XF_NONE || (!RES && !epi_is_swiglu(EPI)), "transforms run on the plain schedule");
+  using L = TcSmem<BN, STAGES, epi_out_bytes(EPI), RES>;
   constexpr int NSTEP = epi_is_swiglu(EPI) ? BN / 2 : BN;  // output columns per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * L::kA;
-  uint8_t* sOut = smem + STAGES * L::kStage;  // EPI_TMA staging (1024-aligned)
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * L::kStage + L::kOut);
+  uint8_t* sB = smem + STAGES * L::kA;  // B ring (RES: the resident B block)
+  uint8_t* sOut = smem + STAGES * L::kStage + L::kBres;  // EPI_TMA staging (1024-aligned)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + L::kOut);
   const uint32_t full0 = smem_u32(bars);
   const uint32_t empty0 = full0 + STAGES * 8;
   const uint32_t tfull0 = empty0 + STAGES * 8;
   const uint32_t tempty0 = tfull0 + 2 * 8;
   const uint32_t drain = tempty0 + 2 * 8;
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 5);
+  const uint32_t bfull = drain + 8;    // RES: resident B block loaded
+  const uint32_t bempty = bfull + 8;   // RES: MMAs reading the resident B block done
+  const uint32_t xready0 = bempty + 8;  // XF: stage transformed (one arrival per epilogue warp)
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 7);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   volatile int* s_consumed = reinterpret_cast<volatile int*>(s_tmem + 2);
 
@@ -174,15 +343,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
+      mbar_init(xready0 + 8 * s, kEpiWarps);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
-      mbar_init(tempty0 + 8 * b, 128);
+      mbar_init(tempty0 + 8 * b, 32 * kEpiWarps);
     }
     mbar_init(drain, 1);
+    mbar_init(bfull, 1);
+    mbar_init(bempty, 1);
     fence_mbar_init();
     *s_abort = 0;
     *s_consumed = 0;
+    s_tmem[3] = 0;  // resident B loads consumed by the MMA warp
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
   }
@@ -198,23 +371,46 @@ __global__ void __launch_bounds__(kThreads, 1)
   // no global data, so it overlaps the previous kernel's tail.
   pdl_wait();
 
-  const int tiles_mn = g.tiles_m * g.tiles_n;
-  const int total = tiles_mn * g.splits;
+  const int total = g.tiles_m * g.tiles_n * g.splits;
   int issued = 0;
+  int b_issued = 0;  // RES: resident B loads issued (producer) / consumed (MMA)
+  volatile int* s_b_consumed = reinterpret_cast<volatile int*>(s_tmem + 3);
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      const int split = t / tiles_mn;
-      const int mn = t - split * tiles_mn;
-      const int m0 = (mn / g.tiles_n) * kBM;
-      const int n0 = (mn % g.tiles_n) * NSTEP;
+    int cur_nt = -1;
+    uint32_t bphase = 0;
+    for (TileWalk<RES> w(total); w.more() && ok; w.next()) {
+      int split, m0, nt;
+      w.coords(g, w.t, split, m0, nt);
+      const int n0 = nt * NSTEP;
       const int kb0 = split * g.kb_per_split;
       int kb1 = kb0 + g.kb_per_split;
       if (kb1 > g.kb_total) kb1 = g.kb_total;
+      if constexpr (RES) {
+        if (nt != cur_nt) {  // load the B block of this N tile once
+          if (!mbar_wait(bempty, bphase ^ 1, g.status, RK_DEV_GEMM_TIMEOUT, s_abort)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(bfull, (uint32_t)(kb1 - kb0) * L::kB);
+          for (int kb = kb0; kb < kb1; ++kb) {
+            const uint32_t b_dst = smem_u32(sB + (kb - kb0) * L::kB);
+            if constexpr (epi_is_swiglu(EPI)) {
+              tma_load_2d(b_dst, &tmB, bfull, kb * kBK, n0);
+              tma_load_2d(b_dst + (BN / 2) * 128, &tmB, bfull, kb * kBK, g.ff + n0);
+            } else {
+              tma_load_2d(b_dst, &tmB, bfull, kb * kBK, n0);
+            }
+          }
+          ++b_issued;
+          bphase ^= 1;
+          cur_nt = nt;
+        }
+      }
       for (int kb = kb0; kb < kb1; ++kb) {
         if (!mbar_wait(empty0 + 8 * stage, phase ^ 1, g.status, RK_DEV_GEMM_TIMEOUT, s_abort)) {
           ok = false;
@@ -223,7 +419,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t fb = full0 + 8 * stage;
         mbar_arrive_expect_tx(fb, L::kStage);
         const uint32_t a_dst = smem_u32(sA + stage * L::kA);
-        const uint32_t b_dst = smem_u32(sB + stage * L::kB);
         const int k0 = kb * kBK;
         if constexpr (A_MN) {
           tma_load_2d(a_dst, &tmA, fb, m0, k0);
@@ -231,14 +426,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           tma_load_2d(a_dst, &tmA, fb, k0, m0);
         }
-        if constexpr (epi_is_swiglu(EPI)) {  // gate rows, then the matching value rows
-          tma_load_2d(b_dst, &tmB, fb, k0, n0);
-          tma_load_2d(b_dst + (BN / 2) * 128, &tmB, fb, k0, g.ff + n0);
-        } else if constexpr (B_MN) {
+        if constexpr (!RES) {
+          const uint32_t b_dst = smem_u32(sB + stage * L::kB);
+          if constexpr (epi_is_swiglu(EPI)) {  // gate rows, then the matching value rows
+            tma_load_2d(b_dst, &tmB, fb, k0, n0);
+            tma_load_2d(b_dst + (BN / 2) * 128, &tmB, fb, k0, g.ff + n0);
+          } else if constexpr (B_MN) {
 #pragma unroll
-          for (int c = 0; c < BN / 64; ++c) tma_load_2d(b_dst + c * 8192, &tmB, fb, n0 + 64 * c, k0);
-        } else {
-          tma_load_2d(b_dst, &tmB, fb, k0, n0);
+            for (int c = 0; c < BN / 64; ++c) tma_load_2d(b_dst + c * 8192, &tmB, fb, n0 + 64 * c, k0);
+          } else {
+            tma_load_2d(b_dst, &tmB, fb, k0, n0);
+          }
         }
         ++issued;
         if (++stage == STAGES) {
@@ -254,13 +452,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     int consumed = 0;
+    int b_consumed = 0;
     bool ok = true;
     bool pending = false;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-      const int split = t / tiles_mn;
+    int cur_nt = -1;
+    uint32_t bphase = 0;
+    for (TileWalk<RES> w(total); w.more() && ok; w.next()) {
+      int split, m0, nt;
+      w.coords(g, w.t, split, m0, nt);
       const int kb0 = split * g.kb_per_split;
       int kb1 = kb0 + g.kb_per_split;
       if (kb1 > g.kb_total) kb1 = g.kb_total;
+      if constexpr (RES) {
+        if (nt != cur_nt) {
+          if (!mbar_wait(bfull, bphase, g.status, RK_DEV_GEMM_TIMEOUT, s_abort)) {
+            ok = false;
+            break;
+          }
+          ++b_consumed;
+          bphase ^= 1;
+          cur_nt = nt;
+        }
+      }
       if (!mbar_wait(tempty0 + 8 * acc, acc_phase ^ 1, g.status, RK_DEV_GEMM_TIMEOUT, s_abort)) {
         ok = false;
         break;
@@ -268,14 +481,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * BN;
       for (int kb = kb0; kb < kb1; ++kb) {
-        if (!mbar_wait(full0 + 8 * stage, phase, g.status, RK_DEV_GEMM_TIMEOUT, s_abort)) {
+        const uint32_t ready = XF != XF_NONE ? xready0 + 8 * stage : full0 + 8 * stage;
+        if (!mbar_wait(ready, phase, g.status, RK_DEV_GEMM_TIMEOUT, s_abort)) {
           ok = false;
           break;
         }
         ++consumed;
         tc_fence_after();
         const uint32_t a_base = smem_u32(sA + stage * L::kA);
-        const uint32_t b_base = smem_u32(sB + stage * L::kB);
+        const uint32_t b_base = RES ? smem_u32(sB + (kb - kb0) * L::kB) : smem_u32(sB + stage * L::kB);
 #pragma unroll
         for (int j = 0; j < kBK / 16; ++j) {
           const uint64_t ad = A_MN ? smem_desc_sw128(a_base + j * 2048, 8192, 1024)
@@ -293,12 +507,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) break;
       umma_commit(tfull0 + 8 * acc);
+      if constexpr (RES) {
+        // last tile of this N block: the resident B block may be overwritten
+        // once these MMAs complete
+        if (w.t + 1 < w.end) {
+          int s2, m2, nt2;
+          w.coords(g, w.t + 1, s2, m2, nt2);
+          if (nt2 != nt) umma_commit(bempty);
+        }
+      }
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
       }
     }
     *s_consumed = consumed;
+    *s_b_consumed = b_consumed;
     if (!ok && pending) {
       // Let every MMA already issued finish before tensor memory is released.
       umma_commit(drain);
@@ -306,87 +530,286 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
-    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int quarter = warp & 3;      // TMEM lane quarter this warp may access
+    const int ew = warp - 2;           // epilogue warp 0..kEpiWarps-1
+    const int half = ew / 4;           // column half of the tile this warp stores
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      const int split = t / tiles_mn;
-      const int mn = t - split * tiles_mn;
-      const int m0 = (mn / g.tiles_n) * kBM;
-      const int n0 = (mn % g.tiles_n) * NSTEP;
+    int xstage = 0;                    // XF: ring position, in step with the producer
+    uint32_t xphase = 0;
+    for (TileWalk<RES> w(total); w.more(); w.next()) {
+      int split, m0, nt;
+      w.coords(g, w.t, split, m0, nt);
+      const int n0 = nt * NSTEP;
+      if constexpr (XF != XF_NONE) {
+        // Transform every A stage of this tile as it lands. Thread layout: two
+        // threads per 128-byte smem row (four 16-byte chunks each); the chunk
+        // order is rotated by the row so a warp's accesses spread over all banks.
+        const int tid = threadIdx.x - 64;  // 0..255
+        const int hrow = tid & 1;
+        const int srow = tid >> 1;         // XF_ROWS: token row of the tile; XF_COLS: (box, token) pair
+        const int kb0 = split * g.kb_per_split;
+        int kb1 = kb0 + g.kb_per_split;
+        if (kb1 > g.kb_total) kb1 = g.kb_total;
+        // Per k block each thread needs, for its token: f = exp(m_b - lse) * scale
+        // of the k block's vocabulary block b (block-major, so a warp's loads
+        // are contiguous), the label and the label's gradient. The loads run
+        // four k blocks ahead of their use.
+        struct Coef {
+          float f, gl;
+          int64_t lab;
+        };
+        // XF_ROWS: the token, its label and label gradient are fixed for the tile
+        float row_gl = 0.f;
+        int64_t row_lab = -1;
+        if constexpr (XF == XF_ROWS) {
+          if (m0 + srow < g.tokens) {
+            row_gl = __ldg(&g.rowc[m0 + srow].z);
+            row_lab = __ldg(g.labels + m0 + srow);
+          }
+        }
+        auto fetch = [&](int kb) {
+          Coef c;
+          const int token = XF == XF_ROWS ? m0 + srow : kb * kBK + (srow & 63);
+          const int blk = XF == XF_ROWS ? (kb * kBK) >> 7 : m0 >> 7;
+          if (kb < kb1 && token < g.tokens) {
+            c.f = __ldg(g.fcoef + (int64_t)blk * g.fcoef_ld + token);
+            if constexpr (XF == XF_ROWS) {
+              c.gl = row_gl;
+              c.lab = row_lab;
+            } else {
+              c.gl = __ldg(&g.rowc[token].z);
+              c.lab = __ldg(g.labels + token);
+            }
+          } else {
+            c.f = 0.f;
+            c.gl = 0.f;
+            c.lab = -1;
+          }
+          return c;
+        };
+        auto step = [&](int kb, const Coef& c) -> bool {
+          const ChunkScale cs = chunk_scale<TIn>(c.f);
+          bool sok = mbar_wait(full0 + 8 * xstage, xphase, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
+          sok = __all_sync(0xffffffffu, sok);
+          if (!sok) return false;
+          uint8_t* tile = sA + xstage * L::kA;
+          if constexpr (XF == XF_ROWS) {
+            uint8_t* rowp = tile + srow * 128;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int pc = (hrow * 4 + q + srow) & 7;
+              const int j = pc ^ (srow & 7);
+              softmax_grad_chunk<TIn>(rowp + pc * 16, kb * kBK + j * 8, cs, c.lab, c.gl);
+            }
+          } else {
+            const int box = srow >> 6, k = srow & 63;
+            uint8_t* rowp = tile + box * 8192 + k * 128;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              const int pc = (hrow * 4 + q + k) & 7;
+              const int j = pc ^ (k & 7);
+              softmax_grad_chunk<TIn>(rowp + pc * 16, m0 + box * 64 + j * 8, cs, c.lab, c.gl);
+            }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(xready0 + 8 * xstage);
+          if (++xstage == STAGES) {
+            xstage = 0;
+            xphase ^= 1;
+          }
+          return true;
+        };
+        // four coefficient sets in flight, each reloaded right after its use
+        // (no register copies that would wait on an outstanding load)
+        Coef c0 = fetch(kb0), c1 = fetch(kb0 + 1), c2 = fetch(kb0 + 2), c3 = fetch(kb0 + 3);
+        bool xok = true;
+        for (int kb = kb0; kb < kb1 && xok; kb += 4) {
+          xok = step(kb, c0);
+          c0 = fetch(kb + 4);
+          if (xok && kb + 1 < kb1) {
+            xok = step(kb + 1, c1);
+            c1 = fetch(kb + 5);
+          }
+          if (xok && kb + 2 < kb1) {
+            xok = step(kb + 2, c2);
+            c2 = fetch(kb + 6);
+          }
+          if (xok && kb + 3 < kb1) {
+            xok = step(kb + 3, c3);
+            c3 = fetch(kb + 7);
+          }
+        }
+        if (!xok) break;
+      }
       bool ok = mbar_wait(tfull0 + 8 * acc, acc_phase, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
       if constexpr (epi_is_swiglu(EPI)) {
-        // h = round(silu(round(g))) * round(v) for the tile's 128 columns, 64 at a
-        // time; the same operation order as rk_swiglu_fwd on a bf16 u.
-        uint8_t* stage = sOut + (warp - 2) * (EPI == EPI_SWIGLU_SAVE ? 12288 : 8192);
+        // h = round(silu(round(g))) * round(v) for this warp's 64 of the tile's
+        // 128 columns; the same operation order as rk_swiglu_fwd on a bf16 u.
+        static_assert(BN == 256, "the SwiGLU epilogue pairs 128 gate and 128 value columns");
+        uint8_t* stage = sOut + ew * (EPI == EPI_SWIGLU_SAVE ? 8192 : 4096);
         const int y = m0 + quarter * 32;
-#pragma unroll 1
-        for (int c = 0; c < BN / 2; c += 64) {
-          float gv[64], vv[64];
+        const int c = half * 64;
+        uint8_t* hb = stage;
+        uint8_t* gb = stage + 4096;
+        if (lane == 0) bulk_wait_read<0>();  // this warp's boxes from the previous tile are free
+        __syncwarp();
+        uint32_t vkeep[EPI == EPI_SWIGLU_SAVE ? 32 : 1];  // packed value half, stored after h
+        // two passes of 32 columns: gate and value chunks, then 4 of the 8
+        // 16-byte chunks of each staged row. Conversions are packed (one per
+        // two values); the arithmetic is per value as in rk_swiglu_fwd.
 #pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            float part[32];
-            tmem_ld_32cols(t_row + c + q * 32, part);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) gv[q * 32 + j] = round_to<TOut>(part[j]);
-            tmem_ld_32cols(t_row + BN / 2 + c + q * 32, part);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) vv[q * 32 + j] = round_to<TOut>(part[j]);
+        for (int q = 0; q < 2; ++q) {
+          uint32_t rg[32], rv[32];
+          tmem_ld_32cols_nowait(t_row + c + q * 32, rg);
+          tmem_ld_32cols_nowait(t_row + BN / 2 + c + q * 32, rv);
+          tmem_ld_wait();
+          if (q == 1) {  // TMEM is read: the MMA warp may reuse this accumulator
+            tc_fence_before();
+            mbar_arrive(tempty0 + 8 * acc);
           }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint32_t hw[4], gw[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const int i = j * 8 + 2 * k;
+              gw[k] = pack2_rn<TOut>(__uint_as_float(rg[i]), __uint_as_float(rg[i + 1]));
+              const uint32_t vw = pack2_rn<TOut>(__uint_as_float(rv[i]), __uint_as_float(rv[i + 1]));
+              const float g0 = unpack_half<TOut>(gw[k], 0), g1 = unpack_half<TOut>(gw[k], 1);
+              const uint32_t sw = pack2_rn<TOut>(silu_value(g0), silu_value(g1));
+              hw[k] = pack2_rn<TOut>(__fmul_rn(unpack_half<TOut>(sw, 0), unpack_half<TOut>(vw, 0)),
+                                     __fmul_rn(unpack_half<TOut>(sw, 1), unpack_half<TOut>(vw, 1)));
+              if constexpr (EPI == EPI_SWIGLU_SAVE) vkeep[q * 16 + j * 4 + k] = vw;
+            }
+            const int off = lane * 128 + (((q * 4 + j) ^ (lane & 7)) * 16);
+            *reinterpret_cast<uint4*>(hb + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            if constexpr (EPI == EPI_SWIGLU_SAVE)
+              *reinterpret_cast<uint4*>(gb + off) = make_uint4(gw[0], gw[1], gw[2], gw[3]);
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmC, smem_u32(hb), n0 + c, y);
+          bulk_commit();
           if constexpr (EPI == EPI_SWIGLU_SAVE) {
-            if (lane == 0) bulk_wait_read<0>();
-          } else {
-            if (lane == 0) bulk_wait_read<1>();
+            tma_store_2d(&tmD, smem_u32(gb), n0 + c, y);
+            bulk_commit();
+            bulk_wait_read<1>();  // the h box has been read: reuse it for the value half
           }
+        }
+        if constexpr (EPI == EPI_SWIGLU_SAVE) {
           __syncwarp();
-          uint8_t* hb = EPI == EPI_SWIGLU_SAVE ? stage : stage + ((c / 64) & 1) * 4096;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            uint4 raw;
-            TOut* e = reinterpret_cast<TOut*>(&raw);
-#pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const float gg = gv[j * 8 + k];
-              const float silu = round_to<TOut>(silu_value(gg));
-              e[k] = Dt<TOut>::from_f(__fmul_rn(silu, vv[j * 8 + k]));
-            }
-            *reinterpret_cast<uint4*>(hb + lane * 128 + ((j ^ (lane & 7)) * 16)) = raw;
-          }
-          if constexpr (EPI == EPI_SWIGLU_SAVE) {
-            uint8_t* gb = stage + 4096;
-            uint8_t* vb = stage + 8192;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              uint4 rg, rv;
-              TOut* eg = reinterpret_cast<TOut*>(&rg);
-              TOut* ev = reinterpret_cast<TOut*>(&rv);
-#pragma unroll
-              for (int k = 0; k < 8; ++k) {
-                eg[k] = Dt<TOut>::from_f(gv[j * 8 + k]);
-                ev[k] = Dt<TOut>::from_f(vv[j * 8 + k]);
-              }
-              const int off = lane * 128 + ((j ^ (lane & 7)) * 16);
-              *reinterpret_cast<uint4*>(gb + off) = rg;
-              *reinterpret_cast<uint4*>(vb + off) = rv;
-            }
-          }
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(hb + lane * 128 + ((j ^ (lane & 7)) * 16)) =
+                make_uint4(vkeep[4 * j], vkeep[4 * j + 1], vkeep[4 * j + 2], vkeep[4 * j + 3]);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, smem_u32(hb), n0 + c, y);
-            if constexpr (EPI == EPI_SWIGLU_SAVE) {
-              tma_store_2d(&tmD, smem_u32(stage + 4096), n0 + c, y);
-              tma_store_2d(&tmD, smem_u32(stage + 8192), g.ff + n0 + c, y);
-            }
+            tma_store_2d(&tmD, smem_u32(hb), g.ff + n0 + c, y);
             bulk_commit();
           }
         }
-        tc_fence_before();
-        mbar_arrive(tempty0 + 8 * acc);
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
+      if constexpr (EPI == EPI_LSE) {
+        // This warp's 128-column block of its 32 rows, read from TMEM twice:
+        // first the block max m_b of the rounded logits (and the label's
+        // logit), then e = exp(x - m_b) 64 columns at a time: summed, packed,
+        // staged and TMA-stored.
+        static_assert(sizeof(TOut) == 2 && BN == 256, "16-bit output, 256-column tiles");
+        const int row = m0 + quarter * 32 + lane;
+        const int64_t lab = row < g.M ? g.labels[row] : -1;
+        const int c0 = n0 + half * 128;
+        const int nvalid = g.vocab - c0;  // columns of this block below vocab (may be <= 0 or >= 128)
+        const uint32_t t_blk = t_row + half * 128;
+        const int64_t li = lab - c0;
+        const bool has_label = li >= 0 && li < 128 && li < nvalid;
+        float mx = -INFINITY, xl = 0.f;
+#pragma unroll 1
+        for (int ch = 0; ch < 2; ++ch) {
+          uint32_t r[64];
+          tmem_ld_32cols_nowait(t_blk + ch * 64, r);
+          tmem_ld_32cols_nowait(t_blk + ch * 64 + 32, r + 32);
+          tmem_ld_wait();
+          // rounding is monotonic, so the max of the rounded values is the
+          // rounded max: one conversion per row instead of one per value
+          if (nvalid >= 128) {
+#pragma unroll
+            for (int k = 0; k < 64; ++k) mx = fmaxf(mx, __uint_as_float(r[k]));
+          } else {
+#pragma unroll
+            for (int k = 0; k < 64; ++k)
+              if (ch * 64 + k < nvalid) mx = fmaxf(mx, __uint_as_float(r[k]));
+          }
+          if (has_label && (li >> 6) == ch) {
+#pragma unroll
+            for (int k = 0; k < 64; ++k)
+              if (k == (int)(li & 63)) xl = __uint_as_float(r[k]);
+          }
+        }
+        if (mx != -INFINITY) mx = round_to<TOut>(mx);
+        if (has_label) g.xlabel[row] = round_to<TOut>(xl);
+        const float nm = mx == -INFINITY ? 0.f : -mx * kLog2eF;
+        float sm = 0.f;
+        uint8_t* buf = sOut + ew * 4096;
+        const int y = m0 + quarter * 32;
+#pragma unroll 1
+        for (int ch = 0; ch < 2; ++ch) {
+          uint32_t r[64];
+          tmem_ld_32cols_nowait(t_blk + ch * 64, r);
+          tmem_ld_32cols_nowait(t_blk + ch * 64 + 32, r + 32);
+          tmem_ld_wait();
+          if (ch == 1) {  // last TMEM read of this tile by this warp
+            tc_fence_before();
+            mbar_arrive(tempty0 + 8 * acc);
+          }
+          uint32_t pk[32];
+          if (nvalid >= 128) {  // every column of the block counts
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              const uint32_t xr = pack2_rn<TOut>(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+              const float e0 = ex2_fast(fmaf(unpack_half<TOut>(xr, 0), kLog2eF, nm));
+              const float e1 = ex2_fast(fmaf(unpack_half<TOut>(xr, 1), kLog2eF, nm));
+              sm += e0 + e1;
+              pk[k] = pack2_rn<TOut>(e0, e1);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 32; ++k) {
+              const int c = ch * 64 + 2 * k;
+              const uint32_t xr = pack2_rn<TOut>(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+              const float e0 = c < nvalid ? ex2_fast(fmaf(unpack_half<TOut>(xr, 0), kLog2eF, nm)) : 0.f;
+              const float e1 = c + 1 < nvalid ? ex2_fast(fmaf(unpack_half<TOut>(xr, 1), kLog2eF, nm)) : 0.f;
+              sm += e0 + e1;
+              pk[k] = pack2_rn<TOut>(e0, e1);
+            }
+          }
+          if (lane == 0) bulk_wait_read<0>();
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) =
+                make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmC, smem_u32(buf), c0 + ch * 64, y);
+            bulk_commit();
+          }
+        }
+        if (row < g.M) g.stats[(int64_t)row * g.stats_ld + 2 * nt + half] = make_float2(mx, sm);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
@@ -396,43 +819,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       if constexpr (EPI == EPI_TMA || EPI == EPI_TMA_ADD) {
         // Each warp stages its 32 rows, CW columns at a time, in a 128-byte
         // swizzled layout (16-byte chunk j of row r at j ^ (r % 8): conflict-free
-        // stores) and writes them with one TMA store per chunk; two buffers per
-        // warp let the next chunk be staged while the previous store drains.
+        // stores) and writes them with one TMA store per chunk.
         constexpr int CW = 128 / (int)sizeof(TOut);
-        constexpr int PER16 = 16 / (int)sizeof(TOut);
-        uint8_t* stage = sOut + (warp - 2) * 8192;
+        constexpr int HALF = BN / 2;
+        static_assert(HALF % CW == 0, "column half must be whole staging boxes");
+        uint8_t* buf = sOut + ew * 4096;
+        const int y = split * g.split_rows + m0 + quarter * 32;
 #pragma unroll 1
-        for (int c = 0; c < BN; c += CW) {
-          float v[CW];
+        for (int c = half * HALF; c < (half + 1) * HALF; c += CW) {
+          uint32_t r[CW];
 #pragma unroll
-          for (int q = 0; q < CW / 32; ++q) {
-            float part[32];
-            tmem_ld_32cols(t_row + c + q * 32, part);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) v[q * 32 + j] = part[j];
+          for (int q = 0; q < CW / 32; ++q) tmem_ld_32cols_nowait(t_row + c + q * 32, r + q * 32);
+          tmem_ld_wait();
+          if (c + CW == (half + 1) * HALF) {  // last TMEM read of this tile by this warp
+            tc_fence_before();
+            mbar_arrive(tempty0 + 8 * acc);
           }
-          if (lane == 0) bulk_wait_read<1>();
+          if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
-          uint8_t* buf = stage + ((c / CW) & 1) * 4096;
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             uint4 raw;
-            TOut* e = reinterpret_cast<TOut*>(&raw);
-#pragma unroll
-            for (int k = 0; k < PER16; ++k) e[k] = Dt<TOut>::from_f(v[j * PER16 + k]);
+            if constexpr (sizeof(TOut) == 2) {  // packed conversions: one per two values
+              const uint32_t* q = r + j * 8;
+              raw = make_uint4(pack2_rn<TOut>(__uint_as_float(q[0]), __uint_as_float(q[1])),
+                               pack2_rn<TOut>(__uint_as_float(q[2]), __uint_as_float(q[3])),
+                               pack2_rn<TOut>(__uint_as_float(q[4]), __uint_as_float(q[5])),
+                               pack2_rn<TOut>(__uint_as_float(q[6]), __uint_as_float(q[7])));
+            } else {
+              raw = make_uint4(r[j * 4], r[j * 4 + 1], r[j * 4 + 2], r[j * 4 + 3]);
+            }
             *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) = raw;
           }
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            const int y = split * g.split_rows + m0 + quarter * 32;
             if constexpr (EPI == EPI_TMA_ADD) tma_reduce_add_2d(&tmC, smem_u32(buf), n0 + c, y);
             else tma_store_2d(&tmC, smem_u32(buf), n0 + c, y);
             bulk_commit();
           }
         }
-        tc_fence_before();
-        mbar_arrive(tempty0 + 8 * acc);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
@@ -452,7 +878,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool vec_ok = ((ldo * (int64_t)sizeof(TOut)) % 16 == 0) &&
                           ((reinterpret_cast<uintptr_t>(out_row) & 15) == 0);
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
+      for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
         float v[32];
         tmem_ld_32cols(t_row + c, v);
         const int col = n0 + c;
@@ -479,6 +905,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int consumed = *s_consumed;
     for (int i = consumed; i < issued; ++i)
       mbar_wait(full0 + 8 * (i % STAGES), (uint32_t)((i / STAGES) & 1), g.status, RK_DEV_GEMM_TIMEOUT, nullptr);
+    if (RES && b_issued > *s_b_consumed)  // the last resident B load was never waited on
+      mbar_wait(bfull, (uint32_t)((b_issued - 1) & 1), g.status, RK_DEV_GEMM_TIMEOUT, nullptr);
   }
   __syncthreads();
   if (warp == 1) {
@@ -629,11 +1057,22 @@ struct Operand {
   bool mn_major;  // contiguous along M (or N) instead of K
 };
 
-template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, typename TOut>
+// B-resident schedule on/off (REVK_GEMM_RES=0 in the environment turns it off; a tuning switch).
+bool res_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("REVK_GEMM_RES");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, typename TOut, bool RES = false, int XF = XF_NONE,
+          typename TIn = __nv_bfloat16>
 int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, GemmArgs g, int dtype,
               cudaStream_t s, const CUtensorMap* td = nullptr) {
-  using L = TcSmem<BN, STAGES, epi_out_bytes(EPI)>;
-  auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, EPI, TOut>;
+  using L = TcSmem<BN, STAGES, epi_out_bytes(EPI), RES>;
+  static_assert(L::kTotal <= 232448, "shared memory over the per-block limit");
+  auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, EPI, TOut, RES, XF, TIn>;
   rk_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)L::kTotal);
   const int total = g.tiles_m * g.tiles_n * g.splits;
   int grid = sm_count();
@@ -647,7 +1086,14 @@ template <int BN, int EPI, typename TOut>
 int dispatch_major(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, bool a_mn, bool b_mn,
                    const GemmArgs& g, int dtype, cudaStream_t s) {
   constexpr int ST = BN == 256 ? 4 : 6;
-  if (!a_mn && !b_mn) return launch_tc<BN, ST, false, false, EPI, TOut>(ta, tb, tc, g, dtype, s);
+  if (!a_mn && !b_mn) {
+    // K <= 256 with one slice: keep the B block resident (fprop of the d_model-wide inputs)
+    if constexpr (EPI == EPI_TMA || EPI == EPI_STORE) {
+      if (g.kb_total <= kResKb && g.splits == 1 && res_enabled())
+        return launch_tc<BN, 4, false, false, EPI, TOut, true>(ta, tb, tc, g, dtype, s);
+    }
+    return launch_tc<BN, ST, false, false, EPI, TOut>(ta, tb, tc, g, dtype, s);
+  }
   if (!a_mn && b_mn) return launch_tc<BN, ST, false, true, EPI, TOut>(ta, tb, tc, g, dtype, s);
   if (a_mn && b_mn) return launch_tc<BN, ST, true, true, EPI, TOut>(ta, tb, tc, g, dtype, s);
   return RK_ERR_UNSUPPORTED;
@@ -698,7 +1144,7 @@ int tc_gemm(Operand a, Operand b, int M, int N, int K, int dtype, void* out, int
   if (b.mn_major) ok = make_map(&tb, b.ptr, (uint64_t)N, (uint64_t)K, (uint64_t)b.ld, dtype, 64, 64);
   else ok = make_map(&tb, b.ptr, (uint64_t)K, (uint64_t)N, (uint64_t)b.ld, dtype, 64, (uint32_t)BN);
   if (!ok) return RK_ERR_LAUNCH;
-  GemmArgs g;
+  GemmArgs g{};
   g.M = M;
   g.N = N;
   g.K = K;
@@ -911,8 +1357,283 @@ extern "C" int rk_gemm_fprop_swiglu(const void* x, int64_t ldx, const void* w_up
   g.status = rk_host::device_status_ptr();
   if (dtype == RK_BF16) {
     if (u) return launch_tc<256, 3, false, false, EPI_SWIGLU_SAVE, __nv_bfloat16>(ta, tb, tc, g, dtype, s, &td);
+    if (g.kb_total <= kResKb && res_enabled())
+      return launch_tc<256, 4, false, false, EPI_SWIGLU, __nv_bfloat16, true>(ta, tb, tc, g, dtype, s);
     return launch_tc<256, 4, false, false, EPI_SWIGLU, __nv_bfloat16>(ta, tb, tc, g, dtype, s);
   }
   if (u) return launch_tc<256, 3, false, false, EPI_SWIGLU_SAVE, __half>(ta, tb, tc, g, dtype, s, &td);
   return launch_tc<256, 4, false, false, EPI_SWIGLU, __half>(ta, tb, tc, g, dtype, s);
+}
+
+// ---------------------------------------------------------------- softmax head
+// The vocabulary head and its cross-entropy without a pass of their own over
+// the logits (the head GEMM and F.cross_entropy of model.py:104 and
+// train_baseline.py:262, and their backward):
+//   rk_head_fprop : e = exp(logit - m_b) (16-bit; m_b the max of the row's
+//                   128-column block b of rounded logits), (m_b, sum e) per
+//                   (row, b), and the logit at each row's label;
+//   rk_head_loss  : lse = log-sum-exp over the blocks, loss = lse - logit[label],
+//                   and per row (-lse*log2 e, scale, (exp(logit[label]-lse)-1)*scale);
+//   rk_head_dgrad : dhidden = dlogits . W and
+//   rk_head_wgrad : dW (+)= dlogits^T . hidden, each GEMM forming
+//                   dlogit = e * exp(m_b - lse) * scale (label entry exact) in
+//                   shared memory, so dlogits never exist in global memory.
+namespace rk {
+
+// 32 rows per CTA: warp w reduces rows w, w+8, .. of the CTA's 32 (lse, loss,
+// rowc), then the CTA writes fcoef[b][row] = exp(m_b - lse) * scale for every
+// block b with 32 consecutive rows per store (coalesced).
+__global__ void __launch_bounds__(256) head_loss_kernel(const float2* __restrict__ stats, int width,
+                                                        const float* __restrict__ xlabel, int vocab,
+                                                        const int64_t* __restrict__ labels, int rows, float scale,
+                                                        const float* __restrict__ scale_dev,
+                                                        float* __restrict__ loss_rows, float4* __restrict__ rowc,
+                                                        float* __restrict__ fcoef, int64_t fcoef_ld,
+                                                        int ignore_index, unsigned int* status) {
+  pdl_wait();  // inputs are the previous kernel's outputs
+  __shared__ float s_nl[32], s_sc[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * 32;
+  if (scale_dev) scale *= *scale_dev;
+  for (int rr = warp; rr < 32; rr += 8) {
+    const int row = row0 + rr;
+    if (row >= rows) {
+      if (lane == 0) {
+        s_nl[rr] = 0.f;
+        s_sc[rr] = 0.f;
+      }
+      continue;
+    }
+    const float2* st = stats + (int64_t)row * width;
+    float m = -INFINITY, s = 0.f;
+    for (int i = lane; i < width; i += 32) {
+      const float2 p = st[i];
+      lse_merge(m, s, p.x, p.y);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      lse_merge(m, s, m2, s2);
+    }
+    if (lane == 0) {
+      const int64_t label = labels[row];
+      const bool ignored = label == ignore_index;
+      const bool bad = !ignored && (label < 0 || label >= vocab);
+      if (bad) flag_error(status, RK_DEV_CE_LABEL);
+      if (ignored || bad) {
+        loss_rows[row] = 0.f;
+        rowc[row] = make_float4(0.f, 0.f, 0.f, 0.f);
+        s_nl[rr] = 0.f;
+        s_sc[rr] = 0.f;
+      } else {
+        const float lse = m + logf(s);
+        const float xl = xlabel[row];
+        const float nl = -lse * kLog2eF;
+        loss_rows[row] = lse - xl;
+        rowc[row] = make_float4(nl, scale, (ex2_fast(fmaf(xl, kLog2eF, nl)) - 1.f) * scale, 0.f);
+        s_nl[rr] = nl;
+        s_sc[rr] = scale;
+      }
+    }
+  }
+  __syncthreads();
+  // 32 blocks x 32 rows at a time: row-contiguous reads of m_b, transposed
+  // through shared memory, block-contiguous writes
+  __shared__ float s_m[32][33];
+  const int nrow = min(32, rows - row0);
+  for (int b0 = 0; b0 < width; b0 += 32) {
+    for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
+      const int rr = i >> 5, bb = i & 31;
+      s_m[rr][bb] = (rr < nrow && b0 + bb < width) ? stats[(int64_t)(row0 + rr) * width + b0 + bb].x : -INFINITY;
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
+      const int bb = i >> 5, rr = i & 31;
+      if (rr < nrow && b0 + bb < width) {
+        const float mb = s_m[rr][bb];
+        const float sc = s_sc[rr];
+        fcoef[(int64_t)(b0 + bb) * fcoef_ld + row0 + rr] =
+            (sc == 0.f || mb == -INFINITY) ? 0.f : ex2_fast(fmaf(mb, kLog2eF, s_nl[rr])) * sc;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+}  // namespace rk
+
+extern "C" int64_t rk_head_stats_width(int64_t vocab) { return vocab > 0 ? 2 * ((vocab + 255) / 256) : 0; }
+
+extern "C" int rk_head_fprop(const void* hidden, int64_t ldh, const void* w, int64_t ldw, const int64_t* labels,
+                             void* expo, int64_t lde, float* stats, float* xlabel, int64_t M, int64_t V, int64_t K,
+                             int dtype, void* stream) {
+  if (!hidden || !w || !labels || !expo || !stats || !xlabel || !dims_ok(M, V, K) || K == 0 || ldh < K ||
+      ldw < K || lde < V)
+    return RK_ERR_ARG;
+  if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
+  if (M == 0) return RK_OK;
+  if (!rk_host::aligned(hidden, 16) || !rk_host::aligned(w, 16) || !rk_host::aligned(expo, 16) ||
+      !rk_host::aligned(stats, 8) || (ldh * 2) % 16 || (ldw * 2) % 16 || (lde * 2) % 16)
+    return RK_ERR_ALIGN;
+  CUtensorMap ta, tb, tc;
+  if (!make_map(&ta, hidden, (uint64_t)K, (uint64_t)M, (uint64_t)ldh, dtype, 64, kBM) ||
+      !make_map(&tb, w, (uint64_t)K, (uint64_t)V, (uint64_t)ldw, dtype, 64, 256) ||
+      !make_out_map(&tc, expo, (uint64_t)V, (uint64_t)M, (uint64_t)lde, dtype))
+    return RK_ERR_LAUNCH;
+  GemmArgs g{};
+  g.M = (int)M;
+  g.N = (int)V;
+  g.K = (int)K;
+  g.tiles_m = (int)((M + kBM - 1) / kBM);
+  g.tiles_n = (int)((V + 255) / 256);
+  g.kb_total = (int)((K + kBK - 1) / kBK);
+  g.splits = 1;
+  g.kb_per_split = g.kb_total;
+  g.out = expo;
+  g.ldo = lde;
+  g.out_dtype = dtype;
+  g.status = rk_host::device_status_ptr();
+  g.stats = reinterpret_cast<float2*>(stats);
+  g.stats_ld = 2 * g.tiles_n;
+  g.labels = labels;
+  g.xlabel = xlabel;
+  g.vocab = (int)V;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool res = g.kb_total <= kResKb && res_enabled();
+  if (dtype == RK_BF16) {
+    if (res) return launch_tc<256, 4, false, false, EPI_LSE, __nv_bfloat16, true>(ta, tb, tc, g, dtype, s);
+    return launch_tc<256, 4, false, false, EPI_LSE, __nv_bfloat16>(ta, tb, tc, g, dtype, s);
+  }
+  if (res) return launch_tc<256, 4, false, false, EPI_LSE, __half, true>(ta, tb, tc, g, dtype, s);
+  return launch_tc<256, 4, false, false, EPI_LSE, __half>(ta, tb, tc, g, dtype, s);
+}
+
+extern "C" int rk_head_loss(const float* stats, int64_t width, const float* xlabel, const int64_t* labels,
+                            int64_t rows, int64_t V, float grad_scale, const float* grad_scale_dev, float* loss_rows,
+                            float* rowc, float* fcoef, int64_t fcoef_ld, int ignore_index, void* stream) {
+  if (!stats || !xlabel || !labels || !loss_rows || !rowc || !fcoef || rows < 0 || V <= 0 || fcoef_ld < rows ||
+      width < rk_head_stats_width(V) || rows >= (1ll << 31) || V >= (1ll << 31))
+    return RK_ERR_ARG;
+  if (!rk_host::aligned(stats, 8) || !rk_host::aligned(rowc, 16)) return RK_ERR_ALIGN;
+  if (rows == 0) return RK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  rk_host::launch_k(head_loss_kernel, (unsigned)((rows + 31) / 32), 256, 0, s, reinterpret_cast<const float2*>(stats),
+                    (int)width, xlabel, (int)V, labels, (int)rows, grad_scale, grad_scale_dev, loss_rows,
+                    reinterpret_cast<float4*>(rowc), fcoef, fcoef_ld, ignore_index, rk_host::device_status_ptr());
+  return rk_host::launch_status();
+}
+
+namespace {
+template <typename TIn>
+int head_dgrad_typed(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& g,
+                     int dtype, int out_dtype, cudaStream_t s) {
+  switch (out_dtype) {
+    case RK_F32: return launch_tc<256, 4, false, true, EPI_TMA, float, false, XF_ROWS, TIn>(ta, tb, tc, g, dtype, s);
+    case RK_BF16:
+      return launch_tc<256, 4, false, true, EPI_TMA, __nv_bfloat16, false, XF_ROWS, TIn>(ta, tb, tc, g, dtype, s);
+    case RK_F16: return launch_tc<256, 4, false, true, EPI_TMA, __half, false, XF_ROWS, TIn>(ta, tb, tc, g, dtype, s);
+    default: return RK_ERR_DTYPE;
+  }
+}
+template <typename TIn>
+int head_wgrad_typed(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const GemmArgs& g,
+                     int dtype, bool accumulate, cudaStream_t s) {
+  if (accumulate) return launch_tc<256, 4, true, true, EPI_TMA_ADD, float, false, XF_COLS, TIn>(ta, tb, tc, g, dtype, s);
+  return launch_tc<256, 4, true, true, EPI_TMA, float, false, XF_COLS, TIn>(ta, tb, tc, g, dtype, s);
+}
+
+bool head_bwd_args_ok(const void* expo, int64_t lde, const float* fcoef, int64_t fcoef_ld, const float* rowc,
+                      const int64_t* labels, int64_t M, int64_t V) {
+  return expo && fcoef && rowc && labels && lde >= V && fcoef_ld >= M;
+}
+}  // namespace
+
+extern "C" int rk_head_dgrad(const void* expo, int64_t lde, const float* fcoef, int64_t fcoef_ld, const float* rowc,
+                             const int64_t* labels, const void* w, int64_t ldw, void* dx, int64_t lddx, int64_t M,
+                             int64_t V, int64_t K, int dtype, int out_dtype, void* stream) {
+  // DX[M, K] = dlogits[M, V] . W[V, K]: output cols = K, reduction = V.
+  if (!head_bwd_args_ok(expo, lde, fcoef, fcoef_ld, rowc, labels, M, V) || !w || !dx || !dims_ok(M, K, V) || V == 0 ||
+      K == 0 || ldw < K || lddx < K)
+    return RK_ERR_ARG;
+  if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
+  if (M == 0) return RK_OK;
+  const int64_t osz = out_dtype == RK_F32 ? 4 : 2;
+  if (!rk_host::aligned(expo, 16) || !rk_host::aligned(w, 16) || !rk_host::aligned(dx, 16) ||
+      !rk_host::aligned(rowc, 16) || (lde * 2) % 16 || (ldw * 2) % 16 ||
+      (lddx * osz) % 16)
+    return RK_ERR_ALIGN;
+  CUtensorMap ta, tb, tc;
+  if (!make_map(&ta, expo, (uint64_t)V, (uint64_t)M, (uint64_t)lde, dtype, 64, kBM) ||
+      !make_map(&tb, w, (uint64_t)K, (uint64_t)V, (uint64_t)ldw, dtype, 64, 64) ||
+      !make_out_map(&tc, dx, (uint64_t)K, (uint64_t)M, (uint64_t)lddx, out_dtype))
+    return RK_ERR_LAUNCH;
+  GemmArgs g{};
+  g.M = (int)M;
+  g.N = (int)K;
+  g.K = (int)V;
+  g.tiles_m = (int)((M + kBM - 1) / kBM);
+  g.tiles_n = (int)((K + 255) / 256);
+  g.kb_total = (int)((V + kBK - 1) / kBK);
+  g.splits = 1;
+  g.kb_per_split = g.kb_total;
+  g.out = dx;
+  g.ldo = lddx;
+  g.out_dtype = out_dtype;
+  g.status = rk_host::device_status_ptr();
+  g.fcoef = fcoef;
+  g.fcoef_ld = fcoef_ld;
+  g.rowc = reinterpret_cast<const float4*>(rowc);
+  g.labels = labels;
+  g.vocab = (int)V;
+  g.tokens = (int)M;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == RK_BF16) return head_dgrad_typed<__nv_bfloat16>(ta, tb, tc, g, dtype, out_dtype, s);
+  return head_dgrad_typed<__half>(ta, tb, tc, g, dtype, out_dtype, s);
+}
+
+extern "C" int rk_head_wgrad(const void* expo, int64_t lde, const float* fcoef, int64_t fcoef_ld, const float* rowc,
+                             const int64_t* labels, const void* x, int64_t ldx, float* dw, int64_t lddw, int64_t M,
+                             int64_t V, int64_t K, int dtype, int accumulate, void* stream) {
+  // DW[V, K] (+)= dlogits[M, V]^T . X[M, K]: output rows = V, cols = K, reduction = M tokens.
+  if (!head_bwd_args_ok(expo, lde, fcoef, fcoef_ld, rowc, labels, M, V) || !x || !dw || !dims_ok(V, K, M) || V == 0 ||
+      K == 0 || ldx < K || lddw < K)
+    return RK_ERR_ARG;
+  if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (M == 0) {
+    if (!accumulate)
+      for (int64_t r = 0; r < V; ++r) cudaMemsetAsync(dw + r * lddw, 0, sizeof(float) * K, s);
+    return rk_host::launch_status();
+  }
+  if (!rk_host::aligned(expo, 16) || !rk_host::aligned(x, 16) || !rk_host::aligned(dw, 16) ||
+      !rk_host::aligned(rowc, 16) || (lde * 2) % 16 || (ldx * 2) % 16 ||
+      (lddw * 4) % 16)
+    return RK_ERR_ALIGN;
+  CUtensorMap ta, tb, tc;
+  if (!make_map(&ta, expo, (uint64_t)V, (uint64_t)M, (uint64_t)lde, dtype, 64, 64) ||
+      !make_map(&tb, x, (uint64_t)K, (uint64_t)M, (uint64_t)ldx, dtype, 64, 64) ||
+      !make_out_map(&tc, dw, (uint64_t)K, (uint64_t)V, (uint64_t)lddw, RK_F32))
+    return RK_ERR_LAUNCH;
+  GemmArgs g{};
+  g.M = (int)V;
+  g.N = (int)K;
+  g.K = (int)M;
+  g.tiles_m = (int)((V + kBM - 1) / kBM);
+  g.tiles_n = (int)((K + 255) / 256);
+  g.kb_total = (int)((M + kBK - 1) / kBK);
+  g.splits = 1;
+  g.kb_per_split = g.kb_total;
+  g.out = dw;
+  g.ldo = lddw;
+  g.out_dtype = RK_F32;
+  g.status = rk_host::device_status_ptr();
+  g.fcoef = fcoef;
+  g.fcoef_ld = fcoef_ld;
+  g.rowc = reinterpret_cast<const float4*>(rowc);
+  g.labels = labels;
+  g.vocab = (int)V;
+  g.tokens = (int)M;
+  if (dtype == RK_BF16) return head_wgrad_typed<__nv_bfloat16>(ta, tb, tc, g, dtype, accumulate != 0, s);
+  return head_wgrad_typed<__half>(ta, tb, tc, g, dtype, accumulate != 0, s);
 }

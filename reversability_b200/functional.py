@@ -205,6 +205,91 @@ def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor | None = No
     return dw
 
 
+# ------------------------------------------------------------------ softmax head (fused cross-entropy)
+def head_logits_buffer(rows: int, vocab: int, device, dtype) -> torch.Tensor:
+    """[rows, vocab] view of a buffer whose row stride is vocab rounded up to 64
+    (TMA needs 16-byte aligned rows)."""
+    vpad = (vocab + 63) // 64 * 64
+    return torch.empty((rows, vpad), device=device, dtype=dtype)[:, :vocab]
+
+
+class HeadState:
+    """What the softmax-head backward needs from the forward: expo [M, V]
+    (exp(x - m_b), 16-bit), stats [M, width, 2] ((m_b, sum exp) per 128-column
+    block), labels [M], and after head_loss rowc [M, 4] and the per-block
+    factors fcoef [width, M]."""
+
+    def __init__(self, expo, stats, xlabel, labels):
+        self.expo, self.stats, self.xlabel, self.labels = expo, stats, xlabel, labels
+        self.rowc = None
+        self.fcoef = None
+
+
+def head_fprop(hidden: torch.Tensor, w: torch.Tensor, labels: torch.Tensor, expo: torch.Tensor | None = None,
+               stats: torch.Tensor | None = None, xlabel: torch.Tensor | None = None) -> HeadState:
+    """The head GEMM x = hidden @ w.T with the cross-entropy's log-sum-exp
+    partials in its epilogue. hidden [M, K], w [V, K] (bf16/f16), labels [M]."""
+    require_cuda(hidden, w)
+    M, K = hidden.shape
+    V = w.shape[0]
+    if expo is None:
+        expo = head_logits_buffer(M, V, hidden.device, hidden.dtype)
+    width = _lib.lib().rk_head_stats_width(V)
+    if stats is None:
+        stats = torch.empty((M, width, 2), device=hidden.device, dtype=torch.float32)
+    if xlabel is None:
+        xlabel = torch.empty(M, device=hidden.device, dtype=torch.float32)
+    _lib.call("rk_head_fprop", hidden.data_ptr(), _ld(hidden), w.data_ptr(), _ld(w), labels.data_ptr(),
+              expo.data_ptr(), _ld(expo), stats.data_ptr(), xlabel.data_ptr(), M, V, K, _gemm_dtype(hidden, w),
+              _lib.stream_ptr())
+    return HeadState(expo, stats, xlabel, labels)
+
+
+def head_loss(st: HeadState, grad_scale: float = 1.0, grad_scale_dev: torch.Tensor | None = None,
+              ignore_index: int = -100, loss_rows: torch.Tensor | None = None,
+              rowc: torch.Tensor | None = None, fcoef: torch.Tensor | None = None) -> torch.Tensor:
+    """Per-row cross-entropy loss (0 for ignore_index); fills st.rowc and
+    st.fcoef for the backward."""
+    M, V = st.expo.shape
+    dev = st.expo.device
+    if loss_rows is None:
+        loss_rows = torch.empty(M, device=dev, dtype=torch.float32)
+    if rowc is None:
+        rowc = torch.empty((M, 4), device=dev, dtype=torch.float32)
+    if fcoef is None:
+        fcoef = torch.empty((st.stats.shape[1], M), device=dev, dtype=torch.float32)
+    _lib.call("rk_head_loss", st.stats.data_ptr(), st.stats.shape[1], st.xlabel.data_ptr(), st.labels.data_ptr(), M,
+              V, float(grad_scale), _lib.ptr(grad_scale_dev), loss_rows.data_ptr(), rowc.data_ptr(),
+              fcoef.data_ptr(), fcoef.stride(0), int(ignore_index), _lib.stream_ptr())
+    st.rowc, st.fcoef = rowc, fcoef
+    return loss_rows
+
+
+def head_dgrad(st: HeadState, w: torch.Tensor, out_dtype: torch.dtype | None = None) -> torch.Tensor:
+    """dhidden = dlogits @ w, dlogits = (softmax - onehot) * scale formed inside the GEMM."""
+    M, V = st.expo.shape
+    K = w.shape[1]
+    dx = torch.empty((M, K), device=w.device, dtype=out_dtype or w.dtype)
+    _lib.call("rk_head_dgrad", st.expo.data_ptr(), _ld(st.expo), st.fcoef.data_ptr(), st.fcoef.stride(0),
+              st.rowc.data_ptr(), st.labels.data_ptr(), w.data_ptr(), _ld(w), dx.data_ptr(), K, M, V, K,
+              _gemm_dtype(st.expo, w), _lib.code(dx.dtype), _lib.stream_ptr())
+    return dx
+
+
+def head_wgrad(st: HeadState, hidden: torch.Tensor, dw: torch.Tensor | None = None,
+               accumulate: bool = False) -> torch.Tensor:
+    """dw (+)= dlogits^T @ hidden in fp32, dlogits formed inside the GEMM."""
+    M, V = st.expo.shape
+    K = hidden.shape[1]
+    if dw is None:
+        dw = torch.empty((V, K), device=hidden.device, dtype=torch.float32)
+        accumulate = False
+    _lib.call("rk_head_wgrad", st.expo.data_ptr(), _ld(st.expo), st.fcoef.data_ptr(), st.fcoef.stride(0),
+              st.rowc.data_ptr(), st.labels.data_ptr(), hidden.data_ptr(), _ld(hidden), dw.data_ptr(), dw.stride(0),
+              M, V, K, _gemm_dtype(st.expo, hidden), int(accumulate), _lib.stream_ptr())
+    return dw
+
+
 # ------------------------------------------------------------------ attention
 def attention_fwd(qkv: torch.Tensor, n_heads: int, out: torch.Tensor | None = None):
     """Causal attention over packed qkv [B, T, 3*D]; returns (o [B, T, D], lse [B, H, T])."""

@@ -161,7 +161,33 @@ def bench_head(iters):
 
     def run(k):
         fn.linear_fwd(hid, w, out=logits)
-    return [("tensor", "head_fprop_gemm", 2 * M * V * D, time_graph(run, 1, max(iters // 10, 3)))]
+    out = [("tensor", "head_fprop_gemm", 2 * M * V * D, time_graph(run, 1, max(iters // 10, 3)))]
+    # softmax head: fprop with log-sum-exp partials, loss, and the dgrad/wgrad
+    # GEMMs that form dlogits from the logits in shared memory
+    labels = torch.randint(0, V, (M,), device="cuda")
+    stats = torch.empty((M, _lib.lib().rk_head_stats_width(V), 2), device="cuda")
+    xlab = torch.empty(M, device="cuda")
+    dw = torch.zeros(V, D, device="cuda")
+    st = fn.head_fprop(hid, w, labels, expo=logits, stats=stats, xlabel=xlab)
+    fn.head_loss(st, grad_scale=1.0 / M)
+
+    def fprop(k):
+        fn.head_fprop(hid, w, labels, expo=logits, stats=stats, xlabel=xlab)
+
+    def loss(k):
+        fn.head_loss(st, grad_scale=1.0 / M, rowc=st.rowc, fcoef=st.fcoef)
+
+    def dgrad(k):
+        fn.head_dgrad(st, w)
+
+    def wgrad(k):
+        fn.head_wgrad(st, hid, dw=dw, accumulate=True)
+    n = max(iters // 10, 3)
+    out += [("tensor", "head_fprop_lse", 2 * M * V * D, time_graph(fprop, 1, n)),
+            ("hbm", "head_loss", M * stats.shape[1] * 12 + M * 28, time_graph(loss, 1, n)),
+            ("tensor", "head_dgrad_softmax", 2 * M * V * D, time_graph(dgrad, 1, n)),
+            ("tensor", "head_wgrad_softmax", 2 * M * V * D, time_graph(wgrad, 1, n))]
+    return out
 
 
 def bench_attention(iters):

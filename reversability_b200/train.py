@@ -13,12 +13,17 @@ a CUDA graph and replayed):
                          the GEMM weights and the head are views into it
   - `gflat`  fp32 [P]   gradients; layer i's six gradients are contiguous, so
                          each layer is one data-parallel all-reduce bucket
-  - logits   bf16 [B*T, Vpad]  the microstep's vocabulary logits, reused as the
-                         in-place dlogits; Vpad = V rounded up to 64 so every
-                         row starts 16-byte aligned for TMA
+  - logits   bf16 [B*T, Vpad]  the microstep's vocabulary logits (bf16 runs:
+                         exp(logit - max of its 128-column block)); Vpad = V
+                         rounded up to 64 so every row starts 16-byte aligned
+                         for TMA
+  - head_stats fp32 [B*T, 2*ceil(V/256), 2]  per-row partial (max, sum exp)
+                         pairs written by the head GEMM's epilogue
 Per microstep: embedding gather, the fused stack forward, final norm, head GEMM
-over the whole microstep, fused CE forward+backward in place, head
-dgrad/wgrad, final-norm backward, fused reconstruction backward (engine.py),
+with the log-sum-exp partials in its epilogue, per-row loss, head dgrad/wgrad
+that form dlogits = (softmax - onehot) / targets from the logits inside the
+GEMM (fp32 runs: head GEMM, cross-entropy forward+backward in place, plain
+dgrad/wgrad), final-norm backward, fused reconstruction backward (engine.py),
 deterministic embedding scatter. Every gradient is bitwise reproducible.
 """
 from __future__ import annotations
@@ -54,6 +59,7 @@ class TrainSettings:
     precision: str = "bf16"
     norm_eps: float | None = 1e-6
     mlp_tokens: int = 0
+    fused_head: bool = True  # bf16/f16: cross-entropy inside the head GEMMs (rk_head_*)
 
 
 def learning_rate(s: TrainSettings, committed: int, update_targets: int) -> float:
@@ -123,6 +129,14 @@ class ReversibleTrainer:
         V = self.cfg.vocab_size
         self.vpad = (V + 63) // 64 * 64
         self.logits = torch.empty((self.M, self.vpad), device=dev, dtype=self.cd)
+        self.fused_head = settings.fused_head and self.cd in (torch.bfloat16, torch.float16)
+        if self.fused_head:
+            width = _lib.lib().rk_head_stats_width(V)
+            self.head_stats = torch.empty((self.M, width, 2), device=dev, dtype=F32)
+            self.head_xlabel = torch.empty(self.M, device=dev, dtype=F32)
+            self.head_rowc = torch.empty((self.M, 4), device=dev, dtype=F32)
+            self.head_fcoef = torch.empty((width, self.M), device=dev, dtype=F32)
+        self.loss_rows = torch.empty(self.M, device=dev, dtype=F32)
         self.ids = torch.zeros((settings.accumulation, B, T), device=dev, dtype=torch.int64)
         self.labels = torch.full((settings.accumulation, B, T), -100, device=dev, dtype=torch.int64)
         self.inv_denominator = torch.ones((), device=dev, dtype=F32)
@@ -174,15 +188,28 @@ class ReversibleTrainer:
         hidden, rstd_f = fn.rmsnorm_fwd(out, self.final_w, eps_f, out_dtype=self.cd)
         V = cfg.vocab_size
         logits = self.logits[:, :V]
-        fn.linear_fwd(hidden, self.tok_c, out=logits)
-        loss_rows = torch.empty(self.M, device=self.dev, dtype=F32)
-        # dlogits = (softmax - onehot) / update_targets, in place over the logits
-        _lib.call("rk_cross_entropy_fwd_bwd", logits.data_ptr(), self.vpad, V, labels.data_ptr(), self.M, 1.0,
-                  self.inv_denominator.data_ptr(), loss_rows.data_ptr(), logits.data_ptr(), self.vpad,
-                  _lib.code(self.cd), -100, _lib.stream_ptr())
-        self.loss_sum += loss_rows.sum()
-        dhidden = fn.linear_dgrad(logits, self.tok_c)
-        fn.linear_wgrad(logits, hidden, dw=self.g_tok, accumulate=True)
+        loss_rows = self.loss_rows
+        if self.fused_head:
+            # head GEMM with the log-sum-exp partials in its epilogue (the
+            # buffer receives exp(x - block max)), per-row loss, then the two
+            # backward GEMMs form dlogits = (softmax - onehot) / update_targets
+            # inside the GEMM
+            st = fn.head_fprop(hidden, self.tok_c, labels, expo=logits, stats=self.head_stats,
+                               xlabel=self.head_xlabel)
+            fn.head_loss(st, 1.0, self.inv_denominator, loss_rows=loss_rows, rowc=self.head_rowc,
+                         fcoef=self.head_fcoef)
+            self.loss_sum += loss_rows.sum()
+            dhidden = fn.head_dgrad(st, self.tok_c)
+            fn.head_wgrad(st, hidden, dw=self.g_tok, accumulate=True)
+        else:
+            fn.linear_fwd(hidden, self.tok_c, out=logits)
+            # dlogits = (softmax - onehot) / update_targets, in place over the logits
+            _lib.call("rk_cross_entropy_fwd_bwd", logits.data_ptr(), self.vpad, V, labels.data_ptr(), self.M, 1.0,
+                      self.inv_denominator.data_ptr(), loss_rows.data_ptr(), logits.data_ptr(), self.vpad,
+                      _lib.code(self.cd), -100, _lib.stream_ptr())
+            self.loss_sum += loss_rows.sum()
+            dhidden = fn.linear_dgrad(logits, self.tok_c)
+            fn.linear_wgrad(logits, hidden, dw=self.g_tok, accumulate=True)
         dout, _ = fn.rmsnorm_bwd(out, self.final_w, rstd_f, dhidden, dx_dtype=F32, dw=self.g_final,
                                  accumulate_dw=True)
         # the unused output's cotangent is zero; the engine takes None for it

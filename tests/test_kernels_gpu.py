@@ -120,7 +120,7 @@ def test_midpoint_step_inverts_exactly():
 
 # ------------------------------------------------------------------ GEMMs
 GEMM_SHAPES = [(128, 128, 64), (1000, 768, 256), (1000, 256, 256), (1000, 2048, 256), (1000, 256, 1024),
-               (333, 200, 96), (7, 24, 40), (14848, 2048, 256)]
+               (333, 200, 96), (7, 24, 40), (14848, 2048, 256), (2000, 3001, 200)]
 
 
 def _ref_fprop(x, w):

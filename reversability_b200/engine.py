@@ -98,10 +98,51 @@ class LayerGrads:
 class LayerKernels:
     """Sublayer forward / VJP building blocks on [M, d] row-major activations."""
 
-    def __init__(self, n_heads: int, batch: int, length: int, cd: torch.dtype, mlp_tokens: int = 0):
+    def __init__(self, n_heads: int, batch: int, length: int, cd: torch.dtype, mlp_tokens: int = 0,
+                 wgrad_stream: "torch.cuda.Stream | None" = None):
         self.H, self.B, self.T = n_heads, batch, length
         self.cd = cd
         self.mlp_tokens = mlp_tokens
+        # Weight gradients are off the reverse sweep's critical path: with a
+        # side stream they run there, overlapping the dgrad / attention /
+        # elementwise chain. A layer's wgrad operands stay referenced until the
+        # compute stream has waited for that layer's wgrads (one layer later),
+        # so the allocator never hands their memory out early.
+        self.side = wgrad_stream
+        self._held = []
+        self._prev = None
+
+    def _wgrad(self, dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor):
+        """dw += dy^T x, on the side stream when there is one."""
+        if self.side is None:
+            fn.linear_wgrad(dy, x, dw=dw, accumulate=True)
+            return
+        ready = torch.cuda.Event()
+        ready.record()
+        self.side.wait_event(ready)
+        with torch.cuda.stream(self.side):
+            fn.linear_wgrad(dy, x, dw=dw, accumulate=True)
+        self._held += [dy, x]
+
+    def layer_done(self):
+        """Marks the end of one layer's backward: the compute stream waits for
+        the previous layer's weight gradients and releases their operands."""
+        if self.side is None:
+            return
+        done = torch.cuda.Event()
+        done.record(self.side)
+        if self._prev is not None:
+            torch.cuda.current_stream().wait_event(self._prev[0])
+        self._prev = (done, self._held)
+        self._held = []
+
+    def sync(self):
+        """Joins the side stream into the compute stream (all weight gradients final)."""
+        if self.side is None:
+            return
+        torch.cuda.current_stream().wait_stream(self.side)
+        self._prev = None
+        self._held = []
 
     @staticmethod
     def _eps(eps):
@@ -123,10 +164,10 @@ class LayerKernels:
         n1, rstd1, qkv, o, lse = saved
         o2 = o.view(-1, o.shape[-1])
         do = fn.linear_dgrad(ga, lw.proj_c)
-        fn.linear_wgrad(ga, o2, dw=g.proj, accumulate=True)
+        self._wgrad(ga, o2, g.proj)
         dqkv = fn.attention_bwd(qkv.view(self.B, self.T, -1), o, do.view(o.shape), lse, self.H)
         dqkv2 = dqkv.view(-1, dqkv.shape[-1])
-        fn.linear_wgrad(dqkv2, n1, dw=g.qkv, accumulate=True)
+        self._wgrad(dqkv2, n1, g.qkv)
         dn1 = fn.linear_dgrad(dqkv2, lw.qkv_c)
         dx, _ = fn.rmsnorm_bwd_fused(x, lw.attn_norm, rstd1, dn1, g.attn_norm, residual=residual)
         return dx
@@ -183,11 +224,11 @@ class LayerKernels:
             fn.linear_fwd(hg, lw.down_c, out=m[s:e])
             gm_t = gm[s:e]
             dh = fn.linear_dgrad(gm_t, lw.down_c)
-            fn.linear_wgrad(gm_t, hg, dw=g.down, accumulate=True)
+            self._wgrad(gm_t, hg, g.down)
             del hg
             du = fn.swiglu_bwd(u, dh)
             del u, dh
-            fn.linear_wgrad(du, n2[s:e], dw=g.up, accumulate=True)
+            self._wgrad(du, n2[s:e], g.up)
             dn2 = fn.linear_dgrad(du, lw.up_c)
             del du
             fn.rmsnorm_bwd_fused(ysum[s:e], lw.mlp_norm, rstd2[s:e], dn2, g.mlp_norm,
@@ -262,6 +303,9 @@ def stack_backward(kern: LayerKernels, layers, grads, p, q, dp, dq, method: str,
             p, q, dp, dq = kern.backward_midpoint(layers[i], grads[i], p, q, dp, dq, h)
         else:
             p, q, dp, dq = kern.backward_euler(layers[i], grads[i], p, q, dp, dq)
+        kern.layer_done()
         if on_layer_done is not None:
+            kern.sync()  # layer i's weight gradients are read by the caller
             on_layer_done(i)
+    kern.sync()
     return p, q, dp, dq

@@ -60,6 +60,7 @@ class TrainSettings:
     norm_eps: float | None = 1e-6
     mlp_tokens: int = 0
     fused_head: bool = True  # bf16/f16: cross-entropy inside the head GEMMs (rk_head_*)
+    overlap_wgrad: bool = True  # layer weight gradients on a side stream during the reverse sweep
 
 
 def learning_rate(s: TrainSettings, committed: int, update_targets: int) -> float:
@@ -141,7 +142,8 @@ class ReversibleTrainer:
         self.labels = torch.full((settings.accumulation, B, T), -100, device=dev, dtype=torch.int64)
         self.inv_denominator = torch.ones((), device=dev, dtype=F32)
         self.loss_sum = torch.zeros((), device=dev, dtype=F32)
-        self.kern = engine.LayerKernels(self.cfg.n_heads, B, T, self.cd, settings.mlp_tokens)
+        side = torch.cuda.Stream(device=dev) if (dev.type == "cuda" and settings.overlap_wgrad) else None
+        self.kern = engine.LayerKernels(self.cfg.n_heads, B, T, self.cd, settings.mlp_tokens, wgrad_stream=side)
         # AdamW state (flat, fp32) and the device scalar block of rk_clip_adamw_prepare
         self.exp_avg = torch.zeros_like(self.flat)
         self.exp_avg_sq = torch.zeros_like(self.flat)

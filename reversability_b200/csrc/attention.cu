@@ -18,6 +18,7 @@
 //
 // fp32 kernels: CUDA-core versions (one warp per row) for the fp32 parity
 // configuration.
+#include <cstdlib>
 #include "common.cuh"
 
 namespace rk {
@@ -589,7 +590,20 @@ __global__ void __launch_bounds__(128) bwd_dkv_f32_kernel(const float* __restric
 using namespace rk;
 using namespace rk::attn;
 
+int rk_attn_fwd_tc32(const void* qkv, int64_t ldq, void* out, int64_t ldo, float* lse, int64_t B, int64_t H,
+                     int64_t T, int dtype, cudaStream_t s);
+
 namespace {
+
+// Tensor-core forward for head_dim 32 (attention_tc.cu). REVK_ATTN_TC=0 in the
+// environment selects the mma.sync kernel instead (a tuning switch).
+bool attn_tc_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("REVK_ATTN_TC");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
 
 bool attn_args_ok(const void* a, const void* b, int64_t B, int64_t H, int64_t HD, int64_t T) {
   return a && b && B >= 0 && H > 0 && HD > 0 && T >= 0 && B * H < 65536 && T < (1 << 24);
@@ -648,6 +662,10 @@ extern "C" int rk_attn_fwd(const void* qkv, int64_t ldq, void* out, int64_t ldo,
   }
   if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
   if (!tc_layout_ok(qkv, out, nullptr, ldq, ldo, HD)) return (HD == 32 || HD == 64) ? RK_ERR_ALIGN : RK_ERR_UNSUPPORTED;
+  if (HD == 32 && attn_tc_enabled()) {
+    const int st = rk_attn_fwd_tc32(qkv, ldq, out, ldo, lse, B, H, T, dtype, s);
+    if (st != RK_ERR_UNSUPPORTED) return st;
+  }
   if (dtype == RK_BF16)
     return HD == 32 ? fwd_tc<__nv_bfloat16, 32>(qkv, out, lse, (int)B, (int)H, (int)T, ldq, ldo, s)
                     : fwd_tc<__nv_bfloat16, 64>(qkv, out, lse, (int)B, (int)H, (int)T, ldq, ldo, s);

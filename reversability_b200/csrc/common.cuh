@@ -219,6 +219,12 @@ __host__ __device__ constexpr uint32_t idesc_f16(int M, int N, int ab_fmt, int a
          | ((uint32_t)(M >> 4) << 24);      // M / 16
 }
 
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy reads (TMA stores, tcgen05.mma operands).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ int elect_lane0() { return (threadIdx.x & 31) == 0; }
 
 // Programmatic dependent launch: every librevk kernel is launched with

@@ -204,32 +204,53 @@ def reference_arm(args):
 
 
 # ------------------------------------------------------------------ dominant-kernel roofline
+PROFILES = Path(__file__).resolve().parent / "profiles"
+
+
+def profiled_traffic(name: str):
+    """DRAM bytes per launch (dram__bytes_read.sum + dram__bytes_write.sum of
+    one ncu capture) recorded in profiles/ as `traffic_bytes_per_launch[name]: N`."""
+    for f in sorted(PROFILES.glob("*.md")):
+        for line in f.read_text().splitlines():
+            if line.startswith(f"traffic_bytes_per_launch[{name}]:"):
+                return int(line.split(":", 1)[1].strip())
+    return None
+
+
 def kernel_roofline(trainer, peak_tflops):
-    """Times the head GEMM (the largest single kernel of the step: the
-    [29*512, 256] x [256, 50257] bf16 logits GEMM) with CUDA events on its
-    launching stream and reports algorithmic FLOPs / average launch time."""
-    from reversability_b200 import functional as fn
+    """The dominant kernel of the step, the head GEMM with the log-sum-exp
+    epilogue ([29*512, 256] x [256, 50257] bf16, rk_head_fprop), timed live:
+    CUDA event record nodes around it inside the captured update, read after
+    the timed region (both microsteps of the last update). Falls back to
+    timing it alone when the trainer runs the fp32 path."""
     M, V, d = trainer.M, trainer.cfg.vocab_size, trainer.cfg.d_model
-    hidden = torch.randn(M, d, device=trainer.dev).to(trainer.cd)
-    out = trainer.logits[:, :V]
-    s = torch.cuda.current_stream()
-    for _ in range(5):
-        fn.linear_fwd(hidden, trainer.tok_c, out=out)
-    n = 20
-    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    start.record(s)
-    for _ in range(n):
-        fn.linear_fwd(hidden, trainer.tok_c, out=out)
-    stop.record(s)
-    torch.cuda.synchronize()
-    ms = start.elapsed_time(stop) / n
     flops = 2.0 * M * V * d
+    durations = trainer.head_fprop_ms()
+    if durations:
+        ms = sum(durations) / len(durations)
+        how = "event nodes around it in the timed CUDA graph (last update, %d launches)" % len(durations)
+    else:
+        from reversability_b200 import functional as fn
+        hidden = torch.randn(M, d, device=trainer.dev).to(trainer.cd)
+        out = trainer.logits[:, :V]
+        s = torch.cuda.current_stream()
+        for _ in range(5):
+            fn.linear_fwd(hidden, trainer.tok_c, out=out)
+        n = 20
+        start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize()
+        start.record(s)
+        for _ in range(n):
+            fn.linear_fwd(hidden, trainer.tok_c, out=out)
+        stop.record(s)
+        torch.cuda.synchronize()
+        ms = start.elapsed_time(stop) / n
+        how = "alone, 20 launches"
     achieved = flops / (ms * 1e-3) / 1e12
-    return {"kernel": "gemm_tc_kernel (head fprop, M=%d N=%d K=%d, bf16 in, bf16 out)" % (M, V, d),
+    return {"kernel": "gemm_tc_kernel EPI_LSE (rk_head_fprop, M=%d N=%d K=%d, bf16)" % (M, V, d),
             "bound": "tensor", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
             "frac": achieved / peak_tflops, "avg_launch_us": ms * 1e3, "flops_per_launch": flops,
-            "traffic": None}
+            "timed": how, "traffic": profiled_traffic("rk_head_fprop")}
 
 
 # ------------------------------------------------------------------ main arm
@@ -302,6 +323,8 @@ def main():
     launches_before = _lib.launch_count()
     trainer.update(lr_of(0))
     launches_per_update = _lib.launch_count() - launches_before
+    if trainer.fused_head:
+        trainer.time_head_fprop()
     use_graph = not args.no_graph
     if use_graph:
         try:

@@ -237,6 +237,23 @@ __device__ __forceinline__ float unpack_half(uint32_t u, int which) {
   else return __half2float(__ushort_as_half((unsigned short)b));
 }
 
+// Packed 16-bit max of two pairs (values are already rounded, so this is exact).
+template <typename T>
+__device__ __forceinline__ uint32_t max2_16(uint32_t a, uint32_t b) {
+  uint32_t d;
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) asm("max.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  else asm("max.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+// Two values in [0, 1] rounded to 16 bits and packed. bf16: round to nearest
+// (ties away) by an integer add on the ALU, leaving the exponential unit free.
+template <typename T>
+__device__ __forceinline__ uint32_t pack_unit2(float lo, float hi) {
+  if constexpr (std::is_same_v<T, __nv_bfloat16>)
+    return __byte_perm(__float_as_uint(lo) + 0x8000u, __float_as_uint(hi) + 0x8000u, 0x7632);
+  else return pack2_rn<T>(lo, hi);
+}
+
 // (m, s) += (m2, s2) for online log-sum-exp pairs (s = sum of exp(x - m)).
 __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
   const float mn = fmaxf(m, m2);
@@ -721,84 +738,74 @@ __global__ void __launch_bounds__(kThreads, 1)
         continue;
       }
       if constexpr (EPI == EPI_LSE) {
-        // This warp's 128-column block of its 32 rows, read from TMEM twice:
-        // first the block max m_b of the rounded logits (and the label's
-        // logit), then e = exp(x - m_b) 64 columns at a time: summed, packed,
-        // staged and TMA-stored.
+        // This warp's 128-column block of its 32 rows: two TMEM reads of 64
+        // columns, each rounded to the output type and packed in pairs (the
+        // accumulator is released right after); then the block max m_b (packed
+        // 16-bit max: the values are already rounded), the label's logit,
+        // e = exp(x - m_b) summed and re-packed, staged and TMA-stored.
         static_assert(sizeof(TOut) == 2 && BN == 256, "16-bit output, 256-column tiles");
         const int row = m0 + quarter * 32 + lane;
         const int64_t lab = row < g.M ? g.labels[row] : -1;
         const int c0 = n0 + half * 128;
         const int nvalid = g.vocab - c0;  // columns of this block below vocab (may be <= 0 or >= 128)
         const uint32_t t_blk = t_row + half * 128;
-        const int64_t li = lab - c0;
-        const bool has_label = li >= 0 && li < 128 && li < nvalid;
-        float mx = -INFINITY, xl = 0.f;
-#pragma unroll 1
-        for (int ch = 0; ch < 2; ++ch) {
+        uint32_t xp[64];  // the block's 128 rounded logits, two per word
+#pragma unroll
+        for (int h2 = 0; h2 < 2; ++h2) {
           uint32_t r[64];
-          tmem_ld_32cols_nowait(t_blk + ch * 64, r);
-          tmem_ld_32cols_nowait(t_blk + ch * 64 + 32, r + 32);
+          tmem_ld_32cols_nowait(t_blk + h2 * 64, r);
+          tmem_ld_32cols_nowait(t_blk + h2 * 64 + 32, r + 32);
           tmem_ld_wait();
-          // rounding is monotonic, so the max of the rounded values is the
-          // rounded max: one conversion per row instead of one per value
-          if (nvalid >= 128) {
 #pragma unroll
-            for (int k = 0; k < 64; ++k) mx = fmaxf(mx, __uint_as_float(r[k]));
-          } else {
+          for (int k = 0; k < 32; ++k)
+            xp[h2 * 32 + k] = pack2_rn<TOut>(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+        }
+        tc_fence_before();
+        mbar_arrive(tempty0 + 8 * acc);  // TMEM read: the MMA warp may reuse the accumulator
+        // columns at or past vocab become -inf
+        if (nvalid < 128) {
+          constexpr uint32_t kNegInf = std::is_same_v<TOut, __nv_bfloat16> ? 0xff80u : 0xfc00u;
 #pragma unroll
-            for (int k = 0; k < 64; ++k)
-              if (ch * 64 + k < nvalid) mx = fmaxf(mx, __uint_as_float(r[k]));
-          }
-          if (has_label && (li >> 6) == ch) {
-#pragma unroll
-            for (int k = 0; k < 64; ++k)
-              if (k == (int)(li & 63)) xl = __uint_as_float(r[k]);
+          for (int k = 0; k < 64; ++k) {
+            if (2 * k >= nvalid) xp[k] = (xp[k] & 0xffff0000u) | kNegInf;
+            if (2 * k + 1 >= nvalid) xp[k] = (xp[k] & 0x0000ffffu) | (kNegInf << 16);
           }
         }
-        if (mx != -INFINITY) mx = round_to<TOut>(mx);
-        if (has_label) g.xlabel[row] = round_to<TOut>(xl);
+        uint32_t m4[4] = {xp[0], xp[1], xp[2], xp[3]};
+#pragma unroll
+        for (int k = 4; k < 64; ++k) m4[k & 3] = max2_16<TOut>(m4[k & 3], xp[k]);
+        const uint32_t m2 = max2_16<TOut>(max2_16<TOut>(m4[0], m4[1]), max2_16<TOut>(m4[2], m4[3]));
+        const float mx = fmaxf(unpack_half<TOut>(m2, 0), unpack_half<TOut>(m2, 1));
+        const int64_t li = lab - c0;
+        if (li >= 0 && li < 128 && li < nvalid) {  // this block holds the row's label: keep its logit
+          float xl = 0.f;
+#pragma unroll
+          for (int k = 0; k < 64; ++k)
+            if ((int)(li >> 1) == k) xl = unpack_half<TOut>(xp[k], (int)(li & 1));
+          g.xlabel[row] = xl;
+        }
         const float nm = mx == -INFINITY ? 0.f : -mx * kLog2eF;
-        float sm = 0.f;
+        float sm4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < 64; ++k) {
+          const float e0 = ex2_fast(fmaf(unpack_half<TOut>(xp[k], 0), kLog2eF, nm));
+          const float e1 = ex2_fast(fmaf(unpack_half<TOut>(xp[k], 1), kLog2eF, nm));
+          sm4[k & 3] += e0 + e1;
+          xp[k] = pack_unit2<TOut>(e0, e1);
+        }
+        const float sm = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
+        if (row < g.M) g.stats[(int64_t)row * g.stats_ld + 2 * nt + half] = make_float2(mx, sm);
         uint8_t* buf = sOut + ew * 4096;
         const int y = m0 + quarter * 32;
-#pragma unroll 1
+#pragma unroll
         for (int ch = 0; ch < 2; ++ch) {
-          uint32_t r[64];
-          tmem_ld_32cols_nowait(t_blk + ch * 64, r);
-          tmem_ld_32cols_nowait(t_blk + ch * 64 + 32, r + 32);
-          tmem_ld_wait();
-          if (ch == 1) {  // last TMEM read of this tile by this warp
-            tc_fence_before();
-            mbar_arrive(tempty0 + 8 * acc);
-          }
-          uint32_t pk[32];
-          if (nvalid >= 128) {  // every column of the block counts
-#pragma unroll
-            for (int k = 0; k < 32; ++k) {
-              const uint32_t xr = pack2_rn<TOut>(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
-              const float e0 = ex2_fast(fmaf(unpack_half<TOut>(xr, 0), kLog2eF, nm));
-              const float e1 = ex2_fast(fmaf(unpack_half<TOut>(xr, 1), kLog2eF, nm));
-              sm += e0 + e1;
-              pk[k] = pack2_rn<TOut>(e0, e1);
-            }
-          } else {
-#pragma unroll
-            for (int k = 0; k < 32; ++k) {
-              const int c = ch * 64 + 2 * k;
-              const uint32_t xr = pack2_rn<TOut>(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
-              const float e0 = c < nvalid ? ex2_fast(fmaf(unpack_half<TOut>(xr, 0), kLog2eF, nm)) : 0.f;
-              const float e1 = c + 1 < nvalid ? ex2_fast(fmaf(unpack_half<TOut>(xr, 1), kLog2eF, nm)) : 0.f;
-              sm += e0 + e1;
-              pk[k] = pack2_rn<TOut>(e0, e1);
-            }
-          }
           if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) =
-                make_uint4(pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+                make_uint4(xp[ch * 32 + 4 * j], xp[ch * 32 + 4 * j + 1], xp[ch * 32 + 4 * j + 2],
+                           xp[ch * 32 + 4 * j + 3]);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
@@ -806,7 +813,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             bulk_commit();
           }
         }
-        if (row < g.M) g.stats[(int64_t)row * g.stats_ld + 2 * nt + half] = make_float2(mx, sm);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;

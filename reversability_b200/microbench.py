@@ -1,6 +1,7 @@
 """Isolated kernel microbenchmark and ncu driver.
 
     python -m reversability_b200.microbench [--only NAME[,NAME...]] [--iters N]
+    python -m reversability_b200.microbench --only head|attention --profile   (ncu launch sequence)
 
 Workload: 16,896 tokens x width 256 in bf16 (activations N(0,1), weights
 N(0,0.02)); RMSNorm fwd+bwd, SwiGLU fwd+bwd (gate/up 256->1024, i.e. u is
@@ -210,11 +211,51 @@ BENCHES = {"rmsnorm": bench_rmsnorm, "swiglu": bench_swiglu, "reconstruct": benc
            "mlp_gemms": bench_mlp_gemms, "head": bench_head, "attention": bench_attention}
 
 
+def profile_head():
+    """Eager launches for an ncu capture: twice (rk_head_fprop, rk_head_loss,
+    rk_head_dgrad, rk_head_wgrad) at cfg2; the GEMMs are launches 1, 3, 4 of
+    each round (gemm_tc_kernel), so `-k regex:gemm_tc_kernel -s 3 -c 3` takes
+    the second round's three."""
+    M, V = 29 * 512, 50257
+    g = torch.Generator(device="cpu").manual_seed(0)
+    hid = torch.randn(M, D, generator=g).cuda().bfloat16()
+    w = (torch.randn(V, D, generator=g) * 0.05).cuda().bfloat16()
+    labels = torch.randint(0, V, (M,), generator=g).cuda()
+    dw = torch.zeros(V, D, device="cuda")
+    for _ in range(2):
+        st = fn.head_fprop(hid, w, labels)
+        fn.head_loss(st, grad_scale=1.0 / M)
+        fn.head_dgrad(st, w)
+        fn.head_wgrad(st, hid, dw=dw, accumulate=True)
+    torch.cuda.synchronize()
+
+
+def profile_attention():
+    """Eager launches for an ncu capture: twice (forward, backward dQ, backward
+    dK/dV) at cfg2 (B=29, T=512, 8 heads of 32)."""
+    B, T, H = 29, 512, 8
+    qkv = torch.randn(B, T, 3 * D, device="cuda").bfloat16()
+    for _ in range(2):
+        o, lse = fn.attention_fwd(qkv, H)
+        fn.attention_bwd(qkv, o, torch.randn_like(o), lse, H)
+    torch.cuda.synchronize()
+
+
+PROFILES = {"head": profile_head, "attention": profile_attention}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=",".join(BENCHES))
     ap.add_argument("--iters", type=int, default=50)
+    ap.add_argument("--profile", action="store_true",
+                    help="run the eager launch sequence for an ncu capture instead of timing")
     args = ap.parse_args()
+    if args.profile:
+        for name in args.only.split(","):
+            PROFILES[name]()
+        print("ok", flush=True)
+        return
     hbm, tf, kind = peaks()
     for name in args.only.split(","):
         for bound, kname, work, us in BENCHES[name](args.iters):

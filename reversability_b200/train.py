@@ -155,6 +155,17 @@ class ReversibleTrainer:
         self.buckets = GradBuckets(self.layer_slices + [self.g_tok, self.g_pos, self.g_final], process_group,
                                    dev) if self.world > 1 else None
         self.graph = None
+        self.head_events = None
+
+    def time_head_fprop(self):
+        """Records CUDA events (graph-capturable) around each microstep's head
+        GEMM from now on; head_fprop_ms() reads the durations of the last update."""
+        self.head_events = [(torch.cuda.Event(enable_timing=True, external=True),
+                             torch.cuda.Event(enable_timing=True, external=True))
+                            for _ in range(self.s.accumulation)]
+
+    def head_fprop_ms(self) -> list[float]:
+        return [a.elapsed_time(b) for a, b in self.head_events] if self.head_events else []
 
     # ------------------------------------------------------------------ layout helpers
     def view(self, buf: torch.Tensor, name: str) -> torch.Tensor:
@@ -196,8 +207,13 @@ class ReversibleTrainer:
             # buffer receives exp(x - block max)), per-row loss, then the two
             # backward GEMMs form dlogits = (softmax - onehot) / update_targets
             # inside the GEMM
+            ev = self.head_events[m] if self.head_events is not None else None
+            if ev is not None:
+                ev[0].record()
             st = fn.head_fprop(hidden, self.tok_c, labels, expo=logits, stats=self.head_stats,
                                xlabel=self.head_xlabel)
+            if ev is not None:
+                ev[1].record()
             fn.head_loss(st, 1.0, self.inv_denominator, loss_rows=loss_rows, rowc=self.head_rowc,
                          fcoef=self.head_fcoef)
             self.loss_sum += loss_rows.sum()

@@ -199,6 +199,12 @@ RK_API int rk_attn_fwd(const void* qkv, int64_t ldq, void* out, int64_t ldo, flo
 RK_API int rk_attn_bwd(const void* qkv, int64_t ldq, const void* out, const void* dout, int64_t ldo,
                        const float* lse, float* dsum, void* dqkv, int64_t lddq, int64_t B, int64_t H, int64_t HD,
                        int64_t T, int dtype, void* stream);
+/* The backward in pieces (bf16/f16): piece 0 writes dsum = rowsum(dout*out),
+ * piece 1 dq and piece 2 dk|dv (both read dsum). Pieces 1 and 2 touch disjoint
+ * columns of dqkv and may run concurrently on two streams after piece 0. */
+RK_API int rk_attn_bwd_piece(int piece, const void* qkv, int64_t ldq, const void* out, const void* dout,
+                             int64_t ldo, const float* lse, float* dsum, void* dqkv, int64_t lddq, int64_t B,
+                             int64_t H, int64_t HD, int64_t T, int dtype, void* stream);
 
 /* ---------------------------------------------------------- Cross-entropy
  * Replaces F.cross_entropy(logits, labels, ignore_index=-100, reduction="sum")

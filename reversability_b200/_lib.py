@@ -46,6 +46,7 @@ SIGNATURES: dict[str, tuple] = {
     "rk_gemm_wgrad": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p, _i64, _p]),
     "rk_attn_fwd": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p]),
     "rk_attn_bwd": (_i, [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _p]),
+    "rk_attn_bwd_piece": (_i, [_i, _p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _p]),
     "rk_clip_adamw_workspace": (_i64, []),
     "rk_clip_adamw_prepare": (_i, [_p, _i64, _f, _f, _f, _f, _p, _i64, _p, _p]),
     "rk_adamw_step": (_i, [_p, _p, _p, _p, _p, _i, _i64, _p, _f, _f, _f, _p]),

@@ -254,7 +254,7 @@ __global__ void __launch_bounds__(128) bwd_dq_kernel(const T* __restrict__ qkv, 
                                                      const T* __restrict__ dout, const float* __restrict__ lse,
                                                      float* __restrict__ dsum, T* __restrict__ dqkv, int H,
                                                      int Tlen, int64_t ldq, int64_t ldo, int64_t lddq, float c_log2,
-                                                     float scale) {
+                                                     float scale, int have_dsum) {
   pdl_wait();  // inputs are the previous kernel's outputs
   constexpr int LD = HD + 8;
   extern __shared__ __align__(16) unsigned char dsm[];  // 6 tiles of 64 x LD
@@ -277,8 +277,9 @@ __global__ void __launch_bounds__(128) bwd_dq_kernel(const T* __restrict__ qkv, 
   load_tile<T, HD, LD, 128>(Vs0, base, ldq, 0, 2 * D + h * HD, Tlen);
   cp_async_commit();
 
-  // D = rowsum(dO * O) for this CTA's rows: 2 threads per row.
-  {
+  // D = rowsum(dO * O) for this CTA's rows: 2 threads per row (unless
+  // dsum_kernel has written it already).
+  if (!have_dsum) {
     const int r = threadIdx.x >> 1, half = threadIdx.x & 1;
     const int gr = q0 + r;
     float acc = 0.f;
@@ -350,6 +351,36 @@ __global__ void __launch_bounds__(128) bwd_dq_kernel(const T* __restrict__ qkv, 
     if (gr_lo < Tlen) *reinterpret_cast<uint32_t*>(out + (int64_t)gr_lo * lddq + c) = Mma<T>::pack(dq[i][0] * scale, dq[i][1] * scale);
     if (gr_hi < Tlen) *reinterpret_cast<uint32_t*>(out + (int64_t)gr_hi * lddq + c) = Mma<T>::pack(dq[i][2] * scale, dq[i][3] * scale);
   }
+}
+
+// ------------------------------------------------------------------ backward: D alone
+// D[b, h, t] = rowsum(dO * O) over the head's HD columns, one thread per
+// (row, head), so the dQ and dK/dV kernels can run side by side.
+template <typename T, int HD>
+__global__ void __launch_bounds__(256) dsum_kernel(const T* __restrict__ o, const T* __restrict__ dout,
+                                                   float* __restrict__ dsum, int H, int Tlen, int64_t rows,
+                                                   int64_t ldo) {
+  pdl_wait();  // inputs are the previous kernel's outputs
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // (b*T + t)*H + h
+  if (i >= rows * H) return;
+  const int64_t bt = i / H;
+  const int h = (int)(i - bt * H);
+  const T* orow = o + bt * ldo + h * HD;
+  const T* drow = dout + bt * ldo + h * HD;
+  // two halves summed separately, then added: the order bwd_dq_kernel uses,
+  // so both ways of producing D give the same bits
+  float acc[2] = {0.f, 0.f};
+#pragma unroll
+  for (int c = 0; c < HD; c += 8) {
+    const uint4 a = *reinterpret_cast<const uint4*>(orow + c);
+    const uint4 d = *reinterpret_cast<const uint4*>(drow + c);
+    const T* ae = reinterpret_cast<const T*>(&a);
+    const T* de = reinterpret_cast<const T*>(&d);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[c >= HD / 2] += Dt<T>::to_f(ae[e]) * Dt<T>::to_f(de[e]);
+  }
+  const int64_t b = bt / Tlen, t = bt - b * Tlen;
+  dsum[(b * H + h) * Tlen + t] = acc[0] + acc[1];
 }
 
 // ------------------------------------------------------------------ backward: dK, dV
@@ -632,11 +663,40 @@ int bwd_tc(const void* qkv, const void* o, const void* dout, const float* lse, f
   rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dkv_kernel<T, HD>), smem_dkv);
   rk_host::launch_k(bwd_dq_kernel<T, HD>, grid, 128, smem_dq, s, static_cast<const T*>(qkv), static_cast<const T*>(o),
                                             static_cast<const T*>(dout), lse, dsum, static_cast<T*>(dqkv), H, Tlen,
-                                            ldq, ldo, lddq, c_log2, scale);
+                                            ldq, ldo, lddq, c_log2, scale, 0);
   int st = rk_host::launch_status();
   if (st) return st;
   rk_host::launch_k(bwd_dkv_kernel<T, HD>, grid, 128, smem_dkv, s, static_cast<const T*>(qkv), static_cast<const T*>(dout), lse, dsum,
                                              static_cast<T*>(dqkv), H, Tlen, ldq, ldo, lddq, c_log2, scale);
+  return rk_host::launch_status();
+}
+
+// The backward in three pieces for callers that run dQ and dK/dV on two streams:
+// 0 = D (dsum_kernel), 1 = dQ (reading D), 2 = dK/dV.
+template <typename T, int HD>
+int bwd_piece(int piece, const void* qkv, const void* o, const void* dout, const float* lse, float* dsum, void* dqkv,
+              int B, int H, int Tlen, int64_t ldq, int64_t ldo, int64_t lddq, cudaStream_t s) {
+  dim3 grid((Tlen + BQ - 1) / BQ, B * H);
+  const float scale = 1.f / sqrtf((float)HD);
+  const float c_log2 = 1.4426950408889634f * scale;
+  constexpr int tile_bytes = 64 * (HD + 8) * (int)sizeof(T);
+  constexpr int smem_dq = 6 * tile_bytes;
+  constexpr int smem_dkv = 6 * tile_bytes + 4 * 64 * (int)sizeof(float);
+  if (piece == 0) {
+    const int64_t n = (int64_t)B * Tlen * H;
+    rk_host::launch_k(dsum_kernel<T, HD>, (unsigned)((n + 255) / 256), 256, 0, s, static_cast<const T*>(o),
+                      static_cast<const T*>(dout), dsum, H, Tlen, (int64_t)B * Tlen, ldo);
+  } else if (piece == 1) {
+    rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dq_kernel<T, HD>), smem_dq);
+    rk_host::launch_k(bwd_dq_kernel<T, HD>, grid, 128, smem_dq, s, static_cast<const T*>(qkv),
+                      static_cast<const T*>(o), static_cast<const T*>(dout), lse, dsum, static_cast<T*>(dqkv), H,
+                      Tlen, ldq, ldo, lddq, c_log2, scale, 1);
+  } else {
+    rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dkv_kernel<T, HD>), smem_dkv);
+    rk_host::launch_k(bwd_dkv_kernel<T, HD>, grid, 128, smem_dkv, s, static_cast<const T*>(qkv),
+                      static_cast<const T*>(dout), lse, dsum, static_cast<T*>(dqkv), H, Tlen, ldq, ldo, lddq,
+                      c_log2, scale);
+  }
   return rk_host::launch_status();
 }
 
@@ -706,4 +766,29 @@ extern "C" int rk_attn_bwd(const void* qkv, int64_t ldq, const void* out, const 
                     : bwd_tc<__nv_bfloat16, 64>(qkv, out, dout, lse, dsum, dqkv, (int)B, (int)H, (int)T, ldq, ldo, lddq, s);
   return HD == 32 ? bwd_tc<__half, 32>(qkv, out, dout, lse, dsum, dqkv, (int)B, (int)H, (int)T, ldq, ldo, lddq, s)
                   : bwd_tc<__half, 64>(qkv, out, dout, lse, dsum, dqkv, (int)B, (int)H, (int)T, ldq, ldo, lddq, s);
+}
+
+// Backward pieces (bf16/f16, head_dim 32 or 64): D, then dQ and dK/dV, which
+// may run concurrently on two streams once D is written. Same arguments and
+// layouts as rk_attn_bwd; `out` is needed by the D piece only.
+extern "C" int rk_attn_bwd_piece(int piece, const void* qkv, int64_t ldq, const void* out, const void* dout,
+                                 int64_t ldo, const float* lse, float* dsum, void* dqkv, int64_t lddq, int64_t B,
+                                 int64_t H, int64_t HD, int64_t T, int dtype, void* stream) {
+  if (piece < 0 || piece > 2 || !attn_args_ok(qkv, dout, B, H, HD, T) || !lse || !dsum || !dqkv ||
+      (piece == 0 && !out) || ldq < 3 * H * HD || ldo < H * HD || lddq < 3 * H * HD)
+    return RK_ERR_ARG;
+  if (B == 0 || T == 0) return RK_OK;
+  if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
+  if (!tc_layout_ok(qkv, dout, dqkv, ldq, ldo, HD) || (out && !rk_host::aligned(out, 16)) || lddq % 8)
+    return (HD == 32 || HD == 64) ? RK_ERR_ALIGN : RK_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == RK_BF16)
+    return HD == 32 ? bwd_piece<__nv_bfloat16, 32>(piece, qkv, out, dout, lse, dsum, dqkv, (int)B, (int)H, (int)T, ldq,
+                                                   ldo, lddq, s)
+                    : bwd_piece<__nv_bfloat16, 64>(piece, qkv, out, dout, lse, dsum, dqkv, (int)B, (int)H, (int)T, ldq,
+                                                   ldo, lddq, s);
+  return HD == 32 ? bwd_piece<__half, 32>(piece, qkv, out, dout, lse, dsum, dqkv, (int)B, (int)H, (int)T, ldq, ldo,
+                                          lddq, s)
+                  : bwd_piece<__half, 64>(piece, qkv, out, dout, lse, dsum, dqkv, (int)B, (int)H, (int)T, ldq, ldo,
+                                          lddq, s);
 }

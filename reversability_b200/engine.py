@@ -111,6 +111,9 @@ class LayerKernels:
         self.side = wgrad_stream
         self._held = []
         self._prev = None
+        # attention backward: dK/dV beside dQ on a stream of its own (the
+        # weight-gradient stream is FIFO and may hold queued GEMMs)
+        self.attn_side = torch.cuda.Stream(device=wgrad_stream.device) if wgrad_stream is not None else None
 
     def _wgrad(self, dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor):
         """dw += dy^T x, on the side stream when there is one."""
@@ -165,7 +168,8 @@ class LayerKernels:
         o2 = o.view(-1, o.shape[-1])
         do = fn.linear_dgrad(ga, lw.proj_c)
         self._wgrad(ga, o2, g.proj)
-        dqkv = fn.attention_bwd(qkv.view(self.B, self.T, -1), o, do.view(o.shape), lse, self.H)
+        dqkv = fn.attention_bwd(qkv.view(self.B, self.T, -1), o, do.view(o.shape), lse, self.H,
+                                dkv_stream=self.attn_side)
         dqkv2 = dqkv.view(-1, dqkv.shape[-1])
         self._wgrad(dqkv2, n1, g.qkv)
         dn1 = fn.linear_dgrad(dqkv2, lw.qkv_c)

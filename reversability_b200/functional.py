@@ -308,8 +308,12 @@ def attention_fwd(qkv: torch.Tensor, n_heads: int, out: torch.Tensor | None = No
     return o, lse
 
 
-def attention_bwd(qkv: torch.Tensor, o: torch.Tensor, do: torch.Tensor, lse: torch.Tensor, n_heads: int):
-    """Returns dqkv [B, T, 3*D] for the causal attention of attention_fwd."""
+def attention_bwd(qkv: torch.Tensor, o: torch.Tensor, do: torch.Tensor, lse: torch.Tensor, n_heads: int,
+                  dkv_stream: "torch.cuda.Stream | None" = None):
+    """Returns dqkv [B, T, 3*D] for the causal attention of attention_fwd.
+    With `dkv_stream` (16-bit inputs) the dK/dV kernel runs on that stream
+    beside the dQ kernel, after a small kernel has written D = rowsum(dO*O);
+    the current stream waits for both before returning."""
     require_cuda(qkv, o, do, lse)
     B, T, three_d = qkv.shape
     D = three_d // 3
@@ -320,9 +324,21 @@ def attention_bwd(qkv: torch.Tensor, o: torch.Tensor, do: torch.Tensor, lse: tor
             raise ValueError("dout must share the layout of out")
     dqkv = torch.empty_like(qkv)
     dsum = torch.empty((B, n_heads, T), device=qkv.device, dtype=torch.float32)
-    _lib.call("rk_attn_bwd", qkv.data_ptr(), qkv.stride(1), o.data_ptr(), do.data_ptr(), o.stride(1),
-              lse.data_ptr(), dsum.data_ptr(), dqkv.data_ptr(), dqkv.stride(1), B, n_heads, D // n_heads, T,
-              _lib.code(qkv.dtype), _lib.stream_ptr())
+    args = (qkv.data_ptr(), qkv.stride(1), o.data_ptr(), do.data_ptr(), o.stride(1), lse.data_ptr(), dsum.data_ptr(),
+            dqkv.data_ptr(), dqkv.stride(1), B, n_heads, D // n_heads, T, _lib.code(qkv.dtype))
+    if dkv_stream is None or qkv.dtype not in _TC_DTYPES:
+        _lib.call("rk_attn_bwd", *args, _lib.stream_ptr())
+        return dqkv
+    main = torch.cuda.current_stream()
+    _lib.call("rk_attn_bwd_piece", 0, *args, main.cuda_stream)
+    ready = torch.cuda.Event()
+    ready.record(main)
+    dkv_stream.wait_event(ready)
+    _lib.call("rk_attn_bwd_piece", 2, *args, dkv_stream.cuda_stream)
+    _lib.call("rk_attn_bwd_piece", 1, *args, main.cuda_stream)
+    done = torch.cuda.Event()
+    done.record(dkv_stream)
+    main.wait_event(done)
     return dqkv
 
 

@@ -234,6 +234,21 @@ def test_attention_deterministic():
     assert torch.equal(fn.attention_bwd(qkv, o1, do, l1, 8), fn.attention_bwd(qkv, o1, do, l1, 8))
 
 
+@pytest.mark.parametrize("bthd", [(4, 512, 8, 32), (3, 17, 2, 32), (1, 130, 4, 64)])
+def test_attention_bwd_two_streams_bitwise(bthd):
+    """dK/dV on a second stream beside dQ (D from its own kernel) gives the
+    same bits as the one-stream backward."""
+    from reversability_b200 import functional as fn
+    B, T, H, HD = bthd
+    qkv = torch.randn(B, T, 3 * H * HD, device=DEV).bfloat16()
+    o, lse = fn.attention_fwd(qkv, H)
+    do = torch.randn_like(o)
+    side = torch.cuda.Stream()
+    a = fn.attention_bwd(qkv, o, do, lse, H)
+    b = fn.attention_bwd(qkv, o, do, lse, H, dkv_stream=side)
+    assert torch.equal(a, b)
+
+
 # ------------------------------------------------------------------ clip + AdamW
 @pytest.mark.parametrize("n,max_norm", [(20_340_736, 1.0), (1001, 1e9), (4099, 0.5)])
 def test_clip_adamw_matches_torch(n, max_norm):

@@ -35,6 +35,11 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 METRIC = "train targets/sec (midpoint, 20.3M model)"
+
+
+def metric_name(method: str) -> str:
+    """BASELINE's metric; the Euler configuration (cfg3) names its recurrence."""
+    return METRIC if method == "midpoint" else METRIC.replace("midpoint", method)
 UNIT = "targets/s"
 FLOP_PER_TARGET = 143_255_040  # 4 x body (fwd + attention) + 3 x head, cfg2 (20.3M model)
 
@@ -192,7 +197,7 @@ def reference_arm(args):
     targets = sum(step() for _ in range(args.steps))
     el = time.perf_counter() - t0
     value = targets / el
-    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+    line = {"metric": metric_name(args.method), "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": el / max(args.steps, 1) * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": config_block(args, world), "impl": "reference",
@@ -402,7 +407,7 @@ def main():
         roof["peak_source"] = peak_kind
         model_flops = value * FLOP_PER_TARGET / world / 1e12
         line = {
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": metric_name(args.method), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": config_block(args, world),

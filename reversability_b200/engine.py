@@ -111,9 +111,17 @@ class LayerKernels:
         self.side = wgrad_stream
         self._held = []
         self._prev = None
+        self._side_used = False
         # attention backward: dK/dV beside dQ on a stream of its own (the
         # weight-gradient stream is FIFO and may hold queued GEMMs)
         self.attn_side = torch.cuda.Stream(device=wgrad_stream.device) if wgrad_stream is not None else None
+        # midpoint backward: the MLP down-projection forward and the state
+        # reconstruction (needed only by the next layer) run here beside the
+        # attention VJP; layer_done() joins them
+        self.aux = torch.cuda.Stream(device=wgrad_stream.device) if wgrad_stream is not None else None
+        self._aux_done = None
+        self._aux_held = []
+        self._aux_used = False
 
     def _wgrad(self, dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor):
         """dw += dy^T x, on the side stream when there is one."""
@@ -126,12 +134,47 @@ class LayerKernels:
         with torch.cuda.stream(self.side):
             fn.linear_wgrad(dy, x, dw=dw, accumulate=True)
         self._held += [dy, x]
+        self._side_used = True
+
+    def _on_aux(self, *held):
+        """Context for work on the aux stream after the compute stream's current
+        work; `held` stay referenced until layer_done() joins the aux stream."""
+        ready = torch.cuda.Event()
+        ready.record()
+        self.aux.wait_event(ready)
+        self._aux_held += list(held)
+        self._aux_used = True
+        return torch.cuda.stream(self.aux)
+
+    def side_work(self):
+        """Context for caller work on the weight-gradient stream (after the
+        compute stream's current work); joined by the next sync()."""
+        ready = torch.cuda.Event()
+        ready.record()
+        self.side.wait_event(ready)
+        self._side_used = True
+        return torch.cuda.stream(self.side)
+
+    def reset_streams(self):
+        """Forgets pending cross-stream events (after an aborted graph capture,
+        whose events cannot be waited on outside it)."""
+        self._prev = None
+        self._held = []
+        self._aux_done = None
+        self._aux_held = []
+        self._aux_used = False
+        self._side_used = False
 
     def layer_done(self):
         """Marks the end of one layer's backward: the compute stream waits for
-        the previous layer's weight gradients and releases their operands."""
+        the aux stream (this layer's reconstruction) and for the previous
+        layer's weight gradients, and releases their operands."""
         if self.side is None:
             return
+        if self._aux_done is not None:
+            torch.cuda.current_stream().wait_event(self._aux_done)
+            self._aux_done = None
+            self._aux_held = []
         done = torch.cuda.Event()
         done.record(self.side)
         if self._prev is not None:
@@ -140,10 +183,20 @@ class LayerKernels:
         self._held = []
 
     def sync(self):
-        """Joins the side stream into the compute stream (all weight gradients final)."""
+        """Joins the side streams into the compute stream (all weight gradients
+        final). A stream is joined only if work was put on it since the last
+        join: inside a graph capture, waiting on a stream outside the capture
+        would invalidate it."""
         if self.side is None:
             return
-        torch.cuda.current_stream().wait_stream(self.side)
+        if self._aux_used:
+            torch.cuda.current_stream().wait_stream(self.aux)
+        self._aux_done = None
+        self._aux_held = []
+        self._aux_used = False
+        if self._side_used:
+            torch.cuda.current_stream().wait_stream(self.side)
+        self._side_used = False
         self._prev = None
         self._held = []
 
@@ -208,11 +261,13 @@ class LayerKernels:
     def mlp_forward_vjp(self, lw: LayerWeights, g: LayerGrads, gm: torch.Tensor, y: torch.Tensor | None = None,
                         x: torch.Tensor | None = None, a: torch.Tensor | None = None,
                         residual: torch.Tensor | None = None, lp_add: torch.Tensor | None = None,
-                        want_lp: bool = False):
+                        want_lp: bool = False, m_on_aux: bool = False):
         """M(y) and its VJP for cotangent gm, tile by tile (each tile's forward is
         followed at once by its VJP). Returns (m, dx_out, lp_out) where
         dx_out = M^T gm + residual and lp_out is the low-precision epilogue output
-        of rk_rmsnorm_bwd_fused (round(lp_add + round(M^T gm)) or round(dx_out))."""
+        of rk_rmsnorm_bwd_fused (round(lp_add + round(M^T gm)) or round(dx_out)).
+        With m_on_aux (and an aux stream) m is computed on the aux stream: the
+        caller must consume it there or after layer_done()."""
         n2, ysum, rstd2 = self._mlp_norm(lw, y, x, a, save=True)
         M, d = n2.shape
         m = torch.empty((M, lw.down.shape[0]), device=n2.device, dtype=self.cd)
@@ -225,7 +280,11 @@ class LayerKernels:
             else:
                 u = fn.linear_fwd(n2[s:e], lw.up_c)
                 hg = fn.swiglu_fwd(u)
-            fn.linear_fwd(hg, lw.down_c, out=m[s:e])
+            if m_on_aux and self.aux is not None:
+                with self._on_aux(hg, m):
+                    fn.linear_fwd(hg, lw.down_c, out=m[s:e])
+            else:
+                fn.linear_fwd(hg, lw.down_c, out=m[s:e])
             gm_t = gm[s:e]
             dh = fn.linear_dgrad(gm_t, lw.down_c)
             self._wgrad(gm_t, hg, g.down)
@@ -267,8 +326,16 @@ class LayerKernels:
         a, sa = self.attn_forward(lw, x, save=True)
         gF = fn.cast_scale(dq, self.cd, 2.0 * h)
         # dxacc = M^T gF + dp ; da = round(gF + round(M^T gF)) for the attention VJP
-        m, dxacc, da = self.mlp_forward_vjp(lw, g, gF, x=x, a=a, residual=dp, lp_add=gF, want_lp=True)
-        prev_p = fn.reconstruct_midpoint_sum(q, a, m, 2.0 * h)
+        m, dxacc, da = self.mlp_forward_vjp(lw, g, gF, x=x, a=a, residual=dp, lp_add=gF, want_lp=True,
+                                            m_on_aux=True)
+        if self.aux is not None:  # beside the attention VJP; joined in layer_done()
+            prev_p = torch.empty_like(q)
+            with self._on_aux(q, a, m, prev_p):
+                fn.reconstruct_midpoint_sum(q, a, m, 2.0 * h, out=prev_p)
+                self._aux_done = torch.cuda.Event()
+                self._aux_done.record(self.aux)
+        else:
+            prev_p = fn.reconstruct_midpoint_sum(q, a, m, 2.0 * h)
         del m, gF
         dq_new = self.attn_vjp(lw, g, x, sa, da, residual=dxacc)
         return prev_p, x, dq, dq_new

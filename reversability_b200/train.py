@@ -217,18 +217,14 @@ class ReversibleTrainer:
             fn.head_loss(st, 1.0, self.inv_denominator, loss_rows=loss_rows, rowc=self.head_rowc,
                          fcoef=self.head_fcoef)
             self.loss_sum += loss_rows.sum()
-            side = kern.side
-            if side is not None:
+            if kern.side is not None:
                 # the head weight gradient runs beside the dgrad and the
                 # reverse sweep; the sweep's final join (stack_backward) orders
                 # it before the embedding backward, which also adds into g_tok
-                ready = torch.cuda.Event()
-                ready.record()
-                side.wait_event(ready)
-                with torch.cuda.stream(side):
+                with kern.side_work():
                     fn.head_wgrad(st, hidden, dw=self.g_tok, accumulate=True)
             dhidden = fn.head_dgrad(st, self.tok_c)
-            if side is None:
+            if kern.side is None:
                 fn.head_wgrad(st, hidden, dw=self.g_tok, accumulate=True)
         else:
             fn.linear_fwd(hidden, self.tok_c, out=logits)
@@ -304,6 +300,11 @@ class ReversibleTrainer:
                 self._update_body()
         torch.cuda.current_stream().wait_stream(side)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
-            self._update_body()
+        try:
+            with torch.cuda.graph(self.graph):
+                self._update_body()
+        except Exception:
+            self.graph = None
+            self.kern.reset_streams()
+            raise
         return self.graph

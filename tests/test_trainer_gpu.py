@@ -88,7 +88,10 @@ def test_tiled_mlp_trainer_matches_untiled():
                      float((a.flat - init).double().square().sum())) <= 0.01
 
 
-def test_graph_replay_equals_eager_update():
+@pytest.mark.parametrize("method", ["midpoint", "euler"])
+def test_graph_replay_equals_eager_update(method):
+    """The captured update (side streams for weight gradients, attention dK/dV
+    and the midpoint reconstruction included) replays to the eager bits."""
     import reversability_b200 as rb
     from reversability_b200 import data as rdata
     from reversability_b200.train import ReversibleTrainer, TrainSettings
@@ -98,7 +101,7 @@ def test_graph_replay_equals_eager_update():
     def make():
         torch.manual_seed(1337)
         s = TrainSettings(batch_size=B, sequence_length=T, accumulation=acc)
-        return ReversibleTrainer(rb.ReversibleLM(rb.ModelConfig(**WIDE), "midpoint").to(DEV), s)
+        return ReversibleTrainer(rb.ReversibleLM(rb.ModelConfig(**WIDE), method).to(DEV), s)
 
     eager, graphed = make(), make()
     batches, targets = rdata.update_batches(stream, 0, 0, 1, B, T, acc, len(stream) - 1)

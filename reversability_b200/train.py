@@ -61,6 +61,7 @@ class TrainSettings:
     mlp_tokens: int = 0
     fused_head: bool = True  # bf16/f16: cross-entropy inside the head GEMMs (rk_head_*)
     overlap_wgrad: bool = True  # layer weight gradients on a side stream during the reverse sweep
+    overlap_forward: bool = True  # microstep m+1's forward sweep beside microstep m's backward
 
 
 def learning_rate(s: TrainSettings, committed: int, update_targets: int) -> float:
@@ -143,6 +144,7 @@ class ReversibleTrainer:
         self.inv_denominator = torch.ones((), device=dev, dtype=F32)
         self.loss_sum = torch.zeros((), device=dev, dtype=F32)
         side = torch.cuda.Stream(device=dev) if (dev.type == "cuda" and settings.overlap_wgrad) else None
+        self.fwd_stream = torch.cuda.Stream(device=dev) if (dev.type == "cuda" and settings.overlap_forward) else None
         self.kern = engine.LayerKernels(self.cfg.n_heads, B, T, self.cd, settings.mlp_tokens, wgrad_stream=side)
         # AdamW state (flat, fp32) and the device scalar block of rk_clip_adamw_prepare
         self.exp_avg = torch.zeros_like(self.flat)
@@ -189,13 +191,17 @@ class ReversibleTrainer:
         self.inv_denominator.fill_(1.0 / update_targets)
 
     # ------------------------------------------------------------------ one microstep
-    def _microstep(self, m: int, last: bool):
+    def _forward_states(self, m: int):
+        """Microstep m's embedding and reversible forward sweep: the final (p, q)."""
+        x = fn.embedding_fwd(self.ids[m], self.tok, self.pos)
+        return engine.stack_forward(self.kern, self.layers, x, x, self.model.method, self.model.step_size)
+
+    def _microstep(self, m: int, last: bool, states=None):
         cfg, s, kern = self.cfg, self.s, self.kern
         B, T, d = s.batch_size, s.sequence_length, cfg.d_model
         ids = self.ids[m]
         labels = self.labels[m].reshape(-1)
-        x = fn.embedding_fwd(ids, self.tok, self.pos)
-        p, q = engine.stack_forward(kern, self.layers, x, x, self.model.method, self.model.step_size)
+        p, q = states if states is not None else self._forward_states(m)
         out = q if self.model.method == "midpoint" else p
         eps_f = self.model.final_norm.eps if self.model.final_norm.eps is not None else torch.finfo(F32).eps
         hidden, rstd_f = fn.rmsnorm_fwd(out, self.final_w, eps_f, out_dtype=self.cd)
@@ -252,8 +258,30 @@ class ReversibleTrainer:
     def _update_body(self):
         self.gflat.zero_()
         self.loss_sum.zero_()
-        for m in range(self.s.accumulation):
-            self._microstep(m, last=(m == self.s.accumulation - 1))
+        acc = self.s.accumulation
+        if self.fwd_stream is None or acc == 1:
+            for m in range(acc):
+                self._microstep(m, last=(m == acc - 1))
+        else:
+            # Microstep m+1's forward sweep (weights are fixed within the
+            # update) runs on its own stream beside microstep m's head and
+            # reverse sweep; its final states stay referenced until the join.
+            main = torch.cuda.current_stream()
+            states = self._forward_states(0)
+            for m in range(acc):
+                nxt = None
+                if m + 1 < acc:
+                    ready = torch.cuda.Event()
+                    ready.record(main)
+                    self.fwd_stream.wait_event(ready)
+                    with torch.cuda.stream(self.fwd_stream):
+                        nxt = self._forward_states(m + 1)
+                    done = torch.cuda.Event()
+                    done.record(self.fwd_stream)
+                self._microstep(m, last=(m == acc - 1), states=states)
+                if nxt is not None:
+                    main.wait_event(done)
+                states = nxt
         if self.world > 1:
             n = len(self.layers)
             for i in range(n, n + 3):

@@ -93,12 +93,13 @@ RK_API int rk_add_rmsnorm_fwd(const float* x, const void* a, int a_dtype, const 
  * cotangent bookkeeping fused into its epilogue: dx_out = dx + residual
  * (residual may be NULL); if lp_out is not NULL it receives, in lp_dtype,
  * round(lp_add + round(dx)) when lp_add is given (the low-precision sum
- * autograd forms when a bf16 tensor has two consumers) or round(dx_out)
- * otherwise. Workspace as rk_rmsnorm_bwd. */
+ * autograd forms when a bf16 tensor has two consumers) or
+ * round(round(dx_out) * lp_scale) otherwise (rk_cast_scale of the total;
+ * lp_scale = 1 is the plain cast). Workspace as rk_rmsnorm_bwd. */
 RK_API int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float* rstd, const void* dy, int dy_dtype,
-                                const float* residual, const void* lp_add, void* lp_out, int lp_dtype, float* dx_out,
-                                float* dw, int accumulate_dw, float* dw_partial, int64_t workspace_bytes,
-                                int64_t rows, int64_t width, void* stream);
+                                const float* residual, const void* lp_add, void* lp_out, int lp_dtype, float lp_scale,
+                                float* dx_out, float* dw, int accumulate_dw, float* dw_partial,
+                                int64_t workspace_bytes, int64_t rows, int64_t width, void* stream);
 
 /* Allocation-free rk_rmsnorm_bwd. It has no counterpart in the reference: it
  * exists for callers that cannot supply device workspace — foreign-function

@@ -233,12 +233,13 @@ __global__ void __launch_bounds__(256) add_rmsnorm_fwd_kernel(const float* __res
 //   dx_out = dx + residual                         (fp32; residual may be NULL)
 //   LP == 1: lp_out = round(lp_add + round(dx))    (the bf16 sum autograd forms
 //            when a bf16 tensor feeds two consumers)
-//   LP == 2: lp_out = round(dx_out)                (cast of the total)
+//   LP == 2: lp_out = round(round(dx_out) * lp_scale)  (rk_cast_scale of the total: the
+//                                                       next layer's round(2h * dq) in the sweep)
 template <typename Tg, typename Tlp, int NV, bool RES, int LP>
 __global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(
     const float* __restrict__ x, const float* __restrict__ w, const float* __restrict__ rstd, const Tg* __restrict__ dy,
     const float* __restrict__ residual, const Tlp* __restrict__ lp_add, float* __restrict__ dx_out,
-    Tlp* __restrict__ lp_out, float* __restrict__ partial, int64_t rows, int width) {
+    Tlp* __restrict__ lp_out, float* __restrict__ partial, int64_t rows, int width, float lp_scale) {
   pdl_wait();  // inputs are the previous kernel's outputs
   constexpr int V = 4;
   extern __shared__ float red[];  // [8][width]
@@ -294,7 +295,7 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(
         }
         if constexpr (LP == 2) {
 #pragma unroll
-          for (int e = 0; e < V; ++e) lp[e] = o[e];
+          for (int e = 0; e < V; ++e) lp[e] = __fmul_rn(round_to<Tlp>(o[e]), lp_scale);  // as rk_cast_scale
         }
         store_vec<float, V>(dx_out + base + c, o);
         if constexpr (LP != 0) store_vec<Tlp, V>(lp_out + base + c, lp);
@@ -487,7 +488,7 @@ int add_fwd_typed(const float* x, const void* a, const float* w, void* y, float*
 template <typename Tg, typename Tlp, bool RES, int LP>
 int bwd_fused_nv(const float* x, const float* w, const float* rstd, const void* dy, const float* residual,
                  const void* lp_add, float* dx_out, void* lp_out, float* partial, int parts, int64_t rows, int width,
-                 cudaStream_t s) {
+                 float lp_scale, cudaStream_t s) {
   const int nv = (width + 127) / 128;
   const size_t smem = (size_t)8 * width * sizeof(float);
   auto G = static_cast<const Tg*>(dy);
@@ -497,7 +498,7 @@ int bwd_fused_nv(const float* x, const float* w, const float* rstd, const void* 
   do {                                                                                                      \
     auto k = rmsnorm_bwd_fused_kernel<Tg, Tlp, N, RES, LP>;                                                 \
     if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)smem);          \
-    rk_host::launch_k(k, parts, 256, smem, s, x, w, rstd, G, residual, LA, dx_out, LO, partial, rows, width);              \
+    rk_host::launch_k(k, parts, 256, smem, s, x, w, rstd, G, residual, LA, dx_out, LO, partial, rows, width, lp_scale);    \
   } while (0)
   if (nv <= 1) RK_BF(1);
   else if (nv <= 2) RK_BF(2);
@@ -511,13 +512,13 @@ int bwd_fused_nv(const float* x, const float* w, const float* rstd, const void* 
 template <typename Tg, typename Tlp>
 int bwd_fused_modes(const float* x, const float* w, const float* rstd, const void* dy, const float* residual,
                     const void* lp_add, float* dx_out, void* lp_out, float* partial, int parts, int64_t rows,
-                    int width, cudaStream_t s) {
+                    int width, float lp_scale, cudaStream_t s) {
   const bool res = residual != nullptr;
   const int lp = lp_out == nullptr ? 0 : (lp_add != nullptr ? 1 : 2);
 #define RK_M(R, L)                                                                                           \
   if (res == R && lp == L)                                                                                   \
     return bwd_fused_nv<Tg, Tlp, R, L>(x, w, rstd, dy, residual, lp_add, dx_out, lp_out, partial, parts, rows, \
-                                       width, s);
+                                       width, lp_scale, s);
   RK_M(false, 0) RK_M(false, 1) RK_M(false, 2) RK_M(true, 0) RK_M(true, 1) RK_M(true, 2)
 #undef RK_M
   return RK_ERR_ARG;
@@ -545,7 +546,7 @@ extern "C" int rk_add_rmsnorm_fwd(const float* x, const void* a, int a_dtype, co
 
 extern "C" int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float* rstd, const void* dy, int dy_dtype,
                                     const float* residual, const void* lp_add, void* lp_out, int lp_dtype,
-                                    float* dx_out, float* dw, int accumulate_dw, float* dw_partial,
+                                    float lp_scale, float* dx_out, float* dw, int accumulate_dw, float* dw_partial,
                                     int64_t workspace_bytes, int64_t rows, int64_t width, void* stream) {
   if (!x || !w || !rstd || !dy || !dx_out || !dw || !dw_partial || rows < 0 || width <= 0) return RK_ERR_ARG;
   if (lp_add && !lp_out) return RK_ERR_ARG;
@@ -566,12 +567,13 @@ extern "C" int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float*
   const int lpd = lp_out ? lp_dtype : dy_dtype;
   if (dy_dtype == RK_BF16 && lpd == RK_BF16)
     st = bwd_fused_modes<__nv_bfloat16, __nv_bfloat16>(x, w, rstd, dy, residual, lp_add, dx_out, lp_out, dw_partial,
-                                                      parts, rows, W, s);
+                                                      parts, rows, W, lp_scale, s);
   else if (dy_dtype == RK_F16 && lpd == RK_F16)
     st = bwd_fused_modes<__half, __half>(x, w, rstd, dy, residual, lp_add, dx_out, lp_out, dw_partial, parts, rows, W,
-                                        s);
+                                        lp_scale, s);
   else if (dy_dtype == RK_F32 && lpd == RK_F32)
-    st = bwd_fused_modes<float, float>(x, w, rstd, dy, residual, lp_add, dx_out, lp_out, dw_partial, parts, rows, W, s);
+    st = bwd_fused_modes<float, float>(x, w, rstd, dy, residual, lp_add, dx_out, lp_out, dw_partial, parts, rows, W,
+                                       lp_scale, s);
   else
     return RK_ERR_DTYPE;
   if (st != RK_OK) return st;

@@ -31,13 +31,18 @@ class GradBuckets:
         self.pending = []
         self.launched = []
 
-    def launch(self, i: int):
+    def launch(self, i: int, after=None):
+        """All-reduces bucket i after the compute stream's current work, or after
+        the given CUDA events (the streams that produced the bucket)."""
         t = self.slices[i]
         self.launched.append(i)
         if self.cuda:
-            ev = torch.cuda.Event()
-            ev.record(torch.cuda.current_stream(t.device))
-            self.comm.wait_event(ev)
+            if after is None:
+                ev = torch.cuda.Event()
+                ev.record(torch.cuda.current_stream(t.device))
+                after = [ev]
+            for ev in after:
+                self.comm.wait_event(ev)
             with torch.cuda.stream(self.comm):
                 dist.all_reduce(t, group=self.group)
         else:

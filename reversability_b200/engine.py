@@ -200,6 +200,20 @@ class LayerKernels:
         self._prev = None
         self._held = []
 
+    def grads_ready(self):
+        """Events after which the layer just finished (layer_done) has final
+        weight gradients: one on the compute stream (norm weights, joined
+        attention and aux work) and one on the weight-gradient stream. A
+        consumer on another stream waits on these instead of the compute stream
+        joining the weight-gradient queue."""
+        main = torch.cuda.Event()
+        main.record()
+        if self.side is None or not self._side_used:
+            return [main]
+        side = torch.cuda.Event()
+        side.record(self.side)
+        return [main, side]
+
     @staticmethod
     def _eps(eps):
         return eps if eps is not None else torch.finfo(F32).eps
@@ -214,9 +228,11 @@ class LayerKernels:
         return a, ((n1, rstd1, qkv, o, lse) if save else None)
 
     def attn_vjp(self, lw: LayerWeights, g: LayerGrads, x: torch.Tensor, saved, ga: torch.Tensor,
-                 residual: torch.Tensor | None = None) -> torch.Tensor:
+                 residual: torch.Tensor | None = None, lp_scale: float | None = None):
         """dx (fp32) of A at x for cotangent ga (cd), plus `residual` if given
-        (added in the norm's epilogue); accumulates weight grads."""
+        (added in the norm's epilogue); accumulates weight grads. With lp_scale
+        it returns (dx, round(round(dx) * lp_scale)) in cd, the cast_scale of dx
+        formed in the same epilogue."""
         n1, rstd1, qkv, o, lse = saved
         o2 = o.view(-1, o.shape[-1])
         do = fn.linear_dgrad(ga, lw.proj_c)
@@ -226,8 +242,11 @@ class LayerKernels:
         dqkv2 = dqkv.view(-1, dqkv.shape[-1])
         self._wgrad(dqkv2, n1, g.qkv)
         dn1 = fn.linear_dgrad(dqkv2, lw.qkv_c)
-        dx, _ = fn.rmsnorm_bwd_fused(x, lw.attn_norm, rstd1, dn1, g.attn_norm, residual=residual)
-        return dx
+        if lp_scale is None:
+            dx, _ = fn.rmsnorm_bwd_fused(x, lw.attn_norm, rstd1, dn1, g.attn_norm, residual=residual)
+            return dx
+        return fn.rmsnorm_bwd_fused(x, lw.attn_norm, rstd1, dn1, g.attn_norm, residual=residual,
+                                    lp_dtype=self.cd, lp_scale=lp_scale)
 
     # ---------------------------------------------------------- MLP sublayer
     def _tiles(self, M):
@@ -319,12 +338,15 @@ class LayerKernels:
         m = self.mlp_forward(lw, y=nq)
         return fn.reconstruct_midpoint(p, m, -1.0), nq
 
-    def backward_midpoint(self, lw, g: LayerGrads, p, q, dp, dq, h):
+    def backward_midpoint(self, lw, g: LayerGrads, p, q, dp, dq, h, gF=None, carry=False):
         """Reconstructs (p_{n-1}, q_{n-1}) and returns them with their cotangents.
-        dp may be None (a zero cotangent)."""
+        dp may be None (a zero cotangent). gF = round(2h * round(dq)) when the
+        previous layer's epilogue formed it; with carry the result gains the next
+        layer's gF, formed in this layer's attention-norm epilogue."""
         x = p
         a, sa = self.attn_forward(lw, x, save=True)
-        gF = fn.cast_scale(dq, self.cd, 2.0 * h)
+        if gF is None:
+            gF = fn.cast_scale(dq, self.cd, 2.0 * h)
         # dxacc = M^T gF + dp ; da = round(gF + round(M^T gF)) for the attention VJP
         m, dxacc, da = self.mlp_forward_vjp(lw, g, gF, x=x, a=a, residual=dp, lp_add=gF, want_lp=True,
                                             m_on_aux=True)
@@ -337,12 +359,16 @@ class LayerKernels:
         else:
             prev_p = fn.reconstruct_midpoint_sum(q, a, m, 2.0 * h)
         del m, gF
-        dq_new = self.attn_vjp(lw, g, x, sa, da, residual=dxacc)
-        return prev_p, x, dq, dq_new
+        if not carry:
+            return prev_p, x, dq, self.attn_vjp(lw, g, x, sa, da, residual=dxacc)
+        dq_new, gF_next = self.attn_vjp(lw, g, x, sa, da, residual=dxacc, lp_scale=2.0 * h)
+        return prev_p, x, dq, dq_new, gF_next
 
-    def backward_euler(self, lw, g: LayerGrads, p, q, dp, dq):
-        """dq may be None (a zero cotangent)."""
-        gm = fn.cast_scale(dp, self.cd, 1.0)
+    def backward_euler(self, lw, g: LayerGrads, p, q, dp, dq, gm=None, carry=False):
+        """dq may be None (a zero cotangent). gm = round(dp) when the previous
+        layer's epilogue formed it; with carry the result gains the next layer's gm."""
+        if gm is None:
+            gm = fn.cast_scale(dp, self.cd, 1.0)
         # dq_eff = dq' + M^T round(dp'); ga = round(dq_eff)
         m, dq_eff, ga = self.mlp_forward_vjp(lw, g, gm, y=q, residual=dq, want_lp=True)
         prev_p = fn.reconstruct_euler(p, m)
@@ -350,8 +376,10 @@ class LayerKernels:
         a, sa = self.attn_forward(lw, prev_p, save=True)
         prev_q = fn.reconstruct_euler(q, a)
         del a
-        dp_new = self.attn_vjp(lw, g, prev_p, sa, ga, residual=dp)
-        return prev_p, prev_q, dp_new, dq_eff
+        if not carry:
+            return prev_p, prev_q, self.attn_vjp(lw, g, prev_p, sa, ga, residual=dp), dq_eff
+        dp_new, gm_next = self.attn_vjp(lw, g, prev_p, sa, ga, residual=dp, lp_scale=1.0)
+        return prev_p, prev_q, dp_new, dq_eff, gm_next
 
 
 def compute_dtype(amp_enabled: bool, amp_dtype: torch.dtype, state_dtype: torch.dtype) -> torch.dtype:
@@ -367,16 +395,19 @@ def stack_forward(kern: LayerKernels, layers, p, q, method: str, h: float):
 
 def stack_backward(kern: LayerKernels, layers, grads, p, q, dp, dq, method: str, h: float, on_layer_done=None):
     """Reverse sweep over all layers; grads[i] receives layer i's weight grads.
-    on_layer_done(i) is called after layer i's gradients are complete (used to
-    launch that layer's data-parallel gradient bucket)."""
+    on_layer_done(i, events) is called once layer i's backward is issued; its
+    weight gradients are final after `events` (used to launch that layer's
+    data-parallel gradient bucket on a communication stream)."""
+    g_lp = None  # the next layer's low-precision cotangent, formed in the previous epilogue
     for i in reversed(range(len(layers))):
         if method == "midpoint":
-            p, q, dp, dq = kern.backward_midpoint(layers[i], grads[i], p, q, dp, dq, h)
+            out = kern.backward_midpoint(layers[i], grads[i], p, q, dp, dq, h, gF=g_lp, carry=i > 0)
         else:
-            p, q, dp, dq = kern.backward_euler(layers[i], grads[i], p, q, dp, dq)
+            out = kern.backward_euler(layers[i], grads[i], p, q, dp, dq, gm=g_lp, carry=i > 0)
+        p, q, dp, dq = out[:4]
+        g_lp = out[4] if i > 0 else None
         kern.layer_done()
         if on_layer_done is not None:
-            kern.sync()  # layer i's weight gradients are read by the caller
-            on_layer_done(i)
+            on_layer_done(i, kern.grads_ready() if torch.cuda.is_available() and p.is_cuda else None)
     kern.sync()
     return p, q, dp, dq

@@ -386,9 +386,10 @@ def add_rmsnorm_fwd(x: torch.Tensor, a: torch.Tensor, weight: torch.Tensor, eps:
 def rmsnorm_bwd_fused(x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor, dy: torch.Tensor,
                       dw: torch.Tensor, residual: torch.Tensor | None = None, lp_add: torch.Tensor | None = None,
                       lp_dtype: torch.dtype | None = None, dx_out: torch.Tensor | None = None,
-                      lp_out: torch.Tensor | None = None, accumulate_dw: bool = True):
+                      lp_out: torch.Tensor | None = None, accumulate_dw: bool = True, lp_scale: float = 1.0):
     """dx_out = rmsnorm_bwd(dy) + residual (fp32); lp_out = round(lp_add + round(dx)) if lp_add else
-    round(dx_out) when lp_dtype is given. dw accumulates. Returns (dx_out, lp_out)."""
+    round(round(dx_out) * lp_scale) (cast_scale of the total) when lp_dtype is given. dw
+    accumulates. Returns (dx_out, lp_out)."""
     require_cuda(x, weight, rstd, dy)
     rows, width = x.shape
     dx_out = dx_out if dx_out is not None else torch.empty((rows, width), device=x.device, dtype=torch.float32)
@@ -398,7 +399,7 @@ def rmsnorm_bwd_fused(x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor,
     ws = torch.empty(max(ws_bytes // 4, 1), device=x.device, dtype=torch.float32)
     _lib.call("rk_rmsnorm_bwd_fused", x.data_ptr(), weight.data_ptr(), rstd.data_ptr(), dy.data_ptr(),
               _lib.code(dy.dtype), _lib.ptr(residual), _lib.ptr(lp_add), _lib.ptr(lp_out),
-              _lib.code(lp_out.dtype) if lp_out is not None else _lib.code(dy.dtype), dx_out.data_ptr(),
+              _lib.code(lp_out.dtype) if lp_out is not None else _lib.code(dy.dtype), float(lp_scale), dx_out.data_ptr(),
               dw.data_ptr(), int(accumulate_dw), ws.data_ptr(), ws_bytes, rows, width, _lib.stream_ptr())
     return dx_out, lp_out
 

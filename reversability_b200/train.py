@@ -251,8 +251,8 @@ class ReversibleTrainer:
         # boundary p = q = embedding: both cotangents reach it (summed inside the kernel)
         fn.embedding_bwd(ids, dp, self.g_tok, self.g_pos, dx2=dq)
 
-    def _bucket_hook(self, layer: int):
-        self.buckets.launch(layer)
+    def _bucket_hook(self, layer: int, events=None):
+        self.buckets.launch(layer, after=events)
 
     # ------------------------------------------------------------------ one update
     def _update_body(self):

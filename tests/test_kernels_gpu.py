@@ -313,7 +313,7 @@ def test_add_rmsnorm_fwd_matches_unfused(cd):
     assert torch.equal(s, s_ref) and torch.equal(y, y_ref) and torch.equal(r, r_ref)
 
 
-@pytest.mark.parametrize("mode", ["plain", "res", "res_lpadd", "lp_total", "lpadd"])
+@pytest.mark.parametrize("mode", ["plain", "res", "res_lpadd", "lp_total", "lpadd", "lp_scaled"])
 def test_rmsnorm_bwd_fused_epilogues(mode):
     from reversability_b200 import functional as fn
     rows = 3000
@@ -321,20 +321,21 @@ def test_rmsnorm_bwd_fused_epilogues(mode):
     w = torch.randn(256, device=DEV)
     _, rstd = fn.rmsnorm_fwd(x, w, 1e-6)
     g = torch.randn(rows, 256, device=DEV).bfloat16()
-    res = torch.randn(rows, 256, device=DEV) if "res" in mode else None
+    res = torch.randn(rows, 256, device=DEV) if "res" in mode or mode == "lp_scaled" else None
     lpa = torch.randn(rows, 256, device=DEV).bfloat16() if "lpadd" in mode else None
-    want_lp = mode in ("res_lpadd", "lp_total", "lpadd")
+    want_lp = mode in ("res_lpadd", "lp_total", "lpadd", "lp_scaled")
+    scale = 0.3 if mode == "lp_scaled" else 1.0  # not a power of two: the second rounding matters
     dx_ref, dw_ref = fn.rmsnorm_bwd(x, w, rstd, g, dx_dtype=torch.float32)
     dw = torch.zeros(256, device=DEV)
     dxo, lp = fn.rmsnorm_bwd_fused(x, w, rstd, g, dw, residual=res, lp_add=lpa,
-                                   lp_dtype=torch.bfloat16 if want_lp else None)
+                                   lp_dtype=torch.bfloat16 if want_lp else None, lp_scale=scale)
     total = dx_ref + (res if res is not None else 0)
     assert torch.equal(dxo, total)
     assert torch.equal(dw, dw_ref)
     if lpa is not None:
         assert torch.equal(lp, lpa + dx_ref.bfloat16())
-    elif want_lp:
-        assert torch.equal(lp, total.bfloat16())
+    elif want_lp:  # rk_cast_scale of the total, formed in the same epilogue
+        assert torch.equal(lp, fn.cast_scale(total, torch.bfloat16, scale))
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])

@@ -178,6 +178,13 @@ RK_API int rk_gemm_dgrad(const void* dy, int64_t lddy, const void* w, int64_t ld
  * receives u itself (the backward needs it). bf16/f16 only; ff % 128 == 0. */
 RK_API int rk_gemm_fprop_swiglu(const void* x, int64_t ldx, const void* w_up, int64_t ldw, void* h, int64_t ldh,
                                 void* u, int64_t ldu, int64_t M, int64_t ff, int64_t K, int dtype, void* stream);
+/* MLP down projection's dgrad with the SwiGLU backward fused into the
+ * epilogue (model.py:55-56 backward): dh = round(DY[M,N] . W_down[N,ff]) and
+ * du[M,2ff] = rk_swiglu_bwd(u, dh), bit-identical to rk_gemm_dgrad followed by
+ * rk_swiglu_bwd; dh is never written. u/du hold the gate half in columns
+ * [0, ff) and the value half in [ff, 2ff). bf16/f16 only; ff % 64 == 0. */
+RK_API int rk_gemm_dgrad_swiglu(const void* dy, int64_t lddy, const void* w, int64_t ldw, const void* u, int64_t ldu,
+                                void* du, int64_t lddu, int64_t M, int64_t ff, int64_t N, int dtype, void* stream);
 RK_API int64_t rk_gemm_wgrad_workspace(int64_t M, int64_t N, int64_t K);
 RK_API int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_t ldx, float* dw, int64_t lddw, int64_t M,
                   int64_t N, int64_t K, int dtype, int accumulate, float* workspace, int64_t workspace_bytes,

@@ -75,7 +75,7 @@ struct GemmArgs {
 // to g.xlabel. Columns at or past g.vocab do not count.
 enum {
   EPI_STORE = 0, EPI_PARTIAL = 1, EPI_ACCUM = 2, EPI_TMA = 3, EPI_TMA_ADD = 4, EPI_SWIGLU = 5, EPI_SWIGLU_SAVE = 6,
-  EPI_LSE = 7
+  EPI_LSE = 7, EPI_SWIGLU_BWD = 8
 };
 // A-operand transforms (XF): the A tile holds e = exp(x - m_b) from the LSE
 // epilogue and is turned, in shared memory before the MMA reads it, into the
@@ -87,13 +87,17 @@ enum { XF_NONE = 0, XF_ROWS = 1, XF_COLS = 2 };
 
 __host__ __device__ constexpr bool epi_is_swiglu(int e) { return e == EPI_SWIGLU || e == EPI_SWIGLU_SAVE; }
 __host__ __device__ constexpr bool epi_stages_out(int e) {
-  return e == EPI_TMA || e == EPI_TMA_ADD || e == EPI_LSE || epi_is_swiglu(e);
+  return e == EPI_TMA || e == EPI_TMA_ADD || e == EPI_LSE || e == EPI_SWIGLU_BWD || epi_is_swiglu(e);
 }
 constexpr int kEpiWarps = 8;
 // Output staging: one 4 KB box (32 rows x 128 bytes) per epilogue warp, two for
-// SWIGLU_SAVE (h and the gate half of u; the value half reuses the first).
+// SWIGLU_SAVE (h and the gate half of u; the value half reuses the first), and
+// for SWIGLU_BWD two chunks of (gate box, value box) per warp: u is loaded
+// into them and du computed in place.
 __host__ __device__ constexpr uint32_t epi_out_bytes(int e) {
-  return e == EPI_SWIGLU_SAVE ? kEpiWarps * 2 * 4096 : (epi_stages_out(e) ? kEpiWarps * 4096 : 0);
+  return e == EPI_SWIGLU_BWD    ? kEpiWarps * 2 * 8192
+         : e == EPI_SWIGLU_SAVE ? kEpiWarps * 2 * 4096
+                                : (epi_stages_out(e) ? kEpiWarps * 4096 : 0);
 }
 
 constexpr int kBM = 128;
@@ -112,7 +116,7 @@ struct TcSmem {
   static constexpr uint32_t kStage = RES ? kA : kA + kB;
   static constexpr uint32_t kBres = RES ? kResKb * kB : 0;
   static constexpr uint32_t kOut = OUT_BYTES;  // epilogue staging (epi_out_bytes)
-  static constexpr uint32_t kBarriers = (3 * STAGES + 7) * 8;
+  static constexpr uint32_t kBarriers = (3 * STAGES + 7 + 2 * kEpiWarps) * 8;
   static constexpr uint32_t kTotal = 1024 /*align slack*/ + STAGES * kStage + kBres + kOut + kBarriers + 16;
 };
 
@@ -254,6 +258,38 @@ __device__ __forceinline__ uint32_t pack_unit2(float lo, float hi) {
   else return pack2_rn<T>(lo, hi);
 }
 
+// pack2_rn on the integer ALU for bf16 (round to nearest even by adding
+// 0x7fff plus the kept lowest bit; identical to the conversion for every
+// non-NaN value), keeping the conversion unit for the exponentials.
+template <typename T>
+__device__ __forceinline__ uint32_t pack2_rne_alu(float lo, float hi) {
+  if constexpr (std::is_same_v<T, __nv_bfloat16>) {
+    const uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
+    return __byte_perm(a + 0x7fffu + ((a >> 16) & 1u), b + 0x7fffu + ((b >> 16) & 1u), 0x7632);
+  } else {
+    return pack2_rn<T>(lo, hi);
+  }
+}
+
+// One packed pair of the SwiGLU backward in rk_swiglu_bwd's operation order:
+// gw / vw hold u's (gate, value) pair on entry and (dg, dv) on return; a0, a1
+// are the fp32 dgrad accumulators, rounded to T first (the dh that the
+// unfused path stores). Roundings of pairs are one packed conversion each.
+template <typename T>
+__device__ __forceinline__ void swiglu_bwd_word(uint32_t& gw, uint32_t& vw, uint32_t a0, uint32_t a1) {
+  const uint32_t dw = pack2_rn<T>(__uint_as_float(a0), __uint_as_float(a1));
+  const float g0 = unpack_half<T>(gw, 0), g1 = unpack_half<T>(gw, 1);
+  const float v0 = unpack_half<T>(vw, 0), v1 = unpack_half<T>(vw, 1);
+  const float d0 = unpack_half<T>(dw, 0), d1 = unpack_half<T>(dw, 1);
+  const float s0 = sigmoid_value(g0), s1 = sigmoid_value(g1);
+  const uint32_t sw = pack2_rn<T>(__fmul_rn(g0, s0), __fmul_rn(g1, s1));  // round(silu(g))
+  const uint32_t tw = pack2_rn<T>(__fmul_rn(d0, v0), __fmul_rn(d1, v1));  // round(dh * v)
+  const float sl0 = __fmul_rn(s0, __fadd_rn(1.f, __fmul_rn(g0, __fsub_rn(1.f, s0))));
+  const float sl1 = __fmul_rn(s1, __fadd_rn(1.f, __fmul_rn(g1, __fsub_rn(1.f, s1))));
+  gw = pack2_rne_alu<T>(__fmul_rn(unpack_half<T>(tw, 0), sl0), __fmul_rn(unpack_half<T>(tw, 1), sl1));
+  vw = pack2_rne_alu<T>(__fmul_rn(d0, unpack_half<T>(sw, 0)), __fmul_rn(d1, unpack_half<T>(sw, 1)));
+}
+
 // (m, s) += (m2, s2) for online log-sum-exp pairs (s = sum of exp(x - m)).
 __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
   const float mn = fmaxf(m, m2);
@@ -346,7 +382,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bfull = drain + 8;    // RES: resident B block loaded
   const uint32_t bempty = bfull + 8;   // RES: MMAs reading the resident B block done
   const uint32_t xready0 = bempty + 8;  // XF: stage transformed (one arrival per epilogue warp)
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 7);
+  const uint32_t ubar0 = xready0 + 8 * STAGES;  // SWIGLU_BWD: u chunk (warp, chunk) landed
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 7 + 2 * kEpiWarps);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   volatile int* s_consumed = reinterpret_cast<volatile int*>(s_tmem + 2);
 
@@ -366,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(drain, 1);
     mbar_init(bfull, 1);
     mbar_init(bempty, 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(ubar0 + 8 * i, 1);
     fence_mbar_init();
     *s_abort = 0;
     *s_consumed = 0;
@@ -551,6 +589,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t acc_phase = 0;
     int xstage = 0;                    // XF: ring position, in step with the producer
     uint32_t xphase = 0;
+    uint32_t uphase = 0;               // SWIGLU_BWD: parity of each chunk's u barrier (bit ch)
+    uint32_t upend = 0;                // SWIGLU_BWD: u loads issued and not yet waited on (bit ch)
+    bool uwarm = false;                // SWIGLU_BWD: the first tile's u has been requested
     for (TileWalk<RES> w(total); w.more(); w.next()) {
       int split, m0, nt;
       w.coords(g, w.t, split, m0, nt);
@@ -657,11 +698,98 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!xok) break;
       }
+      // SWIGLU_BWD: this warp's u rows (gate box and value box) of chunk ch of
+      // the tile at index tt go to chunk slot ch; issued by lane 0.
+      auto u_issue = [&](int tt, int ch) {
+        if constexpr (EPI == EPI_SWIGLU_BWD) {
+          int s2, m2, nt2;
+          w.coords(g, tt, s2, m2, nt2);
+          const int col = nt2 * NSTEP + half * 128 + ch * 64;
+          if (col < g.ff) {
+            const uint32_t box = smem_u32(sOut + (ew * 2 + ch) * 8192);
+            const uint32_t ub = ubar0 + 8 * (ew * 2 + ch);
+            mbar_arrive_expect_tx(ub, 8192);
+            tma_load_2d(box, &tmD, ub, col, m2 + quarter * 32);
+            tma_load_2d(box + 4096, &tmD, ub, g.ff + col, m2 + quarter * 32);
+            upend |= 1u << ch;
+          }
+        }
+      };
+      if constexpr (EPI == EPI_SWIGLU_BWD) {
+        // The first tile's u is requested here; every later tile's chunk is
+        // requested as soon as the previous tile's store has read that slot.
+        if (lane == 0 && !uwarm) {
+          u_issue(w.t, 0);
+          u_issue(w.t, 1);
+        }
+        uwarm = true;
+      }
       bool ok = mbar_wait(tfull0 + 8 * acc, acc_phase, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN;
+      if constexpr (EPI == EPI_SWIGLU_BWD) {
+        // du = swiglu_bwd(u, dh) with dh = round(accumulator): the operation
+        // order of rk_swiglu_bwd on the rounded dgrad output, written in place
+        // over the staged u boxes and TMA-stored (gate half, then value half).
+        // Once a slot's store has read it, the slot is refilled with the next
+        // tile's u, whose load then overlaps this tile's remaining work.
+        static_assert(BN == 256 && sizeof(TOut) == 2, "256-column tiles, 16-bit u");
+        const int y = m0 + quarter * 32;
+        const bool has_next = w.t + w.step < w.end;
+        bool uok = true;
+#pragma unroll 1
+        for (int ch = 0; ch < 2; ++ch) {
+          const int c = half * 128 + ch * 64;
+          uint32_t r[64];
+          tmem_ld_32cols_nowait(t_row + c, r);
+          tmem_ld_32cols_nowait(t_row + c + 32, r + 32);
+          tmem_ld_wait();
+          if (ch == 1) {  // TMEM is read: the MMA warp may reuse this accumulator
+            tc_fence_before();
+            mbar_arrive(tempty0 + 8 * acc);
+          }
+          if (n0 + c < g.ff) {
+            const uint32_t ub = ubar0 + 8 * (ew * 2 + ch);
+            uok = mbar_wait(ub, (uphase >> ch) & 1u, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
+            uok = __all_sync(0xffffffffu, uok);
+            if (!uok) break;
+            uphase ^= 1u << ch;
+            upend &= ~(1u << ch);
+            uint8_t* gb = sOut + (ew * 2 + ch) * 8192;
+            uint8_t* vb = gb + 4096;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const int off = lane * 128 + ((j ^ (lane & 7)) * 16);
+              uint4 gw = *reinterpret_cast<const uint4*>(gb + off);
+              uint4 vw = *reinterpret_cast<const uint4*>(vb + off);
+              const uint32_t* q = r + j * 8;
+              swiglu_bwd_word<TOut>(gw.x, vw.x, q[0], q[1]);
+              swiglu_bwd_word<TOut>(gw.y, vw.y, q[2], q[3]);
+              swiglu_bwd_word<TOut>(gw.z, vw.z, q[4], q[5]);
+              swiglu_bwd_word<TOut>(gw.w, vw.w, q[6], q[7]);
+              *reinterpret_cast<uint4*>(gb + off) = gw;
+              *reinterpret_cast<uint4*>(vb + off) = vw;
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&tmC, smem_u32(gb), n0 + c, y);
+              tma_store_2d(&tmC, smem_u32(vb), g.ff + n0 + c, y);
+              bulk_commit();
+              if (has_next) bulk_wait_read<0>();  // the slot is free once the store has read it
+            }
+          }
+          if (lane == 0 && has_next) u_issue(w.t + w.step, ch);
+        }
+        if (!uok) break;
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
       if constexpr (epi_is_swiglu(EPI)) {
         // h = round(silu(round(g))) * round(v) for this warp's 64 of the tile's
         // 128 columns; the same operation order as rk_swiglu_fwd on a bf16 u.
@@ -895,6 +1023,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (++acc == 2) {
         acc = 0;
         acc_phase ^= 1;
+      }
+    }
+    if constexpr (EPI == EPI_SWIGLU_BWD) {
+      // u loads issued for a tile that was abandoned land before the CTA exits
+      if (lane == 0) {
+        for (int ch = 0; ch < 2; ++ch)
+          if (upend & (1u << ch))
+            mbar_wait(ubar0 + 8 * (ew * 2 + ch), (uphase >> ch) & 1u, g.status, RK_DEV_GEMM_TIMEOUT, nullptr);
       }
     }
   }
@@ -1366,6 +1502,49 @@ extern "C" int rk_gemm_fprop_swiglu(const void* x, int64_t ldx, const void* w_up
   }
   if (u) return launch_tc<256, 3, false, false, EPI_SWIGLU_SAVE, __half>(ta, tb, tc, g, dtype, s, &td);
   return launch_tc<256, 4, false, false, EPI_SWIGLU, __half>(ta, tb, tc, g, dtype, s);
+}
+
+// ---------------------------------------------------------------- fused down-projection dgrad + SwiGLU backward
+// du = swiglu_bwd(u, round(dy . w)): the down projection's dgrad (dy [M, N],
+// w [N, ff], N = d_model) with rk_swiglu_bwd applied in the epilogue to the
+// rounded result, reading u [M, 2ff] (gate columns first) and writing du of
+// the same layout; dh never reaches global memory.
+extern "C" int rk_gemm_dgrad_swiglu(const void* dy, int64_t lddy, const void* w, int64_t ldw, const void* u,
+                                    int64_t ldu, void* du, int64_t lddu, int64_t M, int64_t ff, int64_t N, int dtype,
+                                    void* stream) {
+  if (!dy || !w || !u || !du || M < 0 || ff <= 0 || N <= 0 || lddy < N || ldw < ff || ldu < 2 * ff ||
+      lddu < 2 * ff || M > INT32_MAX || ff > INT32_MAX / 2 || N > INT32_MAX)
+    return RK_ERR_ARG;
+  if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
+  if (ff % 64) return RK_ERR_UNSUPPORTED;
+  if (M == 0) return RK_OK;
+  if (!rk_host::aligned(dy, 16) || !rk_host::aligned(w, 16) || !rk_host::aligned(u, 16) || !rk_host::aligned(du, 16) ||
+      (lddy * 2) % 16 || (ldw * 2) % 16 || (ldu * 2) % 16 || (lddu * 2) % 16)
+    return RK_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap ta, tb, tc, td;
+  if (!make_map(&ta, dy, (uint64_t)N, (uint64_t)M, (uint64_t)lddy, dtype, 64, kBM) ||
+      !make_map(&tb, w, (uint64_t)ff, (uint64_t)N, (uint64_t)ldw, dtype, 64, 64) ||
+      !make_out_map(&tc, du, (uint64_t)(2 * ff), (uint64_t)M, (uint64_t)lddu, dtype) ||
+      !make_out_map(&td, const_cast<void*>(u), (uint64_t)(2 * ff), (uint64_t)M, (uint64_t)ldu, dtype))
+    return RK_ERR_LAUNCH;
+  GemmArgs g{};
+  g.M = (int)M;
+  g.N = (int)ff;
+  g.K = (int)N;
+  g.tiles_m = (int)((M + kBM - 1) / kBM);
+  g.tiles_n = (int)((ff + 255) / 256);
+  g.kb_total = (int)((N + kBK - 1) / kBK);
+  g.splits = 1;
+  g.kb_per_split = g.kb_total;
+  g.ff = (int)ff;
+  g.out = du;
+  g.ldo = lddu;
+  g.out_dtype = dtype;
+  g.status = rk_host::device_status_ptr();
+  if (dtype == RK_BF16)
+    return launch_tc<256, 2, false, true, EPI_SWIGLU_BWD, __nv_bfloat16>(ta, tb, tc, g, dtype, s, &td);
+  return launch_tc<256, 2, false, true, EPI_SWIGLU_BWD, __half>(ta, tb, tc, g, dtype, s, &td);
 }
 
 // ---------------------------------------------------------------- softmax head

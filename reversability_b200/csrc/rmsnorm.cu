@@ -168,8 +168,18 @@ __global__ void __launch_bounds__(1024) rmsnorm_dw_reduce_kernel(const float* __
   const int lc = threadIdx.x & 31, g = threadIdx.x >> 5;
   const int c = blockIdx.x * 32 + lc;
   float s = 0.f;
-  if (c < width)
-    for (int p = g; p < parts; p += 32) s += partial[(int64_t)p * width + c];
+  if (c < width) {
+    // eight partials in flight per thread, added in part order
+    int p = g;
+    for (; p + 7 * 32 < parts; p += 8 * 32) {
+      float t[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) t[k] = partial[(int64_t)(p + 32 * k) * width + c];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s += t[k];
+    }
+    for (; p < parts; p += 32) s += partial[(int64_t)p * width + c];
+  }
   grp[g][lc] = s;
   __syncthreads();
   if (g == 0 && c < width) {
@@ -255,50 +265,68 @@ __global__ void __launch_bounds__(256) rmsnorm_bwd_fused_kernel(
     for (int e = 0; e < V; ++e) acc[j][e] = 0.f;
     if (c < width) load_vec<float, V>(w + c, wv[j]);
   }
-  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < rows; row += stride) {
-    const float r = __ldg(rstd + row);
-    const int64_t base = row * width;
-    float xv[NV][V], gv[NV][V];
-    float dot = 0.f;
+  // R rows per iteration (rows `row`, `row + stride`, ..., the order of the
+  // weight-gradient sums unchanged), every load of them issued first
+  constexpr int R = NV <= 4 ? 2 : 1;
+  for (int64_t row = (int64_t)blockIdx.x * 8 + warp; row < rows; row += R * stride) {
+    float xv[R][NV][V], gv[R][NV][V], res[R][NV][V], la[R][NV][V], rr[R];
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int c = (j * 32 + lane) * V;
-      if (c < width) {
-        load_vec<float, V>(x + base + c, xv[j]);
-        load_vec<Tg, V>(dy + base + c, gv[j]);
+    for (int h = 0; h < R; ++h) {
+      const int64_t rw = row + h * stride;
+      rr[h] = rw < rows ? __ldg(rstd + rw) : 0.f;
 #pragma unroll
-        for (int e = 0; e < V; ++e) {
-          dot += (gv[j][e] * wv[j][e]) * xv[j][e];
-          acc[j][e] += gv[j][e] * (xv[j][e] * r);
+      for (int j = 0; j < NV; ++j) {
+        const int c = (j * 32 + lane) * V;
+        if (rw < rows && c < width) {
+          load_vec<float, V>(x + rw * width + c, xv[h][j]);
+          load_vec<Tg, V>(dy + rw * width + c, gv[h][j]);
+          if constexpr (RES) load_vec<float, V>(residual + rw * width + c, res[h][j]);
+          if constexpr (LP == 1) load_vec<Tlp, V>(lp_add + rw * width + c, la[h][j]);
         }
       }
     }
-    dot = warp_sum(dot);
-    const float corr = dot / (float)width * r * r;
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int c = (j * 32 + lane) * V;
-      if (c < width) {
-        float o[V], res[V], lp[V];
+    for (int h = 0; h < R; ++h) {
+      const int64_t rw = row + h * stride;
+      if (rw >= rows) break;
+      const float r = rr[h];
+      const int64_t base = rw * width;
+      float dot = 0.f;
 #pragma unroll
-        for (int e = 0; e < V; ++e) o[e] = (gv[j][e] * wv[j][e] - xv[j][e] * corr) * r;
-        if constexpr (LP == 1) {
-          float la[V];
-          load_vec<Tlp, V>(lp_add + base + c, la);
+      for (int j = 0; j < NV; ++j) {
+        const int c = (j * 32 + lane) * V;
+        if (c < width) {
 #pragma unroll
-          for (int e = 0; e < V; ++e) lp[e] = __fadd_rn(la[e], round_to<Tlp>(o[e]));
+          for (int e = 0; e < V; ++e) {
+            dot += (gv[h][j][e] * wv[j][e]) * xv[h][j][e];
+            acc[j][e] += gv[h][j][e] * (xv[h][j][e] * r);
+          }
         }
-        if constexpr (RES) {
-          load_vec<float, V>(residual + base + c, res);
+      }
+      dot = warp_sum(dot);
+      const float corr = dot / (float)width * r * r;
 #pragma unroll
-          for (int e = 0; e < V; ++e) o[e] = __fadd_rn(o[e], res[e]);  // no contraction into the last multiply
-        }
-        if constexpr (LP == 2) {
+      for (int j = 0; j < NV; ++j) {
+        const int c = (j * 32 + lane) * V;
+        if (c < width) {
+          float o[V], lp[V];
 #pragma unroll
-          for (int e = 0; e < V; ++e) lp[e] = __fmul_rn(round_to<Tlp>(o[e]), lp_scale);  // as rk_cast_scale
+          for (int e = 0; e < V; ++e) o[e] = (gv[h][j][e] * wv[j][e] - xv[h][j][e] * corr) * r;
+          if constexpr (LP == 1) {
+#pragma unroll
+            for (int e = 0; e < V; ++e) lp[e] = __fadd_rn(la[h][j][e], round_to<Tlp>(o[e]));
+          }
+          if constexpr (RES) {
+#pragma unroll
+            for (int e = 0; e < V; ++e) o[e] = __fadd_rn(o[e], res[h][j][e]);  // no contraction into the last multiply
+          }
+          if constexpr (LP == 2) {
+#pragma unroll
+            for (int e = 0; e < V; ++e) lp[e] = __fmul_rn(round_to<Tlp>(o[e]), lp_scale);  // as rk_cast_scale
+          }
+          store_vec<float, V>(dx_out + base + c, o);
+          if constexpr (LP != 0) store_vec<Tlp, V>(lp_out + base + c, lp);
         }
-        store_vec<float, V>(dx_out + base + c, o);
-        if constexpr (LP != 0) store_vec<Tlp, V>(lp_out + base + c, lp);
       }
     }
   }

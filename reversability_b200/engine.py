@@ -305,11 +305,15 @@ class LayerKernels:
             else:
                 fn.linear_fwd(hg, lw.down_c, out=m[s:e])
             gm_t = gm[s:e]
-            dh = fn.linear_dgrad(gm_t, lw.down_c)
-            self._wgrad(gm_t, hg, g.down)
-            del hg
-            du = fn.swiglu_bwd(u, dh)
-            del u, dh
+            if fn.dgrad_swiglu_fusable(gm_t, lw.down_c, u):  # SwiGLU backward in the dgrad epilogue
+                du = fn.linear_dgrad_swiglu(gm_t, lw.down_c, u)
+                self._wgrad(gm_t, hg, g.down)
+            else:
+                dh = fn.linear_dgrad(gm_t, lw.down_c)
+                self._wgrad(gm_t, hg, g.down)
+                du = fn.swiglu_bwd(u, dh)
+                del dh
+            del hg, u
             self._wgrad(du, n2[s:e], g.up)
             dn2 = fn.linear_dgrad(du, lw.up_c)
             del du

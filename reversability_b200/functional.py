@@ -439,6 +439,26 @@ def linear_swiglu_fwd(x: torch.Tensor, w_up: torch.Tensor, save_u: bool = False)
     return h, u
 
 
+def linear_dgrad_swiglu(dy: torch.Tensor, w_down: torch.Tensor, u: torch.Tensor) -> torch.Tensor:
+    """du = swiglu_bwd(u, linear_dgrad(dy, w_down)) in one GEMM (the SwiGLU
+    backward in the epilogue; dh never written). dy [M, d], w_down [d, ff],
+    u [M, 2ff] (gate columns first). Returns du like u."""
+    require_cuda(dy, w_down, u)
+    M, d = dy.shape
+    ff = w_down.shape[1]
+    du = torch.empty_like(u)
+    _lib.call("rk_gemm_dgrad_swiglu", dy.data_ptr(), dy.stride(0), w_down.data_ptr(), w_down.stride(0), u.data_ptr(),
+              u.stride(0), du.data_ptr(), du.stride(0), M, ff, d, _gemm_dtype(dy, w_down), _lib.stream_ptr())
+    return du
+
+
+def dgrad_swiglu_fusable(dy: torch.Tensor, w_down: torch.Tensor, u: torch.Tensor) -> bool:
+    return dy.dtype in _TC_DTYPES and w_down.dtype == dy.dtype and u.dtype == dy.dtype and \
+        w_down.shape[1] % 64 == 0 and dy.is_contiguous() and w_down.is_contiguous() and u.is_contiguous() and \
+        u.shape[1] == 2 * w_down.shape[1] and (dy.shape[1] * 2) % 16 == 0 and \
+        all(t.data_ptr() % 16 == 0 for t in (dy, w_down, u))
+
+
 def swiglu_fusable(x: torch.Tensor, w_up: torch.Tensor) -> bool:
     return x.dtype in _TC_DTYPES and w_up.dtype == x.dtype and (w_up.shape[0] // 2) % 128 == 0 and \
         x.is_contiguous() and w_up.is_contiguous() and (x.shape[1] * 2) % 16 == 0

@@ -88,9 +88,24 @@ def bench_rmsnorm(iters):
         _lib.call("rk_rmsnorm_bwd", xs[k].data_ptr(), _lib.BF16, D, w.data_ptr(), rs[k].data_ptr(), gs[k].data_ptr(),
                   _lib.BF16, D, dxs[k].data_ptr(), _lib.BF16, D, dw.data_ptr(), 0, ws.data_ptr(), ws_bytes, N_TOK, D,
                   s())
+    # the reverse sweep's fused form: fp32 x and residual, bf16 dy and lp_add
+    # in; fp32 dx_out and bf16 lp_out = round(lp_add + round(dx)) out
+    nf = sets_for(18 * N_TOK * D)
+    xf = [torch.randn(N_TOK, D, device="cuda") for _ in range(nf)]
+    res = [torch.randn(N_TOK, D, device="cuda") for _ in range(nf)]
+    lpa = [torch.randn(N_TOK, D, device="cuda").bfloat16() for _ in range(nf)]
+    dxo = [torch.empty(N_TOK, D, device="cuda") for _ in range(nf)]
+    lpo = [torch.empty(N_TOK, D, device="cuda", dtype=torch.bfloat16) for _ in range(nf)]
+
+    def bwd_fused(k):
+        f = k % nf
+        _lib.call("rk_rmsnorm_bwd_fused", xf[f].data_ptr(), w.data_ptr(), rs[f].data_ptr(), gs[f].data_ptr(),
+                  _lib.BF16, res[f].data_ptr(), lpa[f].data_ptr(), lpo[f].data_ptr(), _lib.BF16, 1.0,
+                  dxo[f].data_ptr(), dw.data_ptr(), 1, ws.data_ptr(), ws_bytes, N_TOK, D, s())
     out = []
     for name, f, nbytes in (("rmsnorm_fwd", fwd, 4 * N_TOK * D + 4 * N_TOK),
-                            ("rmsnorm_bwd", bwd, 6 * N_TOK * D + 4 * N_TOK)):
+                            ("rmsnorm_bwd", bwd, 6 * N_TOK * D + 4 * N_TOK),
+                            ("rmsnorm_bwd_fused_res_lpadd", bwd_fused, 18 * N_TOK * D + 4 * N_TOK)):
         us = time_graph(f, ns, iters)
         out.append(("hbm", name, nbytes, us))
     return out
@@ -110,8 +125,22 @@ def bench_swiglu(iters):
     def bwd(k):
         _lib.call("rk_swiglu_bwd", us_[k].data_ptr(), dhs[k].data_ptr(), dus[k].data_ptr(), _lib.BF16, N_TOK, FF,
                   _lib.stream_ptr())
+    down = (torch.randn(D, FF, device="cuda") * 0.02).bfloat16()
+    gys = [torch.randn(N_TOK, D, device="cuda").bfloat16() for _ in range(ns)]
+
+    def dgrad_fused(k):  # down-projection dgrad with the SwiGLU backward in its epilogue
+        _lib.call("rk_gemm_dgrad_swiglu", gys[k].data_ptr(), D, down.data_ptr(), FF, us_[k].data_ptr(), 2 * FF,
+                  dus[k].data_ptr(), 2 * FF, N_TOK, FF, D, _lib.BF16, _lib.stream_ptr())
+
+    def dgrad_separate(k):  # the same result from rk_gemm_dgrad + rk_swiglu_bwd
+        _lib.call("rk_gemm_dgrad", gys[k].data_ptr(), D, down.data_ptr(), FF, dhs[k].data_ptr(), FF, N_TOK, D, FF,
+                  _lib.BF16, _lib.BF16, _lib.stream_ptr())
+        bwd(k)
+    fused_bytes = 2 * N_TOK * D + 2 * D * FF + 2 * N_TOK * 2 * FF * 2
     return [("hbm", "swiglu_fwd", 2 * N_TOK * 2 * FF + 2 * N_TOK * FF, time_graph(fwd, ns, iters)),
-            ("hbm", "swiglu_bwd", 2 * N_TOK * 2 * FF * 2 + 2 * N_TOK * FF, time_graph(bwd, ns, iters))]
+            ("hbm", "swiglu_bwd", 2 * N_TOK * 2 * FF * 2 + 2 * N_TOK * FF, time_graph(bwd, ns, iters)),
+            ("hbm", "dgrad_swiglu_fused", fused_bytes, time_graph(dgrad_fused, ns, iters)),
+            ("hbm", "dgrad_then_swiglu_bwd", fused_bytes, time_graph(dgrad_separate, ns, iters))]
 
 
 def bench_reconstruct(iters):
@@ -241,7 +270,19 @@ def profile_attention():
     torch.cuda.synchronize()
 
 
-PROFILES = {"head": profile_head, "attention": profile_attention}
+def profile_swiglu():
+    """Eager launches for an ncu capture: twice (rk_gemm_dgrad_swiglu) on the
+    microbench shape (16,896 tokens, d 256, ff 1024)."""
+    g = torch.Generator(device="cpu").manual_seed(0)
+    gy = torch.randn(N_TOK, D, generator=g).cuda().bfloat16()
+    down = (torch.randn(D, FF, generator=g) * 0.02).cuda().bfloat16()
+    u = torch.randn(N_TOK, 2 * FF, generator=g).cuda().bfloat16()
+    for _ in range(2):
+        fn.linear_dgrad_swiglu(gy, down, u)
+    torch.cuda.synchronize()
+
+
+PROFILES = {"head": profile_head, "attention": profile_attention, "swiglu": profile_swiglu}
 
 
 def main():

@@ -362,3 +362,22 @@ def test_swiglu_fused_up_gemm_bitwise(M, save):
     assert torch.equal(h, h_ref)
     if save:
         assert torch.equal(u, u_ref)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,ff,d", [(14848, 1024, 256), (333, 1024, 256), (1000, 192, 200), (129, 64, 64),
+                                    (8192, 4096, 1024)])
+def test_dgrad_swiglu_fused_bitwise(dtype, M, ff, d):
+    """rk_gemm_dgrad_swiglu equals rk_gemm_dgrad followed by rk_swiglu_bwd bit
+    for bit, including ragged rows, ff not a multiple of the 256-column tile
+    and a reduction width that is not a multiple of 64."""
+    from reversability_b200 import _lib, functional as fn
+    g = torch.Generator(device="cpu").manual_seed(M + ff + d)
+    dy = (torch.randn(M, d, generator=g) * 1e-2).to(DEV, dtype)
+    w = (torch.randn(d, ff, generator=g) * 0.05).to(DEV, dtype)
+    u = (torch.randn(M, 2 * ff, generator=g) * 2).to(DEV, dtype)
+    assert fn.dgrad_swiglu_fusable(dy, w, u)
+    du = fn.linear_dgrad_swiglu(dy, w, u)
+    ref = fn.swiglu_bwd(u, fn.linear_dgrad(dy, w))
+    assert _lib.device_status() == 0
+    assert torch.equal(du, ref)

@@ -7,11 +7,14 @@
 //   warp 1      : allocates 2*BN tensor-memory columns (two accumulators) and
 //                 issues tcgen05.mma (M=128, N=BN, K=16) from one thread;
 //                 tcgen05.commit frees smem stages and publishes accumulators.
-//   warps 2..9  : epilogue; warp w reads TMEM lanes 32*(w%4)..+31 (one output
-//                 row per thread) of one column half of the tile ((w-2)/4)
-//                 with tcgen05.ld and stores to global memory. Two warps per
-//                 lane quarter (two per SM sub-partition) hide each other's
-//                 TMEM-load and store latency.
+//   warps 2..   : epilogue; warp w reads TMEM lanes 32*(w%4)..+31 (one output
+//                 row per thread) of one column group of the tile ((w-2)/4)
+//                 with tcgen05.ld and stores to global memory. Eight warps
+//                 (two column halves, two warps per SM sub-partition) by
+//                 default; sixteen (four column quarters) for the SwiGLU
+//                 backward epilogue, whose per-element arithmetic bounds the
+//                 tile, so that four warps per sub-partition hide each
+//                 other's latency.
 // The accumulator is double buffered so the epilogue of tile i overlaps the
 // MMAs of tile i+1. Operands may be K-major or MN-major (the transposed views
 // that dgrad and wgrad need) without any transposition pass: TMA loads
@@ -69,6 +72,10 @@ struct GemmArgs {
 // tile holds W rows [n0, n0+128) (gate) and [ff+n0, ff+n0+128) (value), so the
 // accumulator has gate | value for the same 128 columns and the epilogue writes
 // h = round(silu(round(g))) * round(v) only; SWIGLU_SAVE also writes u itself.
+// SWIGLU_BWD: dgrad of the MLP down projection with the SwiGLU backward in the
+// epilogue: u's gate and value columns matching the tile are TMA-loaded into
+// the staging boxes, du = swiglu_bwd(u, round(acc)) is written over them and
+// TMA-stored (gate and value halves of du).
 // LSE (softmax head forward): per row and 128-column block b, the rounded
 // logits x give m_b = max x and e = exp(x - m_b); e is TMA-stored (16-bit)
 // instead of x, (m_b, sum e) goes to g.stats and the logit at the row's label
@@ -89,20 +96,23 @@ __host__ __device__ constexpr bool epi_is_swiglu(int e) { return e == EPI_SWIGLU
 __host__ __device__ constexpr bool epi_stages_out(int e) {
   return e == EPI_TMA || e == EPI_TMA_ADD || e == EPI_LSE || e == EPI_SWIGLU_BWD || epi_is_swiglu(e);
 }
-constexpr int kEpiWarps = 8;
-// Output staging: one 4 KB box (32 rows x 128 bytes) per epilogue warp, two for
-// SWIGLU_SAVE (h and the gate half of u; the value half reuses the first), and
-// for SWIGLU_BWD two chunks of (gate box, value box) per warp: u is loaded
-// into them and du computed in place.
+// Epilogue warps per CTA (a multiple of 4: one per TMEM lane quarter and
+// column group) and threads per CTA (producer warp, MMA warp, epilogue).
+__host__ __device__ constexpr int epi_warps(int e) { return e == EPI_SWIGLU_BWD ? 16 : 8; }
+__host__ __device__ constexpr int gemm_threads(int e) { return 64 + 32 * epi_warps(e); }
+constexpr int kMaxEpiWarps = 16;
+// Output staging per epilogue warp: one 4 KB box (32 rows x 128 bytes); two
+// for SWIGLU_SAVE (h and the gate half of u; the value half reuses the
+// first); for SWIGLU_BWD two chunk slots of (gate box, value box), 2 KB each:
+// u is loaded into them and du computed in place.
 __host__ __device__ constexpr uint32_t epi_out_bytes(int e) {
-  return e == EPI_SWIGLU_BWD    ? kEpiWarps * 2 * 8192
-         : e == EPI_SWIGLU_SAVE ? kEpiWarps * 2 * 4096
-                                : (epi_stages_out(e) ? kEpiWarps * 4096 : 0);
+  return e == EPI_SWIGLU_BWD    ? epi_warps(e) * 2 * 4096
+         : e == EPI_SWIGLU_SAVE ? epi_warps(e) * 2 * 4096
+                                : (epi_stages_out(e) ? epi_warps(e) * 4096 : 0);
 }
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 // B-resident mode (RES): K <= kResK; the whole BN x K operand tile stays in
 // shared memory while the CTA walks consecutive M tiles of one N block, so a
@@ -116,7 +126,7 @@ struct TcSmem {
   static constexpr uint32_t kStage = RES ? kA : kA + kB;
   static constexpr uint32_t kBres = RES ? kResKb * kB : 0;
   static constexpr uint32_t kOut = OUT_BYTES;  // epilogue staging (epi_out_bytes)
-  static constexpr uint32_t kBarriers = (3 * STAGES + 7 + 2 * kEpiWarps) * 8;
+  static constexpr uint32_t kBarriers = (3 * STAGES + 7 + 2 * kMaxEpiWarps) * 8;
   static constexpr uint32_t kTotal = 1024 /*align slack*/ + STAGES * kStage + kBres + kOut + kBarriers + 16;
 };
 
@@ -359,7 +369,7 @@ __device__ __forceinline__ void softmax_grad_chunk(uint8_t* p, int v0, const Chu
 
 template <int BN, int STAGES, bool A_MN, bool B_MN, int EPI, typename TOut, bool RES = false, int XF = XF_NONE,
           typename TIn = __nv_bfloat16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(gemm_threads(EPI), 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmD,
                    const GemmArgs g, const uint32_t idesc) {
@@ -368,6 +378,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   static_assert(XF == XF_NONE || (!RES && !epi_is_swiglu(EPI)), "transforms run on the plain schedule");
   using L = TcSmem<BN, STAGES, epi_out_bytes(EPI), RES>;
   constexpr int NSTEP = epi_is_swiglu(EPI) ? BN / 2 : BN;  // output columns per tile
+  constexpr int EW = epi_warps(EPI);
+  static_assert(EW == 8 || (BN == 256 && XF == XF_NONE), "16 epilogue warps: 256-column tiles, no transform");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -383,7 +395,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t bempty = bfull + 8;   // RES: MMAs reading the resident B block done
   const uint32_t xready0 = bempty + 8;  // XF: stage transformed (one arrival per epilogue warp)
   const uint32_t ubar0 = xready0 + 8 * STAGES;  // SWIGLU_BWD: u chunk (warp, chunk) landed
-  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 7 + 2 * kEpiWarps);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(bars + 3 * STAGES + 7 + 2 * kMaxEpiWarps);
   volatile int* s_abort = reinterpret_cast<volatile int*>(s_tmem + 1);
   volatile int* s_consumed = reinterpret_cast<volatile int*>(s_tmem + 2);
 
@@ -394,16 +406,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
-      mbar_init(xready0 + 8 * s, kEpiWarps);
+      mbar_init(xready0 + 8 * s, EW);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(tfull0 + 8 * b, 1);
-      mbar_init(tempty0 + 8 * b, 32 * kEpiWarps);
+      mbar_init(tempty0 + 8 * b, 32 * EW);
     }
     mbar_init(drain, 1);
     mbar_init(bfull, 1);
     mbar_init(bempty, 1);
-    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(ubar0 + 8 * i, 1);
+    for (int i = 0; i < 2 * kMaxEpiWarps; ++i) mbar_init(ubar0 + 8 * i, 1);
     fence_mbar_init();
     *s_abort = 0;
     *s_consumed = 0;
@@ -583,8 +595,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;      // TMEM lane quarter this warp may access
-    const int ew = warp - 2;           // epilogue warp 0..kEpiWarps-1
-    const int half = ew / 4;           // column half of the tile this warp stores
+    const int ew = warp - 2;           // epilogue warp 0..EW-1
+    const int half = ew / 4;           // column group of the tile this warp stores (a half when EW == 8)
     int acc = 0;
     uint32_t acc_phase = 0;
     int xstage = 0;                    // XF: ring position, in step with the producer
@@ -698,19 +710,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!xok) break;
       }
-      // SWIGLU_BWD: this warp's u rows (gate box and value box) of chunk ch of
-      // the tile at index tt go to chunk slot ch; issued by lane 0.
+      // SWIGLU_BWD: this warp's u rows (gate box and value box, 32 columns
+      // each) of chunk ch of the tile at index tt go to chunk slot ch; issued
+      // by lane 0.
       auto u_issue = [&](int tt, int ch) {
         if constexpr (EPI == EPI_SWIGLU_BWD) {
           int s2, m2, nt2;
           w.coords(g, tt, s2, m2, nt2);
-          const int col = nt2 * NSTEP + half * 128 + ch * 64;
+          const int col = nt2 * NSTEP + half * 64 + ch * 32;
           if (col < g.ff) {
-            const uint32_t box = smem_u32(sOut + (ew * 2 + ch) * 8192);
+            const uint32_t box = smem_u32(sOut + (ew * 2 + ch) * 4096);
             const uint32_t ub = ubar0 + 8 * (ew * 2 + ch);
-            mbar_arrive_expect_tx(ub, 8192);
+            mbar_arrive_expect_tx(ub, 4096);
             tma_load_2d(box, &tmD, ub, col, m2 + quarter * 32);
-            tma_load_2d(box + 4096, &tmD, ub, g.ff + col, m2 + quarter * 32);
+            tma_load_2d(box + 2048, &tmD, ub, g.ff + col, m2 + quarter * 32);
             upend |= 1u << ch;
           }
         }
@@ -735,16 +748,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         // over the staged u boxes and TMA-stored (gate half, then value half).
         // Once a slot's store has read it, the slot is refilled with the next
         // tile's u, whose load then overlaps this tile's remaining work.
-        static_assert(BN == 256 && sizeof(TOut) == 2, "256-column tiles, 16-bit u");
+        static_assert(BN == 256 && sizeof(TOut) == 2 && EW == 16, "256-column tiles, 16-bit u, 16 warps");
         const int y = m0 + quarter * 32;
         const bool has_next = w.t + w.step < w.end;
         bool uok = true;
 #pragma unroll 1
         for (int ch = 0; ch < 2; ++ch) {
-          const int c = half * 128 + ch * 64;
-          uint32_t r[64];
+          const int c = half * 64 + ch * 32;
+          uint32_t r[32];
           tmem_ld_32cols_nowait(t_row + c, r);
-          tmem_ld_32cols_nowait(t_row + c + 32, r + 32);
           tmem_ld_wait();
           if (ch == 1) {  // TMEM is read: the MMA warp may reuse this accumulator
             tc_fence_before();
@@ -757,11 +769,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!uok) break;
             uphase ^= 1u << ch;
             upend &= ~(1u << ch);
-            uint8_t* gb = sOut + (ew * 2 + ch) * 8192;
-            uint8_t* vb = gb + 4096;
+            // boxes of 32 rows x 64 bytes, 64-byte swizzle: 16-byte chunk j of
+            // row r at j ^ ((r / 2) % 4)
+            uint8_t* gb = sOut + (ew * 2 + ch) * 4096;
+            uint8_t* vb = gb + 2048;
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              const int off = lane * 128 + ((j ^ (lane & 7)) * 16);
+            for (int j = 0; j < 4; ++j) {
+              const int off = lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16);
               uint4 gw = *reinterpret_cast<const uint4*>(gb + off);
               uint4 vw = *reinterpret_cast<const uint4*>(vb + off);
               const uint32_t* q = r + j * 8;
@@ -1217,7 +1231,7 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
   int grid = sm_count();
   if (total < grid) grid = total;
   const uint32_t idesc = idesc_f16(kBM, BN, dtype == RK_BF16 ? 1 : 0, A_MN ? 1 : 0, B_MN ? 1 : 0);
-  rk_host::launch_k(kern, grid, kThreads, L::kTotal, s, ta, tb, tc, td ? *td : tc, g, idesc);
+  rk_host::launch_k(kern, grid, gemm_threads(EPI), L::kTotal, s, ta, tb, tc, td ? *td : tc, g, idesc);
   return rk_host::launch_status();
 }
 
@@ -1252,6 +1266,21 @@ bool make_out_map(CUtensorMap* map, void* base, uint64_t N, uint64_t M, uint64_t
                                                         : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = fn(map, dt, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// 16-bit [rows, inner] map with 32 x 32 boxes (64-byte rows, 64-byte swizzle):
+// the staging boxes of the 16-warp epilogues (one warp's 32 rows x 32 columns).
+bool make_box32_map(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t ld, int dtype) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {32, 32};
+  cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt = dtype == RK_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -1525,8 +1554,8 @@ extern "C" int rk_gemm_dgrad_swiglu(const void* dy, int64_t lddy, const void* w,
   CUtensorMap ta, tb, tc, td;
   if (!make_map(&ta, dy, (uint64_t)N, (uint64_t)M, (uint64_t)lddy, dtype, 64, kBM) ||
       !make_map(&tb, w, (uint64_t)ff, (uint64_t)N, (uint64_t)ldw, dtype, 64, 64) ||
-      !make_out_map(&tc, du, (uint64_t)(2 * ff), (uint64_t)M, (uint64_t)lddu, dtype) ||
-      !make_out_map(&td, const_cast<void*>(u), (uint64_t)(2 * ff), (uint64_t)M, (uint64_t)ldu, dtype))
+      !make_box32_map(&tc, du, (uint64_t)(2 * ff), (uint64_t)M, (uint64_t)lddu, dtype) ||
+      !make_box32_map(&td, u, (uint64_t)(2 * ff), (uint64_t)M, (uint64_t)ldu, dtype))
     return RK_ERR_LAUNCH;
   GemmArgs g{};
   g.M = (int)M;

@@ -7,6 +7,7 @@ fallback: if the library is missing, every kernel entry point raises.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import re
 import threading
@@ -118,8 +119,29 @@ def call(name: str, *args) -> None:
     check(getattr(lib(), name)(*args), name)
 
 
+_launch_override: list[int] = []  # stack of stream handles set by launch_on()
+
+
 def stream_ptr(device: torch.device | None = None) -> int:
+    """The stream library kernels are launched on: the current CUDA stream, or
+    the innermost launch_on() stream."""
+    if _launch_override:
+        return _launch_override[-1]
     return torch.cuda.current_stream(device).cuda_stream
+
+
+@contextlib.contextmanager
+def launch_on(stream: "torch.cuda.Stream"):
+    """Library kernels issued inside the block go to `stream` while PyTorch
+    keeps allocating on the current stream. The caller orders `stream` after
+    the current stream's work before the block and keeps every tensor the
+    block touches alive until the current stream has waited for `stream`, so
+    the allocator never hands that memory to other work too early."""
+    _launch_override.append(stream.cuda_stream)
+    try:
+        yield
+    finally:
+        _launch_override.pop()
 
 
 def ptr(t: torch.Tensor | None) -> int | None:

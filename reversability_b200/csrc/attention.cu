@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(256) dsum_kernel(const T* __restrict__ o, cons
 
 // ------------------------------------------------------------------ backward: dK, dV
 template <typename T, int HD>
-__global__ void __launch_bounds__(128) bwd_dkv_kernel(const T* __restrict__ qkv, const T* __restrict__ dout,
+__global__ void __launch_bounds__(128, HD <= 32 ? 4 : 1) bwd_dkv_kernel(const T* __restrict__ qkv, const T* __restrict__ dout,
                                                       const float* __restrict__ lse, const float* __restrict__ dsum,
                                                       T* __restrict__ dqkv, int H, int Tlen, int64_t ldq,
                                                       int64_t ldo, int64_t lddq, float c_log2, float scale) {
@@ -452,7 +452,7 @@ __global__ void __launch_bounds__(128) bwd_dkv_kernel(const T* __restrict__ qkv,
     }
     mma_abT<T, HD, LD>(st, ka, Qs0 + buf * BQ * LD, lane);
     mma_abT<T, HD, LD>(dpt, va, dOs0 + buf * BQ * LD, lane);
-    float pt[8][4];
+    // in place: st becomes P^T, dpt becomes dS^T (no third tile of registers)
 #pragma unroll
     for (int nt = 0; nt < 8; ++nt) {
       const int qc = nt * 8 + 2 * tig;
@@ -462,12 +462,12 @@ __global__ void __launch_bounds__(128) bwd_dkv_kernel(const T* __restrict__ qkv,
         const int qq = i * BQ + qi;
         const int kk = (e < 2) ? key_lo : key_hi;
         const float p = (qq < kk) ? 0.f : ex2(fmaf(st[nt][e], c_log2, -Ls[buf][qi]));
-        pt[nt][e] = p;
-        st[nt][e] = p * (dpt[nt][e] - Ds[buf][qi]);  // dS^T
+        st[nt][e] = p;
+        dpt[nt][e] = p * (dpt[nt][e] - Ds[buf][qi]);  // dS^T
       }
     }
-    mma_pv<T, HD, LD>(dv, pt, dOs0 + buf * BQ * LD, lane);
-    mma_pv<T, HD, LD>(dk, st, Qs0 + buf * BQ * LD, lane);
+    mma_pv<T, HD, LD>(dv, st, dOs0 + buf * BQ * LD, lane);
+    mma_pv<T, HD, LD>(dk, dpt, Qs0 + buf * BQ * LD, lane);
     __syncthreads();
   }
   T* out = dqkv + (int64_t)b * Tlen * lddq;

@@ -1617,9 +1617,13 @@ __global__ void __launch_bounds__(256) head_loss_kernel(const float2* __restrict
     }
     const float2* st = stats + (int64_t)row * width;
     float m = -INFINITY, s = 0.f;
-    for (int i = lane; i < width; i += 32) {
-      const float2 p = st[i];
-      lse_merge(m, s, p.x, p.y);
+    // entries lane, lane + 32, ... merged in that order, eight loads in flight
+    for (int i0 = lane; i0 < width; i0 += 8 * 32) {
+      float2 p[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) p[k] = i0 + 32 * k < width ? st[i0 + 32 * k] : make_float2(-INFINITY, 0.f);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) lse_merge(m, s, p[k].x, p[k].y);
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -1649,17 +1653,30 @@ __global__ void __launch_bounds__(256) head_loss_kernel(const float2* __restrict
     }
   }
   __syncthreads();
-  // 32 blocks x 32 rows at a time: row-contiguous reads of m_b, transposed
-  // through shared memory, block-contiguous writes
-  __shared__ float s_m[32][33];
+  // 128 blocks x 32 rows at a time: row-contiguous reads of m_b (each thread
+  // four in flight), transposed through shared memory, block-contiguous writes
+  __shared__ float s_m[32][129];
   const int nrow = min(32, rows - row0);
-  for (int b0 = 0; b0 < width; b0 += 32) {
-    for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
-      const int rr = i >> 5, bb = i & 31;
-      s_m[rr][bb] = (rr < nrow && b0 + bb < width) ? stats[(int64_t)(row0 + rr) * width + b0 + bb].x : -INFINITY;
+  for (int b0 = 0; b0 < width; b0 += 128) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = threadIdx.x + q * 256;  // 0..1023: (row rr, block pair) of the 32 x 128 tile
+      const int rr = i >> 5, bb = (i & 31) * 4;
+      float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      if (rr < nrow) {
+        const float2* src = stats + (int64_t)(row0 + rr) * width + b0 + bb;
+        if (b0 + bb < width) v.x = src[0].x;
+        if (b0 + bb + 1 < width) v.y = src[1].x;
+        if (b0 + bb + 2 < width) v.z = src[2].x;
+        if (b0 + bb + 3 < width) v.w = src[3].x;
+      }
+      s_m[rr][bb] = v.x;
+      s_m[rr][bb + 1] = v.y;
+      s_m[rr][bb + 2] = v.z;
+      s_m[rr][bb + 3] = v.w;
     }
     __syncthreads();
-    for (int i = threadIdx.x; i < 1024; i += blockDim.x) {
+    for (int i = threadIdx.x; i < 4096; i += blockDim.x) {
       const int bb = i >> 5, rr = i & 31;
       if (rr < nrow && b0 + bb < width) {
         const float mb = s_m[rr][bb];

@@ -29,16 +29,25 @@ optimized_v3.py:135-177): inside the backward each tile's forward is followed
 immediately by its VJP (its cotangent is known before the layer starts), so
 the [tile, 2*d_ff] intermediate is bounded without recomputing the MLP.
 
+With one MLP tile and the stream layout on, the sweep is software-pipelined:
+a layer's forward recompute (everything above that needs only the layer's
+input states: A and M with their saved internals and the reconstructed
+states) depends on nothing from the VJP of the layer above, so layer i-1's
+recompute runs on a stream of its own while layer i's VJP runs on the
+compute stream (the first one beside the head), and the VJP of each layer
+waits only for its own recompute.
+
 Weight gradients accumulate in fp32 (deterministic split reductions), never
 written to .grad here; callers decide where they go.
 """
 from __future__ import annotations
 
 from dataclasses import dataclass
+from types import SimpleNamespace
 
 import torch
 
-from . import functional as fn
+from . import _lib, functional as fn
 
 F32 = torch.float32
 
@@ -119,6 +128,8 @@ class LayerKernels:
         # reconstruction (needed only by the next layer) run here beside the
         # attention VJP; layer_done() joins them
         self.aux = torch.cuda.Stream(device=wgrad_stream.device) if wgrad_stream is not None else None
+        # pipelined sweep: layer i-1's forward recompute beside layer i's VJP
+        self.rec = torch.cuda.Stream(device=wgrad_stream.device) if wgrad_stream is not None else None
         self._aux_done = None
         self._aux_held = []
         self._aux_used = False
@@ -386,6 +397,103 @@ class LayerKernels:
         return prev_p, prev_q, dp_new, dq_eff, gm_next
 
 
+    # ------------------------------------------------------- pipelined sweep
+    def pipelined(self, M: int) -> bool:
+        """The split recompute / VJP sweep applies: stream layout on and the
+        MLP in one tile (a tiled MLP interleaves each tile's forward and VJP
+        to bound its intermediate, which the split would not)."""
+        return self.rec is not None and (not self.mlp_tokens or self.mlp_tokens <= 0 or self.mlp_tokens >= M)
+
+    def _mlp_forward_saved(self, lw, y=None, x=None, a=None):
+        """M's forward with what its VJP needs: (m, n2, ysum, rstd2, hg, u)."""
+        n2, ysum, rstd2 = self._mlp_norm(lw, y, x, a, save=True)
+        if fn.swiglu_fusable(n2, lw.up_c):
+            hg, u = fn.linear_swiglu_fwd(n2, lw.up_c, save_u=True)
+        else:
+            u = fn.linear_fwd(n2, lw.up_c)
+            hg = fn.swiglu_fwd(u)
+        return fn.linear_fwd(hg, lw.down_c), n2, ysum, rstd2, hg, u
+
+    def recompute(self, lw, p, q, method: str, h: float):
+        """Issues a layer's forward recompute at states (p, q): for midpoint
+        x = p, a = A(x), m = M(x + a), p_prev = q - round(2h (a + m)),
+        q_prev = x; for Euler m = M(q), p_prev = p - m, a = A(p_prev),
+        q_prev = q - a. With the stream layout the kernels go to the recompute
+        stream after the compute stream's queued work; tensors are allocated
+        in the compute stream's order and stay referenced by the returned
+        record until vjp() has made the compute stream wait for them."""
+        if self.rec is not None:
+            ready = torch.cuda.Event()
+            ready.record()
+            self.rec.wait_event(ready)
+            ctx = _lib.launch_on(self.rec)
+        else:
+            ctx = _nullcontext()
+        r = SimpleNamespace(method=method, p=p, q=q)
+        with ctx:
+            if method == "midpoint":
+                x = p
+                a, sa = self.attn_forward(lw, x, save=True)
+                m, n2, ysum, rstd2, hg, u = self._mlp_forward_saved(lw, x=x, a=a)
+                r.prev_p = fn.reconstruct_midpoint_sum(q, a, m, 2.0 * h)
+                r.prev_q = x
+            else:
+                m, n2, ysum, rstd2, hg, u = self._mlp_forward_saved(lw, y=q)
+                r.prev_p = fn.reconstruct_euler(p, m)
+                x = r.prev_p
+                a, sa = self.attn_forward(lw, x, save=True)
+                r.prev_q = fn.reconstruct_euler(q, a)
+        r.x, r.sa, r.n2, r.ysum, r.rstd2, r.hg, r.u, r.a, r.m = x, sa, n2, ysum, rstd2, hg, u, a, m
+        if self.rec is not None:
+            r.done = torch.cuda.Event()
+            r.done.record(self.rec)
+        return r
+
+    def vjp(self, lw, g: LayerGrads, r, dp, dq, h: float, g_lp=None, carry: bool = False):
+        """The VJP of the layer recomputed in `r` (issued on the compute
+        stream after it). Midpoint: gF = g_lp or round(2h round(dq)); returns
+        (p_prev, q_prev, dq, dq_new[, gF of the layer below]). Euler: gm = g_lp
+        or round(dp); returns (p_prev, q_prev, dp_new, dq_eff[, gm below])."""
+        if self.rec is not None:
+            torch.cuda.current_stream().wait_event(r.done)
+        mid = r.method == "midpoint"
+        gm = g_lp if g_lp is not None else fn.cast_scale(dq if mid else dp, self.cd, 2.0 * h if mid else 1.0)
+        if fn.dgrad_swiglu_fusable(gm, lw.down_c, r.u):  # SwiGLU backward in the dgrad epilogue
+            du = fn.linear_dgrad_swiglu(gm, lw.down_c, r.u)
+            self._wgrad(gm, r.hg, g.down)
+        else:
+            dh = fn.linear_dgrad(gm, lw.down_c)
+            self._wgrad(gm, r.hg, g.down)
+            du = fn.swiglu_bwd(r.u, dh)
+            del dh
+        self._wgrad(du, r.n2, g.up)
+        dn2 = fn.linear_dgrad(du, lw.up_c)
+        del du
+        if mid:
+            # dxacc = M^T gF + dp ; da = round(gF + round(M^T gF))
+            dxacc, da = fn.rmsnorm_bwd_fused(r.ysum, lw.mlp_norm, r.rstd2, dn2, g.mlp_norm, residual=dp, lp_add=gm,
+                                             lp_dtype=self.cd)
+            if not carry:
+                return r.prev_p, r.prev_q, dq, self.attn_vjp(lw, g, r.x, r.sa, da, residual=dxacc)
+            dq_new, g_next = self.attn_vjp(lw, g, r.x, r.sa, da, residual=dxacc, lp_scale=2.0 * h)
+            return r.prev_p, r.prev_q, dq, dq_new, g_next
+        # dq_eff = dq' + M^T round(dp') ; ga = round(dq_eff)
+        dq_eff, ga = fn.rmsnorm_bwd_fused(r.ysum, lw.mlp_norm, r.rstd2, dn2, g.mlp_norm, residual=dq,
+                                          lp_dtype=self.cd)
+        if not carry:
+            return r.prev_p, r.prev_q, self.attn_vjp(lw, g, r.x, r.sa, ga, residual=dp), dq_eff
+        dp_new, g_next = self.attn_vjp(lw, g, r.x, r.sa, ga, residual=dp, lp_scale=1.0)
+        return r.prev_p, r.prev_q, dp_new, dq_eff, g_next
+
+
+class _nullcontext:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
 def compute_dtype(amp_enabled: bool, amp_dtype: torch.dtype, state_dtype: torch.dtype) -> torch.dtype:
     return amp_dtype if amp_enabled else state_dtype
 
@@ -397,11 +505,14 @@ def stack_forward(kern: LayerKernels, layers, p, q, method: str, h: float):
     return p, q
 
 
-def stack_backward(kern: LayerKernels, layers, grads, p, q, dp, dq, method: str, h: float, on_layer_done=None):
+def stack_backward(kern: LayerKernels, layers, grads, p, q, dp, dq, method: str, h: float, on_layer_done=None,
+                   first=None):
     """Reverse sweep over all layers; grads[i] receives layer i's weight grads.
     on_layer_done(i, events) is called once layer i's backward is issued; its
     weight gradients are final after `events` (used to launch that layer's
     data-parallel gradient bucket on a communication stream)."""
+    if first is not None or kern.pipelined(p.shape[0]):
+        return _stack_backward_pipelined(kern, layers, grads, p, q, dp, dq, method, h, on_layer_done, first)
     g_lp = None  # the next layer's low-precision cotangent, formed in the previous epilogue
     for i in reversed(range(len(layers))):
         if method == "midpoint":
@@ -413,5 +524,26 @@ def stack_backward(kern: LayerKernels, layers, grads, p, q, dp, dq, method: str,
         kern.layer_done()
         if on_layer_done is not None:
             on_layer_done(i, kern.grads_ready() if torch.cuda.is_available() and p.is_cuda else None)
+    kern.sync()
+    return p, q, dp, dq
+
+
+def _stack_backward_pipelined(kern: LayerKernels, layers, grads, p, q, dp, dq, method: str, h: float,
+                              on_layer_done, first):
+    """The reverse sweep with layer i-1's recompute issued before layer i's
+    VJP (so it runs beside it); `first` is the top layer's recompute if the
+    caller issued it already (beside the head)."""
+    n = len(layers)
+    cur = first if first is not None else kern.recompute(layers[n - 1], p, q, method, h)
+    g_lp = None
+    for i in reversed(range(n)):
+        nxt = kern.recompute(layers[i - 1], cur.prev_p, cur.prev_q, method, h) if i > 0 else None
+        out = kern.vjp(layers[i], grads[i], cur, dp, dq, h, g_lp, carry=i > 0)
+        p, q, dp, dq = out[:4]
+        g_lp = out[4] if i > 0 else None
+        cur = nxt
+        kern.layer_done()
+        if on_layer_done is not None:
+            on_layer_done(i, kern.grads_ready() if p.is_cuda else None)
     kern.sync()
     return p, q, dp, dq

@@ -136,8 +136,22 @@ def bench_swiglu(iters):
         _lib.call("rk_gemm_dgrad", gys[k].data_ptr(), D, down.data_ptr(), FF, dhs[k].data_ptr(), FF, N_TOK, D, FF,
                   _lib.BF16, _lib.BF16, _lib.stream_ptr())
         bwd(k)
+    ns_x = sets_for(2 * N_TOK * D + 2 * N_TOK * 3 * FF)
+    xs = [torch.randn(N_TOK, D, device="cuda").bfloat16() for _ in range(ns_x)]
+    up = (torch.randn(2 * FF, D, device="cuda") * 0.02).bfloat16()
+
+    def up_fused(k):  # up projection with SwiGLU in the epilogue (h only)
+        _lib.call("rk_gemm_fprop_swiglu", xs[k % ns_x].data_ptr(), D, up.data_ptr(), D, hs[k].data_ptr(), FF, None,
+                  2 * FF, N_TOK, FF, D, _lib.BF16, _lib.stream_ptr())
+
+    def up_fused_save(k):  # the same, also writing u for the backward
+        _lib.call("rk_gemm_fprop_swiglu", xs[k % ns_x].data_ptr(), D, up.data_ptr(), D, hs[k].data_ptr(), FF,
+                  us_[k].data_ptr(), 2 * FF, N_TOK, FF, D, _lib.BF16, _lib.stream_ptr())
+    up_flops = 2 * N_TOK * D * 2 * FF
     fused_bytes = 2 * N_TOK * D + 2 * D * FF + 2 * N_TOK * 2 * FF * 2
-    return [("hbm", "swiglu_fwd", 2 * N_TOK * 2 * FF + 2 * N_TOK * FF, time_graph(fwd, ns, iters)),
+    return [("tensor", "up_gemm_swiglu", up_flops, time_graph(up_fused, ns, iters)),
+            ("tensor", "up_gemm_swiglu_save_u", up_flops, time_graph(up_fused_save, ns, iters)),
+            ("hbm", "swiglu_fwd", 2 * N_TOK * 2 * FF + 2 * N_TOK * FF, time_graph(fwd, ns, iters)),
             ("hbm", "swiglu_bwd", 2 * N_TOK * 2 * FF * 2 + 2 * N_TOK * FF, time_graph(bwd, ns, iters)),
             ("hbm", "dgrad_swiglu_fused", fused_bytes, time_graph(dgrad_fused, ns, iters)),
             ("hbm", "dgrad_then_swiglu_bwd", fused_bytes, time_graph(dgrad_separate, ns, iters))]

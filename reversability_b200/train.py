@@ -153,9 +153,11 @@ class ReversibleTrainer:
         self.opt_scalars[0] = settings.learning_rate
         self.norm_ws = torch.empty(_lib.lib().rk_clip_adamw_workspace() // 4, device=dev, dtype=F32)
         # DP buckets: one per layer (launched as the last microstep's sweep passes it),
-        # then the embedding, position and final-norm gradients
-        self.buckets = GradBuckets(self.layer_slices + [self.g_tok, self.g_pos, self.g_final], process_group,
-                                   dev) if self.world > 1 else None
+        # then the embedding, position and final-norm gradients, and the loss sum
+        # (launched once the last microstep's loss is in, so every rank returns
+        # the global loss)
+        self.buckets = GradBuckets(self.layer_slices + [self.g_tok, self.g_pos, self.g_final, self.loss_sum],
+                                   process_group, dev) if self.world > 1 else None
         self.graph = None
         self.head_events = None
 
@@ -202,6 +204,10 @@ class ReversibleTrainer:
         ids = self.ids[m]
         labels = self.labels[m].reshape(-1)
         p, q = states if states is not None else self._forward_states(m)
+        # the top layer's forward recompute only needs the final states: issued
+        # now, it runs beside the head
+        first = kern.recompute(self.layers[-1], p, q, self.model.method, self.model.step_size) \
+            if kern.pipelined(p.shape[0]) else None
         out = q if self.model.method == "midpoint" else p
         eps_f = self.model.final_norm.eps if self.model.final_norm.eps is not None else torch.finfo(F32).eps
         hidden, rstd_f = fn.rmsnorm_fwd(out, self.final_w, eps_f, out_dtype=self.cd)
@@ -223,6 +229,7 @@ class ReversibleTrainer:
             fn.head_loss(st, 1.0, self.inv_denominator, loss_rows=loss_rows, rowc=self.head_rowc,
                          fcoef=self.head_fcoef)
             self.loss_sum += loss_rows.sum()
+            self._loss_bucket(last)
             if kern.side is not None:
                 # the head weight gradient runs beside the dgrad and the
                 # reverse sweep; the sweep's final join (stack_backward) orders
@@ -239,6 +246,7 @@ class ReversibleTrainer:
                       self.inv_denominator.data_ptr(), loss_rows.data_ptr(), logits.data_ptr(), self.vpad,
                       _lib.code(self.cd), -100, _lib.stream_ptr())
             self.loss_sum += loss_rows.sum()
+            self._loss_bucket(last)
             dhidden = fn.linear_dgrad(logits, self.tok_c)
             fn.linear_wgrad(logits, hidden, dw=self.g_tok, accumulate=True)
         dout, _ = fn.rmsnorm_bwd(out, self.final_w, rstd_f, dhidden, dx_dtype=F32, dw=self.g_final,
@@ -247,9 +255,13 @@ class ReversibleTrainer:
         dp, dq = (None, dout) if self.model.method == "midpoint" else (dout, None)
         hook = self._bucket_hook if (last and self.world > 1) else None
         _, _, dp, dq = engine.stack_backward(kern, self.layers, self.layer_grads, p, q, dp, dq, self.model.method,
-                                             self.model.step_size, on_layer_done=hook)
+                                             self.model.step_size, on_layer_done=hook, first=first)
         # boundary p = q = embedding: both cotangents reach it (summed inside the kernel)
         fn.embedding_bwd(ids, dp, self.g_tok, self.g_pos, dx2=dq)
+
+    def _loss_bucket(self, last: bool):
+        if last and self.world > 1:
+            self.buckets.launch(len(self.layers) + 3)
 
     def _bucket_hook(self, layer: int, events=None):
         self.buckets.launch(layer, after=events)

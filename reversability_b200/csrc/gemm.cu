@@ -1404,12 +1404,24 @@ bool dims_ok(int64_t M, int64_t N, int64_t K) {
   return M >= 0 && N > 0 && K >= 0 && M < (1ll << 31) && N < (1ll << 31) && K < (1ll << 31);
 }
 
+// Output-tile width of the split weight-gradient GEMM: 256 (each 64-token
+// k-block brings 48 KB for 4.2 MFLOP instead of 32 KB for 2.1 MFLOP, and the
+// operand loads from L2, not the MMA, bound the narrow tiles; the MLP
+// backward GEMMs measured 86 us against 97 us with 128-wide tiles).
+// REVK_WGRAD_BN=128 in the environment selects the narrow tiles (a tuning switch).
+int wgrad_bn() {
+  static const int bn = [] {
+    const char* e = getenv("REVK_WGRAD_BN");
+    return (e && atoi(e) == 128) ? 128 : 256;
+  }();
+  return bn;
+}
+
 int wgrad_splits(int64_t M, int64_t N, int64_t K) {
-  // Output tiles of dW[N,K] (128x128 when split: the fp32 slice traffic is
-  // slices x N x K, and narrower tiles halve the slice count for the same
-  // SM fill); choose slices so that tiles*slices fills ~the SMs, with each
-  // slice at least 8 k-blocks (512 tokens) long. Fixed per shape.
-  const int64_t tiles = ((N + 127) / 128) * ((K + 127) / 128);
+  // Output tiles of dW[N,K] (128 x wgrad_bn() when split); choose slices so
+  // that tiles*slices fills ~the SMs, with each slice at least 8 k-blocks
+  // (512 tokens) long. Fixed per shape.
+  const int64_t tiles = ((N + 127) / 128) * ((K + wgrad_bn() - 1) / wgrad_bn());
   const int64_t kb = (M + 63) / 64;
   int64_t s = (148 + tiles - 1) / tiles;
   if (s > kb / 8) s = kb / 8;
@@ -1479,7 +1491,7 @@ extern "C" int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_
   const int64_t need = (int64_t)splits * slice_rows * K * (int64_t)sizeof(float);
   if (!workspace || workspace_bytes < need) return RK_ERR_WORKSPACE;
   const int st = tc_gemm({dy, lddy, true}, {x, ldx, true}, (int)N, (int)K, (int)M, dtype, workspace, K, RK_F32,
-                         splits, s, false, (int)slice_rows, 128);
+                         splits, s, false, (int)slice_rows, wgrad_bn());
   if (st != RK_OK) return st;
   const bool vec = K % 4 == 0 && lddw % 4 == 0 && rk_host::aligned(dw, 16) && rk_host::aligned(workspace, 16);
   int64_t blocks = (N * K / (vec ? 4 : 1) + 255) / 256;

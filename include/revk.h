@@ -100,6 +100,13 @@ RK_API int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float* rst
                                 const float* residual, const void* lp_add, void* lp_out, int lp_dtype, float lp_scale,
                                 float* dx_out, float* dw, int accumulate_dw, float* dw_partial,
                                 int64_t workspace_bytes, int64_t rows, int64_t width, void* stream);
+/* The weight-gradient reduction of rk_rmsnorm_bwd_fused on its own: called
+ * with dw = NULL, rk_rmsnorm_bwd_fused leaves its per-CTA partials in
+ * dw_partial; this sums them in the same fixed order into dw (dw += sum when
+ * accumulate_dw != 0), on any stream ordered after it. rows and width are
+ * those of the backward that wrote the partials. */
+RK_API int rk_rmsnorm_dw_reduce(const float* dw_partial, int64_t rows, int64_t width, float* dw, int accumulate_dw,
+                                void* stream);
 
 /* Allocation-free rk_rmsnorm_bwd. It has no counterpart in the reference: it
  * exists for callers that cannot supply device workspace — foreign-function

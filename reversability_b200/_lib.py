@@ -59,6 +59,7 @@ SIGNATURES: dict[str, tuple] = {
     "rk_cast_scale": (_i, [_p, _p, _i, _f, _i64, _p]),
     "rk_add_rmsnorm_fwd": (_i, [_p, _p, _i, _p, _p, _i, _p, _p, _i64, _i64, _f, _p]),
     "rk_rmsnorm_bwd_fused": (_i, [_p, _p, _p, _p, _i, _p, _p, _p, _i, _f, _p, _p, _i, _p, _i64, _i64, _i64, _p]),
+    "rk_rmsnorm_dw_reduce": (_i, [_p, _i64, _i64, _p, _i, _p]),
     "rk_cross_entropy_fwd_bwd": (_i, [_p, _i64, _i64, _p, _i64, _f, _p, _p, _p, _i64, _i, _i, _p]),
     "rk_head_stats_width": (_i64, [_i64]),
     "rk_head_fprop": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _p, _i64, _i64, _i64, _i, _p]),

@@ -53,10 +53,10 @@ __global__ void keys_kernel(const int64_t* __restrict__ ids, int64_t* __restrict
 }
 
 // Token-gradient reduction in two fixed-order passes over the sorted rows.
-// Pass 1: warp w owns sorted positions [32w, 32w+32); it sums the rows of each
-// run piece inside its range in position order (lanes over columns, one
-// 16-byte vector per lane per row) and writes the piece's sum at
-// piece[start of the piece]. Pass 2: the CTA of each run start adds the pieces
+// Pass 1: warp w owns sorted positions [32r, 32r+32) and 128-column chunk c
+// (w = r * chunks + c); it sums the rows of each run piece inside its range in
+// position order (one 16-byte vector per lane per row, eight row loads in
+// flight) and writes the piece's sum at piece[start of the piece]. Pass 2: the CTA of each run start adds the pieces
 // of its run (one per 32-row range it overlaps) in range order into g_tok.
 // Every sum has a fixed order, so g_tok is bitwise reproducible, and a long
 // run (a frequent token) is read by many warps in parallel.
@@ -67,33 +67,53 @@ __global__ void __launch_bounds__(256) emb_tok_piece_kernel(const int64_t* __res
                                                             int64_t rows, int d) {
   pdl_wait();  // inputs are the previous kernel's outputs
   const int lane = threadIdx.x & 31;
-  const int64_t r0 = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * 32;
+  // warp gw: 32-row range gw / nch, 128-column chunk gw % nch
+  const int nch = (d + 127) / 128;
+  const int64_t gw = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int64_t r0 = gw / nch * 32;
   if (r0 >= rows) return;
-  const int64_t r1 = r0 + 32 < rows ? r0 + 32 : rows;
-  for (int c0 = 0; c0 < d; c0 += 128) {
-    const int c = c0 + lane * 4;
-    int64_t start = r0;
+  const int n = (int)(r0 + 32 < rows ? 32 : rows - r0);
+  // the warp's sorted rows and run ends, one per lane; every row load is
+  // issued ahead of its add (eight in flight), the adds stay in row order
+  const int my_row = lane < n ? srows[r0 + lane] : 0;
+  const int64_t my_key = lane < n ? skeys[r0 + lane] : 0;
+  const int64_t next_key = lane + 1 < n ? skeys[r0 + lane + 1] : my_key;
+  const unsigned run_end = __ballot_sync(0xffffffffu, lane < n && (lane + 1 == n || next_key != my_key));
+  {
+    const int c = (int)(gw % nch) * 128 + lane * 4;
+    int start = 0;
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int64_t j = r0; j < r1; ++j) {
-      if (c < d) {
-        float v[4];
-        const int64_t off = (int64_t)srows[j] * d + c;
-        load_vec<float, 4>(dx + off, v);
-        if (dx2) {
-          float v2[4];
-          load_vec<float, 4>(dx2 + off, v2);
+    for (int j0 = 0; j0 < n; j0 += 8) {
+      float v[8][4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) v[e] += v2[e];
+      for (int u = 0; u < 8; ++u) {
+        const int row = __shfl_sync(0xffffffffu, my_row, (j0 + u) & 31);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) v[u][e] = 0.f;
+        if (j0 + u < n && c < d) {
+          const int64_t off = (int64_t)row * d + c;
+          load_vec<float, 4>(dx + off, v[u]);
+          if (dx2) {
+            float v2[4];
+            load_vec<float, 4>(dx2 + off, v2);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) v[u][e] += v2[e];
+          }
         }
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] += v[e];
       }
-      const bool last = (j + 1 == r1) || (skeys[j + 1] != skeys[j]);
-      if (last) {
-        if (c < d) store_vec<float, 4>(piece + start * d + c, acc);
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] = 0.f;
-        start = j + 1;
+      for (int u = 0; u < 8; ++u) {
+        const int j = j0 + u;
+        if (j < n) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[e] += v[u][e];
+          if ((run_end >> j) & 1u) {
+            if (c < d) store_vec<float, 4>(piece + (r0 + start) * d + c, acc);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[e] = 0.f;
+            start = j + 1;
+          }
+        }
       }
     }
   }
@@ -116,9 +136,27 @@ __global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restr
     if (skeys[mid] == id) lo = mid + 1; else hi = mid;
   }
   const int64_t end = lo;
+  // one piece per 32-row range of the run, summed in range order with eight
+  // loads in flight
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
     float s = 0.f;
-    for (int64_t p = i; p < end; p = (p / 32 + 1) * 32) s += piece[p * d + c];  // one piece per 32-row range
+    int64_t p = i;
+    while (p < end) {
+      float t[8];
+      int cnt = 0;
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        t[u] = 0.f;
+        if (p < end) {
+          t[u] = piece[p * d + c];
+          p = (p / 32 + 1) * 32;
+          ++cnt;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (u < cnt) s += t[u];
+    }
     g_tok[id * d + c] += s;
   }
 }
@@ -200,7 +238,9 @@ extern "C" int rk_embedding_bwd(const int64_t* ids, const float* dx, const float
       cudaSuccess)
     return RK_ERR_LAUNCH;
   rk_host::count_launch();
-  rk_host::launch_k(emb_tok_piece_kernel, (unsigned)((rows + 255) / 256), 256, 0, s, skeys, srows, dx, dx2, piece, rows, (int)d);
+  const int64_t piece_warps = (rows + 31) / 32 * ((d + 127) / 128);
+  rk_host::launch_k(emb_tok_piece_kernel, (unsigned)((piece_warps + 7) / 8), 256, 0, s, skeys, srows, dx, dx2, piece,
+                    rows, (int)d);
   st = rk_host::launch_status();
   if (st) return st;
   rk_host::launch_k(emb_tok_bwd_kernel, (unsigned)rows, 256, 0, s, skeys, piece, g_tok, rows, (int)d, V, rk_host::device_status_ptr());

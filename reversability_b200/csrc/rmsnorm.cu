@@ -576,7 +576,7 @@ extern "C" int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float*
                                     const float* residual, const void* lp_add, void* lp_out, int lp_dtype,
                                     float lp_scale, float* dx_out, float* dw, int accumulate_dw, float* dw_partial,
                                     int64_t workspace_bytes, int64_t rows, int64_t width, void* stream) {
-  if (!x || !w || !rstd || !dy || !dx_out || !dw || !dw_partial || rows < 0 || width <= 0) return RK_ERR_ARG;
+  if (!x || !w || !rstd || !dy || !dx_out || !dw_partial || rows < 0 || width <= 0) return RK_ERR_ARG;
   if (lp_add && !lp_out) return RK_ERR_ARG;
   if (width > 1024) return RK_ERR_UNSUPPORTED;
   if (width % 4 || !rk_host::aligned(x, 16) || !rk_host::aligned(w, 16) || !rk_host::aligned(dx_out, 16) ||
@@ -586,7 +586,7 @@ extern "C" int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float*
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int W = (int)width;
   if (rows == 0) {
-    if (!accumulate_dw) cudaMemsetAsync(dw, 0, sizeof(float) * W, s);
+    if (dw && !accumulate_dw) cudaMemsetAsync(dw, 0, sizeof(float) * W, s);
     return rk_host::launch_status();
   }
   const int parts = rms_parts(rows);
@@ -605,7 +605,19 @@ extern "C" int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float*
   else
     return RK_ERR_DTYPE;
   if (st != RK_OK) return st;
+  if (!dw) return RK_OK;  // partials left for rk_rmsnorm_dw_reduce
   rk_host::launch_k(rmsnorm_dw_reduce_kernel, (W + 31) / 32, 1024, 0, s, dw_partial, dw, parts, W, accumulate_dw);
+  return rk_host::launch_status();
+}
+
+extern "C" int rk_rmsnorm_dw_reduce(const float* dw_partial, int64_t rows, int64_t width, float* dw,
+                                    int accumulate_dw, void* stream) {
+  if (!dw_partial || !dw || rows <= 0 || width <= 0) return RK_ERR_ARG;
+  if (width > 1024) return RK_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int W = (int)width;
+  rk_host::launch_k(rmsnorm_dw_reduce_kernel, (W + 31) / 32, 1024, 0, s, dw_partial, dw, rms_parts(rows), W,
+                    accumulate_dw);
   return rk_host::launch_status();
 }
 

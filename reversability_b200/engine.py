@@ -147,6 +147,25 @@ class LayerKernels:
         self._held += [dy, x]
         self._side_used = True
 
+    def _norm_bwd(self, x, w, rstd, dy, dw, residual=None, lp_add=None, lp_dtype=None, lp_scale=1.0, dx_out=None,
+                  lp_out=None):
+        """rmsnorm_bwd_fused; with a side stream its weight-gradient reduction
+        (dw += fixed-order sum of the per-CTA partials) runs there, off the
+        compute stream's chain, the partials held until a later join."""
+        if self.side is None:
+            return fn.rmsnorm_bwd_fused(x, w, rstd, dy, dw, residual=residual, lp_add=lp_add, lp_dtype=lp_dtype,
+                                        lp_scale=lp_scale, dx_out=dx_out, lp_out=lp_out)
+        dx, lp, part = fn._rmsnorm_bwd_fused(x, w, rstd, dy, None, residual, lp_add, lp_dtype, dx_out, lp_out, True,
+                                             lp_scale)
+        ready = torch.cuda.Event()
+        ready.record()
+        self.side.wait_event(ready)
+        with torch.cuda.stream(self.side):
+            fn.rmsnorm_dw_reduce(part, x.shape[0], x.shape[1], dw)
+        self._held.append(part)
+        self._side_used = True
+        return dx, lp
+
     def _on_aux(self, *held):
         """Context for work on the aux stream after the compute stream's current
         work; `held` stay referenced until layer_done() joins the aux stream."""
@@ -254,10 +273,10 @@ class LayerKernels:
         self._wgrad(dqkv2, n1, g.qkv)
         dn1 = fn.linear_dgrad(dqkv2, lw.qkv_c)
         if lp_scale is None:
-            dx, _ = fn.rmsnorm_bwd_fused(x, lw.attn_norm, rstd1, dn1, g.attn_norm, residual=residual)
+            dx, _ = self._norm_bwd(x, lw.attn_norm, rstd1, dn1, g.attn_norm, residual=residual)
             return dx
-        return fn.rmsnorm_bwd_fused(x, lw.attn_norm, rstd1, dn1, g.attn_norm, residual=residual,
-                                    lp_dtype=self.cd, lp_scale=lp_scale)
+        return self._norm_bwd(x, lw.attn_norm, rstd1, dn1, g.attn_norm, residual=residual,
+                              lp_dtype=self.cd, lp_scale=lp_scale)
 
     # ---------------------------------------------------------- MLP sublayer
     def _tiles(self, M):
@@ -328,10 +347,10 @@ class LayerKernels:
             self._wgrad(du, n2[s:e], g.up)
             dn2 = fn.linear_dgrad(du, lw.up_c)
             del du
-            fn.rmsnorm_bwd_fused(ysum[s:e], lw.mlp_norm, rstd2[s:e], dn2, g.mlp_norm,
-                                 residual=None if residual is None else residual[s:e],
-                                 lp_add=None if lp_add is None else lp_add[s:e],
-                                 dx_out=dxo[s:e], lp_out=None if lp is None else lp[s:e])
+            self._norm_bwd(ysum[s:e], lw.mlp_norm, rstd2[s:e], dn2, g.mlp_norm,
+                           residual=None if residual is None else residual[s:e],
+                           lp_add=None if lp_add is None else lp_add[s:e],
+                           dx_out=dxo[s:e], lp_out=None if lp is None else lp[s:e])
         return m, dxo, lp
 
     # ---------------------------------------------------------- layer steps
@@ -471,15 +490,15 @@ class LayerKernels:
         del du
         if mid:
             # dxacc = M^T gF + dp ; da = round(gF + round(M^T gF))
-            dxacc, da = fn.rmsnorm_bwd_fused(r.ysum, lw.mlp_norm, r.rstd2, dn2, g.mlp_norm, residual=dp, lp_add=gm,
-                                             lp_dtype=self.cd)
+            dxacc, da = self._norm_bwd(r.ysum, lw.mlp_norm, r.rstd2, dn2, g.mlp_norm, residual=dp, lp_add=gm,
+                                       lp_dtype=self.cd)
             if not carry:
                 return r.prev_p, r.prev_q, dq, self.attn_vjp(lw, g, r.x, r.sa, da, residual=dxacc)
             dq_new, g_next = self.attn_vjp(lw, g, r.x, r.sa, da, residual=dxacc, lp_scale=2.0 * h)
             return r.prev_p, r.prev_q, dq, dq_new, g_next
         # dq_eff = dq' + M^T round(dp') ; ga = round(dq_eff)
-        dq_eff, ga = fn.rmsnorm_bwd_fused(r.ysum, lw.mlp_norm, r.rstd2, dn2, g.mlp_norm, residual=dq,
-                                          lp_dtype=self.cd)
+        dq_eff, ga = self._norm_bwd(r.ysum, lw.mlp_norm, r.rstd2, dn2, g.mlp_norm, residual=dq,
+                                    lp_dtype=self.cd)
         if not carry:
             return r.prev_p, r.prev_q, self.attn_vjp(lw, g, r.x, r.sa, ga, residual=dp), dq_eff
         dp_new, g_next = self.attn_vjp(lw, g, r.x, r.sa, ga, residual=dp, lp_scale=1.0)

@@ -390,6 +390,28 @@ def rmsnorm_bwd_fused(x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor,
     """dx_out = rmsnorm_bwd(dy) + residual (fp32); lp_out = round(lp_add + round(dx)) if lp_add else
     round(round(dx_out) * lp_scale) (cast_scale of the total) when lp_dtype is given. dw
     accumulates. Returns (dx_out, lp_out)."""
+    dx_out, lp_out, _ = _rmsnorm_bwd_fused(x, weight, rstd, dy, dw, residual, lp_add, lp_dtype, dx_out, lp_out,
+                                           accumulate_dw, lp_scale)
+    return dx_out, lp_out
+
+
+def rmsnorm_bwd_fused_deferred(x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor, dy: torch.Tensor,
+                               residual: torch.Tensor | None = None, lp_add: torch.Tensor | None = None,
+                               lp_dtype: torch.dtype | None = None, lp_scale: float = 1.0):
+    """rmsnorm_bwd_fused without the weight-gradient reduction: returns
+    (dx_out, lp_out, partials); rmsnorm_dw_reduce(partials, rows, width, dw)
+    finishes dw later (on any stream ordered after this one)."""
+    return _rmsnorm_bwd_fused(x, weight, rstd, dy, None, residual, lp_add, lp_dtype, None, None, True, lp_scale)
+
+
+def rmsnorm_dw_reduce(partials: torch.Tensor, rows: int, width: int, dw: torch.Tensor, accumulate: bool = True):
+    """dw (+)= the fixed-order sum of the partials a deferred rmsnorm_bwd_fused left."""
+    require_cuda(partials, dw)
+    _lib.call("rk_rmsnorm_dw_reduce", partials.data_ptr(), rows, width, dw.data_ptr(), int(accumulate),
+              _lib.stream_ptr())
+
+
+def _rmsnorm_bwd_fused(x, weight, rstd, dy, dw, residual, lp_add, lp_dtype, dx_out, lp_out, accumulate_dw, lp_scale):
     require_cuda(x, weight, rstd, dy)
     rows, width = x.shape
     dx_out = dx_out if dx_out is not None else torch.empty((rows, width), device=x.device, dtype=torch.float32)
@@ -400,8 +422,8 @@ def rmsnorm_bwd_fused(x: torch.Tensor, weight: torch.Tensor, rstd: torch.Tensor,
     _lib.call("rk_rmsnorm_bwd_fused", x.data_ptr(), weight.data_ptr(), rstd.data_ptr(), dy.data_ptr(),
               _lib.code(dy.dtype), _lib.ptr(residual), _lib.ptr(lp_add), _lib.ptr(lp_out),
               _lib.code(lp_out.dtype) if lp_out is not None else _lib.code(dy.dtype), float(lp_scale), dx_out.data_ptr(),
-              dw.data_ptr(), int(accumulate_dw), ws.data_ptr(), ws_bytes, rows, width, _lib.stream_ptr())
-    return dx_out, lp_out
+              _lib.ptr(dw), int(accumulate_dw), ws.data_ptr(), ws_bytes, rows, width, _lib.stream_ptr())
+    return dx_out, lp_out, ws
 
 
 def reconstruct_midpoint_sum(x_next: torch.Tensor, a: torch.Tensor, m: torch.Tensor, coeff: float,

@@ -381,3 +381,27 @@ def test_dgrad_swiglu_fused_bitwise(dtype, M, ff, d):
     ref = fn.swiglu_bwd(u, fn.linear_dgrad(dy, w))
     assert _lib.device_status() == 0
     assert torch.equal(du, ref)
+
+
+def test_rmsnorm_bwd_fused_deferred_dw_reduce_bitwise():
+    """dw = NULL leaves the partials; rk_rmsnorm_dw_reduce on another stream
+    gives the same bits as the reduction inside rk_rmsnorm_bwd_fused."""
+    from reversability_b200 import functional as fn
+    rows = 14848
+    x = torch.randn(rows, 256, device=DEV)
+    w = torch.randn(256, device=DEV)
+    _, rstd = fn.rmsnorm_fwd(x, w, 1e-6)
+    g = torch.randn(rows, 256, device=DEV).bfloat16()
+    res = torch.randn(rows, 256, device=DEV)
+    base = torch.randn(256, device=DEV)
+    dw_a = base.clone()
+    dxa, lpa = fn.rmsnorm_bwd_fused(x, w, rstd, g, dw_a, residual=res, lp_dtype=torch.bfloat16, lp_scale=0.5)
+    dxb, lpb, part = fn.rmsnorm_bwd_fused_deferred(x, w, rstd, g, residual=res, lp_dtype=torch.bfloat16,
+                                                   lp_scale=0.5)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    dw_b = base.clone()
+    with torch.cuda.stream(side):
+        fn.rmsnorm_dw_reduce(part, rows, 256, dw_b)
+    torch.cuda.current_stream().wait_stream(side)
+    assert torch.equal(dxa, dxb) and torch.equal(lpa, lpb) and torch.equal(dw_a, dw_b)

@@ -1417,13 +1417,27 @@ int wgrad_bn() {
   return bn;
 }
 
+// CTAs the split weight-gradient GEMM aims for: about half the SMs. The
+// trainer runs these GEMMs on a side stream beside the reverse sweep, where
+// fewer slices (less fp32 partial traffic, fewer SMs held) measured faster
+// than filling the GPU (8.79 against 8.97 ms per cfg2 update).
+// REVK_WGRAD_CTAS in the environment sets it (a tuning switch).
+int wgrad_ctas() {
+  static const int n = [] {
+    const char* e = getenv("REVK_WGRAD_CTAS");
+    const int v = e ? atoi(e) : 0;
+    return v > 0 ? v : 74;
+  }();
+  return n;
+}
+
 int wgrad_splits(int64_t M, int64_t N, int64_t K) {
   // Output tiles of dW[N,K] (128 x wgrad_bn() when split); choose slices so
-  // that tiles*slices fills ~the SMs, with each slice at least 8 k-blocks
-  // (512 tokens) long. Fixed per shape.
+  // that tiles*slices fills ~wgrad_ctas() CTAs, with each slice at least 8
+  // k-blocks (512 tokens) long. Fixed per shape.
   const int64_t tiles = ((N + 127) / 128) * ((K + wgrad_bn() - 1) / wgrad_bn());
   const int64_t kb = (M + 63) / 64;
-  int64_t s = (148 + tiles - 1) / tiles;
+  int64_t s = (wgrad_ctas() + tiles - 1) / tiles;
   if (s > kb / 8) s = kb / 8;
   if (s < 1) s = 1;
   if (s > 64) s = 64;

@@ -36,6 +36,12 @@ constexpr int kKT = 64;     // keys per key tile
 constexpr int kHD = 32;     // head dim
 constexpr int kThreads = 192;
 constexpr int kKVStages = 4;
+// Score buffers in TMEM and resident CTAs per SM. One buffer and three CTAs
+// (twelve softmax warps per SM, 128 TMEM columns each, two K/V stages) measured
+// 46.5 us against 26.9 us for two buffers and two CTAs at cfg2 (the softmax
+// warps then spill).
+constexpr int kSBufs = 2;
+constexpr int kCtasPerSm = 2;
 constexpr uint32_t kQBytes = kTile * kHD * 2;     // 8 KB
 constexpr uint32_t kKVBytes = kKT * kHD * 2;      // 4 KB each for K and V
 constexpr uint32_t kPBytes = kTile * kKT * 2;     // 16 KB (one 64-key swizzle atom)
@@ -46,7 +52,8 @@ constexpr uint32_t kOffP = kOffV + kKVStages * kKVBytes;
 constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
 constexpr uint32_t kNumBars = 26;
 constexpr uint32_t kSmem = 1024 + kOffBar + kNumBars * 8 + 32;
-constexpr uint32_t kTmemCols = 256;  // S0 [0,64), S1 [64,128), O [128,160)
+constexpr uint32_t kOCol = kSBufs * kKT;                  // S [0, 64 * kSBufs), O [kOCol, kOCol + 32)
+constexpr uint32_t kTmemCols = kSBufs == 1 ? 128 : 256;    // power of two >= kOCol + 32
 // Lazy rescale: P is formed against a reference max that only moves when a
 // row's max exceeds it by more than 2^8, so P <= 256 (exact in bf16's range)
 // and the O accumulator in TMEM is rescaled rarely.
@@ -122,13 +129,13 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return d;
 }
 
-// Persistent: grid = min(2 x SMs, items); item i (longest query tiles first)
+// Persistent: grid = min(kCtasPerSm x SMs, items); item i (longest query tiles first)
 // is (qt, bh) = (ntq - 1 - i / BH, i % BH); query tile qt meets key tiles
 // 0 .. 2*qt+1 (64 keys each). All roles walk the same item sequence and keep
 // running tile counters for the barrier phases: K/V tile g uses ring stage
-// g % 4; S tile and P/O tile t use buffer t % 2.
+// g % kKVStages; S tile t uses buffer t % kSBufs, P tile t buffer t % 2.
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 2)
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
     fwd_tc_kernel(const __grid_constant__ CUtensorMap tm, T* __restrict__ out, float* __restrict__ lse, int H,
                   int BH, int ntq, int Tlen, int64_t ldo, float c_log2, unsigned int* status) {
   extern __shared__ uint8_t smem_raw[];
@@ -239,8 +246,9 @@ __global__ void __launch_bounds__(kThreads, 2)
         const int st = g % kKVStages;
         if (!mbar_wait(bb.kv_full0 + 8 * st, (g / kKVStages) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort)) return false;
         ++g;
-        const int sb = gs & 1;
-        if (gs >= 2 && !mbar_wait(bb.s_empty0 + 8 * sb, ((gs - 2) >> 1) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort))
+        const int sb = gs % kSBufs;
+        if (gs >= kSBufs &&
+            !mbar_wait(bb.s_empty0 + 8 * sb, ((gs - kSBufs) / kSBufs) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort))
           return false;
         tc_fence_after();
         const uint32_t ka = sbase + kOffK + st * kKVBytes;
@@ -288,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 2)
           const uint32_t va = sbase + kOffV + st_j * kKVBytes;
 #pragma unroll
           for (int kk = 0; kk < kKT / 16; ++kk)
-            umma_f16(tmem + 128, smem_desc(pa + kk * 32, 16, 1024, 2), smem_desc(va + kk * 1024, 4096, 512, 4),
+            umma_f16(tmem + kOCol, smem_desc(pa + kk * 32, 16, 1024, 2), smem_desc(va + kk * 1024, 4096, 512, 4),
                      idPV, (j > 0 || kk > 0) ? 1u : 0u);
           umma_commit(bb.o_full0);
           umma_commit(bb.kv_empty0 + 8 * st_j);
@@ -311,7 +319,6 @@ __global__ void __launch_bounds__(kThreads, 2)
     const uint32_t t_lane = tmem + ((uint32_t)(quarter * 32) << 16);
     int gs = 0, gp = 0;
     bool ok = true;
-    float oacc[kHD];
     for (int it = blockIdx.x; it < items && ok; it += gridDim.x) {
       const int qt = ntq - 1 - it / BH, bh = it - (it / BH) * BH;
       const int b = bh / H, h = bh - (bh / H) * H;
@@ -327,8 +334,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         return w;
       };
       for (int j = 0; j < nk; ++j) {
-        const int sb = gs & 1;
-        bool w = mbar_wait(bb.s_full0 + 8 * sb, (gs >> 1) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort);
+        const int sb = gs % kSBufs;
+        bool w = mbar_wait(bb.s_full0 + 8 * sb, (gs / kSBufs) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort);
         w = __all_sync(0xffffffffu, w);
         if (!w) {
           ok = false;
@@ -383,11 +390,11 @@ __global__ void __launch_bounds__(kThreads, 2)
               break;
             }
             uint32_t o[32];
-            tmem_ld_32cols_nowait(t_lane + 128, o);
+            tmem_ld_32cols_nowait(t_lane + kOCol, o);
             tmem_ld_wait();
 #pragma unroll
             for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * f);
-            tmem_st_32cols(t_lane + 128, o);
+            tmem_st_32cols(t_lane + kOCol, o);
             tmem_st_wait();
           }
           l_run *= f;
@@ -437,21 +444,20 @@ __global__ void __launch_bounds__(kThreads, 2)
       }
       {
         uint32_t o[32];
-        tmem_ld_32cols_nowait(t_lane + 128, o);
+        tmem_ld_32cols_nowait(t_lane + kOCol, o);
         tmem_ld_wait();
+        if (grow < Tlen) {
+          const float inv = 1.f / l_run;
+          T* orow = out + ((int64_t)b * Tlen + grow) * ldo + h * kHD;
 #pragma unroll
-        for (int i = 0; i < 32; ++i) oacc[i] = __uint_as_float(o[i]);
-      }
-      const float m_run = m_ref;
-      if (grow < Tlen) {
-        const float inv = 1.f / l_run;
-        T* orow = out + ((int64_t)b * Tlen + grow) * ldo + h * kHD;
-#pragma unroll
-        for (int q = 0; q < kHD / 8; ++q)
-          reinterpret_cast<uint4*>(orow)[q] = make_uint4(
-              pack2<T>(oacc[8 * q] * inv, oacc[8 * q + 1] * inv), pack2<T>(oacc[8 * q + 2] * inv, oacc[8 * q + 3] * inv),
-              pack2<T>(oacc[8 * q + 4] * inv, oacc[8 * q + 5] * inv), pack2<T>(oacc[8 * q + 6] * inv, oacc[8 * q + 7] * inv));
-        lse[(int64_t)bh * Tlen + grow] = m_run + __log2f(l_run);
+          for (int q = 0; q < kHD / 8; ++q) {
+            const float* oq = reinterpret_cast<const float*>(o + 8 * q);
+            reinterpret_cast<uint4*>(orow)[q] =
+                make_uint4(pack2<T>(oq[0] * inv, oq[1] * inv), pack2<T>(oq[2] * inv, oq[3] * inv),
+                           pack2<T>(oq[4] * inv, oq[5] * inv), pack2<T>(oq[6] * inv, oq[7] * inv));
+          }
+          lse[(int64_t)bh * Tlen + grow] = m_ref + __log2f(l_run);
+        }
       }
     }
   }
@@ -519,7 +525,7 @@ int rk_attn_fwd_tc32(const void* qkv, int64_t ldq, void* out, int64_t ldo, float
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
-  const unsigned grid = (unsigned)(items < 2 * sms ? items : 2 * sms);
+  const unsigned grid = (unsigned)(items < kCtasPerSm * sms ? items : kCtasPerSm * sms);
   const float c_log2 = 1.4426950408889634f / sqrtf((float)kHD);
   unsigned int* st = rk_host::device_status_ptr();
   if (dtype == RK_BF16) {

@@ -84,6 +84,8 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.first = threading.Event()
+        self.start = 0
 
     def __enter__(self):
         try:
@@ -92,6 +94,10 @@ class ClockSampler:
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.reader = threading.Thread(target=self._read, daemon=True)
             self.reader.start()
+            # nvidia-smi can take longer to start than the timed region lasts:
+            # the region begins once it is sampling
+            self.first.wait(timeout=10.0)
+            self.start = len(self.lines)
         except OSError:
             self.proc = None
         return self
@@ -99,6 +105,7 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+            self.first.set()
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -112,7 +119,10 @@ class ClockSampler:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.lines:
+        # samples taken during the region; the last one before it if the region
+        # was shorter than the sampling interval
+        lines = self.lines[self.start:] or self.lines[max(self.start - 1, 0):self.start]
+        for line in lines:
             parts = [p.strip() for p in line.split(",")]
             if len(parts) < 9:
                 continue
@@ -354,9 +364,10 @@ def main():
     first = args.warmup + 1
     cs = torch.cuda.current_stream()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier()
-    torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local) as clocks:  # sampling before the barrier, so every rank starts together
+        barrier()
+        torch.cuda.synchronize()
+        clocks.start = len(clocks.lines)
         start.record(cs)
         for k in range(args.steps):
             u = first + k

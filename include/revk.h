@@ -179,6 +179,16 @@ RK_API int rk_gemm_fprop(const void* x, int64_t ldx, const void* w, int64_t ldw,
                   int64_t N, int64_t K, int dtype, int out_dtype, void* stream);
 RK_API int rk_gemm_dgrad(const void* dy, int64_t lddy, const void* w, int64_t ldw, void* dx, int64_t lddx, int64_t M,
                   int64_t N, int64_t K, int dtype, int out_dtype, void* stream);
+/* Attention output projection's dgrad with the attention backward's
+ * D = rowsum(dO * O) in its epilogue (model.py:45 backward and the D term of
+ * F.scaled_dot_product_attention's backward): DX[M,K] = DY[M,N] . W[N,K] as
+ * rk_gemm_dgrad (16-bit, dtype), and dsum[b, h, t] = sum over head h's 32
+ * columns of DX[b*T + t] * O[b*T + t] with O [M, K], K = H * 32, M = B * T;
+ * bit-identical to rk_gemm_dgrad followed by rk_attn_bwd_piece(0). Returns
+ * RK_ERR_UNSUPPORTED when the layout does not fit the TMA epilogue. */
+RK_API int rk_gemm_dgrad_dsum(const void* dy, int64_t lddy, const void* w, int64_t ldw, void* dx, int64_t lddx,
+                              int64_t M, int64_t N, int64_t K, int dtype, const void* o, int64_t ldo, float* dsum,
+                              int64_t T, int64_t H, void* stream);
 /* MLP up projection with SwiGLU fused into the epilogue (model.py:55-56):
  * u = X[M,K] . W_up[2ff,K]^T, h[M,ff] = round(silu(u[:, :ff])) * u[:, ff:] with
  * the same rounding as rk_swiglu_fwd on a bf16/f16 u. If u is not NULL it also

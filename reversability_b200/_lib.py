@@ -19,6 +19,7 @@ LIB_PATH = Path(__file__).resolve().parent / "librevk.so"
 HEADER = Path(__file__).resolve().parents[1] / "include" / "revk.h"
 
 F32, BF16, F16 = 0, 1, 2
+ERR_UNSUPPORTED = 5  # RK_ERR_UNSUPPORTED: the shape or layout is outside what a kernel implements
 DTYPE_CODE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 
 _p = ctypes.c_void_p
@@ -45,6 +46,7 @@ SIGNATURES: dict[str, tuple] = {
     "rk_gemm_wgrad_workspace": (_i64, [_i64, _i64, _i64]),
     "rk_gemm_fprop_swiglu": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p]),
     "rk_gemm_dgrad_swiglu": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p]),
+    "rk_gemm_dgrad_dsum": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p, _i64, _p, _i64, _i64, _p]),
     "rk_gemm_wgrad": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p, _i64, _p]),
     "rk_attn_fwd": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p]),
     "rk_attn_bwd": (_i, [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _p]),

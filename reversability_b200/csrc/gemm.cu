@@ -61,6 +61,12 @@ struct GemmArgs {
   float* xlabel;          // EPI_LSE: per token, the rounded logit at its label
   int vocab;              // EPI_LSE / XF: valid vocabulary entries
   int tokens;             // XF: valid token rows
+  // EPI_TMA_DSUM (attention output projection's dgrad): D[b, h, t] =
+  // rowsum over head h's 32 columns of round(dx) * o
+  const void* dsum_o;     // o [M, N] (16-bit, row stride dsum_ldo)
+  int64_t dsum_ldo;
+  float* dsum;            // [B, H, T], M = B * T
+  int dsum_T, dsum_H;
 };
 
 // STORE: direct row stores; PARTIAL: fp32 split slices; ACCUM: fp32 out += acc;
@@ -82,7 +88,7 @@ struct GemmArgs {
 // to g.xlabel. Columns at or past g.vocab do not count.
 enum {
   EPI_STORE = 0, EPI_PARTIAL = 1, EPI_ACCUM = 2, EPI_TMA = 3, EPI_TMA_ADD = 4, EPI_SWIGLU = 5, EPI_SWIGLU_SAVE = 6,
-  EPI_LSE = 7, EPI_SWIGLU_BWD = 8
+  EPI_LSE = 7, EPI_SWIGLU_BWD = 8, EPI_TMA_DSUM = 9
 };
 // A-operand transforms (XF): the A tile holds e = exp(x - m_b) from the LSE
 // epilogue and is turned, in shared memory before the MMA reads it, into the
@@ -94,7 +100,8 @@ enum { XF_NONE = 0, XF_ROWS = 1, XF_COLS = 2 };
 
 __host__ __device__ constexpr bool epi_is_swiglu(int e) { return e == EPI_SWIGLU || e == EPI_SWIGLU_SAVE; }
 __host__ __device__ constexpr bool epi_stages_out(int e) {
-  return e == EPI_TMA || e == EPI_TMA_ADD || e == EPI_LSE || e == EPI_SWIGLU_BWD || epi_is_swiglu(e);
+  return e == EPI_TMA || e == EPI_TMA_ADD || e == EPI_TMA_DSUM || e == EPI_LSE || e == EPI_SWIGLU_BWD ||
+         epi_is_swiglu(e);
 }
 // Epilogue warps per CTA (a multiple of 4: one per TMEM lane quarter and
 // column group) and threads per CTA (producer warp, MMA warp, epilogue).
@@ -961,10 +968,13 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         }
         continue;
       }
-      if constexpr (EPI == EPI_TMA || EPI == EPI_TMA_ADD) {
+      if constexpr (EPI == EPI_TMA || EPI == EPI_TMA_ADD || EPI == EPI_TMA_DSUM) {
         // Each warp stages its 32 rows, CW columns at a time, in a 128-byte
         // swizzled layout (16-byte chunk j of row r at j ^ (r % 8): conflict-free
-        // stores) and writes them with one TMA store per chunk.
+        // stores) and writes them with one TMA store per chunk. DSUM: each
+        // 64-column chunk is two 32-column heads; D = rowsum(round(acc) * o)
+        // per head in dsum_kernel's order (two 16-column halves summed
+        // separately, then added), o read while the TMEM load is in flight.
         constexpr int CW = 128 / (int)sizeof(TOut);
         constexpr int HALF = BN / 2;
         static_assert(HALF % CW == 0, "column half must be whole staging boxes");
@@ -975,6 +985,15 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           uint32_t r[CW];
 #pragma unroll
           for (int q = 0; q < CW / 32; ++q) tmem_ld_32cols_nowait(t_row + c + q * 32, r + q * 32);
+          uint4 ov[EPI == EPI_TMA_DSUM ? 8 : 1];
+          const int drow = m0 + quarter * 32 + lane;
+          if constexpr (EPI == EPI_TMA_DSUM) {
+            static_assert(sizeof(TOut) == 2 && CW == 64, "16-bit output, two 32-column heads per chunk");
+            const uint4* op =
+                reinterpret_cast<const uint4*>(static_cast<const TOut*>(g.dsum_o) + (int64_t)drow * g.dsum_ldo + n0 + c);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) ov[j] = drow < g.M ? __ldg(op + j) : make_uint4(0u, 0u, 0u, 0u);
+          }
           tmem_ld_wait();
           if (c + CW == (half + 1) * HALF) {  // last TMEM read of this tile by this warp
             tc_fence_before();
@@ -982,6 +1001,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           }
           if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
+          float dacc[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // DSUM: [head][16-column half]
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             uint4 raw;
@@ -994,7 +1014,24 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
             } else {
               raw = make_uint4(r[j * 4], r[j * 4 + 1], r[j * 4 + 2], r[j * 4 + 3]);
             }
+            if constexpr (EPI == EPI_TMA_DSUM) {
+              float& a = dacc[j >> 2][(j & 3) >> 1];
+              const uint32_t dw[4] = {raw.x, raw.y, raw.z, raw.w};
+              const uint32_t owd[4] = {ov[j].x, ov[j].y, ov[j].z, ov[j].w};
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                a += unpack_half<TOut>(owd[e >> 1], e & 1) * unpack_half<TOut>(dw[e >> 1], e & 1);
+            }
             *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) = raw;
+          }
+          if constexpr (EPI == EPI_TMA_DSUM) {
+            if (drow < g.M) {
+              const int b = drow / g.dsum_T, t = drow - b * g.dsum_T;
+              const int h0 = (n0 + c) >> 5;
+#pragma unroll
+              for (int hh = 0; hh < 2; ++hh)
+                g.dsum[((int64_t)b * g.dsum_H + h0 + hh) * g.dsum_T + t] = dacc[hh][0] + dacc[hh][1];
+            }
           }
           fence_proxy_async_smem();
           __syncwarp();
@@ -1299,7 +1336,8 @@ int pick_bn(int M, int N) {
 
 // Tensor-core GEMM: C[M,N] = sum_k A(m,k) B(n,k).
 int tc_gemm(Operand a, Operand b, int M, int N, int K, int dtype, void* out, int64_t ldo, int out_dtype, int splits,
-            cudaStream_t s, bool accumulate = false, int split_rows = 0, int bn = 0) {
+            cudaStream_t s, bool accumulate = false, int split_rows = 0, int bn = 0, const void* dsum_o = nullptr,
+            int64_t dsum_ldo = 0, float* dsum = nullptr, int dsum_T = 0, int dsum_H = 0) {
   const size_t esz = 2;
   if (!rk_host::aligned(a.ptr, 16) || !rk_host::aligned(b.ptr, 16)) return RK_ERR_ALIGN;
   if ((a.ld * esz) % 16 || (b.ld * esz) % 16) return RK_ERR_ALIGN;
@@ -1354,6 +1392,19 @@ int tc_gemm(Operand a, Operand b, int M, int N, int K, int dtype, void* out, int
   }
   const bool tma_out = rk_host::aligned(out, 16) && (ldo * (int64_t)osz) % 16 == 0 &&
                        make_out_map(&tc, out, (uint64_t)N, (uint64_t)M, (uint64_t)ldo, out_dtype);
+  if (dsum) {  // output projection dgrad with D = rowsum(dO * O) per 32-column head
+    if (!tma_out || BN != 256 || N % 64 || out_dtype != dtype || !dsum_o || dsum_T <= 0 || dsum_H * 32 != N ||
+        M % dsum_T || !rk_host::aligned(dsum_o, 16) || (dsum_ldo * 2) % 16)
+      return RK_ERR_UNSUPPORTED;
+    g.dsum_o = dsum_o;
+    g.dsum_ldo = dsum_ldo;
+    g.dsum = dsum;
+    g.dsum_T = dsum_T;
+    g.dsum_H = dsum_H;
+    if (out_dtype == RK_BF16) return dispatch_major<256, EPI_TMA_DSUM, __nv_bfloat16>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+    if (out_dtype == RK_F16) return dispatch_major<256, EPI_TMA_DSUM, __half>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
+    return RK_ERR_DTYPE;
+  }
   switch (out_dtype) {
     case RK_F32:
       if (tma_out) {
@@ -1473,6 +1524,21 @@ extern "C" int rk_gemm_dgrad(const void* dy, int64_t lddy, const void* w, int64_
                     (int)M, (int)K, (int)N, 0, s);
   if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
   return tc_gemm({dy, lddy, false}, {w, ldw, true}, (int)M, (int)K, (int)N, dtype, dx, lddx, out_dtype, 1, s);
+}
+
+extern "C" int rk_gemm_dgrad_dsum(const void* dy, int64_t lddy, const void* w, int64_t ldw, void* dx, int64_t lddx,
+                                  int64_t M, int64_t N, int64_t K, int dtype, const void* o, int64_t ldo, float* dsum,
+                                  int64_t T, int64_t H, void* stream) {
+  // DX[M,K] = DY[M,N] . W[N,K] as rk_gemm_dgrad (16-bit out), and D[b, h, t] =
+  // sum over head h's 32 columns of DX * O, O [M, K] with K = H * 32.
+  if (!dy || !w || !dx || !o || !dsum || !dims_ok(M, K, N) || lddy < N || ldw < K || lddx < K || ldo < K || N == 0 ||
+      K == 0 || T <= 0 || H <= 0 || K != H * 32 || M % T)
+    return RK_ERR_ARG;
+  if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
+  if (M == 0) return RK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  return tc_gemm({dy, lddy, false}, {w, ldw, true}, (int)M, (int)K, (int)N, dtype, dx, lddx, dtype, 1, s, false, 0,
+                 256, o, ldo, dsum, (int)T, (int)H);
 }
 
 extern "C" int64_t rk_gemm_wgrad_workspace(int64_t M, int64_t N, int64_t K) {

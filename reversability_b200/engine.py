@@ -265,10 +265,15 @@ class LayerKernels:
         formed in the same epilogue."""
         n1, rstd1, qkv, o, lse = saved
         o2 = o.view(-1, o.shape[-1])
-        do = fn.linear_dgrad(ga, lw.proj_c)
+        dsum = None
+        fused = fn.linear_dgrad_dsum(ga, lw.proj_c, o2, self.H, self.T) if self.attn_side is not None else None
+        if fused is not None:  # D = rowsum(dO * O) formed in the dgrad epilogue
+            do, dsum = fused
+        else:
+            do = fn.linear_dgrad(ga, lw.proj_c)
         self._wgrad(ga, o2, g.proj)
         dqkv = fn.attention_bwd(qkv.view(self.B, self.T, -1), o, do.view(o.shape), lse, self.H,
-                                dkv_stream=self.attn_side)
+                                dkv_stream=self.attn_side, dsum=dsum)
         dqkv2 = dqkv.view(-1, dqkv.shape[-1])
         self._wgrad(dqkv2, n1, g.qkv)
         dn1 = fn.linear_dgrad(dqkv2, lw.qkv_c)

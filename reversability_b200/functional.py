@@ -183,6 +183,28 @@ def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype | Non
     return dx
 
 
+def linear_dgrad_dsum(dy: torch.Tensor, w: torch.Tensor, o: torch.Tensor, n_heads: int, length: int):
+    """(do, dsum) with do = dy @ w (16-bit, as linear_dgrad) and the attention
+    backward's D = rowsum(do * o) per 32-wide head, [B, H, T] fp32, formed in
+    the GEMM epilogue; None when the shapes do not fit that epilogue.
+    dy [M, N], w [N, K], o [M, K] with K = n_heads * 32, M = B * length."""
+    require_cuda(dy, w, o)
+    M, N = dy.shape
+    K = w.shape[1]
+    if dy.dtype not in _TC_DTYPES or w.dtype != dy.dtype or o.dtype != dy.dtype or K != 32 * n_heads or \
+            M % length or not (dy.is_contiguous() and w.is_contiguous() and o.is_contiguous()):
+        return None
+    do = torch.empty((M, K), device=dy.device, dtype=dy.dtype)
+    dsum = torch.empty((M // length, n_heads, length), device=dy.device, dtype=torch.float32)
+    st = _lib.lib().rk_gemm_dgrad_dsum(dy.data_ptr(), N, w.data_ptr(), K, do.data_ptr(), K, M, N, K,
+                                       _lib.code(dy.dtype), o.data_ptr(), K, dsum.data_ptr(), length, n_heads,
+                                       _lib.stream_ptr())
+    if st == _lib.ERR_UNSUPPORTED:
+        return None
+    _lib.check(st, "rk_gemm_dgrad_dsum")
+    return do, dsum
+
+
 def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, dw: torch.Tensor | None = None,
                  accumulate: bool = False) -> torch.Tensor:
     """dw (+)= dy^T @ x in fp32; dy [..., N], x [..., K] -> dw [N, K]."""
@@ -309,11 +331,12 @@ def attention_fwd(qkv: torch.Tensor, n_heads: int, out: torch.Tensor | None = No
 
 
 def attention_bwd(qkv: torch.Tensor, o: torch.Tensor, do: torch.Tensor, lse: torch.Tensor, n_heads: int,
-                  dkv_stream: "torch.cuda.Stream | None" = None):
+                  dkv_stream: "torch.cuda.Stream | None" = None, dsum: torch.Tensor | None = None):
     """Returns dqkv [B, T, 3*D] for the causal attention of attention_fwd.
     With `dkv_stream` (16-bit inputs) the dK/dV kernel runs on that stream
-    beside the dQ kernel, after a small kernel has written D = rowsum(dO*O);
-    the current stream waits for both before returning."""
+    beside the dQ kernel, after D = rowsum(dO*O) is in place: `dsum`
+    [B, H, T] when the caller formed it (linear_dgrad_dsum), else a small
+    kernel writes it; the current stream waits for both before returning."""
     require_cuda(qkv, o, do, lse)
     B, T, three_d = qkv.shape
     D = three_d // 3
@@ -323,14 +346,17 @@ def attention_bwd(qkv: torch.Tensor, o: torch.Tensor, do: torch.Tensor, lse: tor
         if do.stride() != o.stride():
             raise ValueError("dout must share the layout of out")
     dqkv = torch.empty_like(qkv)
-    dsum = torch.empty((B, n_heads, T), device=qkv.device, dtype=torch.float32)
+    have_dsum = dsum is not None and dkv_stream is not None and qkv.dtype in _TC_DTYPES
+    if not have_dsum:
+        dsum = torch.empty((B, n_heads, T), device=qkv.device, dtype=torch.float32)
     args = (qkv.data_ptr(), qkv.stride(1), o.data_ptr(), do.data_ptr(), o.stride(1), lse.data_ptr(), dsum.data_ptr(),
             dqkv.data_ptr(), dqkv.stride(1), B, n_heads, D // n_heads, T, _lib.code(qkv.dtype))
     if dkv_stream is None or qkv.dtype not in _TC_DTYPES:
         _lib.call("rk_attn_bwd", *args, _lib.stream_ptr())
         return dqkv
     main = torch.cuda.current_stream()
-    _lib.call("rk_attn_bwd_piece", 0, *args, main.cuda_stream)
+    if not have_dsum:
+        _lib.call("rk_attn_bwd_piece", 0, *args, main.cuda_stream)
     ready = torch.cuda.Event()
     ready.record(main)
     dkv_stream.wait_event(ready)

@@ -405,3 +405,32 @@ def test_rmsnorm_bwd_fused_deferred_dw_reduce_bitwise():
         fn.rmsnorm_dw_reduce(part, rows, 256, dw_b)
     torch.cuda.current_stream().wait_stream(side)
     assert torch.equal(dxa, dxb) and torch.equal(lpa, lpb) and torch.equal(dw_a, dw_b)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,T", [(29, 512), (3, 64), (5, 100)])
+def test_dgrad_dsum_fused_bitwise(dtype, B, T):
+    """rk_gemm_dgrad_dsum: the output projection's dgrad equals rk_gemm_dgrad
+    and its D = rowsum(dO * O) per head equals the D kernel of the attention
+    backward, bit for bit (ragged row tiles included)."""
+    from reversability_b200 import _lib, functional as fn
+    H, d = 8, 256
+    M = B * T
+    g = torch.Generator(device="cpu").manual_seed(B * T)
+    ga = (torch.randn(M, d, generator=g) * 0.1).to(DEV, dtype)
+    w = (torch.randn(d, d, generator=g) * 0.05).to(DEV, dtype)
+    o = torch.randn(M, d, generator=g).to(DEV, dtype)
+    out = fn.linear_dgrad_dsum(ga, w, o, H, T)
+    assert out is not None
+    do, dsum = out
+    do_ref = fn.linear_dgrad(ga, w)
+    qkv = torch.zeros(B, T, 3 * d, device=DEV, dtype=dtype)
+    lse = torch.zeros(B, H, T, device=DEV)
+    ref = torch.empty(B, H, T, device=DEV)
+    dqkv = torch.empty_like(qkv)
+    _lib.call("rk_attn_bwd_piece", 0, qkv.data_ptr(), qkv.stride(1), o.data_ptr(), do_ref.data_ptr(), d,
+              lse.data_ptr(), ref.data_ptr(), dqkv.data_ptr(), dqkv.stride(1), B, H, d // H, T, _lib.code(dtype),
+              _lib.stream_ptr())
+    assert _lib.device_status() == 0
+    assert torch.equal(do, do_ref)
+    assert torch.equal(dsum, ref)

@@ -176,6 +176,11 @@ class LayerKernels:
         self._aux_used = True
         return torch.cuda.stream(self.aux)
 
+    def hold(self, *tensors):
+        """Keeps tensors the weight-gradient stream reads referenced until the
+        compute stream has waited for that stream (a later layer_done or sync)."""
+        self._held += list(tensors)
+
     def side_work(self):
         """Context for caller work on the weight-gradient stream (after the
         compute stream's current work); joined by the next sync()."""

@@ -257,7 +257,14 @@ class ReversibleTrainer:
         _, _, dp, dq = engine.stack_backward(kern, self.layers, self.layer_grads, p, q, dp, dq, self.model.method,
                                              self.model.step_size, on_layer_done=hook, first=first)
         # boundary p = q = embedding: both cotangents reach it (summed inside the kernel)
-        fn.embedding_bwd(ids, dp, self.g_tok, self.g_pos, dx2=dq)
+        if not last and kern.side is not None:
+            # before the next microstep's head: on the weight-gradient stream,
+            # ahead of that head's weight gradient (the other writer of g_tok)
+            with kern.side_work():
+                fn.embedding_bwd(ids, dp, self.g_tok, self.g_pos, dx2=dq)
+            kern.hold(dp, dq)
+        else:
+            fn.embedding_bwd(ids, dp, self.g_tok, self.g_pos, dx2=dq)
 
     def _loss_bucket(self, last: bool):
         if last and self.world > 1:

@@ -288,3 +288,31 @@ def test_pipelined_sweep_equals_sequential(method, amp):
     for ga, gb in zip(g0, g1):
         for ta, tb in zip(ga.as_tuple(), gb.as_tuple()):
             assert torch.equal(ta, tb)
+
+
+SCALED = dict(vocab_size=101, max_sequence_length=2048, n_layers=2, n_heads=16, d_model=1024, d_ff=4096)
+
+
+@pytest.mark.parametrize("method", ["midpoint", "euler"])
+def test_scaled_config_layers_match_oracle(method):
+    """The scaled configuration's layer shape (d_model 1024, 16 heads of 64,
+    SwiGLU hidden 4096, context 2048; two layers, one sequence) through the
+    module path: fp32 gradients within the 1e-5 gate and bf16 autocast within
+    2e-2 of the oracle."""
+    cfg = SCALED
+    ids, labels, denom = batch(cfg, 1, 13)
+    p = om.init_params(om.Config(**cfg), seed=1337)
+    model = product_model(cfg, method, 0.5, 1e-6)
+    total, grads = product_step(model, ids, labels, denom)
+    ref_total, ref_grads, _ = om.loss_and_grads(p, om.Config(**cfg), ids, labels, method, 0.5, eps=1e-6,
+                                                denominator=denom)
+    assert abs(total.item() - ref_total.item()) <= 1e-5 * abs(ref_total.item())
+    worst = {n: rel_l2(grads[n], ref_grads[n]) for n in ref_grads}
+    assert max(worst.values()) <= 1e-5, sorted(worst.items(), key=lambda kv: -kv[1])[:3]
+    model = product_model(cfg, method, 0.5, 1e-6)
+    total, grads = product_step(model, ids, labels, denom, low=torch.bfloat16)
+    ref_total, ref_grads, _ = om.loss_and_grads(p, om.Config(**cfg), ids, labels, method, 0.5, low=torch.bfloat16,
+                                                eps=1e-6, denominator=denom)
+    assert abs(total.item() - ref_total.item()) <= 2e-3 * abs(ref_total.item())
+    worst = {n: rel_l2(grads[n], ref_grads[n]) for n in ref_grads}
+    assert max(worst.values()) <= 2e-2, sorted(worst.items(), key=lambda kv: -kv[1])[:3]

@@ -111,8 +111,7 @@ RK_API int rk_rmsnorm_dw_reduce(const float* dw_partial, int64_t rows, int64_t w
 /* Allocation-free rk_rmsnorm_bwd. It has no counterpart in the reference: it
  * exists for callers that cannot supply device workspace — foreign-function
  * hosts without a device allocator, plugins whose framework allocator owns all
- * device memory, work issued during CUDA-graph capture — and is otherwise the
- * same computation with the same arguments minus dw_partial/workspace_bytes.
+ * device memory — and is otherwise the same computation with the same arguments minus dw_partial/workspace_bytes.
  * The weight-gradient partials live in a static device array of 2,424,832
  * bytes (592 x 1024 fp32), held on every GPU that loads the library until exit;
  * widths above 1024 return RK_ERR_SCRATCH. The library allocates nothing here.

@@ -626,9 +626,8 @@ extern "C" int rk_rmsnorm_dw_reduce(const float* dw_partial, int64_t rows, int64
 //
 // Some callers cannot hand the library a workspace: a host runtime reaching
 // this library through a foreign-function binding with no device allocator of
-// its own, a plugin inside a framework whose caching allocator owns all device
-// memory, or code issuing work while a CUDA graph is being captured, where a
-// cudaMalloc would either be forbidden or synchronise the device. For them the
+// its own, or a plugin inside a framework whose caching allocator owns all
+// device memory and hands none to third-party libraries. For them the
 // weight-gradient partials live in this file-scope device array instead, sized
 // for the largest request the kernel accepts: up to 592 partial rows (the
 // backward uses one per CTA, at most 296 today) x 1024 columns of fp32 =

@@ -3,9 +3,8 @@ workspace-taking entry point (rk_rmsnorm_bwd), both called through the C ABI.
 
 The no-allocation entry point serves callers that cannot give the library
 device workspace: a host runtime that binds the library through an FFI and
-has no device allocator of its own, a plugin whose framework allocator owns all
-device memory, or work issued while a CUDA graph is being captured, where a
-cudaMalloc is forbidden or would synchronise the device. Its scratch is a
+has no device allocator of its own, or a plugin whose framework allocator owns
+all device memory and hands out none to third-party libraries. Its scratch is a
 static device array shared by every call, so the test makes two calls in a row
 with different shapes: the second must not be disturbed by what the first left
 in the scratch. This file is collected last so a run that stops at the first

@@ -1,7 +1,7 @@
 """Isolated kernel microbenchmark and ncu driver.
 
     python -m reversability_b200.microbench [--only NAME[,NAME...]] [--iters N]
-    python -m reversability_b200.microbench --only head|attention --profile   (ncu launch sequence)
+    python -m reversability_b200.microbench --only head|attention|swiglu|membound --profile   (ncu launch sequence)
 
 Workload: 16,896 tokens x width 256 in bf16 (activations N(0,1), weights
 N(0,0.02)); RMSNorm fwd+bwd, SwiGLU fwd+bwd (gate/up 256->1024, i.e. u is
@@ -296,7 +296,44 @@ def profile_swiglu():
     torch.cuda.synchronize()
 
 
-PROFILES = {"head": profile_head, "attention": profile_attention, "swiglu": profile_swiglu}
+def profile_membound():
+    """Eager launches for an ncu capture of the HBM-bound kernels on the
+    microbench shape (16,896 tokens x 256; u [N, 2048]): twice each of
+    rk_rmsnorm_fwd (bf16 in/out), rk_rmsnorm_bwd (bf16; bwd kernel + dW
+    reduce), rk_rmsnorm_bwd_fused (fp32 x/residual/dx_out, bf16 dy/lp),
+    rk_swiglu_fwd, rk_swiglu_bwd and rk_reconstruct_midpoint (fp32 states and
+    force, 2h = 1), in that order."""
+    g = torch.Generator(device="cpu").manual_seed(0)
+    rnd = lambda *s: torch.randn(*s, generator=g).cuda()
+    w = rnd(D) * 0.02 + 1
+    xb, dyb = rnd(N_TOK, D).bfloat16(), rnd(N_TOK, D).bfloat16()
+    yb, dxb = torch.empty_like(xb), torch.empty_like(xb)
+    rstd, dw = torch.empty(N_TOK, device="cuda"), torch.empty(D, device="cuda")
+    ws_bytes = _lib.lib().rk_rmsnorm_bwd_workspace(N_TOK, D)
+    ws = torch.empty(ws_bytes // 4, device="cuda")
+    xf, res, lpa = rnd(N_TOK, D), rnd(N_TOK, D), rnd(N_TOK, D).bfloat16()
+    dxo, lpo = torch.empty_like(xf), torch.empty_like(lpa)
+    u, dh = rnd(N_TOK, 2 * FF).bfloat16(), rnd(N_TOK, FF).bfloat16()
+    h, du = torch.empty(N_TOK, FF, device="cuda", dtype=torch.bfloat16), torch.empty_like(u)
+    xn, f = rnd(N_TOK * D), rnd(N_TOK * D)
+    xp = torch.empty_like(xn)
+    s = _lib.stream_ptr()
+    for _ in range(2):
+        _lib.call("rk_rmsnorm_fwd", xb.data_ptr(), _lib.BF16, D, w.data_ptr(), yb.data_ptr(), _lib.BF16, D,
+                  rstd.data_ptr(), N_TOK, D, 1e-6, s)
+        _lib.call("rk_rmsnorm_bwd", xb.data_ptr(), _lib.BF16, D, w.data_ptr(), rstd.data_ptr(), dyb.data_ptr(),
+                  _lib.BF16, D, dxb.data_ptr(), _lib.BF16, D, dw.data_ptr(), 0, ws.data_ptr(), ws_bytes, N_TOK, D, s)
+        _lib.call("rk_rmsnorm_bwd_fused", xf.data_ptr(), w.data_ptr(), rstd.data_ptr(), dyb.data_ptr(), _lib.BF16,
+                  res.data_ptr(), lpa.data_ptr(), lpo.data_ptr(), _lib.BF16, 1.0, dxo.data_ptr(), dw.data_ptr(), 1,
+                  ws.data_ptr(), ws_bytes, N_TOK, D, s)
+        _lib.call("rk_swiglu_fwd", u.data_ptr(), h.data_ptr(), _lib.BF16, N_TOK, FF, s)
+        _lib.call("rk_swiglu_bwd", u.data_ptr(), dh.data_ptr(), du.data_ptr(), _lib.BF16, N_TOK, FF, s)
+        _lib.call("rk_reconstruct_midpoint", xn.data_ptr(), f.data_ptr(), _lib.F32, 1.0, xp.data_ptr(), N_TOK * D, s)
+    torch.cuda.synchronize()
+
+
+PROFILES = {"head": profile_head, "attention": profile_attention, "swiglu": profile_swiglu,
+            "membound": profile_membound}
 
 
 def main():

@@ -7,6 +7,10 @@
  *    allocates device memory. Workspaces (RMSNorm weight-gradient partials,
  *    GEMM split partials) are passed in by the caller with their size.
  *  - Sizes and leading dimensions are element counts (int64_t).
+ *  - RMSNorm, SwiGLU and the reconstruct steps accept zero rows (elements):
+ *    they return RK_OK without touching the data arrays, which may then be
+ *    null (an empty torch tensor has a null data pointer). The RMSNorm
+ *    backward still sets dw to zero unless it accumulates.
  *  - `stream` is a cudaStream_t passed as void*; launches are stream ordered
  *    and nothing here synchronises the host.
  *  - Return value: RK_OK (0) or one of the RK_ERR_* codes below. No C++

@@ -117,15 +117,17 @@ int dispatch(const float* xn, const void* f, int dt, float coeff, float* xp, int
 
 extern "C" int rk_reconstruct_midpoint(const float* x_next, const void* force, int force_dtype, float coeff,
                                        float* x_prev, int64_t n, void* stream) {
-  if (!x_next || !force || !x_prev || n < 0) return RK_ERR_ARG;
-  if (n == 0) return RK_OK;
+  if (n < 0) return RK_ERR_ARG;
+  if (n == 0) return RK_OK;  // nothing is read or written, so the pointers may be null
+  if (!x_next || !force || !x_prev) return RK_ERR_ARG;
   return dispatch<true>(x_next, force, force_dtype, coeff, x_prev, n, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int rk_reconstruct_euler(const float* state, const void* sublayer_out, int out_dtype, float* state_prev,
                                     int64_t n, void* stream) {
-  if (!state || !sublayer_out || !state_prev || n < 0) return RK_ERR_ARG;
-  if (n == 0) return RK_OK;
+  if (n < 0) return RK_ERR_ARG;
+  if (n == 0) return RK_OK;  // nothing is read or written, so the pointers may be null
+  if (!state || !sublayer_out || !state_prev) return RK_ERR_ARG;
   return dispatch<false>(state, sublayer_out, out_dtype, 1.f, state_prev, n, static_cast<cudaStream_t>(stream));
 }
 
@@ -160,8 +162,9 @@ int cast_launch(const float* x, void* out, float scale, int64_t n, cudaStream_t 
 
 extern "C" int rk_reconstruct_midpoint_sum(const float* x_next, const void* a, const void* m, int dtype, float coeff,
                                            float* x_prev, int64_t n, void* stream) {
-  if (!x_next || !a || !m || !x_prev || n < 0) return RK_ERR_ARG;
-  if (n == 0) return RK_OK;
+  if (n < 0) return RK_ERR_ARG;
+  if (n == 0) return RK_OK;  // nothing is read or written, so the pointers may be null
+  if (!x_next || !a || !m || !x_prev) return RK_ERR_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case RK_F32: return sum_launch<float>(x_next, a, m, coeff, x_prev, n, s);

@@ -440,9 +440,10 @@ int bwd_typed(const void* x, int64_t ldx, const float* w, const float* rstd, con
 
 extern "C" int rk_rmsnorm_fwd(const void* x, int x_dtype, int64_t ldx, const float* w, void* y, int y_dtype,
                               int64_t ldy, float* rstd, int64_t rows, int64_t width, float eps, void* stream) {
-  if (!x || !w || !y || rows < 0 || width <= 0 || ldx < width || ldy < width) return RK_ERR_ARG;
+  if (rows < 0 || width <= 0 || ldx < width || ldy < width) return RK_ERR_ARG;
   if (width > 1024) return RK_ERR_UNSUPPORTED;
-  if (rows == 0) return RK_OK;
+  if (rows == 0) return RK_OK;  // nothing is read or written, so the pointers may be null
+  if (!x || !w || !y) return RK_ERR_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int W = (int)width;
   if (x_dtype == RK_F32 && y_dtype == RK_F32) return fwd_typed<float, float>(x, ldx, w, y, ldy, rstd, rows, W, eps, s);
@@ -463,15 +464,17 @@ extern "C" int rk_rmsnorm_bwd(const void* x, int x_dtype, int64_t ldx, const flo
                               const void* dy, int dy_dtype, int64_t lddy, void* dx, int dx_dtype, int64_t lddx,
                               float* dw, int accumulate_dw, float* dw_partial, int64_t workspace_bytes, int64_t rows,
                               int64_t width, void* stream) {
-  if (!x || !w || !rstd || !dy || !dx || !dw || !dw_partial || rows < 0 || width <= 0) return RK_ERR_ARG;
+  if (!dw || rows < 0 || width <= 0) return RK_ERR_ARG;
   if (ldx < width || lddy < width || lddx < width) return RK_ERR_ARG;
   if (width > 1024) return RK_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int W = (int)width;
-  if (rows == 0) {
-    if (!accumulate_dw) cudaMemsetAsync(dw, 0, sizeof(float) * W, s);
+  if (rows == 0) {  // dw = 0 (or unchanged); the row pointers and the workspace may be null
+    if (accumulate_dw) return RK_OK;
+    cudaMemsetAsync(dw, 0, sizeof(float) * W, s);
     return rk_host::launch_status();
   }
+  if (!x || !w || !rstd || !dy || !dx || !dw_partial) return RK_ERR_ARG;
   const int parts = rms_parts(rows);
   if (workspace_bytes < (int64_t)parts * W * (int64_t)sizeof(float)) return RK_ERR_WORKSPACE;
   int st;

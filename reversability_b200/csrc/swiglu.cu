@@ -107,8 +107,9 @@ int bwd_typed(const void* u, const void* dh, void* du, int64_t rows, int64_t wid
 }  // namespace
 
 extern "C" int rk_swiglu_fwd(const void* u, void* h, int dtype, int64_t rows, int64_t width, void* stream) {
-  if (!u || !h || rows < 0 || width <= 0) return RK_ERR_ARG;
-  if (rows == 0) return RK_OK;
+  if (rows < 0 || width <= 0) return RK_ERR_ARG;
+  if (rows == 0) return RK_OK;  // nothing is read or written, so the pointers may be null
+  if (!u || !h) return RK_ERR_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case RK_F32: return fwd_typed<float>(u, h, rows, width, s);
@@ -120,8 +121,9 @@ extern "C" int rk_swiglu_fwd(const void* u, void* h, int dtype, int64_t rows, in
 
 extern "C" int rk_swiglu_bwd(const void* u, const void* dh, void* du, int dtype, int64_t rows, int64_t width,
                              void* stream) {
-  if (!u || !dh || !du || rows < 0 || width <= 0) return RK_ERR_ARG;
-  if (rows == 0) return RK_OK;
+  if (rows < 0 || width <= 0) return RK_ERR_ARG;
+  if (rows == 0) return RK_OK;  // nothing is read or written, so the pointers may be null
+  if (!u || !dh || !du) return RK_ERR_ARG;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case RK_F32: return bwd_typed<float>(u, dh, du, rows, width, s);

@@ -33,6 +33,26 @@ def test_library_rejects_bad_arguments_without_launching():
     assert lib.rk_cross_entropy_fwd_bwd(None, 0, 0, None, 1, 1.0, None, None, None, 0, 1, -100, None) == 1
 
 
+def test_zero_rows_accept_null_arrays_without_cuda_calls():
+    """An empty batch (zero rows) touches no memory: the data pointers of an
+    empty tensor are null, and the call returns RK_OK without a CUDA call."""
+    lib = _lib.lib()
+    assert lib.rk_rmsnorm_fwd(None, 1, 256, None, None, 1, 256, None, 0, 256, 1e-6, None) == 0
+    assert lib.rk_swiglu_fwd(None, None, 1, 0, 1024, None) == 0
+    assert lib.rk_swiglu_bwd(None, None, None, 1, 0, 1024, None) == 0
+    assert lib.rk_reconstruct_midpoint(None, None, 0, 1.0, None, 0, None) == 0
+    assert lib.rk_reconstruct_euler(None, None, 0, None, 0, None) == 0
+    assert lib.rk_reconstruct_midpoint_sum(None, None, None, 1, 1.0, None, 0, None) == 0
+    # accumulating into dw over zero rows leaves it alone; dw itself is still required
+    assert lib.rk_rmsnorm_bwd(None, 1, 256, None, None, None, 1, 256, None, 1, 256, 16, 1,
+                              None, 0, 0, 256, None) == 0
+    assert lib.rk_rmsnorm_bwd(None, 1, 256, None, None, None, 1, 256, None, 1, 256, None, 1,
+                              None, 0, 0, 256, None) == 1
+    # with rows, null arrays are still rejected
+    assert lib.rk_swiglu_fwd(None, None, 1, 3, 1024, None) == 1
+    assert lib.rk_reconstruct_midpoint(None, None, 0, 1.0, None, 5, None) == 1
+
+
 def test_public_names_match_reference_package():
     from reversability_b200 import kernels, kernels_v3, optimized, optimized_v3, reversible
     assert rb.__all__ == ["BaselineLM", "ModelConfig", "ReversibleLM", "build_model"]

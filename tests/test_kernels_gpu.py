@@ -18,6 +18,35 @@ def _seed():
     torch.manual_seed(1234)
 
 
+# ------------------------------------------------------------------ empty batches
+def test_empty_batches_return_empty_results():
+    """Zero rows through the reference-facing autograd Functions and the
+    functional layer: empty outputs and gradients of the right shapes, a zero
+    RMSNorm weight gradient (or an untouched one when accumulating)."""
+    from reversability_b200 import functional as fn
+    from reversability_b200.kernels import FusedSwiGLU
+    from reversability_b200.kernels_v3 import FusedRMSNorm
+    w = (torch.randn(256, device=DEV) * 0.02 + 1).requires_grad_()
+    x = torch.empty(2, 0, 256, device=DEV, requires_grad=True)
+    y = FusedRMSNorm.apply(x, w, 1e-6)
+    assert y.shape == (2, 0, 256)
+    y.sum().backward()
+    assert x.grad.shape == (2, 0, 256) and torch.equal(w.grad, torch.zeros_like(w))
+    for dt in (torch.float32, torch.bfloat16):
+        u = torch.empty(0, 128, device=DEV, dtype=dt, requires_grad=True)
+        h = FusedSwiGLU.apply(u)
+        assert h.shape == (0, 64) and h.dtype == dt
+        h.sum().backward()
+        assert u.grad.shape == (0, 128)
+    e = torch.empty(0, 256, device=DEV)
+    assert fn.reconstruct_midpoint(e, e, 1.0).shape == (0, 256)
+    assert fn.reconstruct_midpoint_sum(e, e.bfloat16(), e.bfloat16(), 1.0).shape == (0, 256)
+    dw = torch.full((256,), 3.0, device=DEV)
+    _, dw_out = fn.rmsnorm_bwd(e, w.detach(), torch.empty(0, device=DEV), e, dw=dw, accumulate_dw=True)
+    assert torch.equal(dw_out, torch.full_like(dw, 3.0))
+    torch.cuda.synchronize()
+
+
 # ------------------------------------------------------------------ RMSNorm
 @pytest.mark.parametrize("shape", [(3, 23, 256), (5, 8), (17, 33), (4, 1024), (300, 256)])
 def test_rmsnorm_fp32_matches_torch(shape):

@@ -1106,7 +1106,9 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
 }
 
 // dw[r, c] (+)= sum_s partial[s][r][c] (slices `slice_rows` rows apart), in
-// slice order; 4 consecutive columns per thread when cols % 4 == 0.
+// slice order; 4 consecutive columns per thread when cols % 4 == 0. The loads
+// of up to eight slices (and of dw when accumulating) are issued before their
+// sums, which stay in slice order, so the result does not depend on the batch.
 template <int V>
 __global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restrict__ partial, int splits, int64_t rows,
                                                            int64_t cols, int64_t slice_rows, float* __restrict__ dw,
@@ -1116,20 +1118,27 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restri
   const int64_t slice = slice_rows * cols;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i = t * V;
+    const int64_t r = i / cols, c = i - r * cols;
+    float* d = dw + r * lddw + c;
+    float o[V];
+    if (accumulate) load_vec<float, V>(d, o);
     float s[V];
 #pragma unroll
     for (int e = 0; e < V; ++e) s[e] = 0.f;
-    for (int k = 0; k < splits; ++k) {
-      float v[V];
-      load_vec<float, V>(partial + (int64_t)k * slice + i, v);
+    constexpr int B = 8;
+    for (int k = 0; k < splits; k += B) {
+      float v[B][V];
 #pragma unroll
-      for (int e = 0; e < V; ++e) s[e] += v[e];
+      for (int b = 0; b < B; ++b)
+        if (k + b < splits) load_vec<float, V>(partial + (int64_t)(k + b) * slice + i, v[b]);
+#pragma unroll
+      for (int b = 0; b < B; ++b)
+        if (k + b < splits) {
+#pragma unroll
+          for (int e = 0; e < V; ++e) s[e] += v[b][e];
+        }
     }
-    const int64_t r = i / cols, c = i - r * cols;
-    float* d = dw + r * lddw + c;
     if (accumulate) {
-      float o[V];
-      load_vec<float, V>(d, o);
 #pragma unroll
       for (int e = 0; e < V; ++e) s[e] += o[e];
     }

@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--accumulation", type=int, default=2)
     ap.add_argument("--no-graph", action="store_true", help="run updates eagerly instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--reference-memory", action="store_true",
+                    help="measure the reference's own peak allocated HBM at this shape (needs baseline/_ref)")
     return ap.parse_args()
 
 
@@ -147,64 +149,72 @@ def measured_peaks():
 
 
 # ------------------------------------------------------------------ CPU baseline (oracle port)
-def cpu_baseline(method: str, seconds_budget: float = 20.0):
-    """The reference's pure-PyTorch fp32 CPU path (forward + reconstruction
-    backward + clip + AdamW, restated in oracle/), timed on this host's cores
-    on a bounded sample: updates of 4x512 targets x accumulation 1."""
+def _cpu_trainer(method: str, batch: int, seq: int, accumulation: int, updates: int):
+    """The reference's pure-PyTorch fp32 CPU update (forward + reconstruction
+    backward + clip + AdamW, restated in oracle/), on every host thread, over
+    the benchmark's own update shape, one microstep at a time: returns
+    (threads, microstep) where microstep() runs the next batch x seq microstep
+    of the seeded stream (the clip + AdamW step after every `accumulation`-th)
+    and returns its target count."""
     from oracle import model as om, stream as ost
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     cfg = om.Config()
-    params = om.init_params(cfg, seed=1337)
-    tr = om.Trainer(params, cfg, om.TrainConfig(), method, eps=1e-6)
-    B, T = 4, 512
-    data = ost.synthetic_stream(B * T * 16 + 1, seed=1337)
-    committed = 0
+    tr = om.Trainer(om.init_params(cfg, seed=1337), cfg, om.TrainConfig(), method, eps=1e-6)
+    per_update = batch * seq * accumulation
+    data = ost.synthetic_stream(per_update * (updates + 1) + 1, seed=1337)
+    state = {"committed": 0, "m": 0, "loss": 0.0}
 
-    def one():
-        nonlocal committed
-        x, y, c = ost.batch_at(data, committed, B, T, committed + B * T)
-        tr.update([(x, y, c)], committed)
-        committed += c
-        return c
+    def microstep():
+        c0, m = state["committed"], state["m"]
+        if m == 0:
+            tr.opt.zero_grad(set_to_none=True)
+            state["loss"] = 0.0
+        x, y, n = ost.batch_at(data, c0 + m * batch * seq, batch, seq, c0 + per_update)
+        state["loss"] += tr.microstep(x, y, per_update)
+        if m + 1 == accumulation:
+            tr.finish(c0, per_update, state["loss"])
+            state["committed"], state["m"] = c0 + per_update, 0
+        else:
+            state["m"] = m + 1
+        return n
 
-    one()  # warm-up
-    start, targets, n = time.perf_counter(), 0, 0
-    while True:
-        targets += one()
-        n += 1
-        if time.perf_counter() - start > seconds_budget or n >= 8:
-            break
+    return threads, microstep
+
+
+def cpu_baseline(method: str, batch: int, seq: int, accumulation: int):
+    """The reference's CPU path timed on this host's cores on a bounded sample
+    of the benchmark's own workload (about 10-30 s): after one warm-up
+    microstep, the timed sample is the rest of that update — the next
+    batch x seq microsteps through the clip + AdamW step."""
+    threads, microstep = _cpu_trainer(method, batch, seq, accumulation, 1)
+    microstep()  # warm-up
+    n = max(accumulation - 1, 1)
+    start = time.perf_counter()
+    targets = sum(microstep() for _ in range(n))
     el = time.perf_counter() - start
     return {"value": targets / el, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{n} updates of {B}x{T} targets (accumulation 1), fp32, full 20.3M model, oracle port of "
-                      f"ReversibleLM + _InverseStack + AdamW on {threads} host threads, {el:.1f} s"}
+            "sample": f"{n} microstep(s) of {batch}x{seq} targets closing an update of accumulation {accumulation} "
+                      f"(clip + AdamW included; the benchmarked update shape) after a warm-up microstep, fp32, full "
+                      f"20.3M model, oracle port of ReversibleLM + _InverseStack + AdamW on {threads} host threads, "
+                      f"{el:.1f} s"}
 
 
 def reference_arm(args):
+    """The reference's CPU implementation of the path (the oracle port), rank 0
+    only. Each step is one microstep of the benchmark's update (batch x seq
+    targets; the clip + AdamW step closes every accumulation-th), so K steps
+    time K / accumulation updates of the benchmarked shape within minutes."""
     rank, world, _ = env_rank()
     if rank != 0:
         return
-    from oracle import model as om, stream as ost
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    cfg = om.Config()
-    tr = om.Trainer(om.init_params(cfg, seed=1337), cfg, om.TrainConfig(), args.method, eps=1e-6)
-    B, T = 2, 512  # bounded sample per step so that the whole run ends within minutes
-    data = ost.synthetic_stream(B * T * (args.steps + args.warmup + 1) + 1, seed=1337)
-    committed = 0
-
-    def step():
-        nonlocal committed
-        x, y, c = ost.batch_at(data, committed, B, T, committed + B * T)
-        tr.update([(x, y, c)], committed)
-        committed += c
-        return c
-
+    total = args.steps + args.warmup
+    threads, microstep = _cpu_trainer(args.method, args.batch, args.seq, args.accumulation,
+                                      total // args.accumulation + 1)
     for _ in range(args.warmup):
-        step()
+        microstep()
     t0 = time.perf_counter()
-    targets = sum(step() for _ in range(args.steps))
+    targets = sum(microstep() for _ in range(args.steps))
     el = time.perf_counter() - t0
     value = targets / el
     line = {"metric": metric_name(args.method), "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
@@ -212,10 +222,62 @@ def reference_arm(args):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": config_block(args, world), "impl": "reference",
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                             "sample": f"each step: one update of {B}x{T} targets (accumulation 1), fp32 CPU oracle "
-                                       f"port of the reference path, {threads} threads"},
+                             "sample": f"each step: one {args.batch}x{args.seq} microstep of the benchmarked update "
+                                       f"(accumulation {args.accumulation}; clip + AdamW after every "
+                                       f"{args.accumulation}th), fp32 CPU oracle port of the reference path, "
+                                       f"{threads} threads"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def reference_memory(args):
+    """Peak allocated HBM of the REFERENCE's own training microsteps on cuda:0
+    at the benchmark's shape (train_baseline.py:256-280 under bf16 autocast,
+    accumulation included, AdamW step), for its plain reversible trainer path
+    (ReversibleLM + full-logit F.cross_entropy) and its optimised path
+    (install_v3(core_mode='split', mlp_tokens=8192) + cached_head_backward with
+    1024-token chunks; Triton options off). Needs the unmodified reference
+    package installed under baseline/_ref; prints one JSON line."""
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not (ref_dir / "reversibility").is_dir():
+        print(json.dumps({"reference_peak_alloc": "unavailable", "why": "baseline/_ref holds no reference install"}))
+        return
+    sys.path.insert(0, str(ref_dir))
+    import torch.nn.functional as F
+    from reversibility import ModelConfig, ReversibleLM
+    from reversibility.optimized_v3 import cached_head_backward, install_v3
+    from reversability_b200 import data as rdata
+    dev = torch.device("cuda", 0)
+    B, T, acc = args.batch, args.seq, args.accumulation
+    stream = rdata.synthetic_stream(B * T * acc + 1, seed=1337)
+    batches, targets = rdata.update_batches(stream, 0, 0, 1, B, T, acc, len(stream) - 1)
+    out = {}
+    for path in ("reversible_trainer", "optimized_split_tiled_cached_head"):
+        torch.manual_seed(1337)
+        model = ReversibleLM(ModelConfig(), args.method).to(dev)
+        if path != "reversible_trainer":
+            install_v3(model, core_mode="split", mlp_tokens=8192)
+        opt = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), weight_decay=0.1)
+        torch.cuda.synchronize()
+        torch.cuda.reset_peak_memory_stats(dev)
+        for x, y, _ in batches:
+            x, y = x.to(dev), y.to(dev)
+            if path == "reversible_trainer":
+                with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+                    logits = model(x)
+                    loss = F.cross_entropy(logits.flatten(0, 1), y.flatten(), ignore_index=-100, reduction="sum")
+                    (loss / targets).backward()
+                del logits, loss
+            else:
+                cached_head_backward(model, x, y, targets, 1024, precision="bf16")
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        torch.cuda.synchronize()
+        out[path] = torch.cuda.max_memory_allocated(dev)
+        del model, opt
+        torch.cuda.empty_cache()
+    print(json.dumps({"reference_peak_alloc_bytes": out, "config": config_block(args, 1),
+                      "device": torch.cuda.get_device_name(dev)}), flush=True)
 
 
 # ------------------------------------------------------------------ dominant-kernel roofline
@@ -271,6 +333,9 @@ def kernel_roofline(trainer, peak_tflops):
 # ------------------------------------------------------------------ main arm
 def main():
     args = parse()
+    if args.reference_memory:
+        reference_memory(args)
+        return
     if args.impl == "reference":
         reference_arm(args)
         return
@@ -436,7 +501,7 @@ def main():
             "losses_finite": finite, "device_status": status,
         }
         if not args.no_cpu_baseline and world == 1:
-            line["cpu_baseline"] = cpu_baseline(args.method)
+            line["cpu_baseline"] = cpu_baseline(args.method, args.batch, args.seq, args.accumulation)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

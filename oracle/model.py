@@ -312,17 +312,27 @@ class Trainer:
         """batches: list of (x, y, count) for one update. Returns loss, grad norm and lr."""
         update_targets = sum(c for _, _, c in batches)
         self.opt.zero_grad(set_to_none=True)
-        loss_total = 0.0
-        for x, y, _ in batches:
-            total, grads, _ = loss_and_grads(self.params, self.cfg, x, y, self.method, self.h, self.low, self.eps,
-                                             denominator=update_targets, core=self.core)
-            for n in self.names:
-                g = grads[n]
-                if g is None:
-                    continue
-                t = self.params[n]
-                t.grad = g.clone() if t.grad is None else t.grad + g
-            loss_total += float(total)
+        loss_total = sum(self.microstep(x, y, update_targets) for x, y, _ in batches)
+        return self.finish(committed, update_targets, loss_total)
+
+    def microstep(self, x, y, update_targets: int) -> float:
+        """One accumulation microstep (train_baseline.py:256-268): loss_sum /
+        update_targets backward, gradients added to the accumulated ones.
+        Returns the microstep's loss sum."""
+        total, grads, _ = loss_and_grads(self.params, self.cfg, x, y, self.method, self.h, self.low, self.eps,
+                                         denominator=update_targets, core=self.core)
+        for n in self.names:
+            g = grads[n]
+            if g is None:
+                continue
+            t = self.params[n]
+            t.grad = g.clone() if t.grad is None else t.grad + g
+        return float(total)
+
+    def finish(self, committed: int, update_targets: int, loss_total: float) -> dict:
+        """End of an update (train_baseline.py:272-285): clip the global norm,
+        set the scheduled learning rate, AdamW step. The clipped gradients stay
+        in .grad until the next update zeroes them."""
         norm = torch.nn.utils.clip_grad_norm_([self.params[n] for n in self.names], self.tc.grad_clip)
         lr = learning_rate(self.tc, committed, update_targets)
         for group in self.opt.param_groups:

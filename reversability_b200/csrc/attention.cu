@@ -659,8 +659,8 @@ int bwd_tc(const void* qkv, const void* o, const void* dout, const float* lse, f
   constexpr int smem_dq = 6 * tile_bytes;
   constexpr int smem_dkv = 6 * tile_bytes + 4 * 64 * (int)sizeof(float);
   static_assert(smem_dkv <= 227 * 1024, "attention backward tiles exceed shared memory");
-  rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dq_kernel<T, HD>), smem_dq);
-  rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dkv_kernel<T, HD>), smem_dkv);
+  if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dq_kernel<T, HD>), smem_dq)) return e_;
+  if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dkv_kernel<T, HD>), smem_dkv)) return e_;
   rk_host::launch_k(bwd_dq_kernel<T, HD>, grid, 128, smem_dq, s, static_cast<const T*>(qkv), static_cast<const T*>(o),
                                             static_cast<const T*>(dout), lse, dsum, static_cast<T*>(dqkv), H, Tlen,
                                             ldq, ldo, lddq, c_log2, scale, 0);
@@ -687,12 +687,12 @@ int bwd_piece(int piece, const void* qkv, const void* o, const void* dout, const
     rk_host::launch_k(dsum_kernel<T, HD>, (unsigned)((n + 255) / 256), 256, 0, s, static_cast<const T*>(o),
                       static_cast<const T*>(dout), dsum, H, Tlen, (int64_t)B * Tlen, ldo);
   } else if (piece == 1) {
-    rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dq_kernel<T, HD>), smem_dq);
+    if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dq_kernel<T, HD>), smem_dq)) return e_;
     rk_host::launch_k(bwd_dq_kernel<T, HD>, grid, 128, smem_dq, s, static_cast<const T*>(qkv),
                       static_cast<const T*>(o), static_cast<const T*>(dout), lse, dsum, static_cast<T*>(dqkv), H,
                       Tlen, ldq, ldo, lddq, c_log2, scale, 1);
   } else {
-    rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dkv_kernel<T, HD>), smem_dkv);
+    if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dkv_kernel<T, HD>), smem_dkv)) return e_;
     rk_host::launch_k(bwd_dkv_kernel<T, HD>, grid, 128, smem_dkv, s, static_cast<const T*>(qkv),
                       static_cast<const T*>(dout), lse, dsum, static_cast<T*>(dqkv), H, Tlen, ldq, ldo, lddq,
                       c_log2, scale);
@@ -715,7 +715,7 @@ extern "C" int rk_attn_fwd(const void* qkv, int64_t ldq, void* out, int64_t ldo,
   if (dtype == RK_F32) {
     dim3 grid((unsigned)((T + 3) / 4), (unsigned)(B * H));
     const size_t smem = 4 * T * sizeof(float);
-    if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(fwd_f32_kernel), (int)smem);
+    if (smem > 48 * 1024) { if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(fwd_f32_kernel), (int)smem)) return e_; }
     rk_host::launch_k(fwd_f32_kernel, grid, 128, smem, s, static_cast<const float*>(qkv), static_cast<float*>(out), lse, (int)H,
                                            (int)HD, (int)T, ldq, ldo, 1.f / sqrtf((float)HD));
     return rk_host::launch_status();
@@ -745,14 +745,14 @@ extern "C" int rk_attn_bwd(const void* qkv, int64_t ldq, const void* out, const 
     dim3 grid((unsigned)((T + 3) / 4), (unsigned)(B * H));
     const float scale = 1.f / sqrtf((float)HD);
     size_t smem = 4 * T * sizeof(float);
-    if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dq_f32_kernel), (int)smem);
+    if (smem > 48 * 1024) { if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dq_f32_kernel), (int)smem)) return e_; }
     rk_host::launch_k(bwd_dq_f32_kernel, grid, 128, smem, s, static_cast<const float*>(qkv), static_cast<const float*>(out),
                                               static_cast<const float*>(dout), lse, dsum, static_cast<float*>(dqkv),
                                               (int)H, (int)HD, (int)T, ldq, ldo, lddq, scale);
     int st = rk_host::launch_status();
     if (st) return st;
     smem = 8 * T * sizeof(float);
-    if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dkv_f32_kernel), (int)smem);
+    if (smem > 48 * 1024) { if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(bwd_dkv_f32_kernel), (int)smem)) return e_; }
     rk_host::launch_k(bwd_dkv_f32_kernel, grid, 128, smem, s, static_cast<const float*>(qkv), static_cast<const float*>(dout), lse,
                                                dsum, static_cast<float*>(dqkv), (int)H, (int)HD, (int)T, ldq, ldo,
                                                lddq, scale);

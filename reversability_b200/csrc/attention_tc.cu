@@ -530,12 +530,12 @@ int rk_attn_fwd_tc32(const void* qkv, int64_t ldq, void* out, int64_t ldo, float
   unsigned int* st = rk_host::device_status_ptr();
   if (dtype == RK_BF16) {
     auto k = fwd_tc_kernel<__nv_bfloat16>;
-    rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)kSmem);
+    if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)kSmem)) return e_;
     rk_host::launch_k(k, grid, kThreads, kSmem, s, tm, static_cast<__nv_bfloat16*>(out), lse, (int)H, BH, ntq, (int)T,
                       ldo, c_log2, st);
   } else {
     auto k = fwd_tc_kernel<__half>;
-    rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)kSmem);
+    if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)kSmem)) return e_;
     rk_host::launch_k(k, grid, kThreads, kSmem, s, tm, static_cast<__half*>(out), lse, (int)H, BH, ntq, (int)T, ldo,
                       c_log2, st);
   }

@@ -271,9 +271,10 @@ inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_
 inline size_t dtype_size(int dt) { return dt == RK_F32 ? 4 : 2; }
 // Device address of the status word on the current device (status.cu).
 unsigned int* device_status_ptr();
-// Raises `kernel`'s dynamic shared-memory limit once per (kernel, device), so
-// that calls after the first (e.g. inside CUDA-graph capture) make no
-// attribute calls at all (status.cu).
-void ensure_smem_attr(const void* kernel, int bytes);
+// Raises `kernel`'s dynamic shared-memory limit to at least `bytes` on the
+// current device; the limit set is remembered per (kernel, device), so later
+// calls (e.g. inside CUDA-graph capture) make no attribute calls at all.
+// Returns RK_OK, or RK_ERR_LAUNCH when the attribute call fails (status.cu).
+int ensure_smem_attr(const void* kernel, int bytes);
 inline bool dtype_ok(int dt) { return dt == RK_F32 || dt == RK_BF16 || dt == RK_F16; }
 }  // namespace rk_host

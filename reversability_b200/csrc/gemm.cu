@@ -1272,7 +1272,7 @@ int launch_tc(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& t
   using L = TcSmem<BN, STAGES, epi_out_bytes(EPI), RES>;
   static_assert(L::kTotal <= 232448, "shared memory over the per-block limit");
   auto kern = gemm_tc_kernel<BN, STAGES, A_MN, B_MN, EPI, TOut, RES, XF, TIn>;
-  rk_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)L::kTotal);
+  if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(kern), (int)L::kTotal)) return e_;
   const int total = g.tiles_m * g.tiles_n * g.splits;
   int grid = sm_count();
   if (total < grid) grid = total;

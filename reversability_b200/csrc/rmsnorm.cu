@@ -411,7 +411,7 @@ int bwd_nv(const void* x, int64_t ldx, const float* w, const float* rstd, const 
 #define RK_BWD(N)                                                                                          \
   do {                                                                                                     \
     auto k = rmsnorm_bwd_kernel<Tx, Tg, Tdx, V, N>;                                                        \
-    if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)smem);         \
+    if (smem > 48 * 1024) { if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)smem)) return e_; }         \
     rk_host::launch_k(k, grid, block, smem, s, X, ldx, w, rstd, G, lddy, D, lddx, partial, rows, width);                  \
   } while (0)
   if (nv <= 1) RK_BWD(1);
@@ -528,7 +528,7 @@ int bwd_fused_nv(const float* x, const float* w, const float* rstd, const void* 
 #define RK_BF(N)                                                                                            \
   do {                                                                                                      \
     auto k = rmsnorm_bwd_fused_kernel<Tg, Tlp, N, RES, LP>;                                                 \
-    if (smem > 48 * 1024) rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)smem);          \
+    if (smem > 48 * 1024) { if (const int e_ = rk_host::ensure_smem_attr(reinterpret_cast<const void*>(k), (int)smem)) return e_; }          \
     rk_host::launch_k(k, parts, 256, smem, s, x, w, rstd, G, residual, LA, dx_out, LO, partial, rows, width, lp_scale);    \
   } while (0)
   if (nv <= 1) RK_BF(1);
@@ -558,12 +558,13 @@ int bwd_fused_modes(const float* x, const float* w, const float* rstd, const voi
 
 extern "C" int rk_add_rmsnorm_fwd(const float* x, const void* a, int a_dtype, const float* w, void* y, int y_dtype,
                                   float* sum_out, float* rstd, int64_t rows, int64_t width, float eps, void* stream) {
-  if (!x || !a || !w || !y || rows < 0 || width <= 0) return RK_ERR_ARG;
+  if (rows < 0 || width <= 0) return RK_ERR_ARG;
   if (width > 1024) return RK_ERR_UNSUPPORTED;
+  if (rows == 0) return RK_OK;  // nothing is read or written, so the pointers may be null
+  if (!x || !a || !w || !y) return RK_ERR_ARG;
   if (width % 4 || !rk_host::aligned(x, 16) || !rk_host::aligned(w, 16) || !rk_host::aligned(a, 8) ||
       !rk_host::aligned(y, 8) || (sum_out && !rk_host::aligned(sum_out, 16)))
     return RK_ERR_ALIGN;
-  if (rows == 0) return RK_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int W = (int)width;
   if (a_dtype == RK_BF16 && y_dtype == RK_BF16)
@@ -579,19 +580,21 @@ extern "C" int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float*
                                     const float* residual, const void* lp_add, void* lp_out, int lp_dtype,
                                     float lp_scale, float* dx_out, float* dw, int accumulate_dw, float* dw_partial,
                                     int64_t workspace_bytes, int64_t rows, int64_t width, void* stream) {
-  if (!x || !w || !rstd || !dy || !dx_out || !dw_partial || rows < 0 || width <= 0) return RK_ERR_ARG;
+  if (rows < 0 || width <= 0) return RK_ERR_ARG;
   if (lp_add && !lp_out) return RK_ERR_ARG;
   if (width > 1024) return RK_ERR_UNSUPPORTED;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int W = (int)width;
+  if (rows == 0) {  // dw = 0 (or unchanged); the row pointers and the workspace may be null
+    if (!dw || accumulate_dw) return RK_OK;
+    cudaMemsetAsync(dw, 0, sizeof(float) * W, s);
+    return rk_host::launch_status();
+  }
+  if (!x || !w || !rstd || !dy || !dx_out || !dw_partial) return RK_ERR_ARG;
   if (width % 4 || !rk_host::aligned(x, 16) || !rk_host::aligned(w, 16) || !rk_host::aligned(dx_out, 16) ||
       (residual && !rk_host::aligned(residual, 16)) || !rk_host::aligned(dy, 8) ||
       (lp_add && !rk_host::aligned(lp_add, 8)) || (lp_out && !rk_host::aligned(lp_out, 8)))
     return RK_ERR_ALIGN;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const int W = (int)width;
-  if (rows == 0) {
-    if (dw && !accumulate_dw) cudaMemsetAsync(dw, 0, sizeof(float) * W, s);
-    return rk_host::launch_status();
-  }
   const int parts = rms_parts(rows);
   if (workspace_bytes < (int64_t)parts * W * (int64_t)sizeof(float)) return RK_ERR_WORKSPACE;
   int st;
@@ -615,10 +618,16 @@ extern "C" int rk_rmsnorm_bwd_fused(const float* x, const float* w, const float*
 
 extern "C" int rk_rmsnorm_dw_reduce(const float* dw_partial, int64_t rows, int64_t width, float* dw,
                                     int accumulate_dw, void* stream) {
-  if (!dw_partial || !dw || rows <= 0 || width <= 0) return RK_ERR_ARG;
+  if (!dw || rows < 0 || width <= 0) return RK_ERR_ARG;
   if (width > 1024) return RK_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int W = (int)width;
+  if (rows == 0) {  // no partials were written: dw = 0 (or unchanged); dw_partial may be null
+    if (accumulate_dw) return RK_OK;
+    cudaMemsetAsync(dw, 0, sizeof(float) * W, s);
+    return rk_host::launch_status();
+  }
+  if (!dw_partial) return RK_ERR_ARG;
   rk_host::launch_k(rmsnorm_dw_reduce_kernel, (W + 31) / 32, 1024, 0, s, dw_partial, dw, rms_parts(rows), W,
                     accumulate_dw);
   return rk_host::launch_status();

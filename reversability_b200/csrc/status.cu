@@ -36,18 +36,21 @@ unsigned int* device_status_ptr() {
   return g_status_ptr[dev];
 }
 
-void ensure_smem_attr(const void* kernel, int bytes) {
+int ensure_smem_attr(const void* kernel, int bytes) {
   static std::mutex mu;
-  static std::unordered_map<const void*, std::pair<uint64_t, int>> done;  // kernel -> (device mask, bytes)
+  static std::unordered_map<const void*, std::unordered_map<int, int>> done;  // kernel -> device -> bytes set
   int dev = 0;
-  cudaGetDevice(&dev);
-  const uint64_t bit = dev < 64 ? (1ull << dev) : 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return RK_ERR_LAUNCH;
   std::lock_guard<std::mutex> lock(mu);
-  auto& entry = done[kernel];
-  if (bit && (entry.first & bit) && entry.second >= bytes) return;
-  cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  entry.first |= bit;
-  if (bytes > entry.second) entry.second = bytes;
+  auto& per_dev = done[kernel];
+  auto it = per_dev.find(dev);
+  if (it != per_dev.end() && it->second >= bytes) return RK_OK;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) != cudaSuccess) {
+    cudaGetLastError();  // reported through the return value, not left for the next launch check
+    return RK_ERR_LAUNCH;
+  }
+  per_dev[dev] = bytes;
+  return RK_OK;
 }
 }  // namespace rk_host
 

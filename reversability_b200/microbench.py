@@ -1,6 +1,7 @@
 """Isolated kernel microbenchmark and ncu driver.
 
     python -m reversability_b200.microbench [--only NAME[,NAME...]] [--iters N]
+    python -m reversability_b200.microbench --only versus      (cuBLAS / torch SDPA arms beside librevk)
     python -m reversability_b200.microbench --only head|attention|swiglu|membound --profile   (ncu launch sequence)
 
 Workload: 16,896 tokens x width 256 in bf16 (activations N(0,1), weights
@@ -250,8 +251,85 @@ def bench_attention(iters):
             ("tensor", "attention_bwd", int(2.5 * flops), time_graph(bwd, 1, iters))]
 
 
+def bench_versus(iters):
+    """Same-box comparison arms for the library calls the reference makes at
+    these shapes (model.py:37,45,55-56 F.linear -> cuBLAS; model.py:42-44
+    F.scaled_dot_product_attention), beside librevk on identical operands:
+    the body Linears (forward, input gradient, weight gradient) at cfg2
+    (M = 14,848) and cfg4 (M = 16,896) and the head forward, then causal
+    attention forward and forward + backward at cfg2 (B 29, 8 heads of 32,
+    T 512) and cfg5 (B 16, 16 heads of 64, T 2048) for every SDPA backend that
+    accepts the shape. These arms are measurements only; nothing on the
+    product path calls cuBLAS or SDPA. Kernel names are `arm:op@shape`."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    out = []
+    bf = torch.bfloat16
+    linears = {"qkv": (D, 3 * D), "proj": (D, D), "up": (D, 2 * FF), "down": (FF, D)}
+    for tag, M in (("cfg2", 29 * 512), ("cfg4", N_TOK)):
+        for name, (K, N) in linears.items():
+            x = torch.randn(M, K, device="cuda").to(bf)
+            w = (torch.randn(N, K, device="cuda") * 0.02).to(bf)
+            gy = torch.randn(M, N, device="cuda").to(bf)
+            y = torch.empty(M, N, device="cuda", dtype=bf)
+            dw32 = torch.zeros(N, K, device="cuda")
+            fl = 2 * M * N * K
+            arms = {
+                "cublas:%s_fprop" % name: lambda k: torch.matmul(x, w.t(), out=y),
+                "librevk:%s_fprop" % name: lambda k: fn.linear_fwd(x, w, out=y),
+                "cublas:%s_dgrad" % name: lambda k: torch.matmul(gy, w),
+                "librevk:%s_dgrad" % name: lambda k: fn.linear_dgrad(gy, w),
+                "cublas:%s_wgrad" % name: lambda k: torch.matmul(gy.t(), x),
+                "librevk:%s_wgrad" % name: lambda k: fn.linear_wgrad(gy, x, dw=dw32, accumulate=True),
+            }
+            for kname, f in arms.items():
+                out.append(("tensor", f"{kname}@{tag}", fl, time_graph(f, 1, iters)))
+    M, V = 29 * 512, 50257
+    hid = torch.randn(M, D, device="cuda").to(bf)
+    wv = (torch.randn(V, D, device="cuda") * 0.02).to(bf)
+    logits = torch.empty(M, (V + 63) // 64 * 64, device="cuda", dtype=bf)[:, :V]
+    n = max(iters // 10, 3)
+    out.append(("tensor", "cublas:head_fprop@cfg2", 2 * M * V * D, time_graph(lambda k: F.linear(hid, wv), 1, n)))
+    out.append(("tensor", "librevk:head_fprop@cfg2", 2 * M * V * D,
+                time_graph(lambda k: fn.linear_fwd(hid, wv, out=logits), 1, n)))
+    backends = {"flash": SDPBackend.FLASH_ATTENTION, "efficient": SDPBackend.EFFICIENT_ATTENTION,
+                "cudnn": SDPBackend.CUDNN_ATTENTION}
+    for tag, (B, H, T, hd) in (("cfg2", (29, 8, 512, 32)), ("cfg5", (16, 16, 2048, 64))):
+        Dm = H * hd
+        flops = 4 * (T * (T + 1) // 2) * hd * B * H
+        qkv = torch.randn(B, T, 3 * Dm, device="cuda").to(bf)
+        o, lse = fn.attention_fwd(qkv, H)
+        do = torch.randn_like(o)
+        out.append(("tensor", f"librevk:attn_fwd@{tag}", flops,
+                    time_graph(lambda k: fn.attention_fwd(qkv, H, out=o), 1, iters)))
+        side = torch.cuda.Stream()
+
+        def lib_fb(k):
+            o2, l2 = fn.attention_fwd(qkv, H)
+            fn.attention_bwd(qkv, o2, do, l2, H, dkv_stream=side)
+        out.append(("tensor", f"librevk:attn_fwd_bwd@{tag}", int(3.5 * flops), time_graph(lib_fb, 1, iters)))
+        q, k_, v = (torch.randn(B, H, T, hd, device="cuda").to(bf).requires_grad_(True) for _ in range(3))
+        g = torch.randn(B, H, T, hd, device="cuda").to(bf)
+        for bname, be in backends.items():
+            def fwd(k, be=be):
+                with sdpa_kernel(be):
+                    F.scaled_dot_product_attention(q, k_, v, is_causal=True)
+
+            def fb(k, be=be):
+                with sdpa_kernel(be):
+                    y_ = F.scaled_dot_product_attention(q, k_, v, is_causal=True)
+                torch.autograd.grad(y_, (q, k_, v), g)
+            try:
+                out.append(("tensor", f"sdpa-{bname}:attn_fwd@{tag}", flops, time_graph(fwd, 1, iters)))
+                out.append(("tensor", f"sdpa-{bname}:attn_fwd_bwd@{tag}", int(3.5 * flops), time_graph(fb, 1, iters)))
+            except RuntimeError as exc:  # the backend rejects this shape or device
+                print(json.dumps({"kernel": f"sdpa-{bname}@{tag}", "unavailable": str(exc).splitlines()[0][:160]}),
+                      flush=True)
+    return out
+
+
 BENCHES = {"rmsnorm": bench_rmsnorm, "swiglu": bench_swiglu, "reconstruct": bench_reconstruct,
-           "mlp_gemms": bench_mlp_gemms, "head": bench_head, "attention": bench_attention}
+           "mlp_gemms": bench_mlp_gemms, "head": bench_head, "attention": bench_attention, "versus": bench_versus}
 
 
 def profile_head():
@@ -338,7 +416,8 @@ PROFILES = {"head": profile_head, "attention": profile_attention, "swiglu": prof
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--only", default=",".join(BENCHES))
+    ap.add_argument("--only", default=",".join(k for k in BENCHES if k != "versus"),
+                    help="comma-separated groups; 'versus' (cuBLAS / SDPA comparison arms) runs only when named")
     ap.add_argument("--iters", type=int, default=50)
     ap.add_argument("--profile", action="store_true",
                     help="run the eager launch sequence for an ncu capture instead of timing")

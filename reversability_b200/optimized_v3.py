@@ -1,78 +1,102 @@
 """Per-layer workspace reduction — drop-in for src/reversibility/optimized_v3.py.
 
 mlp_value / TiledMLP (optimized_v3.py:10-63): the MLP over bounded token
-tiles, saving only (x, up, down) and recomputing each tile in backward.
+tiles, saving only (x, up, down) and recomputing each tile in backward. The
+tile's VJP is written out on librevk GEMMs (no autograd graph per tile): the
+recompute keeps u and h, the down projection's dgrad carries the SwiGLU
+backward in its epilogue, and both weight gradients accumulate in fp32 across
+tiles inside the wgrad GEMM.
 SplitMidpoint (optimized_v3.py:66-117): same gradients as ReusedMidpoint; the
 fused engine already runs each layer's MLP VJP before its attention VJP and
 keeps a layer's attention activations only while that layer is processed, so
 it needs no second attention recompute. install_v3 (optimized_v3.py:120-148)
 keeps the reference's feature keys and signature lock; the MLP tile size it
 installs also sets the fused engine's tile. cached_head_backward
-(optimized_v3.py:151-192) keeps the one-cast-per-update head.
+(optimized_v3.py:151-192) casts the head weight once per call and runs the
+vocabulary head on the softmax-head kernels (optimized.head_chunks_backward).
 """
 import types
 
 import torch
-import torch.nn.functional as F
 from torch.autograd.function import once_differentiable
 
-from .functions import linear, swiglu
-from .optimized import ReusedMidpoint, _loss, amp_context, hidden_states
+from . import functional as fn
+from .optimized import (ReusedMidpoint, _LOSS_BACKENDS, _accumulate_grad, amp_context, compute_dtype,
+                        head_chunks_backward, hidden_states)
 from .reversible import stack_backward, stack_forward
 
 
-def mlp_value(x, up, down, fused):
-    """optimized_v3.py:10-18 (both branches run the librevk SwiGLU kernel)."""
-    u = linear(x, up)
-    if fused:
-        from .kernels import FusedSwiGLU
-        value = FusedSwiGLU.apply(u)
+def mlp_value(x, up, down, fused, keep=None):
+    """down(silu(gate) * value) of one token tile, gate | value = up(x), all in
+    x's dtype (optimized_v3.py:10-18). `fused` puts SwiGLU in the up
+    projection's epilogue when the shapes allow it (u then never reaches HBM
+    unless kept); otherwise the standalone SwiGLU kernel runs. With `keep` (a
+    dict) the tile's u and h are stored in it for a hand-written VJP."""
+    want_u = keep is not None
+    if fused and fn.swiglu_fusable(x, up):
+        h, u = fn.linear_swiglu_fwd(x, up, save_u=want_u)
     else:
-        value = swiglu(u)
-    return linear(value, down)
+        u = fn.linear_fwd(x, up)
+        h = fn.swiglu_fwd(u)
+    if want_u:
+        keep["u"], keep["h"] = u, h
+    return fn.linear_fwd(h, down)
+
+
+def _tile_vjp(x, up, down, dy, keep, dup, ddown):
+    """VJP of one mlp_value tile for cotangent dy (x's dtype): returns dx and
+    accumulates dup, ddown (fp32)."""
+    u, h = keep["u"], keep["h"]
+    if fn.dgrad_swiglu_fusable(dy, down, u):
+        du = fn.linear_dgrad_swiglu(dy, down, u)
+    else:
+        du = fn.swiglu_bwd(u, fn.linear_dgrad(dy, down))
+    fn.linear_wgrad(dy, h, dw=ddown, accumulate=True)
+    fn.linear_wgrad(du, x, dw=dup, accumulate=True)
+    return fn.linear_dgrad(du, up)
 
 
 class TiledMLP(torch.autograd.Function):
-    """Save only the normalised input and the weights; recompute bounded token tiles."""
+    """Save only the normalised input and the weights; recompute bounded token tiles.
+
+    Under autocast the input and weights are cast to the autocast dtype once
+    per call (as autocast's Linear would per tile) and the output is in that
+    dtype; dx comes back in x's dtype and the weight gradients in fp32."""
 
     @staticmethod
     def forward(ctx, x, up, down, tokens, fused):
         if tokens < 1:
             raise ValueError('Positive MLP tile size required')
-        ctx.tokens, ctx.fused = tokens, fused
-        ctx.device = x.device.type
-        ctx.amp = torch.is_autocast_enabled(ctx.device)
-        ctx.dtype = torch.get_autocast_dtype(ctx.device)
-        flat = x.reshape(-1, x.shape[-1])
-        output = None
-        with torch.autocast(ctx.device, enabled=ctx.amp, dtype=ctx.dtype, cache_enabled=False):
-            for start in range(0, flat.shape[0], tokens):
-                tile = mlp_value(flat[start:start + tokens], up, down, fused)
-                if output is None:
-                    output = torch.empty((flat.shape[0], down.shape[0]), device=x.device, dtype=tile.dtype)
-                output[start:start + tokens].copy_(tile)
+        fn.require_cuda(x, up, down)
+        dev = x.device.type
+        cd = torch.get_autocast_dtype(dev) if torch.is_autocast_enabled(dev) else x.dtype
+        ctx.tokens, ctx.fused, ctx.cd = tokens, fused, cd
+        flat = x.reshape(-1, x.shape[-1]).to(cd)
+        up_c, down_c = up.detach().to(cd).contiguous(), down.detach().to(cd).contiguous()
+        out = torch.empty((flat.shape[0], down.shape[0]), device=x.device, dtype=cd)
+        for s in range(0, flat.shape[0], tokens):
+            out[s:s + tokens].copy_(mlp_value(flat[s:s + tokens].contiguous(), up_c, down_c, fused))
         ctx.save_for_backward(x, up, down)
-        return output.reshape(*x.shape[:-1], down.shape[0])
+        return out.reshape(*x.shape[:-1], down.shape[0])
 
     @staticmethod
     @once_differentiable
     def backward(ctx, gradient):
         x, up, down = ctx.saved_tensors
-        flat = x.reshape(-1, x.shape[-1])
-        dy = gradient.reshape(-1, gradient.shape[-1])
-        dx = torch.empty_like(flat)
-        dup, ddown = torch.zeros_like(up), torch.zeros_like(down)
-        with torch.autocast(ctx.device, enabled=ctx.amp, dtype=ctx.dtype, cache_enabled=False):
-            for start in range(0, flat.shape[0], ctx.tokens):
-                with torch.enable_grad():
-                    local_x = flat[start:start + ctx.tokens].detach().requires_grad_(True)
-                    y = mlp_value(local_x, up, down, ctx.fused)
-                    local = torch.autograd.grad(y, (local_x, up, down), dy[start:start + ctx.tokens])
-                dx[start:start + ctx.tokens].copy_(local[0])
-                dup.add_(local[1])
-                ddown.add_(local[2])
-                del y, local_x, local
-        return dx.reshape_as(x), dup, ddown, None, None
+        cd, tokens = ctx.cd, ctx.tokens
+        flat = x.reshape(-1, x.shape[-1]).to(cd)
+        dy = gradient.reshape(-1, gradient.shape[-1]).to(cd)
+        up_c, down_c = up.detach().to(cd).contiguous(), down.detach().to(cd).contiguous()
+        dx = torch.empty(flat.shape, device=x.device, dtype=x.dtype)
+        dup = torch.zeros(up.shape, device=x.device, dtype=torch.float32)
+        ddown = torch.zeros(down.shape, device=x.device, dtype=torch.float32)
+        for s in range(0, flat.shape[0], tokens):
+            xt = flat[s:s + tokens].contiguous()
+            keep = {}
+            mlp_value(xt, up_c, down_c, ctx.fused, keep)  # the tile recompute
+            dx[s:s + tokens].copy_(_tile_vjp(xt, up_c, down_c, dy[s:s + tokens].contiguous(), keep, dup, ddown))
+            del keep
+        return dx.reshape_as(x), dup.to(up.dtype), ddown.to(down.dtype), None, None
 
 
 class SplitMidpoint(torch.autograd.Function):
@@ -127,33 +151,21 @@ def install_v3(model, *, core_mode='reference', mlp_tokens=0, swiglu=False, rmsn
 
 def cached_head_backward(model, ids, labels, denominator, chunk_tokens, scaler=None,
                          precision='fp32', reuse=False, loss_backend='torch'):
-    """optimized_v3.py:151-192: one head weight cast per update, fp32 per-chunk adds."""
+    """optimized_v3.py:151-192: the installed core once, the vocabulary head in
+    token chunks with the head weight cast once for the call, the head
+    gradient accumulated in fp32 and added to the tied weight's .grad, then one
+    core backward. Returns the fp32 loss sum."""
     if reuse or chunk_tokens < 1 or denominator < 1:
         raise ValueError('Use installed core mode and positive normalization/chunk')
+    if loss_backend not in _LOSS_BACKENDS:
+        raise ValueError('Unknown loss backend')
     with amp_context(ids.device, precision):
         hidden = hidden_states(model, ids)
-    leaf = hidden.detach().reshape(-1, hidden.shape[-1]).requires_grad_(True)
     weight = model.lm_head.weight
-    dtype = weight.dtype if ids.device.type != 'cuda' or precision == 'fp32' else \
-        {'fp16': torch.float16, 'bf16': torch.bfloat16}[precision]
-    head = weight.detach().to(dtype).requires_grad_(True)
-    targets = labels.reshape(-1)
-    total = torch.zeros((), device=ids.device, dtype=torch.float32)
-    for start in range(0, targets.numel(), chunk_tokens):
-        with amp_context(ids.device, precision, cache=False):
-            logits = linear(leaf[start:start + chunk_tokens], head)
-            loss = _loss(logits, targets[start:start + chunk_tokens], loss_backend)
-            normalized = loss / denominator
-            (normalized if scaler is None else scaler.scale(normalized)).backward()
-        chunk_grad = head.grad.detach().to(weight.dtype)
-        if weight.grad is None:
-            weight.grad = chunk_grad
-        else:
-            weight.grad.add_(chunk_grad)
-        head.grad = None
-        total += loss.detach().float()
-        del logits, loss, normalized, chunk_grad
-    del head
+    flat = hidden.detach().reshape(-1, hidden.shape[-1])
+    total, dhidden, dw = head_chunks_backward(flat, weight, labels.reshape(-1), denominator, chunk_tokens,
+                                              compute_dtype(ids.device, precision, weight.dtype), scaler)
+    _accumulate_grad(weight, dw)
     with amp_context(ids.device, precision):
-        hidden.backward(leaf.grad.reshape_as(hidden))
+        hidden.backward(dhidden.view(hidden.shape).to(hidden.dtype))
     return total

@@ -71,42 +71,23 @@ def _kernels(blocks, p, ctx_amp, ctx_dtype, mlp_tokens=0):
     return engine.LayerKernels(blocks[0].attn.n_heads, B, T, cd, mlp_tokens), cd
 
 
-def _module_backward(ctx, blocks, method, h, p, q, dp, dq):
-    """Reference algorithm (reversible.py:47-69) over the module forward, for
-    configurations the fused engine does not cover (e.g. biased Linears)."""
-    gradients = []
-    with torch.autocast(ctx.device_type, enabled=ctx.amp_enabled, dtype=ctx.amp_dtype):
-        for block in reversed(blocks):
-            with torch.no_grad():
-                p0, q0 = inverse_pair(block, p, q, method, h)
-            with torch.enable_grad():
-                p0 = p0.detach().requires_grad_(True)
-                q0 = q0.detach().requires_grad_(True)
-                next_p, next_q = forward_pair(block, p0, q0, method, h)
-                local_parameters = tuple(block.parameters())
-                local = torch.autograd.grad((next_p, next_q), (p0, q0, *local_parameters), (dp, dq))
-            dp, dq = local[:2]
-            gradients[0:0] = local[2:]
-            p, q = p0.detach(), q0.detach()
-    return dp, dq, gradients
-
-
 def stack_forward(ctx, p, q, blocks, method, h):
     """Shared forward of the stack Functions: records the autocast state on
-    ctx (reversible.py:39-42) and runs every forward_pair without a graph."""
+    ctx (reversible.py:39-42) and runs every forward_pair without a graph, on
+    the fused engine. Configurations outside the reference architecture
+    (biased Linears, non-fp32 or non-CUDA residual states, foreign block
+    types) are rejected here rather than run on a slower second algorithm."""
+    if not fused_supported(blocks, p):
+        raise ValueError("the reconstruction backward runs bias-free reference Blocks on fp32 CUDA residual "
+                         f"states [batch, length, d_model]; got {p.dtype} {tuple(p.shape)} on {p.device.type}")
     ctx.blocks, ctx.method, ctx.h = blocks, method, h
     ctx.device_type = p.device.type
     ctx.amp_enabled = torch.is_autocast_enabled(ctx.device_type)
     ctx.amp_dtype = torch.get_autocast_dtype(ctx.device_type)
-    ctx.fused = fused_supported(blocks, p)
-    if ctx.fused:
-        kern, cd = _kernels(blocks, p, ctx.amp_enabled, ctx.amp_dtype)
-        p2, q2 = engine.stack_forward(kern, _layers(blocks, cd), p.reshape(-1, p.shape[-1]),
-                                      q.reshape(-1, q.shape[-1]), method, h)
-        return p2.view(p.shape), q2.view(q.shape)
-    for block in blocks:
-        p, q = forward_pair(block, p, q, method, h)
-    return p, q
+    kern, cd = _kernels(blocks, p, ctx.amp_enabled, ctx.amp_dtype)
+    p2, q2 = engine.stack_forward(kern, _layers(blocks, cd), p.reshape(-1, p.shape[-1]),
+                                  q.reshape(-1, q.shape[-1]), method, h)
+    return p2.view(p.shape), q2.view(q.shape)
 
 
 def stack_backward(ctx, p, q, dp, dq):
@@ -114,8 +95,6 @@ def stack_backward(ctx, p, q, dp, dq):
     blocks.parameters() order)."""
     dp = torch.zeros_like(p) if dp is None else dp
     dq = torch.zeros_like(q) if dq is None else dq
-    if not ctx.fused:
-        return _module_backward(ctx, ctx.blocks, ctx.method, ctx.h, p, q, dp, dq)
     shape = p.shape
     kern, cd = _kernels(ctx.blocks, p, ctx.amp_enabled, ctx.amp_dtype)
     layers = _layers(ctx.blocks, cd)

@@ -44,7 +44,23 @@ def test_empty_batches_return_empty_results():
     dw = torch.full((256,), 3.0, device=DEV)
     _, dw_out = fn.rmsnorm_bwd(e, w.detach(), torch.empty(0, device=DEV), e, dw=dw, accumulate_dw=True)
     assert torch.equal(dw_out, torch.full_like(dw, 3.0))
+    # the fused forward, the fused backward and its deferred weight-gradient reduction
+    eb = e.bfloat16()
+    n2, ysum, rstd = fn.add_rmsnorm_fwd(e, eb, w.detach(), 1e-6, torch.bfloat16, want_sum=True)
+    assert n2.shape == (0, 256) and ysum.shape == (0, 256) and rstd.shape == (0,)
+    dx, lp = fn.rmsnorm_bwd_fused(e, w.detach(), rstd, eb, dw, residual=e, lp_add=eb, lp_dtype=torch.bfloat16,
+                                  accumulate_dw=False)
+    assert dx.shape == (0, 256) and lp.shape == (0, 256)
     torch.cuda.synchronize()
+    assert torch.equal(dw, torch.zeros_like(dw))
+    dx, lp, part = fn.rmsnorm_bwd_fused_deferred(e, w.detach(), rstd, eb, lp_dtype=torch.bfloat16)
+    dw.fill_(5.0)
+    fn.rmsnorm_dw_reduce(part, 0, 256, dw, accumulate=True)
+    torch.cuda.synchronize()
+    assert torch.equal(dw, torch.full_like(dw, 5.0))
+    fn.rmsnorm_dw_reduce(part, 0, 256, dw, accumulate=False)
+    torch.cuda.synchronize()
+    assert torch.equal(dw, torch.zeros_like(dw))
 
 
 # ------------------------------------------------------------------ RMSNorm

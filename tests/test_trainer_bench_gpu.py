@@ -1,0 +1,74 @@
+"""Parity of the update that bench.py times, at the benchmarked shape.
+
+The configuration is bench.py's cfg2 workload exactly: the 20.3M model
+(vocabulary 50,257 with the tied softmax head, 7 layers, width 256), context
+512, 29 sequences per microstep, 2 accumulated microsteps, bf16 compute,
+AdamW with the global-norm clip, the synthetic Zipf/EOS stream of seed 1337,
+and the trainer's default execution: the fused softmax head (rk_head_*), the
+software-pipelined reverse sweep, the weight-gradient / attention /
+recompute / forward side streams, and the update replayed from a captured
+CUDA graph. The checker is the CPU oracle's restatement of the reference
+update loop (train_baseline.py:247-285) in bf16-autocast mode, whose rounding
+policy tests/test_oracle_golden_cuda.py pins against the reference itself run
+under CUDA autocast.
+
+Gates (the north star's bf16 tolerances and the reference's low-precision
+update gate, validate_reversible.py:20-29): loss within 2e-3 relative,
+pre-clip gradient norm within 2e-2, every parameter's pre-clip gradient of the
+first update within rel-L2 2e-2, and after two updates the parameter change
+within relative update L2 0.05. Token and label indexing is bit-exact by
+construction (the same batch_at windows) and checked in tests/test_data.py.
+"""
+import math
+
+import pytest
+import torch
+
+from conftest import rel_l2
+from oracle import model as om
+from oracle import stream as ost
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.mark.parametrize("method,B", [("midpoint", 29), ("euler", 4)])
+def test_benchmarked_update_matches_oracle(method, B):
+    import reversability_b200 as rb
+    from reversability_b200 import data as rdata
+    from reversability_b200.train import ReversibleTrainer, TrainSettings, learning_rate
+    T, acc, updates = 512, 2, 2
+    s = TrainSettings(batch_size=B, sequence_length=T, accumulation=acc, precision="bf16")
+    assert s.fused_head and s.overlap_wgrad and s.overlap_forward and s.mlp_tokens == 0  # bench.py's settings
+    torch.manual_seed(1337)
+    model = rb.ReversibleLM(rb.ModelConfig(), method).to(DEV)
+    tr = ReversibleTrainer(model, s)
+    cfg = om.Config()
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    ref = om.Trainer(om.init_params(cfg, seed=1337), cfg, om.TrainConfig(), method, low=torch.bfloat16, eps=1e-6)
+    before = {n: p.detach().clone() for n, p in ref.params.items()}
+    stream = ost.synthetic_stream(B * T * acc * updates + 1, seed=1337)
+    tr.capture(warmup=0)  # the graph; capture itself runs no update
+    for u in range(updates):
+        committed = u * B * T * acc
+        batches, targets = rdata.update_batches(stream, committed, 0, 1, B, T, acc, len(stream) - 1)
+        tr.stage_batches(batches, targets)
+        lr = learning_rate(s, committed, targets)
+        loss = tr.update(lr).item() / targets
+        gnorm = float(tr.grad_norm)
+        grads = {n: tr.view(tr.gflat, n).detach().cpu() for n in om.parameter_names(cfg)} if u == 0 else None
+        r = ref.update(batches, committed)
+        assert abs(r["lr"] - lr) <= 1e-12 * lr
+        assert abs(loss - r["loss"]) <= 2e-3 * abs(r["loss"]), (u, loss, r["loss"])
+        assert abs(gnorm - r["grad_norm"]) <= 2e-2 * r["grad_norm"], (u, gnorm, r["grad_norm"])
+        if grads is not None:
+            # the oracle's .grad holds the clipped gradient (clip_grad_norm_ scales in place)
+            coef = min(1.0, s.grad_clip / (r["grad_norm"] + 1e-6))
+            worst = {n: rel_l2(grads[n], ref.params[n].grad.detach() / coef) for n in grads}
+            assert max(worst.values()) <= 2e-2, sorted(worst.items(), key=lambda kv: -kv[1])[:3]
+    diff = sum(float((tr.view(tr.flat, n).detach().cpu() - ref.params[n].detach()).double().square().sum())
+               for n in before)
+    upd = sum(float((ref.params[n].detach() - before[n]).double().square().sum()) for n in before)
+    assert math.sqrt(diff / upd) <= 0.05
+    from reversability_b200 import _lib
+    assert _lib.device_status() == 0

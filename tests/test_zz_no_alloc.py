@@ -16,7 +16,6 @@ import torch
 from reversability_b200 import _lib
 
 DEV = "cuda"
-TOL = {"dx": dict(rtol=5e-5, atol=5e-6), "dw": dict(rtol=5e-5, atol=5e-5)}  # the RMSNorm tests' tolerances
 
 
 def _call_pair(x, w, dy, x_dt, dy_dt, dx_dt):
@@ -55,9 +54,28 @@ def test_noalloc_matches_workspace_entry_point_on_two_calls(dtypes):
         w = torch.randn(width, device=DEV)
         dy = torch.randn(rows, width, device=DEV).to(gd)
         (dx, dw), (dx_ref, dw_ref) = _call_pair(x, w, dy, _lib.code(xd), _lib.code(gd), _lib.code(xd))
-        torch.testing.assert_close(dx.float(), dx_ref.float(), **TOL["dx"])
-        torch.testing.assert_close(dw, dw_ref, **TOL["dw"])
+        # the same kernels with the same partial count and summation order: equal bits
+        assert torch.equal(dx, dx_ref)
+        assert torch.equal(dw, dw_ref)
     assert _lib.device_status() == 0
+
+
+@pytest.mark.gpu
+def test_noalloc_zero_rows_zeroes_dw_and_accepts_null_rows():
+    """An empty batch: RK_OK, dw set to zero (left as is when accumulating),
+    and the row pointers may be null, as for rk_rmsnorm_bwd."""
+    lib = _lib.lib()
+    s = _lib.stream_ptr()
+    w = torch.ones(256, device=DEV)
+    dw = torch.full((256,), 7.0, device=DEV)
+    assert lib.rk_rmsnorm_bwd_noalloc(None, 0, 256, w.data_ptr(), None, None, 0, 256, None, 0, 256, dw.data_ptr(), 1,
+                                      0, 256, s) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(dw, torch.full_like(dw, 7.0))
+    assert lib.rk_rmsnorm_bwd_noalloc(None, 0, 256, w.data_ptr(), None, None, 0, 256, None, 0, 256, dw.data_ptr(), 0,
+                                      0, 256, s) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(dw, torch.zeros_like(dw))
 
 
 @pytest.mark.gpu

@@ -37,11 +37,24 @@ sys.path.insert(0, str(ROOT))
 METRIC = "train targets/sec (midpoint, 20.3M model)"
 
 
-def metric_name(method: str) -> str:
-    """BASELINE's metric; the Euler configuration (cfg3) names its recurrence."""
-    return METRIC if method == "midpoint" else METRIC.replace("midpoint", method)
+def metric_name(method: str, model: str = "cfg2") -> str:
+    """BASELINE's metric; the Euler configuration (cfg3) names its recurrence
+    and the scaled configuration (cfg5) its model."""
+    name = METRIC if method == "midpoint" else METRIC.replace("midpoint", method)
+    return name if model == "cfg2" else name.replace("20.3M", MODELS[model]["name"])
 UNIT = "targets/s"
 FLOP_PER_TARGET = 143_255_040  # 4 x body (fwd + attention) + 3 x head, cfg2 (20.3M model)
+
+# The benchmarked model shapes: cfg2/cfg3 (the 20.3M decoder, BASELINE configs[1]/[2])
+# and cfg5 (the scaled decoder, BASELINE configs[4]). FLOP per target is the
+# midpoint-reversible minimum: 4 x (body GEMMs + causal attention) + 3 x head.
+MODELS = {
+    "cfg2": dict(config={}, batch=29, seq=512, accumulation=2, flop=FLOP_PER_TARGET, name="20.3M",
+                 shape="L7 d256 H8 ff1024 V50257 T512"),
+    "cfg5": dict(config=dict(n_layers=24, d_model=1024, n_heads=16, d_ff=4096, max_sequence_length=2048),
+                 batch=16, seq=2048, accumulation=1, flop=3_932_657_664, name="456M scaled",
+                 shape="L24 d1024 H16 ff4096 V50257 T2048"),
+}
 
 
 def parse():
@@ -51,14 +64,23 @@ def parse():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["librevk", "reference"], default="librevk")
     ap.add_argument("--method", choices=["midpoint", "euler"], default="midpoint")
-    ap.add_argument("--batch", type=int, default=29)
-    ap.add_argument("--seq", type=int, default=512)
-    ap.add_argument("--accumulation", type=int, default=2)
+    ap.add_argument("--model", choices=sorted(MODELS), default="cfg2",
+                    help="cfg2: the 20.3M decoder (default); cfg5: the scaled 24-layer d1024 decoder")
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--seq", type=int, default=None)
+    ap.add_argument("--accumulation", type=int, default=None)
     ap.add_argument("--no-graph", action="store_true", help="run updates eagerly instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-tied-split", action="store_true",
+                    help="data parallel: reduce the tied embedding gradient as one bucket after the sweep")
     ap.add_argument("--reference-memory", action="store_true",
                     help="measure the reference's own peak allocated HBM at this shape (needs baseline/_ref)")
-    return ap.parse_args()
+    args = ap.parse_args()
+    spec = MODELS[args.model]
+    for key in ("batch", "seq", "accumulation"):
+        if getattr(args, key) is None:
+            setattr(args, key, spec[key])
+    return args
 
 
 def env_rank():
@@ -66,13 +88,16 @@ def env_rank():
 
 
 def config_block(args, world):
-    return {"workload": f"cfg2: {args.method}-reversible 20.3M decoder (L7 d256 H8 ff1024 V50257 T512), "
+    spec = MODELS[args.model]
+    tag = args.model if not (args.model == "cfg2" and args.method == "euler") else "cfg3"
+    return {"workload": f"{tag}: {args.method}-reversible {spec['name']} decoder ({spec['shape']}), "
                         f"batch {args.batch}x{args.seq} x accumulation {args.accumulation} per GPU, bf16 autocast, "
                         f"AdamW(0.9,0.95,wd0.1) clip 1.0",
             "method": args.method, "global_batch": args.batch * args.accumulation * world,
             "seq_len": args.seq, "parallelism": f"dp{world}",
             "targets_per_update_per_gpu": args.batch * args.seq * args.accumulation,
-            "l2": "inputs larger than L2 (per-step working set: 1.5 GB logits + 20M-parameter state)"}
+            "l2": f"inputs larger than L2 (per-step working set: "
+                  f"{args.batch * args.seq * 50304 * 2 / 1e9:.1f} GB logits + the parameter state)"}
 
 
 # ------------------------------------------------------------------ clocks
@@ -208,6 +233,10 @@ def reference_arm(args):
     rank, world, _ = env_rank()
     if rank != 0:
         return
+    if args.model != "cfg2":
+        print(json.dumps({"impl": "reference", "unavailable": f"the CPU port of the reference path is timed on the "
+                          f"20.3M model only; one {args.model} microstep takes minutes on the host cores"}))
+        return
     total = args.steps + args.warmup
     threads, microstep = _cpu_trainer(args.method, args.batch, args.seq, args.accumulation,
                                       total // args.accumulation + 1)
@@ -254,7 +283,7 @@ def reference_memory(args):
     out = {}
     for path in ("reversible_trainer", "optimized_split_tiled_cached_head"):
         torch.manual_seed(1337)
-        model = ReversibleLM(ModelConfig(), args.method).to(dev)
+        model = ReversibleLM(ModelConfig(**MODELS[args.model]["config"]), args.method).to(dev)
         if path != "reversible_trainer":
             install_v3(model, core_mode="split", mlp_tokens=8192)
         opt = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), weight_decay=0.1)
@@ -327,7 +356,9 @@ def kernel_roofline(trainer, peak_tflops):
     return {"kernel": "gemm_tc_kernel EPI_LSE (rk_head_fprop, M=%d N=%d K=%d, bf16)" % (M, V, d),
             "bound": "tensor", "achieved": achieved, "peak": peak_tflops, "unit": "TFLOP/s",
             "frac": achieved / peak_tflops, "avg_launch_us": ms * 1e3, "flops_per_launch": flops,
-            "timed": how, "traffic": profiled_traffic("rk_head_fprop")}
+            "timed": how,
+            # the committed capture is of the cfg2 shape (M 14,848, K 256); other shapes have none
+            "traffic": profiled_traffic("rk_head_fprop") if (M, d) == (14848, 256) else None}
 
 
 # ------------------------------------------------------------------ main arm
@@ -357,9 +388,11 @@ def main():
     from reversability_b200 import _lib, data as rdata
     from reversability_b200.train import ReversibleTrainer, TrainSettings, learning_rate
 
-    s = TrainSettings(batch_size=args.batch, sequence_length=args.seq, accumulation=args.accumulation)
+    s = TrainSettings(batch_size=args.batch, sequence_length=args.seq, accumulation=args.accumulation,
+                      tied_split=not args.no_tied_split)
     torch.manual_seed(1337)
-    model = rb.ReversibleLM(rb.ModelConfig(), args.method).to(dev)
+    spec = MODELS[args.model]
+    model = rb.ReversibleLM(rb.ModelConfig(**spec["config"]), args.method).to(dev)
     trainer = ReversibleTrainer(model, s, pg)
     per_update = args.batch * args.seq * args.accumulation
     total_updates = args.warmup + 2 * args.steps + 2
@@ -372,12 +405,14 @@ def main():
                                           limit)
         return committed, b, targets
 
-    # pinned host copies of every update's batches (e2e loop) and device copies (device loop)
+    # device copies of the device loop's batches (the e2e loop reads the
+    # memory-mapped stream file through the trainer's pinned prefetcher)
+    first_e2e_update = args.warmup + 1 + args.steps
     pinned, resident = [], []
-    for u in range(total_updates):
+    for u in range(first_e2e_update):
         committed, b, targets = host_batches(u)
-        ids = torch.stack([x for x, _, _ in b]).pin_memory()
-        lab = torch.stack([y for _, y, _ in b]).pin_memory()
+        ids = torch.stack([x for x, _, _ in b])
+        lab = torch.stack([y for _, y, _ in b])
         pinned.append((committed, ids, lab, targets))
         resident.append((ids.to(dev), lab.to(dev)))
     torch.cuda.synchronize()
@@ -386,12 +421,6 @@ def main():
         _, _, _, targets = pinned[u]
         trainer.ids.copy_(resident[u][0])
         trainer.labels.copy_(resident[u][1])
-        trainer.inv_denominator.fill_(1.0 / targets)
-
-    def stage_host(u):
-        _, ids, lab, targets = pinned[u]
-        trainer.ids.copy_(ids, non_blocking=True)
-        trainer.labels.copy_(lab, non_blocking=True)
         trainer.inv_denominator.fill_(1.0 / targets)
 
     def lr_of(u):
@@ -451,21 +480,34 @@ def main():
     value = per_update * world * args.steps / (ms_max / 1e3)
     peak_alloc = torch.cuda.max_memory_allocated(dev)
 
-    # ---- end-to-end timed region: pinned-host inputs in, loss out, every step
+    # ---- end-to-end timed region through the trainer API: the token stream as
+    # a uint16 file, memory-mapped; each update's batches built by the
+    # prefetch thread into pinned buffers, copied host -> device inside
+    # train(); the loss sum copied back to the host every step
+    import tempfile
     losses = torch.empty(args.steps, dtype=torch.float32).pin_memory()
-    first_e2e = first + args.steps
+    tmpdir = tempfile.TemporaryDirectory(prefix="revk_stream_")
+    mm = rdata.open_stream(rdata.write_stream(Path(tmpdir.name) / "train.bin", stream))
+    e2e_start = first_e2e_update * per_update * world
+    prefetch = rdata.UpdatePrefetcher(mm, rank, world, args.batch, args.seq, args.accumulation,
+                                      min(limit, e2e_start + args.steps * per_update * world), start=e2e_start)
+    h2d = 2 * args.accumulation * args.batch * args.seq * 8  # ids + labels, int64
+
+    def keep_loss(k, staged, loss):
+        losses[k].copy_(loss, non_blocking=True)
+
     barrier()
     torch.cuda.synchronize()
     e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(cs)
-    for k in range(args.steps):
-        u = first_e2e + k
-        stage_host(u)
-        loss = trainer.update(lr_of(u))
-        losses[k].copy_(loss, non_blocking=True)
+    ran = trainer.train(prefetch, max_updates=args.steps, on_update=keep_loss)
     e_stop.record(cs)
     torch.cuda.synchronize()
     barrier()
+    prefetch.close()
+    tmpdir.cleanup()
+    if ran != args.steps:
+        raise RuntimeError(f"the e2e loop ran {ran} of {args.steps} updates")
     e_ms = e_start.elapsed_time(e_stop)
     if world > 1:
         import torch.distributed as dist
@@ -473,7 +515,6 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_ms = t.item()
     e2e_value = per_update * world * args.steps / (e_ms / 1e3)
-    h2d = sum(t.numel() * t.element_size() for t in pinned[0][1:3])
     status = _lib.device_status()
     finite = bool(torch.isfinite(losses).all())
 
@@ -481,17 +522,19 @@ def main():
         hbm, tflops, tflops_sus, peak_kind = measured_peaks()
         roof = kernel_roofline(trainer, tflops)
         roof["peak_source"] = peak_kind
-        model_flops = value * FLOP_PER_TARGET / world / 1e12
+        model_flops = value * spec["flop"] / world / 1e12
         line = {
-            "metric": metric_name(args.method), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "metric": metric_name(args.method, args.model), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": config_block(args, world),
             "roofline": roof,
             "model_roofline": {"achieved": model_flops, "peak": tflops_sus or tflops, "unit": "TFLOP/s per GPU",
                                "frac": model_flops / (tflops_sus or tflops),
-                               "flop_per_target": FLOP_PER_TARGET, "peak_source": peak_kind + " sustained"},
-            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4},
+                               "flop_per_target": spec["flop"], "peak_source": peak_kind + " sustained"},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
+                    "path": "ReversibleTrainer.train over data.UpdatePrefetcher (memory-mapped uint16 stream, "
+                            "pinned buffers filled by a background thread)"},
             "gpu_launches": launches_per_update * args.steps,
             "launches_per_update": launches_per_update,
             "cuda_graph": use_graph,
@@ -500,7 +543,7 @@ def main():
             "loss_first_last": [float(losses[0]) / per_update / world, float(losses[-1]) / per_update / world],
             "losses_finite": finite, "device_status": status,
         }
-        if not args.no_cpu_baseline and world == 1:
+        if not args.no_cpu_baseline and world == 1 and args.model == "cfg2":
             line["cpu_baseline"] = cpu_baseline(args.method, args.batch, args.seq, args.accumulation)
         print(json.dumps(line), flush=True)
     if world > 1:

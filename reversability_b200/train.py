@@ -62,6 +62,7 @@ class TrainSettings:
     fused_head: bool = True  # bf16/f16: cross-entropy inside the head GEMMs (rk_head_*)
     overlap_wgrad: bool = True  # layer weight gradients on a side stream during the reverse sweep
     overlap_forward: bool = True  # microstep m+1's forward sweep beside microstep m's backward
+    tied_split: bool = True  # data parallel: the head's share of the tied gradient reduced beside the sweep
 
 
 def learning_rate(s: TrainSettings, committed: int, update_targets: int) -> float:
@@ -153,10 +154,19 @@ class ReversibleTrainer:
         self.opt_scalars[0] = settings.learning_rate
         self.norm_ws = torch.empty(_lib.lib().rk_clip_adamw_workspace() // 4, device=dev, dtype=F32)
         # DP buckets: one per layer (launched as the last microstep's sweep passes it),
-        # then the embedding, position and final-norm gradients, and the loss sum
+        # then the embedding, position and final-norm gradients, the loss sum
         # (launched once the last microstep's loss is in, so every rank returns
-        # the global loss)
-        self.buckets = GradBuckets(self.layer_slices + [self.g_tok, self.g_pos, self.g_final, self.loss_sum],
+        # the global loss) and the head's share of the tied embedding gradient.
+        # Tied-gradient split (model.py:101,104; reversible.py:106): with more
+        # than one rank the head weight gradients of every microstep and the
+        # embedding scatters of all microsteps but the last accumulate in
+        # g_head, whose bucket is launched as soon as the last head weight
+        # gradient is issued, so it crosses NVLink beside the reverse sweep;
+        # g_tok keeps only the last microstep's embedding scatter, and the two
+        # reduced shares are summed before the optimizer.
+        self.g_head = torch.zeros_like(self.g_tok) if (self.world > 1 and settings.tied_split) else None
+        self.buckets = GradBuckets(self.layer_slices + [self.g_tok, self.g_pos, self.g_final, self.loss_sum]
+                                   + ([self.g_head] if self.g_head is not None else []),
                                    process_group, dev) if self.world > 1 else None
         self.graph = None
         self.head_events = None
@@ -191,6 +201,91 @@ class ReversibleTrainer:
             self.ids[m, :x.shape[0]].copy_(x, non_blocking=True)
             self.labels[m, :y.shape[0]].copy_(y, non_blocking=True)
         self.inv_denominator.fill_(1.0 / update_targets)
+
+    def stage_update(self, staged) -> torch.cuda.Event:
+        """Copies a data.StagedUpdate (pinned ids/labels [accumulation, B, T])
+        into the static device buffers with one asynchronous copy each and
+        returns an event recorded after the copies (hand it to
+        UpdatePrefetcher.release)."""
+        if tuple(staged.ids.shape) != tuple(self.ids.shape):
+            raise ValueError(f"staged batch shape {tuple(staged.ids.shape)} != {tuple(self.ids.shape)}")
+        self.ids.copy_(staged.ids, non_blocking=True)
+        self.labels.copy_(staged.labels, non_blocking=True)
+        self.inv_denominator.fill_(1.0 / staged.update_targets)
+        done = torch.cuda.Event()
+        done.record()
+        return done
+
+    def train(self, prefetcher, max_updates: int | None = None, on_update=None) -> int:
+        """The reference trainer's update loop (train_baseline.py:247-285) over
+        a data.UpdatePrefetcher: stage the update's batches, set the
+        warm-up/cosine learning rate, run the update (the captured graph when
+        capture() was called). on_update(index, staged, loss_sum) sees the
+        device loss sum of each update. Returns the number of updates run."""
+        n = 0
+        for staged in prefetcher:
+            done = self.stage_update(staged)
+            prefetcher.release(staged, done)
+            loss = self.update(lr=learning_rate(self.s, staged.committed, staged.update_targets))
+            if on_update is not None:
+                on_update(n, staged, loss)
+            n += 1
+            if max_updates is not None and n >= max_updates:
+                break
+        return n
+
+    # ------------------------------------------------------------------ checkpoints
+    def _torch_adamw(self, lr: float | None = None) -> torch.optim.AdamW:
+        s = self.s
+        return torch.optim.AdamW(self.model.parameters(), lr=s.learning_rate if lr is None else lr,
+                                 betas=(s.beta1, s.beta2), weight_decay=s.weight_decay)
+
+    def optimizer_state_dict(self) -> dict:
+        """The AdamW state in torch.optim.AdamW.state_dict() format (the
+        reference checkpoint's "optimizer" entry, train_baseline.py:333): per
+        parameter in model.parameters() order its step, exp_avg and exp_avg_sq."""
+        opt = self._torch_adamw(float(self.opt_scalars[0]))
+        step = float(self.opt_scalars[1])
+        if step > 0:
+            for name, p in self.model.named_parameters():
+                opt.state[p] = {"step": torch.tensor(step, dtype=F32),
+                                "exp_avg": self.view(self.exp_avg, name).detach().clone(),
+                                "exp_avg_sq": self.view(self.exp_avg_sq, name).detach().clone()}
+        return opt.state_dict()
+
+    def load_optimizer_state_dict(self, state: dict):
+        """Loads a torch.optim.AdamW state dict (the reference checkpoint's
+        "optimizer" entry) into the flat moment buffers and the step count."""
+        opt = self._torch_adamw()
+        opt.load_state_dict(state)
+        steps = set()
+        for name, p in self.model.named_parameters():
+            st = opt.state.get(p)
+            if not st:
+                self.view(self.exp_avg, name).zero_()
+                self.view(self.exp_avg_sq, name).zero_()
+                steps.add(0.0)
+                continue
+            self.view(self.exp_avg, name).copy_(st["exp_avg"])
+            self.view(self.exp_avg_sq, name).copy_(st["exp_avg_sq"])
+            steps.add(float(st["step"]))
+        if len(steps) > 1:
+            raise ValueError(f"parameters are at different AdamW steps {sorted(steps)}")
+        self.opt_scalars[1] = steps.pop() if steps else 0.0
+        self.opt_scalars[0] = float(opt.param_groups[0]["lr"])
+
+    def state_dict(self) -> dict:
+        """{"model", "optimizer"} as the reference checkpoint holds them
+        (train_baseline.py:332-333): the module state_dict (parameter names of
+        model.py) and the AdamW state."""
+        return {"model": self.model.state_dict(), "optimizer": self.optimizer_state_dict()}
+
+    def load_state_dict(self, state: dict):
+        """Restores a checkpoint written by state_dict() or by the reference
+        trainer (its "model" and "optimizer" entries)."""
+        self.model.load_state_dict(state["model"])
+        self._refresh_compute_copy()
+        self.load_optimizer_state_dict(state["optimizer"])
 
     # ------------------------------------------------------------------ one microstep
     def _forward_states(self, m: int):
@@ -230,15 +325,22 @@ class ReversibleTrainer:
                          fcoef=self.head_fcoef)
             self.loss_sum += loss_rows.sum()
             self._loss_bucket(last)
+            g_head = self.g_head if self.g_head is not None else self.g_tok
             if kern.side is not None:
                 # the head weight gradient runs beside the dgrad and the
                 # reverse sweep; the sweep's final join (stack_backward) orders
                 # it before the embedding backward, which also adds into g_tok
                 with kern.side_work():
-                    fn.head_wgrad(st, hidden, dw=self.g_tok, accumulate=True)
+                    fn.head_wgrad(st, hidden, dw=g_head, accumulate=True)
+                    head_done = torch.cuda.Event()
+                    head_done.record()
+                if last and self.g_head is not None:
+                    self.buckets.launch(self._head_bucket, after=[head_done])
             dhidden = fn.head_dgrad(st, self.tok_c)
             if kern.side is None:
-                fn.head_wgrad(st, hidden, dw=self.g_tok, accumulate=True)
+                fn.head_wgrad(st, hidden, dw=g_head, accumulate=True)
+                if last and self.g_head is not None:
+                    self.buckets.launch(self._head_bucket)
         else:
             fn.linear_fwd(hidden, self.tok_c, out=logits)
             # dlogits = (softmax - onehot) / update_targets, in place over the logits
@@ -248,7 +350,10 @@ class ReversibleTrainer:
             self.loss_sum += loss_rows.sum()
             self._loss_bucket(last)
             dhidden = fn.linear_dgrad(logits, self.tok_c)
-            fn.linear_wgrad(logits, hidden, dw=self.g_tok, accumulate=True)
+            fn.linear_wgrad(logits, hidden, dw=self.g_head if self.g_head is not None else self.g_tok,
+                            accumulate=True)
+            if last and self.g_head is not None:
+                self.buckets.launch(self._head_bucket)
         dout, _ = fn.rmsnorm_bwd(out, self.final_w, rstd_f, dhidden, dx_dtype=F32, dw=self.g_final,
                                  accumulate_dw=True)
         # the unused output's cotangent is zero; the engine takes None for it
@@ -257,14 +362,16 @@ class ReversibleTrainer:
         _, _, dp, dq = engine.stack_backward(kern, self.layers, self.layer_grads, p, q, dp, dq, self.model.method,
                                              self.model.step_size, on_layer_done=hook, first=first)
         # boundary p = q = embedding: both cotangents reach it (summed inside the kernel)
+        # (with the tied-gradient split, earlier microsteps scatter into g_head)
+        g_emb = self.g_head if (self.g_head is not None and not last) else self.g_tok
         if not last and kern.side is not None:
             # before the next microstep's head: on the weight-gradient stream,
             # ahead of that head's weight gradient (the other writer of g_tok)
             with kern.side_work():
-                fn.embedding_bwd(ids, dp, self.g_tok, self.g_pos, dx2=dq)
+                fn.embedding_bwd(ids, dp, g_emb, self.g_pos, dx2=dq)
             kern.hold(dp, dq)
         else:
-            fn.embedding_bwd(ids, dp, self.g_tok, self.g_pos, dx2=dq)
+            fn.embedding_bwd(ids, dp, g_emb, self.g_pos, dx2=dq)
 
     def _loss_bucket(self, last: bool):
         if last and self.world > 1:
@@ -274,8 +381,14 @@ class ReversibleTrainer:
         self.buckets.launch(layer, after=events)
 
     # ------------------------------------------------------------------ one update
+    @property
+    def _head_bucket(self) -> int:
+        return len(self.layers) + 4
+
     def _update_body(self):
         self.gflat.zero_()
+        if self.g_head is not None:
+            self.g_head.zero_()
         self.loss_sum.zero_()
         acc = self.s.accumulation
         if self.fwd_stream is None or acc == 1:
@@ -306,6 +419,8 @@ class ReversibleTrainer:
             for i in range(n, n + 3):
                 self.buckets.launch(i)
             self.buckets.finish()
+            if self.g_head is not None:
+                self.g_tok.add_(self.g_head)  # the two reduced shares of the tied gradient
         self._optimizer_step()
 
     def _optimizer_step(self):

@@ -120,3 +120,51 @@ def test_missing_rank_makes_collective_fail_within_timeout():
     _, outcome, elapsed = survivors[0]
     assert outcome != "no error" and not outcome.startswith("setup"), survivors
     assert elapsed < 60
+
+
+def _tied_split_worker(rank, world, port, queue):
+    """The trainer's bucket order with the tied-gradient split: the loss sum,
+    then the head share of the tied gradient (before the sweep), the layer
+    buckets in reverse, then the embedding scatter share, position and final
+    norm; the two reduced shares summed equal the reduced total."""
+    try:
+        import sys
+        sys.path.insert(0, os.getcwd())
+        from reversability_b200.dist import GradBuckets
+        _init(rank, world, port)
+        g = torch.Generator().manual_seed(100 + rank)
+        n_layers, V, d = 3, 11, 4
+        flat = torch.randn(n_layers * 20 + V * d + 6 + 3, generator=g)
+        layers = [flat[i * 20:(i + 1) * 20] for i in range(n_layers)]
+        o = n_layers * 20
+        g_tok, g_pos, g_final = flat[o:o + V * d].view(V, d), flat[o + V * d:o + V * d + 6], flat[-3:]
+        loss = torch.randn((), generator=g)
+        g_head = torch.randn(V, d, generator=g)
+        total = [None] * world
+        dist.all_gather_object(total, (flat.clone(), g_head.clone(), loss.clone()))
+        b = GradBuckets(layers + [g_tok, g_pos, g_final, loss, g_head], None, torch.device("cpu"))
+        b.launch(n_layers + 3)  # loss
+        b.launch(n_layers + 4)  # head share, beside the sweep
+        for i in reversed(range(n_layers)):
+            b.launch(i)
+        for i in range(n_layers, n_layers + 3):
+            b.launch(i)
+        order = b.finish()
+        g_tok.add_(g_head)
+        exp_flat = sum(t[0] for t in total)
+        exp_tok = sum(t[0][o:o + V * d].view(V, d) + t[1] for t in total)
+        ok = (torch.allclose(g_tok, exp_tok, rtol=1e-6, atol=1e-6)
+              and torch.allclose(flat[:o], exp_flat[:o], rtol=1e-6, atol=1e-6)
+              and torch.allclose(flat[o + V * d:], exp_flat[o + V * d:], rtol=1e-6, atol=1e-6)
+              and torch.allclose(loss, sum(t[2] for t in total), rtol=1e-6))
+        queue.put((rank, ok, order))
+        dist.destroy_process_group()
+    except Exception as exc:
+        queue.put((rank, repr(exc), None))
+
+
+def test_tied_gradient_split_buckets_gloo():
+    res = _run(_tied_split_worker)
+    assert len(res) == 2, res
+    assert all(ok is True for _, ok, _ in res), res
+    assert res[0][2] == res[1][2]

@@ -115,3 +115,61 @@ def test_graph_replay_equals_eager_update(method):
     l2 = graphed.update(1e-4).item()
     assert l1 == l2
     assert torch.equal(eager.flat, graphed.flat)
+
+
+def _trainer(method="midpoint", B=3, T=64, acc=2):
+    import reversability_b200 as rb
+    from reversability_b200.train import ReversibleTrainer, TrainSettings
+    torch.manual_seed(1337)
+    s = TrainSettings(batch_size=B, sequence_length=T, accumulation=acc, warmup_targets=1000)
+    return ReversibleTrainer(rb.ReversibleLM(rb.ModelConfig(**WIDE), method).to(DEV), s)
+
+
+def test_train_loop_over_prefetcher_equals_staged_updates(tmp_path):
+    """trainer.train() over a memory-mapped uint16 stream with the pinned
+    prefetcher runs the same updates, bit for bit, as staging each update's
+    batches by hand with the reference's learning-rate schedule."""
+    from reversability_b200 import data as rdata
+    from reversability_b200.train import learning_rate
+    B, T, acc = 3, 64, 2
+    s = ost.synthetic_stream(B * T * acc * 3 + 1, seed=12, vocab_size=101, eos=100, mean_doc=40.0)
+    mm = rdata.open_stream(rdata.write_stream(tmp_path / "train.bin", s))
+    a, b = _trainer(), _trainer()
+    losses = []
+    pf = rdata.UpdatePrefetcher(mm, 0, 1, B, T, acc, len(s) - 1, depth=2)
+    n = a.train(pf, on_update=lambda i, st, loss: losses.append(float(loss)))
+    pf.close()
+    assert n == 3
+    for u in range(3):
+        committed = u * B * T * acc
+        batches, targets = rdata.update_batches(s, committed, 0, 1, B, T, acc, len(s) - 1)
+        b.stage_batches(batches, targets)
+        assert float(b.update(learning_rate(b.s, committed, targets))) == losses[u]
+    assert torch.equal(a.flat, b.flat) and torch.equal(a.exp_avg_sq, b.exp_avg_sq)
+
+
+def test_checkpoint_roundtrip_and_torch_adamw_format():
+    """state_dict() holds the module state_dict and a torch.optim.AdamW state
+    dict (the reference checkpoint's "model"/"optimizer" entries): it loads
+    into torch's AdamW, and a trainer restored from it continues bit for bit."""
+    from reversability_b200 import data as rdata
+    B, T, acc = 3, 64, 2
+    s = ost.synthetic_stream(B * T * acc * 3 + 1, seed=13, vocab_size=101, eos=100, mean_doc=40.0)
+    a = _trainer()
+    batches, targets = rdata.update_batches(s, 0, 0, 1, B, T, acc, len(s) - 1)
+    a.stage_batches(batches, targets)
+    a.update(3e-4)
+    ckpt = a.state_dict()
+    opt = torch.optim.AdamW(a.model.parameters(), lr=1e-3, betas=(0.9, 0.95), weight_decay=0.1)
+    opt.load_state_dict(ckpt["optimizer"])
+    first = next(iter(a.model.parameters()))
+    assert float(opt.state[first]["step"]) == 1.0
+    assert len(ckpt["optimizer"]["state"]) == len(list(a.model.parameters()))
+    b = _trainer()
+    b.load_state_dict(ckpt)
+    assert torch.equal(a.flat, b.flat) and torch.equal(a.exp_avg, b.exp_avg)
+    batches, targets = rdata.update_batches(s, B * T * acc, 0, 1, B, T, acc, len(s) - 1)
+    for t in (a, b):
+        t.stage_batches(batches, targets)
+    assert float(a.update(2e-4)) == float(b.update(2e-4))
+    assert torch.equal(a.flat, b.flat)

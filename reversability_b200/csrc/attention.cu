@@ -621,16 +621,29 @@ __global__ void __launch_bounds__(128) bwd_dkv_f32_kernel(const float* __restric
 using namespace rk;
 using namespace rk::attn;
 
-int rk_attn_fwd_tc32(const void* qkv, int64_t ldq, void* out, int64_t ldo, float* lse, int64_t B, int64_t H,
-                     int64_t T, int dtype, cudaStream_t s);
+int rk_attn_fwd_tc(const void* qkv, int64_t ldq, void* out, int64_t ldo, float* lse, int64_t B, int64_t H,
+                   int64_t HD, int64_t T, int dtype, cudaStream_t s);
+int rk_attn_bwd_tc(int piece, const void* qkv, int64_t ldq, const void* dout, int64_t ldo, const float* lse,
+                   const float* dsum, void* dqkv, int64_t lddq, int64_t B, int64_t H, int64_t HD, int64_t T, int dtype,
+                   cudaStream_t s);
 
 namespace {
 
-// Tensor-core forward for head_dim 32 (attention_tc.cu). REVK_ATTN_TC=0 in the
-// environment selects the mma.sync kernel instead (a tuning switch).
+// Tensor-core forward for head_dim 32 and 64 (attention_tc.cu). REVK_ATTN_TC=0
+// in the environment selects the mma.sync kernel instead (a tuning switch).
 bool attn_tc_enabled() {
   static const bool on = [] {
     const char* e = getenv("REVK_ATTN_TC");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+// Tensor-core backward (attention_tc.cu); REVK_ATTN_BWD_TC=0 selects the
+// mma.sync kernels (a tuning switch).
+bool attn_bwd_tc_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("REVK_ATTN_BWD_TC");
     return !(e && e[0] == '0');
   }();
   return on;
@@ -650,8 +663,22 @@ int fwd_tc(const void* qkv, void* out, float* lse, int B, int H, int Tlen, int64
 }
 
 template <typename T, int HD>
+int bwd_piece(int piece, const void* qkv, const void* o, const void* dout, const float* lse, float* dsum, void* dqkv,
+              int B, int H, int Tlen, int64_t ldq, int64_t ldo, int64_t lddq, cudaStream_t s);
+
+template <typename T, int HD>
 int bwd_tc(const void* qkv, const void* o, const void* dout, const float* lse, float* dsum, void* dqkv, int B, int H,
            int Tlen, int64_t ldq, int64_t ldo, int64_t lddq, cudaStream_t s) {
+  if (attn_bwd_tc_enabled()) {  // D, then the tensor-core dQ and dK/dV kernels
+    int st = bwd_piece<T, HD>(0, qkv, o, dout, lse, dsum, dqkv, B, H, Tlen, ldq, ldo, lddq, s);
+    if (st) return st;
+    const int dt = std::is_same_v<T, __nv_bfloat16> ? RK_BF16 : RK_F16;
+    st = rk_attn_bwd_tc(1, qkv, ldq, dout, ldo, lse, dsum, dqkv, lddq, B, H, HD, Tlen, dt, s);
+    if (st != RK_ERR_UNSUPPORTED) {
+      if (st) return st;
+      return rk_attn_bwd_tc(2, qkv, ldq, dout, ldo, lse, dsum, dqkv, lddq, B, H, HD, Tlen, dt, s);
+    }
+  }
   dim3 grid((Tlen + BQ - 1) / BQ, B * H);
   const float scale = 1.f / sqrtf((float)HD);
   const float c_log2 = 1.4426950408889634f * scale;
@@ -682,6 +709,11 @@ int bwd_piece(int piece, const void* qkv, const void* o, const void* dout, const
   constexpr int tile_bytes = 64 * (HD + 8) * (int)sizeof(T);
   constexpr int smem_dq = 6 * tile_bytes;
   constexpr int smem_dkv = 6 * tile_bytes + 4 * 64 * (int)sizeof(float);
+  if (piece != 0 && attn_bwd_tc_enabled()) {
+    const int dt = std::is_same_v<T, __nv_bfloat16> ? RK_BF16 : RK_F16;
+    const int st = rk_attn_bwd_tc(piece, qkv, ldq, dout, ldo, lse, dsum, dqkv, lddq, B, H, HD, Tlen, dt, s);
+    if (st != RK_ERR_UNSUPPORTED) return st;
+  }
   if (piece == 0) {
     const int64_t n = (int64_t)B * Tlen * H;
     rk_host::launch_k(dsum_kernel<T, HD>, (unsigned)((n + 255) / 256), 256, 0, s, static_cast<const T*>(o),
@@ -722,8 +754,8 @@ extern "C" int rk_attn_fwd(const void* qkv, int64_t ldq, void* out, int64_t ldo,
   }
   if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
   if (!tc_layout_ok(qkv, out, nullptr, ldq, ldo, HD)) return (HD == 32 || HD == 64) ? RK_ERR_ALIGN : RK_ERR_UNSUPPORTED;
-  if (HD == 32 && attn_tc_enabled()) {
-    const int st = rk_attn_fwd_tc32(qkv, ldq, out, ldo, lse, B, H, T, dtype, s);
+  if (attn_tc_enabled()) {
+    const int st = rk_attn_fwd_tc(qkv, ldq, out, ldo, lse, B, H, HD, T, dtype, s);
     if (st != RK_ERR_UNSUPPORTED) return st;
   }
   if (dtype == RK_BF16)

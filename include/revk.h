@@ -189,6 +189,21 @@ RK_API int rk_gemm_dgrad(const void* dy, int64_t lddy, const void* w, int64_t ld
  * columns of DX[b*T + t] * O[b*T + t] with O [M, K], K = H * 32, M = B * T;
  * bit-identical to rk_gemm_dgrad followed by rk_attn_bwd_piece(0). Returns
  * RK_ERR_UNSUPPORTED when the layout does not fit the TMA epilogue. */
+/* Sublayer output projection with the reversible state update in its
+ * epilogue (replaces the projection + inverse_pair / forward_pair arithmetic of
+ * reversible.py:21-32 and optimized.py:31-32):
+ *   out[M,N] = state[M,N] - round(coeff * round(round(x[M,K] . W[N,K]^T) + addend[M,N]))
+ * with addend null meaning no addend; rounding to the 16-bit dtype (bf16/f16)
+ * where autocast rounds, the subtraction in fp32. Midpoint: the MLP down
+ * projection with addend = the attention output a, coeff = 2h (reconstruction)
+ * or -2h (forward). Euler: coeff = 1 or -1 without an addend. The sublayer
+ * output never reaches global memory; out may equal state. Bit-identical to
+ * rk_gemm_fprop followed by rk_reconstruct_midpoint_sum / rk_reconstruct_midpoint.
+ * N % 32 == 0 (else RK_ERR_UNSUPPORTED); state/out 16-byte aligned with row
+ * strides that are multiples of 4 elements, addend with strides multiple of 8. */
+RK_API int rk_gemm_fprop_reconstruct(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* state,
+                              int64_t lds, const void* addend, int64_t lda, float coeff, float* out, int64_t ldo,
+                              int64_t M, int64_t N, int64_t K, int dtype, void* stream);
 RK_API int rk_gemm_dgrad_dsum(const void* dy, int64_t lddy, const void* w, int64_t ldw, void* dx, int64_t lddx,
                               int64_t M, int64_t N, int64_t K, int dtype, const void* o, int64_t ldo, float* dsum,
                               int64_t T, int64_t H, void* stream);
@@ -252,7 +267,7 @@ RK_API int rk_cross_entropy_fwd_bwd(const void* logits, int64_t ld, int64_t voca
  * The vocabulary head and its cross-entropy with no pass of their own over the
  * logits; together they replace the head Linear, F.cross_entropy(...,
  * reduction="sum") and their backward (model.py:104, train_baseline.py:262,
- * optimized_v3.py cached_head_backward). Blocks b are 128 columns wide.
+ * optimized_v3.py cached_head_backward). Blocks b are 64 columns wide.
  *   rk_head_fprop : expo[M, V] = exp(x - m_b) (bf16/f16) where x = hidden . W^T
  *                   rounded to the compute type and m_b the max of x over the
  *                   row's block b; stats[M][width] float2 = (m_b, sum of exp)
@@ -318,6 +333,73 @@ RK_API int64_t rk_embedding_bwd_workspace(int64_t rows, int64_t V);
 RK_API int rk_embedding_bwd(const int64_t* ids, const float* dx, const float* dx2, float* g_tok, float* g_pos,
                             int64_t rows, int64_t T, int64_t d, int64_t V, void* workspace, int64_t workspace_bytes,
                             void* stream);
+
+/* ------------------------------------------------------------- Reversible layer
+ * One reversible Block step as a single call: the per-layer sequence of the
+ * calls above (RMSNorm, QKV/proj/up/down GEMMs with their fused epilogues,
+ * causal attention, their VJPs and weight gradients), issued in order on
+ * `stream` (no host synchronisation, no allocation). Replaces, per layer:
+ *   rk_layer_fwd_midpoint  forward_pair midpoint (reversible.py:21-23)
+ *   rk_layer_fwd_euler     forward_pair Euler (reversible.py:24-25)
+ *   rk_layer_bwd_midpoint  one iteration of _InverseStack.backward /
+ *                          ReusedMidpoint.backward (reversible.py:47-69,
+ *                          optimized.py:21-41): inverse_pair + recompute + VJP
+ *   rk_layer_bwd_euler     the same for the Euler recurrence
+ * with the force F(x) = A(x) + M(x + A(x)) of reversible.py:16-18 (Block of
+ * model.py:59-69, bias-free). Compute dtype RK_BF16 or RK_F16 (the autocast
+ * rounding points of the reference); states, cotangents, RMSNorm weights and
+ * weight gradients are fp32, GEMM weights are in the compute dtype. States are
+ * [tokens, d_model] row-major with tokens = batch * length (row b*length + t).
+ * Weight gradients accumulate (+=) into `grads`. workspace: at least
+ * rk_layer_workspace(desc, method, backward) bytes, 256-byte aligned; the
+ * caller may reuse it for the next layer once the call's work is ordered
+ * before (same stream). Returns RK_ERR_DTYPE for fp32 compute, which the
+ * separate entry points cover. */
+typedef struct rk_layer_desc {
+  int64_t batch, length;      /* B, T */
+  int64_t d_model, n_heads, d_ff;
+  int64_t mlp_tokens;         /* MLP token tile (TiledMLP); 0 = the whole batch at once */
+  int dtype;                  /* compute dtype: RK_BF16 / RK_F16 */
+  float eps_attn, eps_mlp;    /* RMSNorm eps of attn_norm / mlp_norm */
+  const float* attn_norm;     /* fp32 [d] */
+  const void* qkv;            /* [3d, d] compute dtype (attn.qkv.weight) */
+  const void* proj;           /* [d, d] (attn.proj.weight) */
+  const float* mlp_norm;      /* fp32 [d] */
+  const void* up;             /* [2ff, d] (mlp.up.weight: gate rows, then value rows) */
+  const void* down;           /* [d, ff] (mlp.down.weight) */
+} rk_layer_desc;
+
+typedef struct rk_layer_grads {  /* fp32, Block.parameters() order */
+  float *attn_norm, *qkv, *proj, *mlp_norm, *up, *down;
+} rk_layer_grads;
+
+enum { RK_METHOD_MIDPOINT = 0, RK_METHOD_EULER = 1 };
+
+RK_API int64_t rk_layer_workspace(const rk_layer_desc* desc, int method, int backward);
+/* (p, q) -> (q, q_next = p + round(2h F(q))): the next p is q itself. */
+RK_API int rk_layer_fwd_midpoint(const rk_layer_desc* desc, const float* p, const float* q, float h, float* q_next,
+                                 void* workspace, int64_t workspace_bytes, void* stream);
+/* q_next = q + A(p), p_next = p + M(q_next). */
+RK_API int rk_layer_fwd_euler(const rk_layer_desc* desc, const float* p, const float* q, float* p_next,
+                              float* q_next, void* workspace, int64_t workspace_bytes, void* stream);
+/* From the states after the layer (p, q) and their cotangents (dp, dq; dp may
+ * be NULL for a zero cotangent): p_prev = q - round(2h F(p)) (the previous q
+ * is p itself), dq_prev = dp + J_F(p)^T round(2h round(dq)) (the previous dp
+ * is dq itself). gf_in (compute dtype, may be NULL) is round(2h round(dq))
+ * when the caller has it; gf_out (may be NULL) receives round(2h round(dq_prev))
+ * for the layer below. */
+RK_API int rk_layer_bwd_midpoint(const rk_layer_desc* desc, const rk_layer_grads* grads, const float* p,
+                                 const float* q, const float* dp, const float* dq, const void* gf_in, float h,
+                                 float* p_prev, float* dq_prev, void* gf_out, void* workspace,
+                                 int64_t workspace_bytes, void* stream);
+/* p_prev = p - M(q), q_prev = q - A(p_prev); dq_prev = dq + J_M(q)^T round(dp),
+ * dp_prev = dp + J_A(p_prev)^T round(dq_prev) (dq may be NULL for zero).
+ * gm_in (may be NULL) is round(dp); gm_out (may be NULL) receives
+ * round(dp_prev) for the layer below. */
+RK_API int rk_layer_bwd_euler(const rk_layer_desc* desc, const rk_layer_grads* grads, const float* p, const float* q,
+                              const float* dp, const float* dq, const void* gm_in, float* p_prev, float* q_prev,
+                              float* dp_prev, float* dq_prev, void* gm_out, void* workspace, int64_t workspace_bytes,
+                              void* stream);
 
 #ifdef __cplusplus
 }

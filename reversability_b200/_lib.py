@@ -19,6 +19,7 @@ LIB_PATH = Path(__file__).resolve().parent / "librevk.so"
 HEADER = Path(__file__).resolve().parents[1] / "include" / "revk.h"
 
 F32, BF16, F16 = 0, 1, 2
+ERR_ALIGN = 2  # RK_ERR_ALIGN: a pointer or leading dimension breaks a vector/TMA alignment rule
 ERR_UNSUPPORTED = 5  # RK_ERR_UNSUPPORTED: the shape or layout is outside what a kernel implements
 DTYPE_CODE = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 
@@ -47,6 +48,8 @@ SIGNATURES: dict[str, tuple] = {
     "rk_gemm_fprop_swiglu": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p]),
     "rk_gemm_dgrad_swiglu": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p]),
     "rk_gemm_dgrad_dsum": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p, _i64, _p, _i64, _i64, _p]),
+    "rk_gemm_fprop_reconstruct": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _f, _p, _i64, _i64, _i64, _i64, _i,
+                                       _p]),
     "rk_gemm_wgrad": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p, _i64, _p]),
     "rk_attn_fwd": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p]),
     "rk_attn_bwd": (_i, [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _p]),
@@ -57,6 +60,11 @@ SIGNATURES: dict[str, tuple] = {
     "rk_embedding_fwd": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "rk_embedding_bwd_workspace": (_i64, [_i64, _i64]),
     "rk_embedding_bwd": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _p]),
+    "rk_layer_workspace": (_i64, [_p, _i, _i]),
+    "rk_layer_fwd_midpoint": (_i, [_p, _p, _p, _f, _p, _p, _i64, _p]),
+    "rk_layer_fwd_euler": (_i, [_p, _p, _p, _p, _p, _p, _i64, _p]),
+    "rk_layer_bwd_midpoint": (_i, [_p, _p, _p, _p, _p, _p, _p, _f, _p, _p, _p, _p, _i64, _p]),
+    "rk_layer_bwd_euler": (_i, [_p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _p, _i64, _p]),
     "rk_reconstruct_midpoint_sum": (_i, [_p, _p, _p, _i, _f, _p, _i64, _p]),
     "rk_cast_scale": (_i, [_p, _p, _i, _f, _i64, _p]),
     "rk_add_rmsnorm_fwd": (_i, [_p, _p, _i, _p, _p, _i, _p, _p, _i64, _i64, _f, _p]),
@@ -76,6 +84,21 @@ _lib = None
 
 class KernelLibraryMissing(RuntimeError):
     pass
+
+
+class LayerDesc(ctypes.Structure):
+    """rk_layer_desc of include/revk.h (pointers as integers)."""
+    _fields_ = [("batch", _i64), ("length", _i64), ("d_model", _i64), ("n_heads", _i64), ("d_ff", _i64),
+                ("mlp_tokens", _i64), ("dtype", _i), ("eps_attn", _f), ("eps_mlp", _f),
+                ("attn_norm", _p), ("qkv", _p), ("proj", _p), ("mlp_norm", _p), ("up", _p), ("down", _p)]
+
+
+class LayerGrads(ctypes.Structure):
+    """rk_layer_grads of include/revk.h."""
+    _fields_ = [("attn_norm", _p), ("qkv", _p), ("proj", _p), ("mlp_norm", _p), ("up", _p), ("down", _p)]
+
+
+METHOD_MIDPOINT, METHOD_EULER = 0, 1
 
 
 def header_symbols() -> list[str]:

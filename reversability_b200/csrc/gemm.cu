@@ -53,7 +53,7 @@ struct GemmArgs {
   unsigned int* status;
   // Softmax head (vocabulary logits; 128-column blocks b of a row):
   float2* stats;          // EPI_LSE writes, XF reads: per (row, b) (m_b, sum of exp(x - m_b)), m_b = block max
-  int stats_ld;           // float2 entries per row (2 * ceil(V / 256))
+  int stats_ld;           // float2 entries per row (4 * ceil(V / 256): 64-column blocks)
   const float4* rowc;     // XF: per token (-lse * log2(e), scale, label gradient, -); scale 0 = ignored row
   const float* fcoef;     // XF: per (block b, token) exp(m_b - lse) * scale, block-major (fcoef_ld per block)
   int64_t fcoef_ld;
@@ -67,6 +67,15 @@ struct GemmArgs {
   int64_t dsum_ldo;
   float* dsum;            // [B, H, T], M = B * T
   int dsum_T, dsum_H;
+  // EPI_RECON (sublayer output projection with the reversible state update):
+  // rc_out[r, c] = rc_state[r, c] - round(rc_coeff * round(round(acc) + rc_add[r, c]))
+  const float* rc_state;  // fp32 [M, N], row stride rc_lds
+  int64_t rc_lds;
+  const void* rc_add;     // 16-bit [M, N] addend (row stride rc_lda), or null (no addend)
+  int64_t rc_lda;
+  float* rc_out;          // fp32 [M, N], row stride rc_ldo (may be rc_state itself)
+  int64_t rc_ldo;
+  float rc_coeff;
 };
 
 // STORE: direct row stores; PARTIAL: fp32 split slices; ACCUM: fp32 out += acc;
@@ -82,13 +91,19 @@ struct GemmArgs {
 // epilogue: u's gate and value columns matching the tile are TMA-loaded into
 // the staging boxes, du = swiglu_bwd(u, round(acc)) is written over them and
 // TMA-stored (gate and value halves of du).
-// LSE (softmax head forward): per row and 128-column block b, the rounded
+// LSE (softmax head forward): per row and 64-column block b, the rounded
 // logits x give m_b = max x and e = exp(x - m_b); e is TMA-stored (16-bit)
 // instead of x, (m_b, sum e) goes to g.stats and the logit at the row's label
-// to g.xlabel. Columns at or past g.vocab do not count.
+// to g.xlabel. Columns at or past g.vocab do not count. Sixteen epilogue
+// warps, one per (TMEM lane quarter, 64-column block).
+// RECON: the reversible state update from the sublayer output in the
+// accumulator: out = state - round(coeff * round(round(acc) + add)) in fp32
+// (the rounding points of reconstruct_sum_kernel / reconstruct_kernel), each
+// thread reading and writing its own row chunks; the sublayer output itself
+// never reaches global memory.
 enum {
   EPI_STORE = 0, EPI_PARTIAL = 1, EPI_ACCUM = 2, EPI_TMA = 3, EPI_TMA_ADD = 4, EPI_SWIGLU = 5, EPI_SWIGLU_SAVE = 6,
-  EPI_LSE = 7, EPI_SWIGLU_BWD = 8, EPI_TMA_DSUM = 9
+  EPI_LSE = 7, EPI_SWIGLU_BWD = 8, EPI_TMA_DSUM = 9, EPI_RECON = 10
 };
 // A-operand transforms (XF): the A tile holds e = exp(x - m_b) from the LSE
 // epilogue and is turned, in shared memory before the MMA reads it, into the
@@ -105,16 +120,18 @@ __host__ __device__ constexpr bool epi_stages_out(int e) {
 }
 // Epilogue warps per CTA (a multiple of 4: one per TMEM lane quarter and
 // column group) and threads per CTA (producer warp, MMA warp, epilogue).
-__host__ __device__ constexpr int epi_warps(int e) { return e == EPI_SWIGLU_BWD ? 16 : 8; }
+__host__ __device__ constexpr int epi_warps(int e) { return (e == EPI_SWIGLU_BWD || e == EPI_LSE) ? 16 : 8; }
 __host__ __device__ constexpr int gemm_threads(int e) { return 64 + 32 * epi_warps(e); }
 constexpr int kMaxEpiWarps = 16;
 // Output staging per epilogue warp: one 4 KB box (32 rows x 128 bytes); two
 // for SWIGLU_SAVE (h and the gate half of u; the value half reuses the
 // first); for SWIGLU_BWD two chunk slots of (gate box, value box), 2 KB each:
-// u is loaded into them and du computed in place.
+// u is loaded into them and du computed in place; for LSE one 2 KB box
+// (32 rows x 64 bytes).
 __host__ __device__ constexpr uint32_t epi_out_bytes(int e) {
   return e == EPI_SWIGLU_BWD    ? epi_warps(e) * 2 * 4096
          : e == EPI_SWIGLU_SAVE ? epi_warps(e) * 2 * 4096
+         : e == EPI_LSE         ? epi_warps(e) * 2048
                                 : (epi_stages_out(e) ? epi_warps(e) * 4096 : 0);
 }
 
@@ -645,7 +662,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         auto fetch = [&](int kb) {
           Coef c;
           const int token = XF == XF_ROWS ? m0 + srow : kb * kBK + (srow & 63);
-          const int blk = XF == XF_ROWS ? (kb * kBK) >> 7 : m0 >> 7;
+          const int blk = XF == XF_ROWS ? (kb * kBK) >> 6 : (m0 >> 6) + (srow >> 6);
           if (kb < kb1 && token < g.tokens) {
             c.f = __ldg(g.fcoef + (int64_t)blk * g.fcoef_ld + token);
             if constexpr (XF == XF_ROWS) {
@@ -887,81 +904,82 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         continue;
       }
       if constexpr (EPI == EPI_LSE) {
-        // This warp's 128-column block of its 32 rows: two TMEM reads of 64
-        // columns, each rounded to the output type and packed in pairs (the
+        // This warp's 64-column block of its 32 rows: one TMEM read of 64
+        // columns, rounded to the output type and packed in pairs (the
         // accumulator is released right after); then the block max m_b (packed
-        // 16-bit max: the values are already rounded), the label's logit,
-        // e = exp(x - m_b) summed and re-packed, staged and TMA-stored.
-        static_assert(sizeof(TOut) == 2 && BN == 256, "16-bit output, 256-column tiles");
+        // 16-bit max: the values are already rounded), the label's logit, and
+        // e = exp(x - m_b) summed and re-packed. Each 32-column half is
+        // exponentiated, staged in the warp's 2 KB box (64-byte rows, 64-byte
+        // swizzle: 16-byte chunk j of row r at j ^ ((r / 2) % 4)) and TMA-stored
+        // before the next half, which runs while the store drains the box.
+        static_assert(sizeof(TOut) == 2 && BN == 256 && EW == 16, "16-bit output, 256-column tiles, 16 warps");
+        const int cg = ew >> 2;  // 64-column block of the tile
         const int row = m0 + quarter * 32 + lane;
         const int64_t lab = row < g.M ? g.labels[row] : -1;
-        const int c0 = n0 + half * 128;
-        const int nvalid = g.vocab - c0;  // columns of this block below vocab (may be <= 0 or >= 128)
-        const uint32_t t_blk = t_row + half * 128;
-        uint32_t xp[64];  // the block's 128 rounded logits, two per word
-#pragma unroll
-        for (int h2 = 0; h2 < 2; ++h2) {
+        const int c0 = n0 + cg * 64;
+        const int nvalid = g.vocab - c0;  // columns of this block below vocab (may be <= 0 or >= 64)
+        uint32_t xp[32];                  // the block's 64 rounded logits, two per word
+        {
           uint32_t r[64];
-          tmem_ld_32cols_nowait(t_blk + h2 * 64, r);
-          tmem_ld_32cols_nowait(t_blk + h2 * 64 + 32, r + 32);
+          tmem_ld_32cols_nowait(t_row + cg * 64, r);
+          tmem_ld_32cols_nowait(t_row + cg * 64 + 32, r + 32);
           tmem_ld_wait();
 #pragma unroll
-          for (int k = 0; k < 32; ++k)
-            xp[h2 * 32 + k] = pack2_rn<TOut>(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+          for (int k = 0; k < 32; ++k) xp[k] = pack2_rn<TOut>(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
         }
         tc_fence_before();
         mbar_arrive(tempty0 + 8 * acc);  // TMEM read: the MMA warp may reuse the accumulator
         // columns at or past vocab become -inf
-        if (nvalid < 128) {
+        if (nvalid < 64) {
           constexpr uint32_t kNegInf = std::is_same_v<TOut, __nv_bfloat16> ? 0xff80u : 0xfc00u;
 #pragma unroll
-          for (int k = 0; k < 64; ++k) {
+          for (int k = 0; k < 32; ++k) {
             if (2 * k >= nvalid) xp[k] = (xp[k] & 0xffff0000u) | kNegInf;
             if (2 * k + 1 >= nvalid) xp[k] = (xp[k] & 0x0000ffffu) | (kNegInf << 16);
           }
         }
         uint32_t m4[4] = {xp[0], xp[1], xp[2], xp[3]};
 #pragma unroll
-        for (int k = 4; k < 64; ++k) m4[k & 3] = max2_16<TOut>(m4[k & 3], xp[k]);
+        for (int k = 4; k < 32; ++k) m4[k & 3] = max2_16<TOut>(m4[k & 3], xp[k]);
         const uint32_t m2 = max2_16<TOut>(max2_16<TOut>(m4[0], m4[1]), max2_16<TOut>(m4[2], m4[3]));
         const float mx = fmaxf(unpack_half<TOut>(m2, 0), unpack_half<TOut>(m2, 1));
         const int64_t li = lab - c0;
-        if (li >= 0 && li < 128 && li < nvalid) {  // this block holds the row's label: keep its logit
+        if (li >= 0 && li < 64 && li < nvalid) {  // this block holds the row's label: keep its logit
           float xl = 0.f;
 #pragma unroll
-          for (int k = 0; k < 64; ++k)
+          for (int k = 0; k < 32; ++k)
             if ((int)(li >> 1) == k) xl = unpack_half<TOut>(xp[k], (int)(li & 1));
           g.xlabel[row] = xl;
         }
         const float nm = mx == -INFINITY ? 0.f : -mx * kLog2eF;
         float sm4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int k = 0; k < 64; ++k) {
-          const float e0 = ex2_fast(fmaf(unpack_half<TOut>(xp[k], 0), kLog2eF, nm));
-          const float e1 = ex2_fast(fmaf(unpack_half<TOut>(xp[k], 1), kLog2eF, nm));
-          sm4[k & 3] += e0 + e1;
-          xp[k] = pack_unit2<TOut>(e0, e1);
-        }
-        const float sm = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
-        if (row < g.M) g.stats[(int64_t)row * g.stats_ld + 2 * nt + half] = make_float2(mx, sm);
-        uint8_t* buf = sOut + ew * 4096;
+        uint8_t* buf = sOut + ew * 2048;
         const int y = m0 + quarter * 32;
 #pragma unroll
         for (int ch = 0; ch < 2; ++ch) {
+#pragma unroll
+          for (int k = ch * 16; k < ch * 16 + 16; ++k) {
+            const float e0 = ex2_fast(fmaf(unpack_half<TOut>(xp[k], 0), kLog2eF, nm));
+            const float e1 = ex2_fast(fmaf(unpack_half<TOut>(xp[k], 1), kLog2eF, nm));
+            sm4[k & 3] += e0 + e1;
+            xp[k] = pack_unit2<TOut>(e0, e1);
+          }
           if (lane == 0) bulk_wait_read<0>();
           __syncwarp();
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<uint4*>(buf + lane * 128 + ((j ^ (lane & 7)) * 16)) =
-                make_uint4(xp[ch * 32 + 4 * j], xp[ch * 32 + 4 * j + 1], xp[ch * 32 + 4 * j + 2],
-                           xp[ch * 32 + 4 * j + 3]);
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint4*>(buf + lane * 64 + ((j ^ ((lane >> 1) & 3)) * 16)) =
+                make_uint4(xp[ch * 16 + 4 * j], xp[ch * 16 + 4 * j + 1], xp[ch * 16 + 4 * j + 2],
+                           xp[ch * 16 + 4 * j + 3]);
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmC, smem_u32(buf), c0 + ch * 64, y);
+            tma_store_2d(&tmC, smem_u32(buf), c0 + ch * 32, y);
             bulk_commit();
           }
         }
+        const float sm = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
+        if (row < g.M) g.stats[(int64_t)row * g.stats_ld + 4 * nt + cg] = make_float2(mx, sm);
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
@@ -1039,6 +1057,54 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
             if constexpr (EPI == EPI_TMA_ADD) tma_reduce_add_2d(&tmC, smem_u32(buf), n0 + c, y);
             else tma_store_2d(&tmC, smem_u32(buf), n0 + c, y);
             bulk_commit();
+          }
+        }
+        if (++acc == 2) {
+          acc = 0;
+          acc_phase ^= 1;
+        }
+        continue;
+      }
+      if constexpr (EPI == EPI_RECON) {
+        const int row = m0 + quarter * 32 + lane;
+        const bool rv = row < g.M;
+        const float* xrow = g.rc_state + (int64_t)row * g.rc_lds;
+        const TOut* arow = g.rc_add ? static_cast<const TOut*>(g.rc_add) + (int64_t)row * g.rc_lda : nullptr;
+        float* orow = g.rc_out + (int64_t)row * g.rc_ldo;
+#pragma unroll 1
+        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+          uint32_t r[32];
+          tmem_ld_32cols_nowait(t_row + c, r);
+          const int col = n0 + c;
+          const bool cv = rv && col < g.N;  // N is a multiple of 32 (host check)
+          float4 xv[8];
+          uint4 av[4];
+          if (cv) {  // the state (and addend) chunk loads overlap the TMEM load
+#pragma unroll
+            for (int j = 0; j < 8; ++j) xv[j] = __ldg(reinterpret_cast<const float4*>(xrow + col) + j);
+            if (arow) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) av[j] = __ldg(reinterpret_cast<const uint4*>(arow + col) + j);
+            }
+          }
+          tmem_ld_wait();
+          if (c + 32 == (half + 1) * (BN / 2)) {  // last TMEM read of this tile by this warp
+            tc_fence_before();
+            mbar_arrive(tempty0 + 8 * acc);
+          }
+          if (cv) {
+            const float* xs = reinterpret_cast<const float*>(xv);
+            const uint32_t* aw = reinterpret_cast<const uint32_t*>(av);
+            float o[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const float mv = round_to<TOut>(__uint_as_float(r[e]));
+              const float f = arow ? round_to<TOut>(__fadd_rn(mv, unpack_half<TOut>(aw[e >> 1], e & 1))) : mv;
+              o[e] = __fsub_rn(xs[e], round_to<TOut>(__fmul_rn(g.rc_coeff, f)));
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              reinterpret_cast<float4*>(orow + col)[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
           }
         }
         if (++acc == 2) {
@@ -1592,6 +1658,52 @@ extern "C" int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_
   return rk_host::launch_status();
 }
 
+// ---------------------------------------------------------------- reversible state update
+// out = state - round(coeff * round(round(x W^T) + addend)): the sublayer
+// output projection (the MLP down projection, or the attention output
+// projection for the Euler recurrence) with the reconstruction / forward state
+// update of reversible.py:21-32 in its epilogue, so the sublayer output never
+// reaches HBM. Bitwise equal to rk_gemm_fprop followed by
+// rk_reconstruct_midpoint_sum (addend given) or rk_reconstruct_midpoint.
+extern "C" int rk_gemm_fprop_reconstruct(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* state,
+                                         int64_t lds, const void* addend, int64_t lda, float coeff, float* out,
+                                         int64_t ldo, int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
+  if (!x || !w || !state || !out || !dims_ok(M, N, K) || K == 0 || ldx < K || ldw < K || lds < N || ldo < N ||
+      (addend && lda < N))
+    return RK_ERR_ARG;
+  if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
+  if (N % 32) return RK_ERR_UNSUPPORTED;
+  if (M == 0) return RK_OK;
+  if (!rk_host::aligned(x, 16) || !rk_host::aligned(w, 16) || !rk_host::aligned(state, 16) ||
+      !rk_host::aligned(out, 16) || (addend && !rk_host::aligned(addend, 16)) || (ldx * 2) % 16 || (ldw * 2) % 16 ||
+      lds % 4 || ldo % 4 || (addend && lda % 8))
+    return RK_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  CUtensorMap ta, tb;
+  if (!make_map(&ta, x, (uint64_t)K, (uint64_t)M, (uint64_t)ldx, dtype, 64, kBM) ||
+      !make_map(&tb, w, (uint64_t)K, (uint64_t)N, (uint64_t)ldw, dtype, 64, 256))
+    return RK_ERR_LAUNCH;
+  GemmArgs g{};
+  g.M = (int)M;
+  g.N = (int)N;
+  g.K = (int)K;
+  g.tiles_m = (int)((M + kBM - 1) / kBM);
+  g.tiles_n = (int)((N + 255) / 256);
+  g.kb_total = (int)((K + kBK - 1) / kBK);
+  g.splits = 1;
+  g.kb_per_split = g.kb_total;
+  g.status = rk_host::device_status_ptr();
+  g.rc_state = state;
+  g.rc_lds = lds;
+  g.rc_add = addend;
+  g.rc_lda = lda;
+  g.rc_out = out;
+  g.rc_ldo = ldo;
+  g.rc_coeff = coeff;
+  if (dtype == RK_BF16) return launch_tc<256, 4, false, false, EPI_RECON, __nv_bfloat16>(ta, tb, ta, g, dtype, s);
+  return launch_tc<256, 4, false, false, EPI_RECON, __half>(ta, tb, ta, g, dtype, s);
+}
+
 // ---------------------------------------------------------------- fused SwiGLU up projection
 extern "C" int rk_gemm_fprop_swiglu(const void* x, int64_t ldx, const void* w_up, int64_t ldw, void* h, int64_t ldh,
                                     void* u, int64_t ldu, int64_t M, int64_t ff, int64_t K, int dtype, void* stream) {
@@ -1792,7 +1904,7 @@ __global__ void __launch_bounds__(256) head_loss_kernel(const float2* __restrict
 
 }  // namespace rk
 
-extern "C" int64_t rk_head_stats_width(int64_t vocab) { return vocab > 0 ? 2 * ((vocab + 255) / 256) : 0; }
+extern "C" int64_t rk_head_stats_width(int64_t vocab) { return vocab > 0 ? 4 * ((vocab + 255) / 256) : 0; }
 
 extern "C" int rk_head_fprop(const void* hidden, int64_t ldh, const void* w, int64_t ldw, const int64_t* labels,
                              void* expo, int64_t lde, float* stats, float* xlabel, int64_t M, int64_t V, int64_t K,
@@ -1808,7 +1920,7 @@ extern "C" int rk_head_fprop(const void* hidden, int64_t ldh, const void* w, int
   CUtensorMap ta, tb, tc;
   if (!make_map(&ta, hidden, (uint64_t)K, (uint64_t)M, (uint64_t)ldh, dtype, 64, kBM) ||
       !make_map(&tb, w, (uint64_t)K, (uint64_t)V, (uint64_t)ldw, dtype, 64, 256) ||
-      !make_out_map(&tc, expo, (uint64_t)V, (uint64_t)M, (uint64_t)lde, dtype))
+      !make_box32_map(&tc, expo, (uint64_t)V, (uint64_t)M, (uint64_t)lde, dtype))
     return RK_ERR_LAUNCH;
   GemmArgs g{};
   g.M = (int)M;
@@ -1824,7 +1936,7 @@ extern "C" int rk_head_fprop(const void* hidden, int64_t ldh, const void* w, int
   g.out_dtype = dtype;
   g.status = rk_host::device_status_ptr();
   g.stats = reinterpret_cast<float2*>(stats);
-  g.stats_ld = 2 * g.tiles_n;
+  g.stats_ld = 4 * g.tiles_n;
   g.labels = labels;
   g.xlabel = xlabel;
   g.vocab = (int)V;

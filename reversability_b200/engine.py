@@ -42,6 +42,7 @@ written to .grad here; callers decide where they go.
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 from types import SimpleNamespace
 
@@ -108,10 +109,15 @@ class LayerKernels:
     """Sublayer forward / VJP building blocks on [M, d] row-major activations."""
 
     def __init__(self, n_heads: int, batch: int, length: int, cd: torch.dtype, mlp_tokens: int = 0,
-                 wgrad_stream: "torch.cuda.Stream | None" = None):
+                 wgrad_stream: "torch.cuda.Stream | None" = None, layer_abi: bool = True):
         self.H, self.B, self.T = n_heads, batch, length
         self.cd = cd
         self.mlp_tokens = mlp_tokens
+        # One C call per layer step (rk_layer_*, the same kernel sequence as the
+        # single-stream Python path below) wherever its shape rules hold: the
+        # forward steps always, the backward steps when no side streams are
+        # used (the multi-stream sweep is issued from Python).
+        self.layer_abi = layer_abi
         # Weight gradients are off the reverse sweep's critical path: with a
         # side stream they run there, overlapping the dgrad / attention /
         # elementwise chain. A layer's wgrad operands stay referenced until the
@@ -253,14 +259,87 @@ class LayerKernels:
     def _eps(eps):
         return eps if eps is not None else torch.finfo(F32).eps
 
+    # ------------------------------------------------------- per-layer C calls
+    def _layer_desc(self, lw: LayerWeights, *states):
+        """rk_layer_desc of this layer, or None when the per-layer entry points
+        do not cover it (fp32 compute, head dims other than 32/64, widths the
+        fused epilogues do not take, non-contiguous operands)."""
+        if not self.layer_abi or self.cd not in (torch.bfloat16, torch.float16):
+            return None
+        d, ff = lw.qkv.shape[1], lw.down.shape[1]
+        if d % 32 or ff % 128 or d % self.H or (d // self.H) not in (32, 64):
+            return None
+        ws = (lw.attn_norm, lw.qkv_c, lw.proj_c, lw.mlp_norm, lw.up_c, lw.down_c)
+        if not all(t.is_cuda and t.is_contiguous() and t.data_ptr() % 16 == 0 for t in ws):
+            return None
+        if lw.attn_norm.dtype != F32 or lw.mlp_norm.dtype != F32 or any(t.dtype != self.cd for t in ws[1:3] + ws[4:]):
+            return None
+        if not all(t is None or (t.dtype == F32 and t.is_contiguous() and t.shape == (self.B * self.T, d))
+                   for t in states):
+            return None
+        return _lib.LayerDesc(batch=self.B, length=self.T, d_model=d, n_heads=self.H, d_ff=ff,
+                              mlp_tokens=max(int(self.mlp_tokens or 0), 0), dtype=_lib.code(self.cd),
+                              eps_attn=self._eps(lw.eps_attn), eps_mlp=self._eps(lw.eps_mlp),
+                              attn_norm=lw.attn_norm.data_ptr(), qkv=lw.qkv_c.data_ptr(), proj=lw.proj_c.data_ptr(),
+                              mlp_norm=lw.mlp_norm.data_ptr(), up=lw.up_c.data_ptr(), down=lw.down_c.data_ptr())
+
+    @staticmethod
+    def _layer_call(name: str, desc, method: int, backward: bool, *args):
+        """Runs one rk_layer_* entry point with a workspace from the caching
+        allocator (stream-ordered on the current stream)."""
+        lib = _lib.lib()
+        addr = ctypes.addressof(desc)
+        nbytes = lib.rk_layer_workspace(addr, method, int(backward))
+        ws = torch.empty(max(nbytes, 1), device=torch.device("cuda", torch.cuda.current_device()), dtype=torch.uint8)
+        _lib.call(name, addr, *args, ws.data_ptr(), nbytes, _lib.stream_ptr())
+
+    @staticmethod
+    def _grads_struct(g: "LayerGrads"):
+        return _lib.LayerGrads(*(t.data_ptr() for t in g.as_tuple()))
+
+    # ------------------------------------------------------- state updates
+    @staticmethod
+    def _project(hg, w, recon, rows=None, m=None, keep=None):
+        """A sublayer's output projection hg @ w^T for rows s:e: into m[s:e]
+        (recon None), or with recon = (state, addend, coeff, out) the
+        reversible state update out = state - round(coeff * round(round(hg w^T)
+        + addend)) formed in the GEMM epilogue, the sublayer output never
+        written (the two-step path when the fused epilogue does not apply,
+        e.g. fp32; its temporary goes to `keep` when the kernels run on another
+        stream than the allocating one, so it outlives them)."""
+        s, e = rows if rows is not None else (0, hg.shape[0])
+        if recon is None:
+            fn.linear_fwd(hg, w, out=m[s:e])
+            return
+        state, addend, coeff, out = recon
+        add = None if addend is None else addend[s:e]
+        if fn.linear_reconstruct(hg, w, state[s:e], coeff, addend=add, out=out[s:e]) is not None:
+            return
+        mt = fn.linear_fwd(hg, w)
+        if keep is not None:
+            keep.append(mt)
+        if add is None:
+            fn.reconstruct_midpoint(state[s:e], mt, coeff, out=out[s:e])
+        else:
+            fn.reconstruct_midpoint_sum(state[s:e], add, mt, coeff, out=out[s:e])
+
     # ---------------------------------------------------------- attention sublayer
-    def attn_forward(self, lw: LayerWeights, x: torch.Tensor, save: bool):
-        """A(x) = proj(attn(qkv(rmsnorm(x)))): returns (a [M, d] in cd, saved)."""
+    def attn_forward(self, lw: LayerWeights, x: torch.Tensor, save: bool, recon=None, keep=None):
+        """A(x) = proj(attn(qkv(rmsnorm(x)))): returns (a [M, d] in cd, saved).
+        With recon = (state, coeff) the first result is instead the state
+        update state - round(coeff * a) from the projection's epilogue (the
+        Euler recurrence), and a is not formed."""
         n1, rstd1 = fn.rmsnorm_fwd(x, lw.attn_norm, self._eps(lw.eps_attn), out_dtype=self.cd, want_rstd=save)
         qkv = fn.linear_fwd(n1, lw.qkv_c)
         o, lse = fn.attention_fwd(qkv.view(self.B, self.T, -1), self.H)
-        a = fn.linear_fwd(o.view(-1, o.shape[-1]), lw.proj_c)
-        return a, ((n1, rstd1, qkv, o, lse) if save else None)
+        saved = (n1, rstd1, qkv, o, lse) if save else None
+        o2 = o.view(-1, o.shape[-1])
+        if recon is not None:
+            state, coeff = recon
+            out = torch.empty_like(state)
+            self._project(o2, lw.proj_c, (state, None, coeff, out), keep=keep)
+            return out, saved
+        return fn.linear_fwd(o2, lw.proj_c), saved
 
     def attn_vjp(self, lw: LayerWeights, g: LayerGrads, x: torch.Tensor, saved, ga: torch.Tensor,
                  residual: torch.Tensor | None = None, lp_scale: float | None = None):
@@ -303,33 +382,49 @@ class LayerKernels:
         return n2, y, rstd2
 
     def mlp_forward(self, lw: LayerWeights, y: torch.Tensor | None = None, x: torch.Tensor | None = None,
-                    a: torch.Tensor | None = None) -> torch.Tensor:
-        """M(y) without saving (forward sweep); y = x + a when a is given."""
+                    a: torch.Tensor | None = None, recon=None) -> torch.Tensor:
+        """M(y) without saving (forward sweep); y = x + a when a is given. With
+        recon = (state, addend, coeff) returns the state update
+        state - round(coeff * round(M(y) + addend)) formed in the down
+        projection's epilogue instead (addend None: no addend)."""
         n2, _, _ = self._mlp_norm(lw, y, x, a, save=False)
         M = n2.shape[0]
-        m = torch.empty((M, lw.down.shape[0]), device=n2.device, dtype=self.cd)
+        if recon is None:
+            m = torch.empty((M, lw.down.shape[0]), device=n2.device, dtype=self.cd)
+            rc = None
+        else:
+            m = torch.empty_like(recon[0])
+            rc = (*recon, m)
         fused = fn.swiglu_fusable(n2, lw.up_c)
         for s, e in self._tiles(M):
             if fused:  # SwiGLU in the up-projection epilogue: u never reaches HBM
                 hg, _ = fn.linear_swiglu_fwd(n2[s:e], lw.up_c)
             else:
                 hg = fn.swiglu_fwd(fn.linear_fwd(n2[s:e], lw.up_c))
-            fn.linear_fwd(hg, lw.down_c, out=m[s:e])
+            self._project(hg, lw.down_c, rc, (s, e), m)
         return m
 
     def mlp_forward_vjp(self, lw: LayerWeights, g: LayerGrads, gm: torch.Tensor, y: torch.Tensor | None = None,
                         x: torch.Tensor | None = None, a: torch.Tensor | None = None,
                         residual: torch.Tensor | None = None, lp_add: torch.Tensor | None = None,
-                        want_lp: bool = False, m_on_aux: bool = False):
+                        want_lp: bool = False, m_on_aux: bool = False, recon=None):
         """M(y) and its VJP for cotangent gm, tile by tile (each tile's forward is
         followed at once by its VJP). Returns (m, dx_out, lp_out) where
         dx_out = M^T gm + residual and lp_out is the low-precision epilogue output
         of rk_rmsnorm_bwd_fused (round(lp_add + round(M^T gm)) or round(dx_out)).
         With m_on_aux (and an aux stream) m is computed on the aux stream: the
-        caller must consume it there or after layer_done()."""
+        caller must consume it there or after layer_done(). With recon =
+        (state, addend, coeff) the first result is the state update
+        state - round(coeff * round(M(y) + addend)) from the down projection's
+        epilogue instead of m."""
         n2, ysum, rstd2 = self._mlp_norm(lw, y, x, a, save=True)
         M, d = n2.shape
-        m = torch.empty((M, lw.down.shape[0]), device=n2.device, dtype=self.cd)
+        if recon is None:
+            m = torch.empty((M, lw.down.shape[0]), device=n2.device, dtype=self.cd)
+            rc = None
+        else:
+            m = torch.empty_like(recon[0])
+            rc = (*recon, m)
         dxo = torch.empty((M, d), device=n2.device, dtype=F32)
         lp = torch.empty((M, d), device=n2.device, dtype=self.cd) if want_lp else None
         fused = fn.swiglu_fusable(n2, lw.up_c)
@@ -340,10 +435,10 @@ class LayerKernels:
                 u = fn.linear_fwd(n2[s:e], lw.up_c)
                 hg = fn.swiglu_fwd(u)
             if m_on_aux and self.aux is not None:
-                with self._on_aux(hg, m):
-                    fn.linear_fwd(hg, lw.down_c, out=m[s:e])
+                with self._on_aux(hg, m, *(() if recon is None else [t for t in recon[:2] if t is not None])):
+                    self._project(hg, lw.down_c, rc, (s, e), m)
             else:
-                fn.linear_fwd(hg, lw.down_c, out=m[s:e])
+                self._project(hg, lw.down_c, rc, (s, e), m)
             gm_t = gm[s:e]
             if fn.dgrad_swiglu_fusable(gm_t, lw.down_c, u):  # SwiGLU backward in the dgrad epilogue
                 du = fn.linear_dgrad_swiglu(gm_t, lw.down_c, u)
@@ -370,39 +465,57 @@ class LayerKernels:
         return a + self.mlp_forward(lw, x=x, a=a)
 
     def forward_midpoint(self, lw, p, q, h):
-        """(p, q) -> (q, p + round(2h F(q))) (reversible.py:21-23)."""
+        """(p, q) -> (q, p + round(2h F(q))) (reversible.py:21-23); the update
+        is formed in the MLP down projection's epilogue."""
+        desc = self._layer_desc(lw, p, q)
+        if desc is not None:
+            q_next = torch.empty_like(q)
+            self._layer_call("rk_layer_fwd_midpoint", desc, _lib.METHOD_MIDPOINT, False, p.data_ptr(), q.data_ptr(),
+                             float(h), q_next.data_ptr())
+            return q, q_next
         a, _ = self.attn_forward(lw, q, save=False)
-        m = self.mlp_forward(lw, x=q, a=a)
-        return q, fn.reconstruct_midpoint_sum(p, a, m, -2.0 * h)
+        return q, self.mlp_forward(lw, x=q, a=a, recon=(p, a, -2.0 * h))
 
     def forward_euler(self, lw, p, q):
-        """q' = q + A(p); p' = p + M(q') (reversible.py:24-25)."""
-        a, _ = self.attn_forward(lw, p, save=False)
-        nq = fn.reconstruct_midpoint(q, a, -1.0)
-        m = self.mlp_forward(lw, y=nq)
-        return fn.reconstruct_midpoint(p, m, -1.0), nq
+        """q' = q + A(p); p' = p + M(q') (reversible.py:24-25); each update is
+        formed in its sublayer's output projection epilogue."""
+        desc = self._layer_desc(lw, p, q)
+        if desc is not None:
+            p_next, q_next = torch.empty_like(p), torch.empty_like(q)
+            self._layer_call("rk_layer_fwd_euler", desc, _lib.METHOD_EULER, False, p.data_ptr(), q.data_ptr(),
+                             p_next.data_ptr(), q_next.data_ptr())
+            return p_next, q_next
+        nq, _ = self.attn_forward(lw, p, save=False, recon=(q, -1.0))
+        return self.mlp_forward(lw, y=nq, recon=(p, None, -1.0)), nq
 
     def backward_midpoint(self, lw, g: LayerGrads, p, q, dp, dq, h, gF=None, carry=False):
         """Reconstructs (p_{n-1}, q_{n-1}) and returns them with their cotangents.
         dp may be None (a zero cotangent). gF = round(2h * round(dq)) when the
         previous layer's epilogue formed it; with carry the result gains the next
         layer's gF, formed in this layer's attention-norm epilogue."""
+        desc = self._layer_desc(lw, p, q, dp, dq) if self.side is None else None
+        if desc is not None:
+            prev_p, dq_new = torch.empty_like(q), torch.empty_like(q)
+            gF_next = torch.empty(q.shape, device=q.device, dtype=self.cd) if carry else None
+            gst = self._grads_struct(g)  # referenced until the call returns
+            self._layer_call("rk_layer_bwd_midpoint", desc, _lib.METHOD_MIDPOINT, True,
+                             ctypes.addressof(gst), p.data_ptr(), q.data_ptr(), _lib.ptr(dp),
+                             dq.data_ptr(), _lib.ptr(gF), float(h), prev_p.data_ptr(), dq_new.data_ptr(),
+                             _lib.ptr(gF_next))
+            return (prev_p, p, dq, dq_new, gF_next) if carry else (prev_p, p, dq, dq_new)
         x = p
         a, sa = self.attn_forward(lw, x, save=True)
         if gF is None:
             gF = fn.cast_scale(dq, self.cd, 2.0 * h)
-        # dxacc = M^T gF + dp ; da = round(gF + round(M^T gF)) for the attention VJP
-        m, dxacc, da = self.mlp_forward_vjp(lw, g, gF, x=x, a=a, residual=dp, lp_add=gF, want_lp=True,
-                                            m_on_aux=True)
-        if self.aux is not None:  # beside the attention VJP; joined in layer_done()
-            prev_p = torch.empty_like(q)
-            with self._on_aux(q, a, m, prev_p):
-                fn.reconstruct_midpoint_sum(q, a, m, 2.0 * h, out=prev_p)
-                self._aux_done = torch.cuda.Event()
-                self._aux_done.record(self.aux)
-        else:
-            prev_p = fn.reconstruct_midpoint_sum(q, a, m, 2.0 * h)
-        del m, gF
+        # dxacc = M^T gF + dp ; da = round(gF + round(M^T gF)) for the attention VJP;
+        # p_{n-1} = q - round(2h (a + m)) from the down projection's epilogue
+        # (on the aux stream beside the attention VJP; joined in layer_done())
+        prev_p, dxacc, da = self.mlp_forward_vjp(lw, g, gF, x=x, a=a, residual=dp, lp_add=gF, want_lp=True,
+                                                 m_on_aux=True, recon=(q, a, 2.0 * h))
+        if self.aux is not None and self._aux_used:
+            self._aux_done = torch.cuda.Event()
+            self._aux_done.record(self.aux)
+        del gF
         if not carry:
             return prev_p, x, dq, self.attn_vjp(lw, g, x, sa, da, residual=dxacc)
         dq_new, gF_next = self.attn_vjp(lw, g, x, sa, da, residual=dxacc, lp_scale=2.0 * h)
@@ -411,15 +524,23 @@ class LayerKernels:
     def backward_euler(self, lw, g: LayerGrads, p, q, dp, dq, gm=None, carry=False):
         """dq may be None (a zero cotangent). gm = round(dp) when the previous
         layer's epilogue formed it; with carry the result gains the next layer's gm."""
+        desc = self._layer_desc(lw, p, q, dp, dq) if self.side is None else None
+        if desc is not None:
+            prev_p, prev_q, dp_new, dq_eff = (torch.empty_like(p) for _ in range(4))
+            gm_next = torch.empty(p.shape, device=p.device, dtype=self.cd) if carry else None
+            gst = self._grads_struct(g)  # referenced until the call returns
+            self._layer_call("rk_layer_bwd_euler", desc, _lib.METHOD_EULER, True,
+                             ctypes.addressof(gst), p.data_ptr(), q.data_ptr(), dp.data_ptr(),
+                             _lib.ptr(dq), _lib.ptr(gm), prev_p.data_ptr(), prev_q.data_ptr(), dp_new.data_ptr(),
+                             dq_eff.data_ptr(), _lib.ptr(gm_next))
+            return (prev_p, prev_q, dp_new, dq_eff, gm_next) if carry else (prev_p, prev_q, dp_new, dq_eff)
         if gm is None:
             gm = fn.cast_scale(dp, self.cd, 1.0)
-        # dq_eff = dq' + M^T round(dp'); ga = round(dq_eff)
-        m, dq_eff, ga = self.mlp_forward_vjp(lw, g, gm, y=q, residual=dq, want_lp=True)
-        prev_p = fn.reconstruct_euler(p, m)
-        del m, gm
-        a, sa = self.attn_forward(lw, prev_p, save=True)
-        prev_q = fn.reconstruct_euler(q, a)
-        del a
+        # dq_eff = dq' + M^T round(dp'); ga = round(dq_eff); p = p' - m and
+        # q = q' - a from the output projections' epilogues
+        prev_p, dq_eff, ga = self.mlp_forward_vjp(lw, g, gm, y=q, residual=dq, want_lp=True, recon=(p, None, 1.0))
+        del gm
+        prev_q, sa = self.attn_forward(lw, prev_p, save=True, recon=(q, 1.0))
         if not carry:
             return prev_p, prev_q, self.attn_vjp(lw, g, prev_p, sa, ga, residual=dp), dq_eff
         dp_new, gm_next = self.attn_vjp(lw, g, prev_p, sa, ga, residual=dp, lp_scale=1.0)
@@ -433,15 +554,21 @@ class LayerKernels:
         to bound its intermediate, which the split would not)."""
         return self.rec is not None and (not self.mlp_tokens or self.mlp_tokens <= 0 or self.mlp_tokens >= M)
 
-    def _mlp_forward_saved(self, lw, y=None, x=None, a=None):
-        """M's forward with what its VJP needs: (m, n2, ysum, rstd2, hg, u)."""
+    def _mlp_forward_saved(self, lw, y=None, x=None, a=None, recon=None, keep=None):
+        """M's forward with what its VJP needs: (m, n2, ysum, rstd2, hg, u);
+        with recon = (state, addend, coeff) the first result is the state
+        update from the down projection's epilogue instead of m."""
         n2, ysum, rstd2 = self._mlp_norm(lw, y, x, a, save=True)
         if fn.swiglu_fusable(n2, lw.up_c):
             hg, u = fn.linear_swiglu_fwd(n2, lw.up_c, save_u=True)
         else:
             u = fn.linear_fwd(n2, lw.up_c)
             hg = fn.swiglu_fwd(u)
-        return fn.linear_fwd(hg, lw.down_c), n2, ysum, rstd2, hg, u
+        if recon is None:
+            return fn.linear_fwd(hg, lw.down_c), n2, ysum, rstd2, hg, u
+        out = torch.empty_like(recon[0])
+        self._project(hg, lw.down_c, (*recon, out), keep=keep)
+        return out, n2, ysum, rstd2, hg, u
 
     def recompute(self, lw, p, q, method: str, h: float):
         """Issues a layer's forward recompute at states (p, q): for midpoint
@@ -458,21 +585,21 @@ class LayerKernels:
             ctx = _lib.launch_on(self.rec)
         else:
             ctx = _nullcontext()
-        r = SimpleNamespace(method=method, p=p, q=q)
+        r = SimpleNamespace(method=method, p=p, q=q, keep=[])
         with ctx:
             if method == "midpoint":
                 x = p
                 a, sa = self.attn_forward(lw, x, save=True)
-                m, n2, ysum, rstd2, hg, u = self._mlp_forward_saved(lw, x=x, a=a)
-                r.prev_p = fn.reconstruct_midpoint_sum(q, a, m, 2.0 * h)
+                r.prev_p, n2, ysum, rstd2, hg, u = self._mlp_forward_saved(lw, x=x, a=a, recon=(q, a, 2.0 * h),
+                                                                           keep=r.keep)
                 r.prev_q = x
             else:
-                m, n2, ysum, rstd2, hg, u = self._mlp_forward_saved(lw, y=q)
-                r.prev_p = fn.reconstruct_euler(p, m)
+                r.prev_p, n2, ysum, rstd2, hg, u = self._mlp_forward_saved(lw, y=q, recon=(p, None, 1.0),
+                                                                           keep=r.keep)
                 x = r.prev_p
-                a, sa = self.attn_forward(lw, x, save=True)
-                r.prev_q = fn.reconstruct_euler(q, a)
-        r.x, r.sa, r.n2, r.ysum, r.rstd2, r.hg, r.u, r.a, r.m = x, sa, n2, ysum, rstd2, hg, u, a, m
+                r.prev_q, sa = self.attn_forward(lw, x, save=True, recon=(q, 1.0), keep=r.keep)
+                a = None
+        r.x, r.sa, r.n2, r.ysum, r.rstd2, r.hg, r.u, r.a = x, sa, n2, ysum, rstd2, hg, u, a
         if self.rec is not None:
             r.done = torch.cuda.Event()
             r.done.record(self.rec)

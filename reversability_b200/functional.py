@@ -237,7 +237,7 @@ def head_logits_buffer(rows: int, vocab: int, device, dtype) -> torch.Tensor:
 
 class HeadState:
     """What the softmax-head backward needs from the forward: expo [M, V]
-    (exp(x - m_b), 16-bit), stats [M, width, 2] ((m_b, sum exp) per 128-column
+    (exp(x - m_b), 16-bit), stats [M, width, 2] ((m_b, sum exp) per 64-column
     block), labels [M], and after head_loss rowc [M, 4] and the per-block
     factors fcoef [width, M]."""
 
@@ -461,6 +461,31 @@ def reconstruct_midpoint_sum(x_next: torch.Tensor, a: torch.Tensor, m: torch.Ten
     out = out if out is not None else torch.empty_like(x_next)
     _lib.call("rk_reconstruct_midpoint_sum", x_next.data_ptr(), a.data_ptr(), m.data_ptr(), _lib.code(a.dtype),
               float(coeff), out.data_ptr(), x_next.numel(), _lib.stream_ptr())
+    return out
+
+
+def linear_reconstruct(x: torch.Tensor, w: torch.Tensor, state: torch.Tensor, coeff: float,
+                       addend: torch.Tensor | None = None, out: torch.Tensor | None = None):
+    """out = state - round(coeff * round(round(x @ w^T) + addend)) with the
+    sublayer output x @ w^T only in the GEMM epilogue (rk_gemm_fprop_reconstruct);
+    bitwise equal to linear_fwd followed by reconstruct_midpoint_sum (addend) or
+    reconstruct_midpoint. None when the shapes or dtypes do not fit the fused
+    epilogue (the caller runs the two steps)."""
+    require_cuda(x, w, state)
+    M, K = x.shape
+    N = w.shape[0]
+    if x.dtype not in _TC_DTYPES or w.dtype != x.dtype or state.dtype != torch.float32 or \
+            tuple(state.shape) != (M, N) or (addend is not None and addend.dtype != x.dtype) or N % 32 or \
+            not (x.is_contiguous() and w.is_contiguous() and state.is_contiguous()) or \
+            (addend is not None and not addend.is_contiguous()):
+        return None
+    out = out if out is not None else torch.empty_like(state)
+    st = _lib.lib().rk_gemm_fprop_reconstruct(x.data_ptr(), K, w.data_ptr(), K, state.data_ptr(), N,
+                                              _lib.ptr(addend), N, float(coeff), out.data_ptr(), N, M, N, K,
+                                              _lib.code(x.dtype), _lib.stream_ptr())
+    if st in (_lib.ERR_UNSUPPORTED, _lib.ERR_ALIGN):
+        return None
+    _lib.check(st, "rk_gemm_fprop_reconstruct")
     return out
 
 

@@ -14,10 +14,10 @@ a CUDA graph and replayed):
   - `gflat`  fp32 [P]   gradients; layer i's six gradients are contiguous, so
                          each layer is one data-parallel all-reduce bucket
   - logits   bf16 [B*T, Vpad]  the microstep's vocabulary logits (bf16 runs:
-                         exp(logit - max of its 128-column block)); Vpad = V
+                         exp(logit - max of its 64-column block)); Vpad = V
                          rounded up to 64 so every row starts 16-byte aligned
                          for TMA
-  - head_stats fp32 [B*T, 2*ceil(V/256), 2]  per-row partial (max, sum exp)
+  - head_stats fp32 [B*T, 4*ceil(V/256), 2]  per-row partial (max, sum exp)
                          pairs written by the head GEMM's epilogue
 Per microstep: embedding gather, the fused stack forward, final norm, head GEMM
 with the log-sum-exp partials in its epilogue, per-row loss, head dgrad/wgrad

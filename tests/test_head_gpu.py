@@ -55,12 +55,13 @@ def test_softmax_head_against_fp64_and_separate_path(dtype, mvk):
     # forward outputs against the plain GEMM's logits x (bit-identical accumulation)
     x = fn.head_logits_buffer(M, V, DEV, dtype)
     fn.linear_fwd(hidden, w, out=x)
-    nb = (V + 127) // 128
-    xp = torch.full((M, nb * 128), float("-inf"), device=DEV)
+    BW = 64  # columns per log-sum-exp block
+    nb = (V + BW - 1) // BW
+    xp = torch.full((M, nb * BW), float("-inf"), device=DEV)
     xp[:, :V] = x.float()
-    mb = xp.view(M, nb, 128).amax(dim=2)
+    mb = xp.view(M, nb, BW).amax(dim=2)
     assert torch.equal(st.stats[:, :nb, 0], mb)
-    e_ref = torch.exp(xp.view(M, nb, 128) - mb[:, :, None]).view(M, -1)[:, :V]
+    e_ref = torch.exp(xp.view(M, nb, BW) - mb[:, :, None]).view(M, -1)[:, :V]
     ulp = 2.0 ** -8 if dtype == torch.bfloat16 else 2.0 ** -11
     assert ((st.expo.float() - e_ref).abs() <= 2 * ulp * e_ref + 1e-30).all()
     valid = labels != -100

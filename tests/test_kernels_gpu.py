@@ -249,7 +249,7 @@ def _sdpa_ref(qkv, H):
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
 @pytest.mark.parametrize("bthd", [(2, 512, 8, 32), (3, 17, 2, 32), (1, 130, 4, 64), (29, 512, 8, 32),
-                                  (1, 2048, 2, 64)])
+                                  (1, 2048, 2, 64), (2, 2048, 16, 64), (2, 300, 3, 64)])
 def test_attention_fwd_bwd(dtype, bthd):
     from reversability_b200 import functional as fn
     B, T, H, HD = bthd
@@ -381,6 +381,37 @@ def test_rmsnorm_bwd_fused_epilogues(mode):
         assert torch.equal(lp, lpa + dx_ref.bfloat16())
     elif want_lp:  # rk_cast_scale of the total, formed in the same epilogue
         assert torch.equal(lp, fn.cast_scale(total, torch.bfloat16, scale))
+
+
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,N,K", [(14848, 256, 1024), (1000, 256, 1024), (333, 64, 96), (2048, 1024, 4096),
+                                   (14848, 256, 256)])
+@pytest.mark.parametrize("coeff,with_addend", [(1.0, True), (-1.0, True), (0.5, True), (1.0, False), (-1.0, False)])
+def test_gemm_fprop_reconstruct_bitwise(dt, M, N, K, coeff, with_addend):
+    """The output projection with the reversible state update in its epilogue
+    equals the projection followed by the separate reconstruct kernel, bit for
+    bit (midpoint: addend = attention output; Euler: no addend), in place too."""
+    from reversability_b200 import functional as fn
+    g = torch.Generator(device="cpu").manual_seed(M + N + K)
+    x = torch.randn(M, K, generator=g).to(DEV, dt)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(DEV, dt)
+    state = torch.randn(M, N, generator=g).to(DEV)
+    add = torch.randn(M, N, generator=g).to(DEV, dt) if with_addend else None
+    fused = fn.linear_reconstruct(x, w, state, coeff, addend=add)
+    assert fused is not None
+    m = fn.linear_fwd(x, w)
+    ref = fn.reconstruct_midpoint_sum(state, add, m, coeff) if with_addend else fn.reconstruct_midpoint(state, m, coeff)
+    assert torch.equal(fused, ref)
+    inplace = state.clone()
+    assert fn.linear_reconstruct(x, w, inplace, coeff, addend=add, out=inplace) is not None
+    assert torch.equal(inplace, ref)
+    assert _lib_status() == 0
+
+
+def _lib_status():
+    from reversability_b200 import _lib
+    torch.cuda.synchronize()
+    return _lib.device_status()
 
 
 @pytest.mark.parametrize("dt", [torch.bfloat16, torch.float32])

@@ -290,6 +290,40 @@ def test_pipelined_sweep_equals_sequential(method, amp):
             assert torch.equal(ta, tb)
 
 
+@pytest.mark.parametrize("method", ["midpoint", "euler"])
+@pytest.mark.parametrize("mlp_tokens", [0, 70])
+def test_layer_abi_equals_python_sequence(method, mlp_tokens):
+    """The per-layer C entry points (rk_layer_fwd_* / rk_layer_bwd_*, one call
+    per layer step) issue the same kernels as the single-stream Python
+    sequence: forward states, reconstructed states, cotangents and every
+    weight gradient are bitwise equal."""
+    from reversability_b200 import engine
+    model = product_model(WIDE, method, 0.5, 1e-6)
+    ids, _, _ = batch(WIDE, 3, 7)
+    cd = torch.bfloat16
+    x = model.embed(ids.to(DEV)).detach().reshape(-1, 256)
+    T = WIDE["max_sequence_length"]
+    layers = [engine.LayerWeights.from_block(b, cd) for b in model.blocks]
+    g = torch.Generator(device="cpu").manual_seed(4)
+    results = []
+    for abi in (True, False):
+        kern = engine.LayerKernels(8, 3, T, cd, mlp_tokens, layer_abi=abi)
+        assert (kern._layer_desc(layers[0], x) is not None) == abi
+        p, q = engine.stack_forward(kern, layers, x, x, method, 0.5)
+        dout = torch.randn(p.shape, generator=g.manual_seed(4)).to(DEV)
+        dp, dq = (None, dout) if method == "midpoint" else (dout, None)
+        grads = [engine.LayerGrads.zeros_like(lw) for lw in layers]
+        out = engine.stack_backward(kern, layers, grads, p, q, dp, dq, method, 0.5)
+        torch.cuda.synchronize()
+        results.append(((p, q), out, grads))
+    (f0, o0, g0), (f1, o1, g1) = results
+    for a, b in zip(f0 + tuple(o0), f1 + tuple(o1)):
+        assert torch.equal(a, b)
+    for ga, gb in zip(g0, g1):
+        for ta, tb in zip(ga.as_tuple(), gb.as_tuple()):
+            assert torch.equal(ta, tb)
+
+
 SCALED = dict(vocab_size=101, max_sequence_length=2048, n_layers=2, n_heads=16, d_model=1024, d_ff=4096)
 
 

@@ -71,6 +71,8 @@ def parse():
     ap.add_argument("--accumulation", type=int, default=None)
     ap.add_argument("--no-graph", action="store_true", help="run updates eagerly instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--forward-overlap", choices=["head", "after_head"], default="head",
+                    help="start microstep m+1's forward sweep beside microstep m's head GEMM or after it")
     ap.add_argument("--no-tied-split", action="store_true",
                     help="data parallel: reduce the tied embedding gradient as one bucket after the sweep")
     ap.add_argument("--reference-memory", action="store_true",
@@ -389,7 +391,7 @@ def main():
     from reversability_b200.train import ReversibleTrainer, TrainSettings, learning_rate
 
     s = TrainSettings(batch_size=args.batch, sequence_length=args.seq, accumulation=args.accumulation,
-                      tied_split=not args.no_tied_split)
+                      tied_split=not args.no_tied_split, forward_overlap=args.forward_overlap)
     torch.manual_seed(1337)
     spec = MODELS[args.model]
     model = rb.ReversibleLM(rb.ModelConfig(**spec["config"]), args.method).to(dev)

@@ -267,7 +267,7 @@ RK_API int rk_cross_entropy_fwd_bwd(const void* logits, int64_t ld, int64_t voca
  * The vocabulary head and its cross-entropy with no pass of their own over the
  * logits; together they replace the head Linear, F.cross_entropy(...,
  * reduction="sum") and their backward (model.py:104, train_baseline.py:262,
- * optimized_v3.py cached_head_backward). Blocks b are 64 columns wide.
+ * optimized_v3.py cached_head_backward). Blocks b are 128 columns wide.
  *   rk_head_fprop : expo[M, V] = exp(x - m_b) (bf16/f16) where x = hidden . W^T
  *                   rounded to the compute type and m_b the max of x over the
  *                   row's block b; stats[M][width] float2 = (m_b, sum of exp)

@@ -53,7 +53,7 @@ struct GemmArgs {
   unsigned int* status;
   // Softmax head (vocabulary logits; 128-column blocks b of a row):
   float2* stats;          // EPI_LSE writes, XF reads: per (row, b) (m_b, sum of exp(x - m_b)), m_b = block max
-  int stats_ld;           // float2 entries per row (4 * ceil(V / 256): 64-column blocks)
+  int stats_ld;           // float2 entries per row (2 * ceil(V / 256): 128-column blocks)
   const float4* rowc;     // XF: per token (-lse * log2(e), scale, label gradient, -); scale 0 = ignored row
   const float* fcoef;     // XF: per (block b, token) exp(m_b - lse) * scale, block-major (fcoef_ld per block)
   int64_t fcoef_ld;
@@ -91,11 +91,12 @@ struct GemmArgs {
 // epilogue: u's gate and value columns matching the tile are TMA-loaded into
 // the staging boxes, du = swiglu_bwd(u, round(acc)) is written over them and
 // TMA-stored (gate and value halves of du).
-// LSE (softmax head forward): per row and 64-column block b, the rounded
+// LSE (softmax head forward): per row and 128-column block b, the rounded
 // logits x give m_b = max x and e = exp(x - m_b); e is TMA-stored (16-bit)
 // instead of x, (m_b, sum e) goes to g.stats and the logit at the row's label
 // to g.xlabel. Columns at or past g.vocab do not count. Sixteen epilogue
-// warps, one per (TMEM lane quarter, 64-column block).
+// warps, one per (TMEM lane quarter, 64-column half of a block); the two
+// warps of a block exchange maxima and partial sums in shared memory.
 // RECON: the reversible state update from the sublayer output in the
 // accumulator: out = state - round(coeff * round(round(acc) + add)) in fp32
 // (the rounding points of reconstruct_sum_kernel / reconstruct_kernel), each
@@ -127,11 +128,12 @@ constexpr int kMaxEpiWarps = 16;
 // for SWIGLU_SAVE (h and the gate half of u; the value half reuses the
 // first); for SWIGLU_BWD two chunk slots of (gate box, value box), 2 KB each:
 // u is loaded into them and du computed in place; for LSE one 2 KB box
-// (32 rows x 64 bytes).
+// (32 rows x 64 bytes) per warp, then 1 KB where the two warps of a 128-column
+// block exchange their row maxima and partial sums.
 __host__ __device__ constexpr uint32_t epi_out_bytes(int e) {
   return e == EPI_SWIGLU_BWD    ? epi_warps(e) * 2 * 4096
          : e == EPI_SWIGLU_SAVE ? epi_warps(e) * 2 * 4096
-         : e == EPI_LSE         ? epi_warps(e) * 2048
+         : e == EPI_LSE         ? epi_warps(e) * 2048 + 1024
                                 : (epi_stages_out(e) ? epi_warps(e) * 4096 : 0);
 }
 
@@ -439,7 +441,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     mbar_init(drain, 1);
     mbar_init(bfull, 1);
     mbar_init(bempty, 1);
-    for (int i = 0; i < 2 * kMaxEpiWarps; ++i) mbar_init(ubar0 + 8 * i, 1);
+    for (int i = 0; i < 2 * kMaxEpiWarps; ++i) mbar_init(ubar0 + 8 * i, (EPI == EPI_LSE && i % 4 == 0) ? 2 : 1);
     fence_mbar_init();
     *s_abort = 0;
     *s_consumed = 0;
@@ -628,6 +630,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     uint32_t uphase = 0;               // SWIGLU_BWD: parity of each chunk's u barrier (bit ch)
     uint32_t upend = 0;                // SWIGLU_BWD: u loads issued and not yet waited on (bit ch)
     bool uwarm = false;                // SWIGLU_BWD: the first tile's u has been requested
+    int xtiles = 0;                    // LSE: tiles this warp finished (phase of its block pair's barriers)
     for (TileWalk<RES> w(total); w.more(); w.next()) {
       int split, m0, nt;
       w.coords(g, w.t, split, m0, nt);
@@ -662,7 +665,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         auto fetch = [&](int kb) {
           Coef c;
           const int token = XF == XF_ROWS ? m0 + srow : kb * kBK + (srow & 63);
-          const int blk = XF == XF_ROWS ? (kb * kBK) >> 6 : (m0 >> 6) + (srow >> 6);
+          const int blk = XF == XF_ROWS ? (kb * kBK) >> 7 : m0 >> 7;
           if (kb < kb1 && token < g.tokens) {
             c.f = __ldg(g.fcoef + (int64_t)blk * g.fcoef_ld + token);
             if constexpr (XF == XF_ROWS) {
@@ -904,21 +907,30 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         continue;
       }
       if constexpr (EPI == EPI_LSE) {
-        // This warp's 64-column block of its 32 rows: one TMEM read of 64
-        // columns, rounded to the output type and packed in pairs (the
-        // accumulator is released right after); then the block max m_b (packed
-        // 16-bit max: the values are already rounded), the label's logit, and
-        // e = exp(x - m_b) summed and re-packed. Each 32-column half is
-        // exponentiated, staged in the warp's 2 KB box (64-byte rows, 64-byte
-        // swizzle: 16-byte chunk j of row r at j ^ ((r / 2) % 4)) and TMA-stored
-        // before the next half, which runs while the store drains the box.
+        // This warp's 64-column half h of 128-column block blk, for its 32 rows:
+        // one TMEM read of 64 columns, rounded to the output type and packed in
+        // pairs (the accumulator is released right after); the half's max
+        // (packed 16-bit max: the values are already rounded) is exchanged with
+        // the block's other warp through shared memory, e = exp(x - m_b) is
+        // formed against the block max, each 32-column quarter staged in the
+        // warp's 2 KB box (64-byte rows, 64-byte swizzle: 16-byte chunk j of
+        // row r at j ^ ((r / 2) % 4)) and TMA-stored while the next one is
+        // exponentiated, and the half-1 warp hands its partial sum to the
+        // half-0 warp, which writes (m_b, s0 + s1). Per block pair and tile:
+        // barrier A (both maxima written, two arrivals), B (half 0 has read
+        // the max of half 1), C (the sum of half 1 written), D (half 0 has
+        // read it); every wait bounded.
         static_assert(sizeof(TOut) == 2 && BN == 256 && EW == 16, "16-bit output, 256-column tiles, 16 warps");
-        const int cg = ew >> 2;  // 64-column block of the tile
+        const int cg = ew >> 2;  // 64-column group of the tile: block cg / 2, half cg % 2
+        const int blk = cg >> 1, hf = cg & 1;
+        const int pr = quarter * 2 + blk;  // the block pair's slot
+        const uint32_t barA = ubar0 + 8 * (4 * pr), barB = barA + 8, barC = barA + 16, barD = barA + 24;
+        uint8_t* xch = sOut + EW * 2048 + pr * 128 + lane * 4;  // [pair][lane]: two 16-bit maxima or one fp32 sum
         const int row = m0 + quarter * 32 + lane;
         const int64_t lab = row < g.M ? g.labels[row] : -1;
         const int c0 = n0 + cg * 64;
-        const int nvalid = g.vocab - c0;  // columns of this block below vocab (may be <= 0 or >= 64)
-        uint32_t xp[32];                  // the block's 64 rounded logits, two per word
+        const int nvalid = g.vocab - c0;  // columns of this half below vocab (may be <= 0 or >= 64)
+        uint32_t xp[32];                  // the half's 64 rounded logits, two per word
         {
           uint32_t r[64];
           tmem_ld_32cols_nowait(t_row + cg * 64, r);
@@ -930,8 +942,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         tc_fence_before();
         mbar_arrive(tempty0 + 8 * acc);  // TMEM read: the MMA warp may reuse the accumulator
         // columns at or past vocab become -inf
+        constexpr uint32_t kNegInf = std::is_same_v<TOut, __nv_bfloat16> ? 0xff80u : 0xfc00u;
         if (nvalid < 64) {
-          constexpr uint32_t kNegInf = std::is_same_v<TOut, __nv_bfloat16> ? 0xff80u : 0xfc00u;
 #pragma unroll
           for (int k = 0; k < 32; ++k) {
             if (2 * k >= nvalid) xp[k] = (xp[k] & 0xffff0000u) | kNegInf;
@@ -941,10 +953,27 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         uint32_t m4[4] = {xp[0], xp[1], xp[2], xp[3]};
 #pragma unroll
         for (int k = 4; k < 32; ++k) m4[k & 3] = max2_16<TOut>(m4[k & 3], xp[k]);
-        const uint32_t m2 = max2_16<TOut>(max2_16<TOut>(m4[0], m4[1]), max2_16<TOut>(m4[2], m4[3]));
-        const float mx = fmaxf(unpack_half<TOut>(m2, 0), unpack_half<TOut>(m2, 1));
+        uint32_t m2 = max2_16<TOut>(max2_16<TOut>(m4[0], m4[1]), max2_16<TOut>(m4[2], m4[3]));
+        m2 = max2_16<TOut>(m2, __byte_perm(m2, 0, 0x1032));  // both halves: this half's max
+        bool xok = true;
+        // the half-1 warp reuses the slot (its sum overlapped both maxima) only
+        // once half 0 has read the previous tile's sum
+        if (hf == 1 && xtiles > 0) xok = mbar_wait(barD, (xtiles - 1) & 1, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
+        xok = __all_sync(0xffffffffu, xok);
+        if (!xok) break;
+        *reinterpret_cast<uint16_t*>(xch + 2 * hf) = (uint16_t)(m2 & 0xffffu);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(barA);
+        xok = mbar_wait(barA, xtiles & 1, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
+        xok = __all_sync(0xffffffffu, xok);
+        if (!xok) break;
+        const uint32_t other = *reinterpret_cast<const uint16_t*>(xch + 2 * (hf ^ 1));
+        __syncwarp();
+        if (hf == 0 && lane == 0) mbar_arrive(barB);  // half 1's max is read
+        const uint32_t mb2 = max2_16<TOut>(m2, other | (other << 16));
+        const float mx = unpack_half<TOut>(mb2, 0);  // the block max (-inf when no column is valid)
         const int64_t li = lab - c0;
-        if (li >= 0 && li < 64 && li < nvalid) {  // this block holds the row's label: keep its logit
+        if (li >= 0 && li < 64 && li < nvalid) {  // this half holds the row's label: keep its logit
           float xl = 0.f;
 #pragma unroll
           for (int k = 0; k < 32; ++k)
@@ -979,7 +1008,23 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           }
         }
         const float sm = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
-        if (row < g.M) g.stats[(int64_t)row * g.stats_ld + 4 * nt + cg] = make_float2(mx, sm);
+        if (hf == 1) {
+          xok = mbar_wait(barB, xtiles & 1, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
+          xok = __all_sync(0xffffffffu, xok);
+          if (!xok) break;
+          *reinterpret_cast<float*>(xch) = sm;
+          __syncwarp();
+          if (lane == 0) mbar_arrive(barC);
+        } else {
+          xok = mbar_wait(barC, xtiles & 1, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
+          xok = __all_sync(0xffffffffu, xok);
+          if (!xok) break;
+          const float s1 = *reinterpret_cast<const float*>(xch);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(barD);  // the slot may be reused
+          if (row < g.M) g.stats[(int64_t)row * g.stats_ld + 2 * nt + blk] = make_float2(mx, sm + s1);
+        }
+        ++xtiles;
         if (++acc == 2) {
           acc = 0;
           acc_phase ^= 1;
@@ -1904,7 +1949,7 @@ __global__ void __launch_bounds__(256) head_loss_kernel(const float2* __restrict
 
 }  // namespace rk
 
-extern "C" int64_t rk_head_stats_width(int64_t vocab) { return vocab > 0 ? 4 * ((vocab + 255) / 256) : 0; }
+extern "C" int64_t rk_head_stats_width(int64_t vocab) { return vocab > 0 ? 2 * ((vocab + 255) / 256) : 0; }
 
 extern "C" int rk_head_fprop(const void* hidden, int64_t ldh, const void* w, int64_t ldw, const int64_t* labels,
                              void* expo, int64_t lde, float* stats, float* xlabel, int64_t M, int64_t V, int64_t K,
@@ -1936,7 +1981,7 @@ extern "C" int rk_head_fprop(const void* hidden, int64_t ldh, const void* w, int
   g.out_dtype = dtype;
   g.status = rk_host::device_status_ptr();
   g.stats = reinterpret_cast<float2*>(stats);
-  g.stats_ld = 4 * g.tiles_n;
+  g.stats_ld = 2 * g.tiles_n;
   g.labels = labels;
   g.xlabel = xlabel;
   g.vocab = (int)V;

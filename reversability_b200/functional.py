@@ -237,7 +237,7 @@ def head_logits_buffer(rows: int, vocab: int, device, dtype) -> torch.Tensor:
 
 class HeadState:
     """What the softmax-head backward needs from the forward: expo [M, V]
-    (exp(x - m_b), 16-bit), stats [M, width, 2] ((m_b, sum exp) per 64-column
+    (exp(x - m_b), 16-bit), stats [M, width, 2] ((m_b, sum exp) per 128-column
     block), labels [M], and after head_loss rowc [M, 4] and the per-block
     factors fcoef [width, M]."""
 

@@ -2,7 +2,7 @@
 
     python -m reversability_b200.microbench [--only NAME[,NAME...]] [--iters N]
     python -m reversability_b200.microbench --only versus      (cuBLAS / torch SDPA arms beside librevk)
-    python -m reversability_b200.microbench --only head|attention|swiglu|membound --profile   (ncu launch sequence)
+    python -m reversability_b200.microbench --only head|attention|swiglu|membound|gemms --profile   (ncu launch sequence)
 
 Workload: 16,896 tokens x width 256 in bf16 (activations N(0,1), weights
 N(0,0.02)); RMSNorm fwd+bwd, SwiGLU fwd+bwd (gate/up 256->1024, i.e. u is
@@ -410,8 +410,39 @@ def profile_membound():
     torch.cuda.synchronize()
 
 
+def profile_gemms():
+    """Eager launches for an ncu capture of one layer's body GEMMs at cfg2
+    (29 x 512 = 14,848 tokens, d 256, ff 1024, bf16), twice, in this order:
+    qkv fprop, proj fprop, up fprop with the SwiGLU epilogue (u kept), down
+    fprop with the state update epilogue, down dgrad with the SwiGLU backward,
+    up dgrad, proj dgrad with D = rowsum(dO*O), qkv dgrad, and the split
+    weight-gradient GEMMs of up and qkv (each its GEMM + fixed-order slice
+    reduction). 11 GEMM launches (+ 2 reductions) per round."""
+    M, H = 29 * 512, 8
+    g = torch.Generator(device="cpu").manual_seed(0)
+    rnd = lambda *s: torch.randn(*s, generator=g).cuda()  # noqa: E731
+    x, o = rnd(M, D).bfloat16(), rnd(M, D).bfloat16()
+    wqkv, wproj = (rnd(3 * D, D) * 0.02).bfloat16(), (rnd(D, D) * 0.02).bfloat16()
+    wup, wdown = (rnd(2 * FF, D) * 0.02).bfloat16(), (rnd(D, FF) * 0.02).bfloat16()
+    state, a = rnd(M, D), rnd(M, D).bfloat16()
+    gy, gqkv, gu = rnd(M, D).bfloat16(), rnd(M, 3 * D).bfloat16(), rnd(M, 2 * FF).bfloat16()
+    dw_up, dw_qkv = torch.zeros(2 * FF, D, device="cuda"), torch.zeros(3 * D, D, device="cuda")
+    for _ in range(2):
+        fn.linear_fwd(x, wqkv)
+        fn.linear_fwd(o, wproj)
+        hg, u = fn.linear_swiglu_fwd(x, wup, save_u=True)
+        fn.linear_reconstruct(hg, wdown, state, 1.0, addend=a)
+        fn.linear_dgrad_swiglu(gy, wdown, u)
+        fn.linear_dgrad(gu, wup)
+        fn.linear_dgrad_dsum(gy, wproj, o, H, 512)
+        fn.linear_dgrad(gqkv, wqkv)
+        fn.linear_wgrad(gu, x, dw=dw_up, accumulate=True)
+        fn.linear_wgrad(gqkv, x, dw=dw_qkv, accumulate=True)
+    torch.cuda.synchronize()
+
+
 PROFILES = {"head": profile_head, "attention": profile_attention, "swiglu": profile_swiglu,
-            "membound": profile_membound}
+            "membound": profile_membound, "gemms": profile_gemms}
 
 
 def main():

@@ -14,10 +14,10 @@ a CUDA graph and replayed):
   - `gflat`  fp32 [P]   gradients; layer i's six gradients are contiguous, so
                          each layer is one data-parallel all-reduce bucket
   - logits   bf16 [B*T, Vpad]  the microstep's vocabulary logits (bf16 runs:
-                         exp(logit - max of its 64-column block)); Vpad = V
+                         exp(logit - max of its 128-column block)); Vpad = V
                          rounded up to 64 so every row starts 16-byte aligned
                          for TMA
-  - head_stats fp32 [B*T, 4*ceil(V/256), 2]  per-row partial (max, sum exp)
+  - head_stats fp32 [B*T, 2*ceil(V/256), 2]  per-row partial (max, sum exp)
                          pairs written by the head GEMM's epilogue
 Per microstep: embedding gather, the fused stack forward, final norm, head GEMM
 with the log-sum-exp partials in its epilogue, per-row loss, head dgrad/wgrad
@@ -63,6 +63,10 @@ class TrainSettings:
     overlap_wgrad: bool = True  # layer weight gradients on a side stream during the reverse sweep
     overlap_forward: bool = True  # microstep m+1's forward sweep beside microstep m's backward
     tied_split: bool = True  # data parallel: the head's share of the tied gradient reduced beside the sweep
+    # where microstep m+1's forward sweep starts: beside microstep m's head GEMM
+    # ("head") or once that GEMM is issued, beside the rest of the head and the
+    # reverse sweep ("after_head")
+    forward_overlap: str = "head"
 
 
 def learning_rate(s: TrainSettings, committed: int, update_targets: int) -> float:
@@ -293,7 +297,9 @@ class ReversibleTrainer:
         x = fn.embedding_fwd(self.ids[m], self.tok, self.pos)
         return engine.stack_forward(self.kern, self.layers, x, x, self.model.method, self.model.step_size)
 
-    def _microstep(self, m: int, last: bool, states=None):
+    def _microstep(self, m: int, last: bool, states=None, after_head=None):
+        """after_head(), if given, is called once the head GEMM is issued (the
+        caller issues the next microstep's forward sweep there)."""
         cfg, s, kern = self.cfg, self.s, self.kern
         B, T, d = s.batch_size, s.sequence_length, cfg.d_model
         ids = self.ids[m]
@@ -321,6 +327,8 @@ class ReversibleTrainer:
                                xlabel=self.head_xlabel)
             if ev is not None:
                 ev[1].record()
+            if after_head is not None:
+                after_head()
             fn.head_loss(st, 1.0, self.inv_denominator, loss_rows=loss_rows, rowc=self.head_rowc,
                          fcoef=self.head_fcoef)
             self.loss_sum += loss_rows.sum()
@@ -343,6 +351,8 @@ class ReversibleTrainer:
                     self.buckets.launch(self._head_bucket)
         else:
             fn.linear_fwd(hidden, self.tok_c, out=logits)
+            if after_head is not None:
+                after_head()
             # dlogits = (softmax - onehot) / update_targets, in place over the logits
             _lib.call("rk_cross_entropy_fwd_bwd", logits.data_ptr(), self.vpad, V, labels.data_ptr(), self.M, 1.0,
                       self.inv_denominator.data_ptr(), loss_rows.data_ptr(), logits.data_ptr(), self.vpad,
@@ -401,19 +411,24 @@ class ReversibleTrainer:
             main = torch.cuda.current_stream()
             states = self._forward_states(0)
             for m in range(acc):
-                nxt = None
-                if m + 1 < acc:
+                box = {}
+
+                def issue_next(m=m, box=box):
                     ready = torch.cuda.Event()
                     ready.record(main)
                     self.fwd_stream.wait_event(ready)
                     with torch.cuda.stream(self.fwd_stream):
-                        nxt = self._forward_states(m + 1)
-                    done = torch.cuda.Event()
-                    done.record(self.fwd_stream)
-                self._microstep(m, last=(m == acc - 1), states=states)
-                if nxt is not None:
-                    main.wait_event(done)
-                states = nxt
+                        box["states"] = self._forward_states(m + 1)
+                    box["done"] = torch.cuda.Event()
+                    box["done"].record(self.fwd_stream)
+                later = self.s.forward_overlap == "after_head"
+                if m + 1 < acc and not later:
+                    issue_next()
+                self._microstep(m, last=(m == acc - 1), states=states,
+                                after_head=issue_next if (m + 1 < acc and later) else None)
+                if "done" in box:
+                    main.wait_event(box["done"])
+                states = box.get("states")
         if self.world > 1:
             n = len(self.layers)
             for i in range(n, n + 3):

@@ -55,7 +55,7 @@ def test_softmax_head_against_fp64_and_separate_path(dtype, mvk):
     # forward outputs against the plain GEMM's logits x (bit-identical accumulation)
     x = fn.head_logits_buffer(M, V, DEV, dtype)
     fn.linear_fwd(hidden, w, out=x)
-    BW = 64  # columns per log-sum-exp block
+    BW = 128  # columns per log-sum-exp block
     nb = (V + BW - 1) // BW
     xp = torch.full((M, nb * BW), float("-inf"), device=DEV)
     xp[:, :V] = x.float()

@@ -204,6 +204,20 @@ RK_API int rk_gemm_dgrad(const void* dy, int64_t lddy, const void* w, int64_t ld
 RK_API int rk_gemm_fprop_reconstruct(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* state,
                               int64_t lds, const void* addend, int64_t lda, float coeff, float* out, int64_t ldo,
                               int64_t M, int64_t N, int64_t K, int dtype, void* stream);
+/* rk_gemm_fprop_reconstruct followed, in the same pass, by the RMSNorm forward
+ * of the updated state (the next sublayer's input norm, model.py:62-64;
+ * replaces rk_rmsnorm_fwd on an fp32 state, or rk_add_rmsnorm_fwd when the
+ * state update is the residual add x + a: coeff = -1, no addend):
+ *   y[M,N] = round((out * rstd) * norm_w), rstd[M] = rsqrt(mean(out^2) + eps)
+ * bit-identical to the standalone norm on `out`. rstd may be NULL. If low is
+ * not NULL it also receives round(x . W^T) (what rk_gemm_fprop stores; the
+ * residual branch's a). N must be 256 (RK_ERR_UNSUPPORTED otherwise); y, low
+ * and norm_w 16-byte aligned, ldy and ldl multiples of 8. */
+RK_API int rk_gemm_fprop_reconstruct_norm(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* state,
+                                          int64_t lds, const void* addend, int64_t lda, float coeff, float* out,
+                                          int64_t ldo, void* low, int64_t ldl, const float* norm_w, float eps, void* y,
+                                          int64_t ldy, float* rstd, int64_t M, int64_t N, int64_t K, int dtype,
+                                          void* stream);
 RK_API int rk_gemm_dgrad_dsum(const void* dy, int64_t lddy, const void* w, int64_t ldw, void* dx, int64_t lddx,
                               int64_t M, int64_t N, int64_t K, int dtype, const void* o, int64_t ldo, float* dsum,
                               int64_t T, int64_t H, void* stream);

@@ -50,6 +50,8 @@ SIGNATURES: dict[str, tuple] = {
     "rk_gemm_dgrad_dsum": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p, _i64, _p, _i64, _i64, _p]),
     "rk_gemm_fprop_reconstruct": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _f, _p, _i64, _i64, _i64, _i64, _i,
                                        _p]),
+    "rk_gemm_fprop_reconstruct_norm": (_i, [_p, _i64, _p, _i64, _p, _i64, _p, _i64, _f, _p, _i64, _p, _i64, _p, _f,
+                                            _p, _i64, _p, _i64, _i64, _i64, _i, _p]),
     "rk_gemm_wgrad": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p, _i64, _p]),
     "rk_attn_fwd": (_i, [_p, _i64, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _p]),
     "rk_attn_bwd": (_i, [_p, _i64, _p, _p, _i64, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i, _p]),

@@ -227,6 +227,25 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 
 __device__ __forceinline__ int elect_lane0() { return (threadIdx.x & 31) == 0; }
 
+// RMSNorm row statistics in one fixed order, shared by the standalone norm
+// kernels and the norm fused into the GEMM epilogue so that both give the same
+// bits: a lane's V consecutive squares are chained in column order, the 32
+// lanes of a 32V-column group are added in xor-butterfly order, and the group
+// totals are added in column order; rstd = rsqrt(sum / width + eps).
+template <int V>
+__device__ __forceinline__ float sumsq_chain(const float (&v)[V]) {
+  float t = __fmul_rn(v[0], v[0]);
+#pragma unroll
+  for (int e = 1; e < V; ++e) t = __fmaf_rn(v[e], v[e], t);
+  return t;
+}
+__device__ __forceinline__ float sumsq4(float a, float b, float c, float d) {
+  return __fmaf_rn(d, d, __fmaf_rn(c, c, __fmaf_rn(b, b, __fmul_rn(a, a))));
+}
+__device__ __forceinline__ float rms_rstd(float ss, int width, float eps) {
+  return rsqrtf(__fadd_rn(__fdiv_rn(ss, (float)width), eps));
+}
+
 // Programmatic dependent launch: every librevk kernel is launched with
 // programmatic stream serialization, so it may become resident while the
 // previous kernel on the stream drains. pdl_wait() blocks until that kernel

@@ -76,6 +76,15 @@ struct GemmArgs {
   float* rc_out;          // fp32 [M, N], row stride rc_ldo (may be rc_state itself)
   int64_t rc_ldo;
   float rc_coeff;
+  void* rc_low;           // 16-bit [M, N] round(acc) (row stride rc_ldl), or null
+  int64_t rc_ldl;
+  // EPI_RECON_NORM: the following RMSNorm forward fused (N == BN):
+  // rn_y = round((rc_out * rstd) * rn_w), rstd = rsqrt(mean(rc_out^2) + eps)
+  const float* rn_w;      // fp32 [N] norm weight
+  void* rn_y;             // 16-bit [M, N], row stride rn_ldy
+  int64_t rn_ldy;
+  float* rn_rstd;         // fp32 [M], or null
+  float rn_eps;
 };
 
 // STORE: direct row stores; PARTIAL: fp32 split slices; ACCUM: fp32 out += acc;
@@ -101,10 +110,13 @@ struct GemmArgs {
 // accumulator: out = state - round(coeff * round(round(acc) + add)) in fp32
 // (the rounding points of reconstruct_sum_kernel / reconstruct_kernel), each
 // thread reading and writing its own row chunks; the sublayer output itself
-// never reaches global memory.
+// never reaches global memory. RECON_NORM: the same, then the following
+// RMSNorm forward of the updated state in the same pass (bitwise equal to
+// rmsnorm_fwd_kernel / add_rmsnorm_fwd_kernel on it), and optionally the
+// rounded sublayer output itself (rc_low).
 enum {
   EPI_STORE = 0, EPI_PARTIAL = 1, EPI_ACCUM = 2, EPI_TMA = 3, EPI_TMA_ADD = 4, EPI_SWIGLU = 5, EPI_SWIGLU_SAVE = 6,
-  EPI_LSE = 7, EPI_SWIGLU_BWD = 8, EPI_TMA_DSUM = 9, EPI_RECON = 10
+  EPI_LSE = 7, EPI_SWIGLU_BWD = 8, EPI_TMA_DSUM = 9, EPI_RECON = 10, EPI_RECON_NORM = 11
 };
 // A-operand transforms (XF): the A tile holds e = exp(x - m_b) from the LSE
 // epilogue and is turned, in shared memory before the MMA reads it, into the
@@ -129,11 +141,13 @@ constexpr int kMaxEpiWarps = 16;
 // first); for SWIGLU_BWD two chunk slots of (gate box, value box), 2 KB each:
 // u is loaded into them and du computed in place; for LSE one 2 KB box
 // (32 rows x 64 bytes) per warp, then 1 KB where the two warps of a 128-column
-// block exchange their row maxima and partial sums.
+// block exchange their row maxima and partial sums; for RECON 1 KB where the
+// two warps of the same rows exchange the fused norm's half sums and rstd.
 __host__ __device__ constexpr uint32_t epi_out_bytes(int e) {
   return e == EPI_SWIGLU_BWD    ? epi_warps(e) * 2 * 4096
          : e == EPI_SWIGLU_SAVE ? epi_warps(e) * 2 * 4096
          : e == EPI_LSE         ? epi_warps(e) * 2048 + 1024
+         : e == EPI_RECON_NORM  ? 1024
                                 : (epi_stages_out(e) ? epi_warps(e) * 4096 : 0);
 }
 
@@ -630,7 +644,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
     uint32_t uphase = 0;               // SWIGLU_BWD: parity of each chunk's u barrier (bit ch)
     uint32_t upend = 0;                // SWIGLU_BWD: u loads issued and not yet waited on (bit ch)
     bool uwarm = false;                // SWIGLU_BWD: the first tile's u has been requested
-    int xtiles = 0;                    // LSE: tiles this warp finished (phase of its block pair's barriers)
+    int xtiles = 0;                    // LSE, RECON + norm: tiles this warp finished (phase of its pair's barriers)
     for (TileWalk<RES> w(total); w.more(); w.next()) {
       int split, m0, nt;
       w.coords(g, w.t, split, m0, nt);
@@ -1110,14 +1124,23 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         }
         continue;
       }
-      if constexpr (EPI == EPI_RECON) {
+      if constexpr (EPI == EPI_RECON || EPI == EPI_RECON_NORM) {
+        // Pass 1: the state update of this warp's 32 rows x BN/2 columns, four
+        // 32-column chunks; with the fused RMSNorm (RECON_NORM: the tile spans
+        // the whole row) each thread also forms, per 4-column group of its
+        // half, the sum of squares chained in column order.
+        constexpr bool norm = EPI == EPI_RECON_NORM;
         const int row = m0 + quarter * 32 + lane;
         const bool rv = row < g.M;
         const float* xrow = g.rc_state + (int64_t)row * g.rc_lds;
         const TOut* arow = g.rc_add ? static_cast<const TOut*>(g.rc_add) + (int64_t)row * g.rc_lda : nullptr;
+        TOut* lrow = norm && g.rc_low ? static_cast<TOut*>(g.rc_low) + (int64_t)row * g.rc_ldl : nullptr;
         float* orow = g.rc_out + (int64_t)row * g.rc_ldo;
-#pragma unroll 1
-        for (int c = half * (BN / 2); c < (half + 1) * (BN / 2); c += 32) {
+        float t[norm ? 16 : 1];  // fused norm: this half's 4-column-group sums of squares, first butterfly level applied
+        static_assert(BN == 256, "four 32-column chunks per half");
+#pragma unroll(norm ? 4 : 1)
+        for (int cc = 0; cc < 4; ++cc) {
+          const int c = half * (BN / 2) + cc * 32;
           uint32_t r[32];
           tmem_ld_32cols_nowait(t_row + c, r);
           const int col = n0 + c;
@@ -1133,7 +1156,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
             }
           }
           tmem_ld_wait();
-          if (c + 32 == (half + 1) * (BN / 2)) {  // last TMEM read of this tile by this warp
+          if (cc == 3) {  // last TMEM read of this tile by this warp
             tc_fence_before();
             mbar_arrive(tempty0 + 8 * acc);
           }
@@ -1150,6 +1173,81 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
 #pragma unroll
             for (int j = 0; j < 8; ++j)
               reinterpret_cast<float4*>(orow + col)[j] = make_float4(o[4 * j], o[4 * j + 1], o[4 * j + 2], o[4 * j + 3]);
+            if (norm && lrow) {  // the rounded sublayer output itself (what rk_gemm_fprop stores)
+              uint32_t lo[16];
+#pragma unroll
+              for (int k = 0; k < 16; ++k) lo[k] = pack2_rn<TOut>(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1]));
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<uint4*>(lrow + col)[j] = make_uint4(lo[4 * j], lo[4 * j + 1], lo[4 * j + 2], lo[4 * j + 3]);
+            }
+            if constexpr (norm) {  // group l = 8 cc + k; groups 16..31 are added onto l - 16 (the butterfly's first level)
+#pragma unroll
+              for (int k = 0; k < 8; ++k) {
+                const float q = sumsq4(o[4 * k], o[4 * k + 1], o[4 * k + 2], o[4 * k + 3]);
+                if (cc < 2) t[cc * 8 + k] = q;
+                else t[(cc - 2) * 8 + k] = __fadd_rn(t[(cc - 2) * 8 + k], q);
+              }
+            }
+          }
+        }
+        if constexpr (norm) {
+          // Row total in the standalone RMSNorm's order: the 32 group sums of
+          // each half in xor-butterfly order, then half 0 + half 1. Half 0
+          // hands its total to the half-1 warp of the same rows (barrier A),
+          // which forms rstd and hands it back (barrier B); every wait bounded.
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) {
+#pragma unroll
+            for (int l = 0; l < o; ++l) t[l] = __fadd_rn(t[l], t[l + o]);
+          }
+          const uint32_t barA = ubar0 + 8 * (2 * quarter), barB = barA + 8;
+          float* slot = reinterpret_cast<float*>(sOut) + quarter * 64 + lane;  // [rows][half-0 total | rstd]
+          bool xok = true;
+          float rs;
+          if (half == 0) {
+            slot[0] = t[0];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(barA);
+            xok = mbar_wait(barB, xtiles & 1, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
+            xok = __all_sync(0xffffffffu, xok);
+            if (!xok) break;
+            rs = slot[32];
+          } else {
+            xok = mbar_wait(barA, xtiles & 1, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
+            xok = __all_sync(0xffffffffu, xok);
+            if (!xok) break;
+            rs = rms_rstd(__fadd_rn(slot[0], t[0]), g.N, g.rn_eps);
+            slot[32] = rs;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(barB);
+            if (rv && g.rn_rstd) g.rn_rstd[row] = rs;
+          }
+          ++xtiles;
+          // Pass 2: y = round((state' * rstd) * w) from this thread's own
+          // stores of pass 1 (plain loads: written in this kernel).
+          if (rv) {
+            TOut* yrow = static_cast<TOut*>(g.rn_y) + (int64_t)row * g.rn_ldy;
+#pragma unroll
+            for (int cc = 0; cc < 4; ++cc) {
+              const int col = n0 + half * (BN / 2) + cc * 32;
+              float4 pv[8], wv[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                pv[j] = reinterpret_cast<const float4*>(orow + col)[j];
+                wv[j] = __ldg(reinterpret_cast<const float4*>(g.rn_w + col) + j);
+              }
+              const float* ps = reinterpret_cast<const float*>(pv);
+              const float* ws = reinterpret_cast<const float*>(wv);
+              uint32_t yw[16];
+#pragma unroll
+              for (int k = 0; k < 16; ++k)
+                yw[k] = pack2_rn<TOut>(__fmul_rn(__fmul_rn(ps[2 * k], rs), ws[2 * k]),
+                                       __fmul_rn(__fmul_rn(ps[2 * k + 1], rs), ws[2 * k + 1]));
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                reinterpret_cast<uint4*>(yrow + col)[j] = make_uint4(yw[4 * j], yw[4 * j + 1], yw[4 * j + 2], yw[4 * j + 3]);
+            }
           }
         }
         if (++acc == 2) {
@@ -1704,24 +1802,20 @@ extern "C" int rk_gemm_wgrad(const void* dy, int64_t lddy, const void* x, int64_
 }
 
 // ---------------------------------------------------------------- reversible state update
-// out = state - round(coeff * round(round(x W^T) + addend)): the sublayer
-// output projection (the MLP down projection, or the attention output
-// projection for the Euler recurrence) with the reconstruction / forward state
-// update of reversible.py:21-32 in its epilogue, so the sublayer output never
-// reaches HBM. Bitwise equal to rk_gemm_fprop followed by
-// rk_reconstruct_midpoint_sum (addend given) or rk_reconstruct_midpoint.
-extern "C" int rk_gemm_fprop_reconstruct(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* state,
-                                         int64_t lds, const void* addend, int64_t lda, float coeff, float* out,
-                                         int64_t ldo, int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
+static int fprop_reconstruct(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* state, int64_t lds,
+                             const void* addend, int64_t lda, float coeff, float* out, int64_t ldo, void* low,
+                             int64_t ldl, const float* norm_w, float eps, void* y, int64_t ldy, float* rstd, int64_t M,
+                             int64_t N, int64_t K, int dtype, void* stream) {
   if (!x || !w || !state || !out || !dims_ok(M, N, K) || K == 0 || ldx < K || ldw < K || lds < N || ldo < N ||
-      (addend && lda < N))
+      (addend && lda < N) || (low && ldl < N) || (norm_w && (!y || ldy < N)))
     return RK_ERR_ARG;
   if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
-  if (N % 32) return RK_ERR_UNSUPPORTED;
+  if (N % 32 || (norm_w && N != 256)) return RK_ERR_UNSUPPORTED;
   if (M == 0) return RK_OK;
   if (!rk_host::aligned(x, 16) || !rk_host::aligned(w, 16) || !rk_host::aligned(state, 16) ||
       !rk_host::aligned(out, 16) || (addend && !rk_host::aligned(addend, 16)) || (ldx * 2) % 16 || (ldw * 2) % 16 ||
-      lds % 4 || ldo % 4 || (addend && lda % 8))
+      lds % 4 || ldo % 4 || (addend && lda % 8) || (low && (!rk_host::aligned(low, 16) || ldl % 8)) ||
+      (norm_w && (!rk_host::aligned(norm_w, 16) || !rk_host::aligned(y, 16) || ldy % 8)))
     return RK_ERR_ALIGN;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   CUtensorMap ta, tb;
@@ -1745,8 +1839,49 @@ extern "C" int rk_gemm_fprop_reconstruct(const void* x, int64_t ldx, const void*
   g.rc_out = out;
   g.rc_ldo = ldo;
   g.rc_coeff = coeff;
+  g.rc_low = low;
+  g.rc_ldl = ldl;
+  g.rn_w = norm_w;
+  g.rn_y = y;
+  g.rn_ldy = ldy;
+  g.rn_rstd = rstd;
+  g.rn_eps = eps;
+  if (norm_w) {
+    if (dtype == RK_BF16)
+      return launch_tc<256, 4, false, false, EPI_RECON_NORM, __nv_bfloat16>(ta, tb, ta, g, dtype, s);
+    return launch_tc<256, 4, false, false, EPI_RECON_NORM, __half>(ta, tb, ta, g, dtype, s);
+  }
   if (dtype == RK_BF16) return launch_tc<256, 4, false, false, EPI_RECON, __nv_bfloat16>(ta, tb, ta, g, dtype, s);
   return launch_tc<256, 4, false, false, EPI_RECON, __half>(ta, tb, ta, g, dtype, s);
+}
+
+// out = state - round(coeff * round(round(x W^T) + addend)): the sublayer
+// output projection (the MLP down projection, or the attention output
+// projection for the Euler recurrence) with the reconstruction / forward state
+// update of reversible.py:21-32 in its epilogue, so the sublayer output never
+// reaches HBM. Bitwise equal to rk_gemm_fprop followed by
+// rk_reconstruct_midpoint_sum (addend given) or rk_reconstruct_midpoint.
+extern "C" int rk_gemm_fprop_reconstruct(const void* x, int64_t ldx, const void* w, int64_t ldw, const float* state,
+                                         int64_t lds, const void* addend, int64_t lda, float coeff, float* out,
+                                         int64_t ldo, int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
+  return fprop_reconstruct(x, ldx, w, ldw, state, lds, addend, lda, coeff, out, ldo, nullptr, 0, nullptr, 0.f, nullptr,
+                           0, nullptr, M, N, K, dtype, stream);
+}
+
+// The same state update followed, in the same pass, by the RMSNorm forward of
+// the updated state (the next sublayer's input norm, model.py:62-64):
+// y = round((out * rstd) * norm_w), rstd = rsqrt(mean(out^2) + eps), bitwise
+// equal to rk_rmsnorm_fwd (fp32 x) or rk_add_rmsnorm_fwd on `out`. Optionally
+// (low != NULL) also stores round(x W^T) itself, as rk_gemm_fprop would.
+// N must be 256 (one output tile spans the row).
+extern "C" int rk_gemm_fprop_reconstruct_norm(const void* x, int64_t ldx, const void* w, int64_t ldw,
+                                              const float* state, int64_t lds, const void* addend, int64_t lda,
+                                              float coeff, float* out, int64_t ldo, void* low, int64_t ldl,
+                                              const float* norm_w, float eps, void* y, int64_t ldy, float* rstd,
+                                              int64_t M, int64_t N, int64_t K, int dtype, void* stream) {
+  if (!norm_w) return RK_ERR_ARG;
+  return fprop_reconstruct(x, ldx, w, ldw, state, lds, addend, lda, coeff, out, ldo, low, ldl, norm_w, eps, y, ldy,
+                           rstd, M, N, K, dtype, stream);
 }
 
 // ---------------------------------------------------------------- fused SwiGLU up projection

@@ -46,15 +46,12 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const Tx* __restrict__
     if (row >= rows) break;
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < NV; ++j) {
+    for (int j = 0; j < NV; ++j) {  // group j: lane sums in butterfly order, groups in column order
       const int c = (j * 32 + lane) * V;
-      if (c < width) {
-#pragma unroll
-        for (int e = 0; e < V; ++e) ss += v[r][j][e] * v[r][j][e];
-      }
+      const float sj = warp_sum(c < width ? sumsq_chain<V>(v[r][j]) : 0.f);
+      ss = j == 0 ? sj : __fadd_rn(ss, sj);
     }
-    ss = warp_sum(ss);
-    const float rs = rsqrtf(ss / (float)width + eps);
+    const float rs = rms_rstd(ss, width, eps);
     if (rstd && lane == 0) rstd[row] = rs;
     Ty* yr = y + row * ldy;
 #pragma unroll
@@ -64,7 +61,7 @@ __global__ void __launch_bounds__(256) rmsnorm_fwd_kernel(const Tx* __restrict__
         float wv[V], o[V];
         load_vec<float, V>(w + c, wv);
 #pragma unroll
-        for (int e = 0; e < V; ++e) o[e] = (v[r][j][e] * rs) * wv[e];
+        for (int e = 0; e < V; ++e) o[e] = __fmul_rn(__fmul_rn(v[r][j][e], rs), wv[e]);
         store_vec<Ty, V>(yr + c, o);
       }
     }
@@ -215,15 +212,17 @@ __global__ void __launch_bounds__(256) add_rmsnorm_fwd_kernel(const float* __res
       load_vec<float, V>(x + base + c, xa);
       load_vec<Ta, V>(a + base + c, aa);
 #pragma unroll
-      for (int e = 0; e < V; ++e) {
-        v[j][e] = xa[e] + aa[e];
-        ss += v[j][e] * v[j][e];
-      }
+      for (int e = 0; e < V; ++e) v[j][e] = __fadd_rn(xa[e], aa[e]);
       if (sum_out) store_vec<float, V>(sum_out + base + c, v[j]);
     }
   }
-  ss = warp_sum(ss);
-  const float r = rsqrtf(ss / (float)width + eps);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {  // the order of rmsnorm_fwd_kernel (sumsq_chain, butterfly, groups in order)
+    const int c = (j * 32 + lane) * V;
+    const float sj = warp_sum(c < width ? sumsq_chain<V>(v[j]) : 0.f);
+    ss = j == 0 ? sj : __fadd_rn(ss, sj);
+  }
+  const float r = rms_rstd(ss, width, eps);
   if (rstd && lane == 0) rstd[row] = r;
 #pragma unroll
   for (int j = 0; j < NV; ++j) {
@@ -232,7 +231,7 @@ __global__ void __launch_bounds__(256) add_rmsnorm_fwd_kernel(const float* __res
       float wv[V], o[V];
       load_vec<float, V>(w + c, wv);
 #pragma unroll
-      for (int e = 0; e < V; ++e) o[e] = (v[j][e] * r) * wv[e];
+      for (int e = 0; e < V; ++e) o[e] = __fmul_rn(__fmul_rn(v[j][e], r), wv[e]);
       store_vec<Ty, V>(y + base + c, o);
     }
   }

@@ -465,12 +465,16 @@ def reconstruct_midpoint_sum(x_next: torch.Tensor, a: torch.Tensor, m: torch.Ten
 
 
 def linear_reconstruct(x: torch.Tensor, w: torch.Tensor, state: torch.Tensor, coeff: float,
-                       addend: torch.Tensor | None = None, out: torch.Tensor | None = None):
+                       addend: torch.Tensor | None = None, out: torch.Tensor | None = None, norm=None,
+                       low: torch.Tensor | None = None):
     """out = state - round(coeff * round(round(x @ w^T) + addend)) with the
     sublayer output x @ w^T only in the GEMM epilogue (rk_gemm_fprop_reconstruct);
     bitwise equal to linear_fwd followed by reconstruct_midpoint_sum (addend) or
-    reconstruct_midpoint. None when the shapes or dtypes do not fit the fused
-    epilogue (the caller runs the two steps)."""
+    reconstruct_midpoint. With norm = (weight, eps, y, rstd or None) the RMSNorm
+    forward of `out` runs in the same pass (rk_gemm_fprop_reconstruct_norm,
+    N == 256), bitwise equal to rmsnorm_fwd / add_rmsnorm_fwd; with `low` the
+    rounded x @ w^T is stored there too. None when the shapes or dtypes do not
+    fit the fused epilogue (the caller runs the separate steps)."""
     require_cuda(x, w, state)
     M, K = x.shape
     N = w.shape[0]
@@ -479,13 +483,29 @@ def linear_reconstruct(x: torch.Tensor, w: torch.Tensor, state: torch.Tensor, co
             not (x.is_contiguous() and w.is_contiguous() and state.is_contiguous()) or \
             (addend is not None and not addend.is_contiguous()):
         return None
+    if norm is not None or low is not None:
+        nw, eps, y, rstd = norm if norm is not None else (None, 0.0, None, None)
+        if N != 256 or (nw is not None and (nw.dtype != torch.float32 or not nw.is_contiguous() or
+                                            y.dtype != x.dtype or tuple(y.shape) != (M, N) or not y.is_contiguous())) \
+                or (low is not None and (low.dtype != x.dtype or tuple(low.shape) != (M, N) or
+                                         not low.is_contiguous())) or nw is None:
+            return None
     out = out if out is not None else torch.empty_like(state)
-    st = _lib.lib().rk_gemm_fprop_reconstruct(x.data_ptr(), K, w.data_ptr(), K, state.data_ptr(), N,
-                                              _lib.ptr(addend), N, float(coeff), out.data_ptr(), N, M, N, K,
-                                              _lib.code(x.dtype), _lib.stream_ptr())
+    if norm is None:
+        st = _lib.lib().rk_gemm_fprop_reconstruct(x.data_ptr(), K, w.data_ptr(), K, state.data_ptr(), N,
+                                                  _lib.ptr(addend), N, float(coeff), out.data_ptr(), N, M, N, K,
+                                                  _lib.code(x.dtype), _lib.stream_ptr())
+        name = "rk_gemm_fprop_reconstruct"
+    else:
+        st = _lib.lib().rk_gemm_fprop_reconstruct_norm(x.data_ptr(), K, w.data_ptr(), K, state.data_ptr(), N,
+                                                       _lib.ptr(addend), N, float(coeff), out.data_ptr(), N,
+                                                       _lib.ptr(low), N, nw.data_ptr(), float(eps), y.data_ptr(), N,
+                                                       _lib.ptr(rstd), M, N, K, _lib.code(x.dtype),
+                                                       _lib.stream_ptr())
+        name = "rk_gemm_fprop_reconstruct_norm"
     if st in (_lib.ERR_UNSUPPORTED, _lib.ERR_ALIGN):
         return None
-    _lib.check(st, "rk_gemm_fprop_reconstruct")
+    _lib.check(st, name)
     return out
 
 

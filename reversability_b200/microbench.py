@@ -2,6 +2,7 @@
 
     python -m reversability_b200.microbench [--only NAME[,NAME...]] [--iters N]
     python -m reversability_b200.microbench --only versus      (cuBLAS / torch SDPA arms beside librevk)
+    python -m reversability_b200.microbench --only api --iters 20   (the reference API's training paths on this package)
     python -m reversability_b200.microbench --only head|attention|swiglu|membound|gemms --profile   (ncu launch sequence)
 
 Workload: 16,896 tokens x width 256 in bf16 (activations N(0,1), weights
@@ -445,6 +446,98 @@ PROFILES = {"head": profile_head, "attention": profile_attention, "swiglu": prof
             "membound": profile_membound, "gemms": profile_gemms}
 
 
+def api_rates(updates: int, warmup: int = 3):
+    """Training throughput of the reference's own public calls on this
+    package at the cfg2 update shape (20.3M model, 29 x 512 per microstep,
+    accumulation 2, bf16 autocast, clip 1.0 + AdamW after each update):
+
+    - `module_autograd`: `ReversibleLM(cfg, 'midpoint')`, full logits and
+      `F.cross_entropy(reduction='sum') / targets` under autocast, `.backward()`
+      (train_baseline.py:256-280 with the model from model.py:85-118);
+    - `install_v3_split_tiled_cached_head`: `install_v3(core_mode='split',
+      mlp_tokens=8192)` then `cached_head_backward(..., 1024,
+      precision='bf16')` per microstep (optimized_v3.py:120-192);
+    - `trainer_graph`: the package's own trainer, one update as a CUDA graph.
+
+    The two API paths step `torch.optim.AdamW` (foreach) like the reference's
+    trainer; batches are resident on the device before timing. Prints one JSON
+    object per path: targets/s, ms per update and peak allocated bytes."""
+    import torch.nn.functional as F
+    import reversability_b200 as rb
+    from . import data
+    from .optimized_v3 import cached_head_backward, install_v3
+    from .train import ReversibleTrainer, TrainSettings
+
+    B, T, acc = 29, 512, 2
+    dev = torch.device("cuda", torch.cuda.current_device())
+    per_update = B * T * acc
+    total = warmup + updates
+    stream = data.synthetic_stream(per_update * total + 1, seed=1337)
+    ups = []
+    for u in range(total):
+        b, targets = data.update_batches(stream, u * per_update, 0, 1, B, T, acc, len(stream) - 1)
+        ups.append(([(x.to(dev), y.to(dev)) for x, y, _ in b], targets))
+    torch.cuda.synchronize()
+
+    def api_update(model, opt, path, batches, targets):
+        for x, y in batches:
+            if path == "module_autograd":
+                with torch.autocast(device_type="cuda", dtype=torch.bfloat16):
+                    logits = model(x)
+                    loss = F.cross_entropy(logits.flatten(0, 1), y.flatten(), ignore_index=-100, reduction="sum")
+                (loss / targets).backward()
+                del logits, loss
+            else:
+                cached_head_backward(model, x, y, targets, 1024, precision="bf16")
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        opt.zero_grad(set_to_none=True)
+
+    for path in ("module_autograd", "install_v3_split_tiled_cached_head", "trainer_graph"):
+        torch.manual_seed(1337)
+        model = rb.ReversibleLM(rb.ModelConfig(), "midpoint").to(dev)
+        if path == "trainer_graph":
+            trainer = ReversibleTrainer(model, TrainSettings(batch_size=B, sequence_length=T, accumulation=acc))
+
+            def step(u):
+                batches, targets = ups[u]
+                trainer.ids.copy_(torch.stack([x for x, _ in batches]))
+                trainer.labels.copy_(torch.stack([y for _, y in batches]))
+                trainer.inv_denominator.fill_(1.0 / targets)
+                trainer.update(6e-4)
+            step(0)
+            trainer.capture(warmup=1)
+        else:
+            if path != "module_autograd":
+                install_v3(model, core_mode="split", mlp_tokens=8192)
+            opt = torch.optim.AdamW(model.parameters(), lr=6e-4, betas=(0.9, 0.95), weight_decay=0.1)
+
+            def step(u, model=model, opt=opt, path=path):
+                api_update(model, opt, path, *ups[u])
+        for u in range(warmup):
+            step(u)
+        torch.cuda.synchronize()
+        torch.cuda.reset_peak_memory_stats(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for u in range(warmup, total):
+            step(u)
+        b.record()
+        torch.cuda.synchronize()
+        ms = a.elapsed_time(b) / updates
+        print(json.dumps({"path": path, "metric": "training targets/s (cfg2 update shape)",
+                          "value": per_update / (ms * 1e-3), "unit": "targets/s", "ms_per_update": ms,
+                          "updates": updates, "peak_alloc_bytes": torch.cuda.max_memory_allocated(dev)}),
+              flush=True)
+        if path == "trainer_graph":
+            trainer.graph = None
+            del trainer
+        else:
+            del opt
+        del model
+        torch.cuda.empty_cache()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=",".join(k for k in BENCHES if k != "versus"),
@@ -457,6 +550,9 @@ def main():
         for name in args.only.split(","):
             PROFILES[name]()
         print("ok", flush=True)
+        return
+    if args.only == "api":
+        api_rates(args.iters)
         return
     hbm, tf, kind = peaks()
     for name in args.only.split(","):

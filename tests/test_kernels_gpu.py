@@ -408,6 +408,64 @@ def test_gemm_fprop_reconstruct_bitwise(dt, M, N, K, coeff, with_addend):
     assert _lib_status() == 0
 
 
+@pytest.mark.parametrize("dt", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,K", [(14848, 1024), (14848, 256), (1000, 1024), (333, 96), (7, 256)])
+@pytest.mark.parametrize("mode", ["update", "update_addend", "residual_add"])
+def test_gemm_fprop_reconstruct_norm_bitwise(dt, M, K, mode):
+    """The state update with the next RMSNorm forward in the same epilogue
+    (rk_gemm_fprop_reconstruct_norm, N = 256) equals the separate kernels bit
+    for bit: the update (with or without the midpoint addend) then
+    rk_rmsnorm_fwd of it; and the residual add y = x + round(o W^T) (coeff -1,
+    the rounded projection stored too) equals rk_gemm_fprop followed by
+    rk_add_rmsnorm_fwd (sum, norm and rstd)."""
+    from reversability_b200 import functional as fn
+    N, eps = 256, 1e-6
+    g = torch.Generator(device="cpu").manual_seed(M + K)
+    x = torch.randn(M, K, generator=g).to(DEV, dt)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(DEV, dt)
+    state = (torch.randn(M, N, generator=g) * 3).to(DEV)
+    nw = (1 + 0.1 * torch.randn(N, generator=g)).to(DEV)
+    y, rstd = torch.empty(M, N, device=DEV, dtype=dt), torch.empty(M, device=DEV)
+    if mode == "residual_add":
+        low = torch.empty(M, N, device=DEV, dtype=dt)
+        out = fn.linear_reconstruct(x, w, state, -1.0, norm=(nw, eps, y, rstd), low=low)
+        assert out is not None
+        a = fn.linear_fwd(x, w)
+        y_ref, s_ref, r_ref = fn.add_rmsnorm_fwd(state, a, nw, eps, dt, want_sum=True)
+        assert torch.equal(low, a)
+        assert torch.equal(out, s_ref)
+    else:
+        add = torch.randn(M, N, generator=g).to(DEV, dt) if mode == "update_addend" else None
+        coeff = 1.0 if add is not None else -0.5
+        out = fn.linear_reconstruct(x, w, state, coeff, addend=add, norm=(nw, eps, y, rstd))
+        assert out is not None
+        assert torch.equal(out, fn.linear_reconstruct(x, w, state, coeff, addend=add))
+        y_ref, r_ref = fn.rmsnorm_fwd(out, nw, eps, out_dtype=dt)
+    assert torch.equal(y, y_ref)
+    assert torch.equal(rstd, r_ref)
+    # without rstd, and a width the fused norm does not take
+    y2 = torch.empty_like(y)
+    assert fn.linear_reconstruct(x, w, state, -1.0, norm=(nw, eps, y2, None)) is not None
+    w2 = (torch.randn(128, K, generator=g) * 0.05).to(DEV, dt)
+    assert fn.linear_reconstruct(x, w2, state[:, :128].contiguous(), -1.0,
+                                 norm=(nw[:128].contiguous(), eps, y[:, :128].contiguous(), None)) is None
+    assert _lib_status() == 0
+
+
+def test_rmsnorm_fwd_fixed_order_matches_fp64():
+    """The standalone norm's fixed summation order (per-lane chains, butterfly
+    per 32-lane group, groups in column order) stays within fp32 rounding of
+    an fp64 reference at the widths the models use."""
+    from reversability_b200 import functional as fn
+    for width in (256, 1024, 96):
+        x = torch.randn(4099, width, device=DEV) * 2
+        w = 1 + 0.1 * torch.randn(width, device=DEV)
+        y, r = fn.rmsnorm_fwd(x, w, 1e-6)
+        r64 = torch.rsqrt(x.double().square().mean(-1) + 1e-6)
+        assert torch.allclose(r.double(), r64, rtol=2e-6, atol=0)
+        assert torch.allclose(y.double(), x.double() * r64[:, None] * w.double(), rtol=1e-5, atol=1e-6)
+
+
 def _lib_status():
     from reversability_b200 import _lib
     torch.cuda.synchronize()

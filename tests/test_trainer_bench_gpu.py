@@ -72,3 +72,58 @@ def test_benchmarked_update_matches_oracle(method, B):
     assert math.sqrt(diff / upd) <= 0.05
     from reversability_b200 import _lib
     assert _lib.device_status() == 0
+
+
+def test_scaled_config_full_depth_update_matches_oracle():
+    """The scaled configuration (24 layers, d_model 1024,
+    16 heads of 64, SwiGLU 4096, vocabulary 50,257 tied, context 2048) at full
+    depth through the trainer bench.py runs for it (fused softmax head,
+    pipelined reverse sweep, side streams, replayed CUDA graph), with the batch
+    reduced to one sequence: one bf16 update's loss, pre-clip gradient norm and
+    pre-clip gradients against the oracle's bf16 reconstruction backward.
+
+    Gates: loss 2e-3 and gradient norm 2e-2. Per parameter, rel-L2 2e-2 or,
+    where bf16 reconstruction through the layers above moves the gradient
+    further, three times the reference algorithm's own drift at that depth
+    (the oracle's bf16 reconstruction backward against its bf16 autograd
+    backward over the unrolled stack): zero for the top layer, about 0.11 for
+    the bottom one. Two bf16 reconstructions drift independently, so the
+    product's distance to the oracle is about twice the oracle's own drift."""
+    import reversability_b200 as rb
+    from reversability_b200 import data as rdata
+    from reversability_b200.train import ReversibleTrainer, TrainSettings, learning_rate
+    conf = dict(n_layers=24, d_model=1024, n_heads=16, d_ff=4096, max_sequence_length=2048)
+    B, T, acc = 1, 2048, 1
+    s = TrainSettings(batch_size=B, sequence_length=T, accumulation=acc, precision="bf16")
+    torch.manual_seed(1337)
+    model = rb.ReversibleLM(rb.ModelConfig(**conf), "midpoint").to(DEV)
+    tr = ReversibleTrainer(model, s)
+    assert tr.fused_head
+    cfg = om.Config(**conf)
+    stream = ost.synthetic_stream(B * T * acc + 1, seed=1337)
+    tr.capture(warmup=0)
+    batches, targets = rdata.update_batches(stream, 0, 0, 1, B, T, acc, len(stream) - 1)
+    tr.stage_batches(batches, targets)
+    loss = tr.update(learning_rate(s, 0, targets)).item() / targets
+    gnorm = float(tr.grad_norm)
+    grads = {n: tr.view(tr.gflat, n).detach().cpu() for n in om.parameter_names(cfg)}
+    from reversability_b200 import _lib
+    assert _lib.device_status() == 0
+    del tr, model
+    params = om.init_params(cfg, seed=1337)
+    (x, y, _), = batches
+    kw = dict(low=torch.bfloat16, eps=1e-6, denominator=targets)
+    total, recon, _ = om.loss_and_grads(params, cfg, x, y, "midpoint", 0.5, **kw)
+    _, exact, _ = om.loss_and_grads(params, cfg, x, y, "midpoint", 0.5, mode="autograd", **kw)
+    ref_norm = math.sqrt(sum(float(g.double().square().sum()) for g in recon.values()))
+    assert abs(loss - float(total) / targets) <= 2e-3 * abs(float(total) / targets)
+    assert abs(gnorm - ref_norm) <= 2e-2 * ref_norm, (gnorm, ref_norm)
+    excess = {}
+    for n, g in grads.items():
+        gate = max(2e-2, 3.0 * rel_l2(recon[n], exact[n]))
+        err = rel_l2(g, recon[n])
+        if err > gate:
+            excess[n] = (err, gate)
+    assert not excess, sorted(excess.items(), key=lambda kv: -kv[1][0])[:3]
+    top = [n for n in grads if n.startswith(f"blocks.{conf['n_layers'] - 1}.")]
+    assert max(rel_l2(grads[n], recon[n]) for n in top) <= 2e-2

@@ -82,13 +82,19 @@ def test_scaled_config_full_depth_update_matches_oracle():
     reduced to one sequence: one bf16 update's loss, pre-clip gradient norm and
     pre-clip gradients against the oracle's bf16 reconstruction backward.
 
-    Gates: loss 2e-3 and gradient norm 2e-2. Per parameter, rel-L2 2e-2 or,
-    where bf16 reconstruction through the layers above moves the gradient
-    further, three times the reference algorithm's own drift at that depth
-    (the oracle's bf16 reconstruction backward against its bf16 autograd
-    backward over the unrolled stack): zero for the top layer, about 0.11 for
-    the bottom one. Two bf16 reconstructions drift independently, so the
-    product's distance to the oracle is about twice the oracle's own drift."""
+    Gates: loss 2e-3 and gradient norm 2e-2. Gradients per group (each
+    layer's six parameters together; the embeddings and the final norm
+    together): rel-L2 2e-2 against the oracle or, where bf16 reconstruction
+    through the layers above moves the gradient further, three times the
+    reference algorithm's own drift for that group (the oracle's bf16
+    reconstruction backward against its bf16 autograd backward over the
+    unrolled stack; zero for the top layer, about 0.1 for the bottom one).
+    The product's distance to the exact autograd gradients is held to the same
+    bound: its kernels round differently from the oracle's (about 0.6% at the
+    top layer, where no reconstruction is involved), and the layers above
+    amplify that difference the way they amplify reconstruction error, so it
+    measures 1.5-2.3 times the oracle's own drift (0.170 against 0.073 at the
+    bottom layer on a B200)."""
     import reversability_b200 as rb
     from reversability_b200 import data as rdata
     from reversability_b200.train import ReversibleTrainer, TrainSettings, learning_rate
@@ -118,12 +124,18 @@ def test_scaled_config_full_depth_update_matches_oracle():
     ref_norm = math.sqrt(sum(float(g.double().square().sum()) for g in recon.values()))
     assert abs(loss - float(total) / targets) <= 2e-3 * abs(float(total) / targets)
     assert abs(gnorm - ref_norm) <= 2e-2 * ref_norm, (gnorm, ref_norm)
-    excess = {}
-    for n, g in grads.items():
-        gate = max(2e-2, 3.0 * rel_l2(recon[n], exact[n]))
-        err = rel_l2(g, recon[n])
-        if err > gate:
-            excess[n] = (err, gate)
-    assert not excess, sorted(excess.items(), key=lambda kv: -kv[1][0])[:3]
-    top = [n for n in grads if n.startswith(f"blocks.{conf['n_layers'] - 1}.")]
-    assert max(rel_l2(grads[n], recon[n]) for n in top) <= 2e-2
+    groups = {}
+    for n in grads:
+        key = n.split(".")[1] if n.startswith("blocks.") else "boundary"
+        groups.setdefault(key, []).append(n)
+    cat = lambda d, ns: torch.cat([d[n].reshape(-1).double() for n in ns])  # noqa: E731
+    report = {}
+    for key, ns in groups.items():
+        ours, rec, ex = cat(grads, ns), cat(recon, ns), cat(exact, ns)
+        drift = rel_l2(rec, ex)
+        report[key] = (rel_l2(ours, rec), rel_l2(ours, ex), drift)
+    print("group: (to oracle, to exact autograd, oracle drift)",
+          {k: tuple(round(x, 4) for x in v) for k, v in sorted(report.items())})
+    bad = {k: v for k, v in report.items() if max(v[0], v[1]) > max(2e-2, 3.0 * v[2])}
+    assert not bad, sorted(bad.items())
+    assert report[str(conf["n_layers"] - 1)][0] <= 2e-2  # the top layer: no reconstruction

@@ -71,8 +71,9 @@ def parse():
     ap.add_argument("--accumulation", type=int, default=None)
     ap.add_argument("--no-graph", action="store_true", help="run updates eagerly instead of replaying a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--forward-overlap", choices=["head", "after_head"], default="head",
-                    help="start microstep m+1's forward sweep beside microstep m's head GEMM or after it")
+    ap.add_argument("--forward-overlap", choices=["start", "head", "after_head"], default="start",
+                    help="start the later microsteps' forward sweeps beside microstep 0's (default), or "
+                         "microstep m+1's beside microstep m's head GEMM, or after it")
     ap.add_argument("--no-tied-split", action="store_true",
                     help="data parallel: reduce the tied embedding gradient as one bucket after the sweep")
     ap.add_argument("--reference-memory", action="store_true",

@@ -309,6 +309,19 @@ RK_API int rk_head_loss(const float* stats, int64_t width, const float* xlabel, 
 RK_API int rk_head_dgrad(const void* expo, int64_t lde, const float* fcoef, int64_t fcoef_ld, const float* rowc,
                          const int64_t* labels, const void* w, int64_t ldw, void* dx, int64_t lddx, int64_t M,
                          int64_t V, int64_t K, int dtype, int out_dtype, void* stream);
+/* rk_head_dgrad with the vocabulary reduction split into slices when the
+ * output has fewer 128 x 256 tiles than the GPU has SMs (cfg2: 116 tiles),
+ * so every SM works: fp32 partial slices in `workspace` (at least
+ * rk_head_dgrad_workspace(M, V, K) bytes, 16-byte aligned; 0 = no split for
+ * this shape), then a fixed-order sum into dx (deterministic; the sum order
+ * differs from the unsplit kernel's, so results agree to fp32 rounding of
+ * the partials). Falls back to rk_head_dgrad when the workspace is short, the
+ * shape needs no split, or K / lddx are not multiples of 4. */
+RK_API int64_t rk_head_dgrad_workspace(int64_t M, int64_t V, int64_t K);
+RK_API int rk_head_dgrad_ws(const void* expo, int64_t lde, const float* fcoef, int64_t fcoef_ld, const float* rowc,
+                            const int64_t* labels, const void* w, int64_t ldw, void* dx, int64_t lddx, int64_t M,
+                            int64_t V, int64_t K, int dtype, int out_dtype, float* workspace,
+                            int64_t workspace_bytes, void* stream);
 RK_API int rk_head_wgrad(const void* expo, int64_t lde, const float* fcoef, int64_t fcoef_ld, const float* rowc,
                          const int64_t* labels, const void* x, int64_t ldx, float* dw, int64_t lddw, int64_t M,
                          int64_t V, int64_t K, int dtype, int accumulate, void* stream);

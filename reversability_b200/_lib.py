@@ -77,6 +77,9 @@ SIGNATURES: dict[str, tuple] = {
     "rk_head_fprop": (_i, [_p, _i64, _p, _i64, _p, _p, _i64, _p, _p, _i64, _i64, _i64, _i, _p]),
     "rk_head_loss": (_i, [_p, _i64, _p, _p, _i64, _i64, _f, _p, _p, _p, _p, _i64, _i, _p]),
     "rk_head_dgrad": (_i, [_p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p]),
+    "rk_head_dgrad_workspace": (_i64, [_i64, _i64, _i64]),
+    "rk_head_dgrad_ws": (_i, [_p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p, _i64,
+                              _p]),
     "rk_head_wgrad": (_i, [_p, _i64, _p, _i64, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i, _i, _p]),
 }
 

@@ -995,16 +995,17 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           g.xlabel[row] = xl;
         }
         const float nm = mx == -INFINITY ? 0.f : -mx * kLog2eF;
-        float sm4[4] = {0.f, 0.f, 0.f, 0.f};
+        const float2 l2 = make_float2(kLog2eF, kLog2eF), n2 = make_float2(nm, nm);
+        float2 sm2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};  // packed fp32x2 partial sums
         uint8_t* buf = sOut + ew * 2048;
         const int y = m0 + quarter * 32;
 #pragma unroll
         for (int ch = 0; ch < 2; ++ch) {
 #pragma unroll
-          for (int k = ch * 16; k < ch * 16 + 16; ++k) {
-            const float e0 = ex2_fast(fmaf(unpack_half<TOut>(xp[k], 0), kLog2eF, nm));
-            const float e1 = ex2_fast(fmaf(unpack_half<TOut>(xp[k], 1), kLog2eF, nm));
-            sm4[k & 3] += e0 + e1;
+          for (int k = ch * 16; k < ch * 16 + 16; ++k) {  // a pair per step: one FFMA2, two ex2, one FADD2
+            const float2 t = __ffma2_rn(make_float2(unpack_half<TOut>(xp[k], 0), unpack_half<TOut>(xp[k], 1)), l2, n2);
+            const float e0 = ex2_fast(t.x), e1 = ex2_fast(t.y);
+            sm2[k & 1] = __fadd2_rn(sm2[k & 1], make_float2(e0, e1));
             xp[k] = pack_unit2<TOut>(e0, e1);
           }
           if (lane == 0) bulk_wait_read<0>();
@@ -1021,7 +1022,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
             bulk_commit();
           }
         }
-        const float sm = (sm4[0] + sm4[1]) + (sm4[2] + sm4[3]);
+        const float sm = (sm2[0].x + sm2[1].x) + (sm2[0].y + sm2[1].y);
         if (hf == 1) {
           xok = mbar_wait(barB, xtiles & 1, g.status, RK_DEV_GEMM_TIMEOUT, s_abort);
           xok = __all_sync(0xffffffffu, xok);
@@ -1318,9 +1319,9 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
 // slice order; 4 consecutive columns per thread when cols % 4 == 0. The loads
 // of up to eight slices (and of dw when accumulating) are issued before their
 // sums, which stay in slice order, so the result does not depend on the batch.
-template <int V>
+template <int V, typename TOut = float>
 __global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restrict__ partial, int splits, int64_t rows,
-                                                           int64_t cols, int64_t slice_rows, float* __restrict__ dw,
+                                                           int64_t cols, int64_t slice_rows, TOut* __restrict__ dw,
                                                            int64_t lddw, int accumulate) {
   pdl_wait();  // inputs are the previous kernel's outputs
   const int64_t n = rows * cols / V;
@@ -1328,9 +1329,11 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restri
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < n; t += (int64_t)gridDim.x * blockDim.x) {
     const int64_t i = t * V;
     const int64_t r = i / cols, c = i - r * cols;
-    float* d = dw + r * lddw + c;
+    TOut* d = dw + r * lddw + c;
     float o[V];
-    if (accumulate) load_vec<float, V>(d, o);
+    if constexpr (std::is_same_v<TOut, float>) {  // accumulation is fp32 only (host check)
+      if (accumulate) load_vec<float, V>(d, o);
+    }
     float s[V];
 #pragma unroll
     for (int e = 0; e < V; ++e) s[e] = 0.f;
@@ -1347,11 +1350,13 @@ __global__ void __launch_bounds__(256) split_reduce_kernel(const float* __restri
           for (int e = 0; e < V; ++e) s[e] += v[b][e];
         }
     }
-    if (accumulate) {
+    if constexpr (std::is_same_v<TOut, float>) {
+      if (accumulate) {
 #pragma unroll
-      for (int e = 0; e < V; ++e) s[e] += o[e];
+        for (int e = 0; e < V; ++e) s[e] += o[e];
+      }
     }
-    store_vec<float, V>(d, s);
+    store_vec<TOut, V>(d, s);
   }
 }
 
@@ -2211,6 +2216,99 @@ extern "C" int rk_head_dgrad(const void* expo, int64_t lde, const float* fcoef, 
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == RK_BF16) return head_dgrad_typed<__nv_bfloat16>(ta, tb, tc, g, dtype, out_dtype, s);
   return head_dgrad_typed<__half>(ta, tb, tc, g, dtype, out_dtype, s);
+}
+
+// Token-reduction split of the head dgrad. Its output has one 256-column tile
+// per 128 tokens, fewer tiles than SMs at the training shapes (116 at cfg2), so
+// the vocabulary reduction is cut into S slices, each an independent tile of
+// fp32 partials, with S chosen to minimise the longest CTA's share
+// ceil(tiles*S/SMs)/S (0.8 of a whole tile at cfg2 with S = 5); a
+// fixed-order pass then sums the slices (deterministic). 1 = no split.
+static int head_dgrad_splits(int64_t M, int64_t V, int64_t K) {
+  const int64_t tiles = ((M + kBM - 1) / kBM) * ((K + 255) / 256);
+  const int64_t kb = (V + kBK - 1) / kBK;
+  const int64_t sms = sm_count();
+  if (tiles <= 0 || tiles >= sms) return 1;
+  int best = 1;
+  double best_t = 1.0;
+  for (int S = 2; S <= 8 && S <= kb; ++S) {
+    const double t = (double)((tiles * S + sms - 1) / sms) / S + 0.01 * S;  // + the slices' extra traffic
+    if (t < best_t - 1e-9) {
+      best_t = t;
+      best = S;
+    }
+  }
+  return best;
+}
+
+extern "C" int64_t rk_head_dgrad_workspace(int64_t M, int64_t V, int64_t K) {
+  if (M <= 0 || V <= 0 || K <= 0) return 0;
+  const int S = head_dgrad_splits(M, V, K);
+  return S > 1 ? (int64_t)S * ((M + kBM - 1) / kBM) * kBM * K * 4 : 0;
+}
+
+extern "C" int rk_head_dgrad_ws(const void* expo, int64_t lde, const float* fcoef, int64_t fcoef_ld,
+                                const float* rowc, const int64_t* labels, const void* w, int64_t ldw, void* dx,
+                                int64_t lddx, int64_t M, int64_t V, int64_t K, int dtype, int out_dtype,
+                                float* workspace, int64_t workspace_bytes, void* stream) {
+  const int64_t need = rk_head_dgrad_workspace(M, V, K);
+  const int S = head_dgrad_splits(M, V, K);
+  if (need == 0 || S == 1 || !workspace || workspace_bytes < need || K % 4 || lddx % 4 ||
+      !rk_host::aligned(workspace, 16))
+    return rk_head_dgrad(expo, lde, fcoef, fcoef_ld, rowc, labels, w, ldw, dx, lddx, M, V, K, dtype, out_dtype,
+                         stream);
+  if (!head_bwd_args_ok(expo, lde, fcoef, fcoef_ld, rowc, labels, M, V) || !w || !dx || !dims_ok(M, K, V) ||
+      ldw < K || lddx < K)
+    return RK_ERR_ARG;
+  if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
+  if (out_dtype != RK_F32 && out_dtype != RK_BF16 && out_dtype != RK_F16) return RK_ERR_DTYPE;
+  if (!rk_host::aligned(expo, 16) || !rk_host::aligned(w, 16) || !rk_host::aligned(dx, 16) ||
+      !rk_host::aligned(rowc, 16) || (lde * 2) % 16 || (ldw * 2) % 16)
+    return RK_ERR_ALIGN;
+  const int64_t split_rows = ((M + kBM - 1) / kBM) * kBM;
+  CUtensorMap ta, tb, tc;
+  if (!make_map(&ta, expo, (uint64_t)V, (uint64_t)M, (uint64_t)lde, dtype, 64, kBM) ||
+      !make_map(&tb, w, (uint64_t)K, (uint64_t)V, (uint64_t)ldw, dtype, 64, 64) ||
+      !make_out_map(&tc, workspace, (uint64_t)K, (uint64_t)(split_rows * S), (uint64_t)K, RK_F32))
+    return RK_ERR_LAUNCH;
+  GemmArgs g{};
+  g.M = (int)M;
+  g.N = (int)K;
+  g.K = (int)V;
+  g.tiles_m = (int)((M + kBM - 1) / kBM);
+  g.tiles_n = (int)((K + 255) / 256);
+  g.kb_total = (int)((V + kBK - 1) / kBK);
+  g.splits = S;
+  g.kb_per_split = (g.kb_total + S - 1) / S;
+  g.split_rows = (int)split_rows;
+  g.out = workspace;
+  g.ldo = K;
+  g.out_dtype = RK_F32;
+  g.status = rk_host::device_status_ptr();
+  g.fcoef = fcoef;
+  g.fcoef_ld = fcoef_ld;
+  g.rowc = reinterpret_cast<const float4*>(rowc);
+  g.labels = labels;
+  g.vocab = (int)V;
+  g.tokens = (int)M;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int st = dtype == RK_BF16
+                     ? launch_tc<256, 4, false, true, EPI_TMA, float, false, XF_ROWS, __nv_bfloat16>(ta, tb, tc, g,
+                                                                                                    dtype, s)
+                     : launch_tc<256, 4, false, true, EPI_TMA, float, false, XF_ROWS, __half>(ta, tb, tc, g, dtype, s);
+  if (st != RK_OK) return st;
+  int64_t blocks = (M * K / 4 + 255) / 256;
+  if (blocks > 148 * 16) blocks = 148 * 16;
+  if (out_dtype == RK_F32)
+    rk_host::launch_k(split_reduce_kernel<4, float>, (unsigned)blocks, 256, 0, s, workspace, S, M, K, split_rows,
+                      static_cast<float*>(dx), lddx, 0);
+  else if (out_dtype == RK_BF16)
+    rk_host::launch_k(split_reduce_kernel<4, __nv_bfloat16>, (unsigned)blocks, 256, 0, s, workspace, S, M, K,
+                      split_rows, static_cast<__nv_bfloat16*>(dx), lddx, 0);
+  else
+    rk_host::launch_k(split_reduce_kernel<4, __half>, (unsigned)blocks, 256, 0, s, workspace, S, M, K, split_rows,
+                      static_cast<__half*>(dx), lddx, 0);
+  return rk_host::launch_status();
 }
 
 extern "C" int rk_head_wgrad(const void* expo, int64_t lde, const float* fcoef, int64_t fcoef_ld, const float* rowc,

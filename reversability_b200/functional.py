@@ -287,14 +287,23 @@ def head_loss(st: HeadState, grad_scale: float = 1.0, grad_scale_dev: torch.Tens
     return loss_rows
 
 
-def head_dgrad(st: HeadState, w: torch.Tensor, out_dtype: torch.dtype | None = None) -> torch.Tensor:
-    """dhidden = dlogits @ w, dlogits = (softmax - onehot) * scale formed inside the GEMM."""
+def head_dgrad(st: HeadState, w: torch.Tensor, out_dtype: torch.dtype | None = None,
+               split: bool = True) -> torch.Tensor:
+    """dhidden = dlogits @ w, dlogits = (softmax - onehot) * scale formed inside the GEMM.
+    With split (the default) the vocabulary reduction is sliced across all SMs
+    when the output alone has fewer tiles than SMs (rk_head_dgrad_ws)."""
     M, V = st.expo.shape
     K = w.shape[1]
     dx = torch.empty((M, K), device=w.device, dtype=out_dtype or w.dtype)
-    _lib.call("rk_head_dgrad", st.expo.data_ptr(), _ld(st.expo), st.fcoef.data_ptr(), st.fcoef.stride(0),
-              st.rowc.data_ptr(), st.labels.data_ptr(), w.data_ptr(), _ld(w), dx.data_ptr(), K, M, V, K,
-              _gemm_dtype(st.expo, w), _lib.code(dx.dtype), _lib.stream_ptr())
+    args = (st.expo.data_ptr(), _ld(st.expo), st.fcoef.data_ptr(), st.fcoef.stride(0), st.rowc.data_ptr(),
+            st.labels.data_ptr(), w.data_ptr(), _ld(w), dx.data_ptr(), K, M, V, K, _gemm_dtype(st.expo, w),
+            _lib.code(dx.dtype))
+    ws_bytes = _lib.lib().rk_head_dgrad_workspace(M, V, K) if split else 0
+    if ws_bytes > 0:
+        ws = torch.empty(ws_bytes // 4, device=w.device, dtype=torch.float32)
+        _lib.call("rk_head_dgrad_ws", *args, ws.data_ptr(), ws_bytes, _lib.stream_ptr())
+    else:
+        _lib.call("rk_head_dgrad", *args, _lib.stream_ptr())
     return dx
 
 

@@ -63,10 +63,11 @@ class TrainSettings:
     overlap_wgrad: bool = True  # layer weight gradients on a side stream during the reverse sweep
     overlap_forward: bool = True  # microstep m+1's forward sweep beside microstep m's backward
     tied_split: bool = True  # data parallel: the head's share of the tied gradient reduced beside the sweep
-    # where microstep m+1's forward sweep starts: beside microstep m's head GEMM
-    # ("head") or once that GEMM is issued, beside the rest of the head and the
-    # reverse sweep ("after_head")
-    forward_overlap: str = "head"
+    # where microstep m+1's forward sweep starts: at the start of the update,
+    # beside microstep 0's forward sweep ("start"; measured fastest), beside
+    # microstep m's head GEMM ("head"), or once that GEMM is issued, beside the
+    # rest of the head and the reverse sweep ("after_head")
+    forward_overlap: str = "start"
 
 
 def learning_rate(s: TrainSettings, committed: int, update_targets: int) -> float:
@@ -409,6 +410,24 @@ class ReversibleTrainer:
             # update) runs on its own stream beside microstep m's head and
             # reverse sweep; its final states stay referenced until the join.
             main = torch.cuda.current_stream()
+            if self.s.forward_overlap == "start":
+                # every later microstep's forward sweep beside microstep 0's
+                # (the sweeps keep only their final states)
+                ready = torch.cuda.Event()
+                ready.record(main)
+                self.fwd_stream.wait_event(ready)
+                with torch.cuda.stream(self.fwd_stream):
+                    later = [self._forward_states(m) for m in range(1, acc)]
+                done = torch.cuda.Event()
+                done.record(self.fwd_stream)
+                states = self._forward_states(0)
+                for m in range(acc):
+                    if m == 1:
+                        main.wait_event(done)
+                    self._microstep(m, last=(m == acc - 1), states=states)
+                    states = later[m] if m + 1 < acc else None
+                self._finish_update()
+                return
             states = self._forward_states(0)
             for m in range(acc):
                 box = {}
@@ -429,6 +448,10 @@ class ReversibleTrainer:
                 if "done" in box:
                     main.wait_event(box["done"])
                 states = box.get("states")
+        self._finish_update()
+
+    def _finish_update(self):
+        """The data-parallel exchange of the remaining buckets, then clip + AdamW."""
         if self.world > 1:
             n = len(self.layers)
             for i in range(n, n + 3):

@@ -125,6 +125,37 @@ def _trainer(method="midpoint", B=3, T=64, acc=2):
     return ReversibleTrainer(rb.ReversibleLM(rb.ModelConfig(**WIDE), method).to(DEV), s)
 
 
+@pytest.mark.parametrize("acc", [2, 3])
+def test_forward_overlap_schedules_give_the_same_update(acc):
+    """Where the later microsteps' forward sweeps start (beside the previous
+    head, after it, or beside microstep 0's forward sweep) changes only the
+    stream schedule: the update is bitwise the same, eager and replayed."""
+    import reversability_b200 as rb
+    from reversability_b200 import data as rdata
+    from reversability_b200.train import ReversibleTrainer, TrainSettings
+    B, T = 3, 64
+    stream = ost.synthetic_stream(B * T * acc * 3 + 1, seed=11, vocab_size=101, eos=100, mean_doc=50.0)
+    out = []
+    for mode in ("head", "after_head", "start"):
+        torch.manual_seed(1337)
+        s = TrainSettings(batch_size=B, sequence_length=T, accumulation=acc, warmup_targets=1000,
+                          forward_overlap=mode)
+        tr = ReversibleTrainer(rb.ReversibleLM(rb.ModelConfig(**WIDE), "midpoint").to(DEV), s)
+        losses = []
+        for u in range(2):
+            batches, targets = rdata.update_batches(stream, u * B * T * acc, 0, 1, B, T, acc, len(stream) - 1)
+            tr.stage_batches(batches, targets)
+            if u == 1:
+                tr.capture(warmup=0)
+            losses.append(tr.update(1e-4).item())
+        torch.cuda.synchronize()
+        out.append((losses, tr.flat.clone()))
+        tr.graph = None
+    for losses, flat in out[1:]:
+        assert losses == out[0][0]
+        assert torch.equal(flat, out[0][1])
+
+
 def test_train_loop_over_prefetcher_equals_staged_updates(tmp_path):
     """trainer.train() over a memory-mapped uint16 stream with the pinned
     prefetcher runs the same updates, bit for bit, as staging each update's

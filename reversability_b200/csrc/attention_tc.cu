@@ -11,16 +11,16 @@
 //   warp 1      tcgen05.mma issuer: S_j = Q K_j^T (M=128, N=64, K=HD) into a
 //               TMEM accumulator; O += P_j V_j (M=128, N=HD, K=64) into the
 //               TMEM O accumulator.
-//   warps 2..5  softmax, one query row per thread (TMEM lane = row): pass 1
-//               reads S_j for the row max (no shuffles), pass 2 re-reads it,
-//               writes P_j = exp2(s*c - m) (bf16/f16) into a 128-byte-swizzled
-//               shared tile for the PV MMA and sums it; the previous O_{j-1}
-//               is merged into a register accumulator with the usual online
-//               rescale while PV_j runs.
-// S is single-buffered (the next S waits for pass 2), so two CTAs share an SM
-// (256 TMEM columns and ~107 KB of shared memory each) and hide each other's
-// latencies. lse is written in base 2 (max*c + log2(sum)), the layout the
-// backward kernels read.
+//   warps 2..5  softmax, one query row per thread (TMEM lane = row): one
+//               TMEM read of S_j (64 columns; the buffer is released at
+//               once), the row max (no shuffles), P_j = exp2(s*c - m_ref)
+//               (bf16/f16) into a 128-byte-swizzled shared tile for the PV
+//               MMA and its row sum. m_ref moves only when the row max rises
+//               by more than 2^8 (lazy rescale); O is then rescaled in TMEM.
+// S is double-buffered in TMEM (the MMA warp issues S_{j+1} before waiting
+// for P_j), two CTAs share an SM (256 TMEM columns each) and hide each other's
+// latencies. lse is written in base 2 (m_ref + log2(sum)), the
+// layout the backward kernels read.
 //
 // Every mbarrier wait is bounded (RK_DEV_ATTN_TIMEOUT); on expiry the CTA
 // stops issuing, drains its own MMAs and TMA loads and frees its TMEM.

@@ -1992,7 +1992,7 @@ namespace rk {
 // 32 rows per CTA: warp w reduces rows w, w+8, .. of the CTA's 32 (lse, loss,
 // rowc), then the CTA writes fcoef[b][row] = exp(m_b - lse) * scale for every
 // block b with 32 consecutive rows per store (coalesced).
-__global__ void __launch_bounds__(256) head_loss_kernel(const float2* __restrict__ stats, int width,
+__global__ void __launch_bounds__(256, 4) head_loss_kernel(const float2* __restrict__ stats, int width,
                                                         const float* __restrict__ xlabel, int vocab,
                                                         const int64_t* __restrict__ labels, int rows, float scale,
                                                         const float* __restrict__ scale_dev,
@@ -2004,30 +2004,48 @@ __global__ void __launch_bounds__(256) head_loss_kernel(const float2* __restrict
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * 32;
   if (scale_dev) scale *= *scale_dev;
-  for (int rr = warp; rr < 32; rr += 8) {
+  // the warp's four rows warp, warp + 8, .. are read together (16 loads in
+  // flight per lane); each row's entries lane, lane + 32, ... are merged in
+  // that order
+  float m4[4], s4[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    m4[r] = -INFINITY;
+    s4[r] = 0.f;
+  }
+  for (int i0 = lane; i0 < width; i0 += 4 * 32) {
+    float2 p[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int row = row0 + warp + 8 * r;
+      const float2* st = stats + (int64_t)row * width;
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        p[r][k] = (row < rows && i0 + 32 * k < width) ? st[i0 + 32 * k] : make_float2(-INFINITY, 0.f);
+    }
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) lse_merge(m4[r], s4[r], p[r][k].x, p[r][k].y);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int rr = warp + 8 * r;
     const int row = row0 + rr;
+    float m = m4[r], s = s4[r];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      lse_merge(m, s, m2, s2);
+    }
     if (row >= rows) {
       if (lane == 0) {
         s_nl[rr] = 0.f;
         s_sc[rr] = 0.f;
       }
       continue;
-    }
-    const float2* st = stats + (int64_t)row * width;
-    float m = -INFINITY, s = 0.f;
-    // entries lane, lane + 32, ... merged in that order, eight loads in flight
-    for (int i0 = lane; i0 < width; i0 += 8 * 32) {
-      float2 p[8];
-#pragma unroll
-      for (int k = 0; k < 8; ++k) p[k] = i0 + 32 * k < width ? st[i0 + 32 * k] : make_float2(-INFINITY, 0.f);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) lse_merge(m, s, p[k].x, p[k].y);
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-      lse_merge(m, s, m2, s2);
     }
     if (lane == 0) {
       const int64_t label = labels[row];

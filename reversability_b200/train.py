@@ -365,8 +365,9 @@ class ReversibleTrainer:
                             accumulate=True)
             if last and self.g_head is not None:
                 self.buckets.launch(self._head_bucket)
-        dout, _ = fn.rmsnorm_bwd(out, self.final_w, rstd_f, dhidden, dx_dtype=F32, dw=self.g_final,
-                                 accumulate_dw=True)
+        # final-norm backward; its weight-gradient reduction goes to the
+        # weight-gradient stream when there is one (joined by the sweep's end)
+        dout, _ = kern._norm_bwd(out, self.final_w, rstd_f, dhidden, self.g_final)
         # the unused output's cotangent is zero; the engine takes None for it
         dp, dq = (None, dout) if self.model.method == "midpoint" else (dout, None)
         hook = self._bucket_hook if (last and self.world > 1) else None

@@ -47,12 +47,19 @@ constexpr uint32_t kNumBars = 26;
 constexpr uint32_t kOCol = kSBufs * kKT;          // S [0, 64 * kSBufs), O [kOCol, kOCol + HD)
 constexpr uint32_t kTmemCols = 256;               // power of two >= kOCol + HD
 
-// Per head-dim layout. Shared memory: Q0 Q1 | K ring | V ring | P0 P1 | barriers.
-// HD = 64 keeps two K/V stages so that two CTAs still share an SM.
+// Per head-dim layout. Shared memory: Q0 Q1 | K ring | V ring | P buffers | barriers.
+// The K/V ring must run ahead of the MMA warp: K/V tile j + kKVStages is
+// loaded once PV_j has completed, at the end of the softmax of tile j, and S
+// of that tile is issued at the end of the softmax of tile j + kKVStages - 2.
+// HD = 64 holds three K/V stages and one P buffer (the softmax of tile j+1
+// writes P after PV_j completes, which it has by then) so that two CTAs still
+// share an SM; with two stages the softmax warps waited about 1,100 cycles
+// per tile for S (44% of their time at the scaled model's shape).
 template <int HD>
 struct Fwd {
   static_assert(HD == 32 || HD == 64, "head_dim 32 or 64");
-  static constexpr int kKVStages = HD == 32 ? 4 : 2;
+  static constexpr int kKVStages = HD == 32 ? 4 : 3;
+  static constexpr int kPBufs = HD == 32 ? 2 : 1;
   static constexpr uint32_t kRow = HD * 2;              // bytes per row: the swizzle span
   static constexpr uint32_t kSwz = HD == 32 ? 4 : 2;    // descriptor layout: 64- / 128-byte swizzle
   static constexpr uint32_t kSbo = 8 * kRow;            // bytes between 8-row groups
@@ -62,7 +69,7 @@ struct Fwd {
   static constexpr uint32_t kOffK = 2 * kQBytes;
   static constexpr uint32_t kOffV = kOffK + kKVStages * kKVBytes;
   static constexpr uint32_t kOffP = kOffV + kKVStages * kKVBytes;
-  static constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;
+  static constexpr uint32_t kOffBar = kOffP + kPBufs * kPBytes;
   static constexpr uint32_t kSmem = 1024 + kOffBar + kNumBars * 8 + 32;
   static_assert(kKVStages <= 4 && kOCol + HD <= kTmemCols, "barrier slots and TMEM columns");
   static_assert(2 * (kSmem + 1024) <= 233472, "two CTAs per SM");
@@ -303,8 +310,8 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           } else {
             umma_commit(bb.q_empty0 + 8 * qb);  // every S of this item issued: its Q buffer may be refilled
           }
-          const int pb = gp & 1;
-          if (!mbar_wait(bb.p_full0 + 8 * pb, (gp >> 1) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort)) {
+          const int pb = gp % C::kPBufs;
+          if (!mbar_wait(bb.p_full0 + 8 * pb, (gp / C::kPBufs) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort)) {
             ok = false;
             break;
           }
@@ -384,11 +391,12 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           mx4[((k >> 1) + 2) & 3] = fmax3(mx4[((k >> 1) + 2) & 3], __uint_as_float(rb[k]), __uint_as_float(rb[k + 1]));
         }
         const float mt = fmax3(fmaxf(mx4[0], mx4[1]), mx4[2], mx4[3]) * c_log2;
-        // P buffer free (PV tile gp-2 done): after this wait at most one PV
-        // (gp-1) is outstanding, so the o_full parity wait below is unambiguous
-        const int pb = gp & 1;
-        if (gp >= 2) {
-          w = mbar_wait(bb.p_empty0 + 8 * pb, ((gp - 2) >> 1) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort);
+        // P buffer free (PV tile gp - kPBufs done): after this wait at most one
+        // PV (gp-1) is outstanding, so the o_full parity wait below is unambiguous
+        constexpr int kPB = C::kPBufs;
+        const int pb = gp % kPB;
+        if (gp >= kPB) {
+          w = mbar_wait(bb.p_empty0 + 8 * pb, ((gp - kPB) / kPB) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort);
           w = __all_sync(0xffffffffu, w);
           if (!w) {
             ok = false;
@@ -452,9 +460,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
         ++gs;
         ++gp;
       }
-      // all of this item's PV tiles complete: first gp-2 through its P buffer
-      // barrier (at most one use outstanding there), then gp-1 through o_full
-      if (ok && gp >= 2) {
+      // all of this item's PV tiles complete: with two P buffers first gp-2
+      // through its P buffer barrier (at most one use outstanding there),
+      // then gp-1 through o_full
+      if (ok && C::kPBufs == 2 && gp >= 2) {
         bool w = mbar_wait(bb.p_empty0 + 8 * (gp & 1), ((gp - 2) >> 1) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort);
         ok = __all_sync(0xffffffffu, w);
       }
@@ -528,14 +537,19 @@ struct Bwd {
   static constexpr uint32_t kRow = F::kRow, kSwz = F::kSwz, kSbo = F::kSbo, kVLbo = F::kVLbo;
   static constexpr uint32_t kTile128 = 128 * HD * 2;  // 128 rows x HD
   static constexpr uint32_t kTile64 = 64 * HD * 2;    // 64 rows x HD
-  // dQ kernel smem: Q (kQBufs) | dO (kQBufs) | K ring | V ring | dS x2 | barriers
+  // dQ kernel smem: Q (kQBufs) | dO (kQBufs) | K ring | V ring | dS (kDSBufs) | barriers.
+  // As in the forward, the K/V ring has to run a tile ahead of the MMA warp
+  // (tile j + kKVStages loads once the dQ MMA of tile j completes): HD = 64
+  // holds three stages and one dS buffer (the dS of tile j+1 is written
+  // after the dQ MMA of tile j completes, which it has by then).
   static constexpr int kQBufs = HD == 32 ? 2 : 1;
-  static constexpr int kKVStages = HD == 32 ? 4 : 2;
+  static constexpr int kKVStages = HD == 32 ? 4 : 3;
+  static constexpr int kDSBufs = HD == 32 ? 2 : 1;
   static constexpr uint32_t kQ_OffDO = kQBufs * kTile128;
   static constexpr uint32_t kQ_OffK = 2 * kQBufs * kTile128;
   static constexpr uint32_t kQ_OffV = kQ_OffK + kKVStages * kTile64;
   static constexpr uint32_t kQ_OffS = kQ_OffV + kKVStages * kTile64;
-  static constexpr uint32_t kQ_OffBar = kQ_OffS + 2 * kPBytes;
+  static constexpr uint32_t kQ_OffBar = kQ_OffS + kDSBufs * kPBytes;
   static constexpr uint32_t kQ_Smem = 1024 + kQ_OffBar + 32 * 8 + 32;
   // dK/dV kernel smem: K | V | Q ring | dO ring | P^T (kPBufs) | dS^T (kPBufs) |
   // per-warp lse/D (8 warps x 2 x 32 floats) | barriers
@@ -779,8 +793,8 @@ __global__ void __launch_bounds__(kThreadsBwd, kCtasPerSm)
           } else {
             umma_commit(q_empty0 + 8 * qb);  // every MMA reading Q / dO of this item issued
           }
-          const int pb = gp & 1;
-          if (!mbar_wait(p_full0 + 8 * pb, (gp >> 1) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort)) {
+          const int pb = gp % C::kDSBufs;
+          if (!mbar_wait(p_full0 + 8 * pb, (gp / C::kDSBufs) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort)) {
             ok = false;
             break;
           }
@@ -851,9 +865,10 @@ __global__ void __launch_bounds__(kThreadsBwd, kCtasPerSm)
           else
             bwd_cols<T, 32, false, true>(sv, dv, 32 * ch, c_log2, nullptr, nullptr, -lse_r, -d_r, valid, nullptr, dw);
         }
-        const int pb = gp & 1;
-        if (gp >= 2) {
-          w = mbar_wait(p_empty0 + 8 * pb, ((gp - 2) >> 1) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort);
+        constexpr int kDS = C::kDSBufs;
+        const int pb = gp % kDS;
+        if (gp >= kDS) {  // the dQ MMA of tile gp - kDS has read this dS buffer
+          w = mbar_wait(p_empty0 + 8 * pb, ((gp - kDS) / kDS) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort);
           w = __all_sync(0xffffffffu, w);
           if (!w) {
             ok = false;

@@ -391,11 +391,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm)
           mx4[((k >> 1) + 2) & 3] = fmax3(mx4[((k >> 1) + 2) & 3], __uint_as_float(rb[k]), __uint_as_float(rb[k + 1]));
         }
         const float mt = fmax3(fmaxf(mx4[0], mx4[1]), mx4[2], mx4[3]) * c_log2;
-        // P buffer free (PV tile gp - kPBufs done): after this wait at most one
-        // PV (gp-1) is outstanding, so the o_full parity wait below is unambiguous
+        // P buffer free (PV tile gp - kPBufs done), and at most one PV (gp-1)
+        // outstanding, so the o_full parity wait below is unambiguous. With two
+        // buffers the S_gp just read implies it: the MMA warp committed S_gp
+        // after issuing PV_{gp-2}, and a commit tracks every earlier MMA of
+        // the issuing thread. One buffer needs PV_{gp-1}: wait for it.
         constexpr int kPB = C::kPBufs;
         const int pb = gp % kPB;
-        if (gp >= kPB) {
+        if (kPB == 1 && gp >= 1) {
           w = mbar_wait(bb.p_empty0 + 8 * pb, ((gp - kPB) / kPB) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort);
           w = __all_sync(0xffffffffu, w);
           if (!w) {
@@ -867,7 +870,10 @@ __global__ void __launch_bounds__(kThreadsBwd, kCtasPerSm)
         }
         constexpr int kDS = C::kDSBufs;
         const int pb = gp % kDS;
-        if (gp >= kDS) {  // the dQ MMA of tile gp - kDS has read this dS buffer
+        // the dQ MMA of tile gp - kDS has read this dS buffer: implied for two
+        // buffers by S_gp (committed after the dQ MMA of tile gp - 2 was
+        // issued), waited for with one
+        if (kDS == 1 && gp >= 1) {
           w = mbar_wait(p_empty0 + 8 * pb, ((gp - kDS) / kDS) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort);
           w = __all_sync(0xffffffffu, w);
           if (!w) {
@@ -1155,8 +1161,11 @@ __global__ void __launch_bounds__(kThreadsBwd, kCtasPerSm)
             bwd_cols<T, 16, true, false>(sv, dv, c0, c_log2, lrow, lrow + 32, 0.f, 0.f, valid, pw, dw);
           else
             bwd_cols<T, 16, true, true>(sv, dv, c0, c_log2, lrow, lrow + 32, 0.f, 0.f, valid, pw, dw);
-          if (piece == 0 && gp >= kPB) {
-            w = mbar_wait(p_empty0 + 8 * pb, ((gp - kPB) / kPB) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort);
+          // the dV / dK MMAs of tile gp - kPB have read these buffers: implied
+          // for two buffers by S^T_gp (committed after those MMAs of tile
+          // gp - 2 were issued), waited for with one
+          if (piece == 0 && kPB == 1 && gp >= 1) {
+            w = mbar_wait(p_empty0 + 8 * pb, (gp - 1) & 1, status, RK_DEV_ATTN_TIMEOUT, s_abort);
             w = __all_sync(0xffffffffu, w);
             if (!w) {
               ok = false;

@@ -185,8 +185,9 @@ RK_API int rk_gemm_dgrad(const void* dy, int64_t lddy, const void* w, int64_t ld
 /* Attention output projection's dgrad with the attention backward's
  * D = rowsum(dO * O) in its epilogue (model.py:45 backward and the D term of
  * F.scaled_dot_product_attention's backward): DX[M,K] = DY[M,N] . W[N,K] as
- * rk_gemm_dgrad (16-bit, dtype), and dsum[b, h, t] = sum over head h's 32
- * columns of DX[b*T + t] * O[b*T + t] with O [M, K], K = H * 32, M = B * T;
+ * rk_gemm_dgrad (16-bit, dtype), and dsum[b, h, t] = sum over head h's
+ * columns of DX[b*T + t] * O[b*T + t] with O [M, K], K = H * 32 or H * 64,
+ * M = B * T;
  * bit-identical to rk_gemm_dgrad followed by rk_attn_bwd_piece(0). Returns
  * RK_ERR_UNSUPPORTED when the layout does not fit the TMA epilogue. */
 /* Sublayer output projection with the reversible state update in its

@@ -62,11 +62,12 @@ struct GemmArgs {
   int vocab;              // EPI_LSE / XF: valid vocabulary entries
   int tokens;             // XF: valid token rows
   // EPI_TMA_DSUM (attention output projection's dgrad): D[b, h, t] =
-  // rowsum over head h's 32 columns of round(dx) * o
+  // rowsum over head h's 32 or 64 columns of round(dx) * o
   const void* dsum_o;     // o [M, N] (16-bit, row stride dsum_ldo)
   int64_t dsum_ldo;
   float* dsum;            // [B, H, T], M = B * T
   int dsum_T, dsum_H;
+  int dsum_hw;            // head width: 32 (two heads per 64-column chunk) or 64 (one)
   // EPI_RECON (sublayer output projection with the reversible state update):
   // rc_out[r, c] = rc_state[r, c] - round(rc_coeff * round(round(acc) + rc_add[r, c]))
   const float* rc_state;  // fp32 [M, N], row stride rc_lds
@@ -1050,9 +1051,10 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
         // Each warp stages its 32 rows, CW columns at a time, in a 128-byte
         // swizzled layout (16-byte chunk j of row r at j ^ (r % 8): conflict-free
         // stores) and writes them with one TMA store per chunk. DSUM: each
-        // 64-column chunk is two 32-column heads; D = rowsum(round(acc) * o)
-        // per head in dsum_kernel's order (two 16-column halves summed
-        // separately, then added), o read while the TMEM load is in flight.
+        // 64-column chunk is two 32-column heads or one 64-column head;
+        // D = rowsum(round(acc) * o) per head in dsum_kernel's order (the two
+        // column halves of a head summed separately, then added), o read
+        // while the TMEM load is in flight.
         constexpr int CW = 128 / (int)sizeof(TOut);
         constexpr int HALF = BN / 2;
         static_assert(HALF % CW == 0, "column half must be whole staging boxes");
@@ -1066,7 +1068,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           uint4 ov[EPI == EPI_TMA_DSUM ? 8 : 1];
           const int drow = m0 + quarter * 32 + lane;
           if constexpr (EPI == EPI_TMA_DSUM) {
-            static_assert(sizeof(TOut) == 2 && CW == 64, "16-bit output, two 32-column heads per chunk");
+            static_assert(sizeof(TOut) == 2 && CW == 64, "16-bit output, 64-column chunks");
             const uint4* op =
                 reinterpret_cast<const uint4*>(static_cast<const TOut*>(g.dsum_o) + (int64_t)drow * g.dsum_ldo + n0 + c);
 #pragma unroll
@@ -1093,7 +1095,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
               raw = make_uint4(r[j * 4], r[j * 4 + 1], r[j * 4 + 2], r[j * 4 + 3]);
             }
             if constexpr (EPI == EPI_TMA_DSUM) {
-              float& a = dacc[j >> 2][(j & 3) >> 1];
+              // 32-column heads: head j / 4, half (j % 4) / 2; 64-column: half j / 4
+              float& a = g.dsum_hw == 32 ? dacc[j >> 2][(j & 3) >> 1] : dacc[0][j >> 2];
               const uint32_t dw[4] = {raw.x, raw.y, raw.z, raw.w};
               const uint32_t owd[4] = {ov[j].x, ov[j].y, ov[j].z, ov[j].w};
 #pragma unroll
@@ -1105,10 +1108,14 @@ __global__ void __launch_bounds__(gemm_threads(EPI), 1)
           if constexpr (EPI == EPI_TMA_DSUM) {
             if (drow < g.M) {
               const int b = drow / g.dsum_T, t = drow - b * g.dsum_T;
-              const int h0 = (n0 + c) >> 5;
+              if (g.dsum_hw == 32) {
+                const int h0 = (n0 + c) >> 5;
 #pragma unroll
-              for (int hh = 0; hh < 2; ++hh)
-                g.dsum[((int64_t)b * g.dsum_H + h0 + hh) * g.dsum_T + t] = dacc[hh][0] + dacc[hh][1];
+                for (int hh = 0; hh < 2; ++hh)
+                  g.dsum[((int64_t)b * g.dsum_H + h0 + hh) * g.dsum_T + t] = dacc[hh][0] + dacc[hh][1];
+              } else {
+                g.dsum[((int64_t)b * g.dsum_H + ((n0 + c) >> 6)) * g.dsum_T + t] = dacc[0][0] + dacc[0][1];
+              }
             }
           }
           fence_proxy_async_smem();
@@ -1615,8 +1622,9 @@ int tc_gemm(Operand a, Operand b, int M, int N, int K, int dtype, void* out, int
   }
   const bool tma_out = rk_host::aligned(out, 16) && (ldo * (int64_t)osz) % 16 == 0 &&
                        make_out_map(&tc, out, (uint64_t)N, (uint64_t)M, (uint64_t)ldo, out_dtype);
-  if (dsum) {  // output projection dgrad with D = rowsum(dO * O) per 32-column head
-    if (!tma_out || BN != 256 || N % 64 || out_dtype != dtype || !dsum_o || dsum_T <= 0 || dsum_H * 32 != N ||
+  if (dsum) {  // output projection dgrad with D = rowsum(dO * O) per 32- or 64-column head
+    if (!tma_out || BN != 256 || N % 64 || out_dtype != dtype || !dsum_o || dsum_T <= 0 || dsum_H <= 0 ||
+        (dsum_H * 32 != N && dsum_H * 64 != N) ||
         M % dsum_T || !rk_host::aligned(dsum_o, 16) || (dsum_ldo * 2) % 16)
       return RK_ERR_UNSUPPORTED;
     g.dsum_o = dsum_o;
@@ -1624,6 +1632,7 @@ int tc_gemm(Operand a, Operand b, int M, int N, int K, int dtype, void* out, int
     g.dsum = dsum;
     g.dsum_T = dsum_T;
     g.dsum_H = dsum_H;
+    g.dsum_hw = N / dsum_H;
     if (out_dtype == RK_BF16) return dispatch_major<256, EPI_TMA_DSUM, __nv_bfloat16>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
     if (out_dtype == RK_F16) return dispatch_major<256, EPI_TMA_DSUM, __half>(ta, tb, tc, mn_a, mn_b, g, dtype, s);
     return RK_ERR_DTYPE;
@@ -1753,9 +1762,9 @@ extern "C" int rk_gemm_dgrad_dsum(const void* dy, int64_t lddy, const void* w, i
                                   int64_t M, int64_t N, int64_t K, int dtype, const void* o, int64_t ldo, float* dsum,
                                   int64_t T, int64_t H, void* stream) {
   // DX[M,K] = DY[M,N] . W[N,K] as rk_gemm_dgrad (16-bit out), and D[b, h, t] =
-  // sum over head h's 32 columns of DX * O, O [M, K] with K = H * 32.
+  // sum over head h's columns of DX * O, O [M, K] with K = H * 32 or H * 64.
   if (!dy || !w || !dx || !o || !dsum || !dims_ok(M, K, N) || lddy < N || ldw < K || lddx < K || ldo < K || N == 0 ||
-      K == 0 || T <= 0 || H <= 0 || K != H * 32 || M % T)
+      K == 0 || T <= 0 || H <= 0 || (K != H * 32 && K != H * 64) || M % T)
     return RK_ERR_ARG;
   if (dtype != RK_BF16 && dtype != RK_F16) return RK_ERR_DTYPE;
   if (M == 0) return RK_OK;

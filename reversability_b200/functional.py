@@ -185,13 +185,14 @@ def linear_dgrad(dy: torch.Tensor, w: torch.Tensor, out_dtype: torch.dtype | Non
 
 def linear_dgrad_dsum(dy: torch.Tensor, w: torch.Tensor, o: torch.Tensor, n_heads: int, length: int):
     """(do, dsum) with do = dy @ w (16-bit, as linear_dgrad) and the attention
-    backward's D = rowsum(do * o) per 32-wide head, [B, H, T] fp32, formed in
-    the GEMM epilogue; None when the shapes do not fit that epilogue.
-    dy [M, N], w [N, K], o [M, K] with K = n_heads * 32, M = B * length."""
+    backward's D = rowsum(do * o) per head (32 or 64 wide), [B, H, T] fp32,
+    formed in the GEMM epilogue; None when the shapes do not fit that epilogue.
+    dy [M, N], w [N, K], o [M, K] with K = n_heads * (32 or 64), M = B * length."""
     require_cuda(dy, w, o)
     M, N = dy.shape
     K = w.shape[1]
-    if dy.dtype not in _TC_DTYPES or w.dtype != dy.dtype or o.dtype != dy.dtype or K != 32 * n_heads or \
+    if dy.dtype not in _TC_DTYPES or w.dtype != dy.dtype or o.dtype != dy.dtype or \
+            K not in (32 * n_heads, 64 * n_heads) or \
             M % length or not (dy.is_contiguous() and w.is_contiguous() and o.is_contiguous()):
         return None
     do = torch.empty((M, K), device=dy.device, dtype=dy.dtype)

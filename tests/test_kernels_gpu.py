@@ -542,13 +542,13 @@ def test_rmsnorm_bwd_fused_deferred_dw_reduce_bitwise():
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("B,T", [(29, 512), (3, 64), (5, 100)])
-def test_dgrad_dsum_fused_bitwise(dtype, B, T):
+@pytest.mark.parametrize("B,T,H,d", [(29, 512, 8, 256), (3, 64, 8, 256), (5, 100, 8, 256), (2, 2048, 16, 1024),
+                                     (3, 100, 4, 256)])
+def test_dgrad_dsum_fused_bitwise(dtype, B, T, H, d):
     """rk_gemm_dgrad_dsum: the output projection's dgrad equals rk_gemm_dgrad
-    and its D = rowsum(dO * O) per head equals the D kernel of the attention
-    backward, bit for bit (ragged row tiles included)."""
+    and its D = rowsum(dO * O) per head (32 or 64 wide) equals the D kernel of
+    the attention backward, bit for bit (ragged row tiles included)."""
     from reversability_b200 import _lib, functional as fn
-    H, d = 8, 256
     M = B * T
     g = torch.Generator(device="cpu").manual_seed(B * T)
     ga = (torch.randn(M, d, generator=g) * 0.1).to(DEV, dtype)

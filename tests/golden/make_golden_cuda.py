@@ -3,7 +3,7 @@ autocast — the precision mode the reference trains in (train_baseline.py:
 205-207) and which it enables only on CUDA, so these cannot be made on a CPU.
 
     python tests/golden/make_golden_cuda.py --reference baseline/_ref \
-        --out gpurun_out/golden_cuda_bf16.pt
+        --out tests/golden/cuda_bf16.pt
 
 `--reference` is a directory holding the unmodified reference package
 `reversibility` (an install of its src/reversibility). The microstep is the

@@ -345,8 +345,11 @@ __device__ __forceinline__ void swiglu_bwd_word(uint32_t& gw, uint32_t& vw, uint
 __device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
   const float mn = fmaxf(m, m2);
   if (mn == -INFINITY) return;
-  s = (m == -INFINITY ? 0.f : s * ex2_fast((m - mn) * kLog2eF)) +
-      (m2 == -INFINITY ? 0.f : s2 * ex2_fast((m2 - mn) * kLog2eF));
+  // one exponential: the sum with the smaller max is scaled to the larger one
+  const bool first = m >= m2;
+  const float lo = first ? m2 : m, slo = first ? s2 : s, shi = first ? s : s2;
+  const float e = lo == -INFINITY ? 0.f : ex2_fast((lo - mn) * kLog2eF);
+  s = __fadd_rn(shi, __fmul_rn(slo, e));
   m = mn;
 }
 

@@ -332,8 +332,17 @@ class ReversibleTrainer:
                 after_head()
             fn.head_loss(st, 1.0, self.inv_denominator, loss_rows=loss_rows, rowc=self.head_rowc,
                          fcoef=self.head_fcoef)
-            self.loss_sum += loss_rows.sum()
-            self._loss_bucket(last)
+            if kern.side is not None:
+                # the loss sum (and its data-parallel bucket) off the dgrad's path
+                with kern.side_work():
+                    self.loss_sum += loss_rows.sum()
+                    loss_done = torch.cuda.Event()
+                    loss_done.record()
+                if last and self.world > 1:
+                    self.buckets.launch(len(self.layers) + 3, after=[loss_done])
+            else:
+                self.loss_sum += loss_rows.sum()
+                self._loss_bucket(last)
             g_head = self.g_head if self.g_head is not None else self.g_tok
             if kern.side is not None:
                 # the head weight gradient runs beside the dgrad and the

@@ -354,13 +354,29 @@ RK_API int rk_adamw_step(float* params, const float* grads, float* exp_avg, floa
  * p = q = embedding receives, reversible.py:91) into g_tok [V, d] and g_pos [>= T, d] (fp32) in a fixed
  * order: rows are grouped by id with a stable radix sort and each group is
  * summed in row order, so results are bitwise reproducible. workspace: at
- * least rk_embedding_bwd_workspace(rows, V) bytes. d must be a multiple of 4. */
+ * least rk_embedding_bwd_workspace(rows, V) bytes, 16-byte aligned. d must be
+ * a multiple of 4. */
 RK_API int rk_embedding_fwd(const int64_t* ids, const float* tok, const float* pos, float* out, int64_t rows,
                             int64_t T, int64_t d, int64_t V, void* stream);
 RK_API int64_t rk_embedding_bwd_workspace(int64_t rows, int64_t V);
 RK_API int rk_embedding_bwd(const int64_t* ids, const float* dx, const float* dx2, float* g_tok, float* g_pos,
                             int64_t rows, int64_t T, int64_t d, int64_t V, void* workspace, int64_t workspace_bytes,
                             void* stream);
+/* rk_embedding_bwd in two calls. The grouping of rows by id depends on the ids
+ * alone, so a caller can issue it early on another stream, off the path of
+ * the backward: rk_embedding_bwd_sort writes it into `sorted` (at least
+ * rk_embedding_bwd_sort_bytes(rows, V) bytes, 16-byte aligned, left untouched
+ * until the matching rk_embedding_bwd_sorted has run), and
+ * rk_embedding_bwd_sorted accumulates dx (+ dx2) into g_tok and g_pos from it,
+ * with a workspace of at least rk_embedding_bwd_sorted_workspace(rows, d)
+ * bytes. Same results as rk_embedding_bwd, bit for bit. */
+RK_API int64_t rk_embedding_bwd_sort_bytes(int64_t rows, int64_t V);
+RK_API int rk_embedding_bwd_sort(const int64_t* ids, int64_t rows, int64_t V, void* sorted, int64_t sorted_bytes,
+                                 void* stream);
+RK_API int64_t rk_embedding_bwd_sorted_workspace(int64_t rows, int64_t d);
+RK_API int rk_embedding_bwd_sorted(const void* sorted, int64_t sorted_bytes, const float* dx, const float* dx2,
+                                   float* g_tok, float* g_pos, int64_t rows, int64_t T, int64_t d, int64_t V,
+                                   void* workspace, int64_t workspace_bytes, void* stream);
 
 /* ------------------------------------------------------------- Reversible layer
  * One reversible Block step as a single call: the per-layer sequence of the

@@ -62,6 +62,10 @@ SIGNATURES: dict[str, tuple] = {
     "rk_embedding_fwd": (_i, [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _p]),
     "rk_embedding_bwd_workspace": (_i64, [_i64, _i64]),
     "rk_embedding_bwd": (_i, [_p, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _p]),
+    "rk_embedding_bwd_sort_bytes": (_i64, [_i64, _i64]),
+    "rk_embedding_bwd_sort": (_i, [_p, _i64, _i64, _p, _i64, _p]),
+    "rk_embedding_bwd_sorted_workspace": (_i64, [_i64, _i64]),
+    "rk_embedding_bwd_sorted": (_i, [_p, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _p, _i64, _p]),
     "rk_layer_workspace": (_i64, [_p, _i, _i]),
     "rk_layer_fwd_midpoint": (_i, [_p, _p, _p, _f, _p, _p, _i64, _p]),
     "rk_layer_fwd_euler": (_i, [_p, _p, _p, _p, _p, _p, _i64, _p]),

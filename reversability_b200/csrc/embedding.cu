@@ -7,8 +7,13 @@
 //   1. rows are sorted by token id with a stable radix sort (CUB, keys = ids,
 //      values = row indices), so equal ids become contiguous runs in row order;
 //   2. each run is summed in two fixed-order passes (per-32-row pieces, then
-//      the pieces of a run in order) and added into g_tok[id];
-//   3. one CTA per position t sums dx[b*T + t] over b in order into g_pos[t].
+//      the pieces of a run in order, one warp per run) and added into g_tok[id];
+//   3. one thread per (position t, 4 columns) sums dx[b*T + t] over b in
+//      order into g_pos[t].
+// Step 1 depends on the ids alone: rk_embedding_bwd_sort runs it by itself
+// (a caller can issue it early, on another stream) and
+// rk_embedding_bwd_sorted runs steps 2 and 3 from its result;
+// rk_embedding_bwd is the two in sequence.
 // The row cotangent is dx (+ dx2 when given: the boundary state p = q = x of
 // the reversible stack receives one cotangent through each).
 // Ids outside [0, V) set RK_DEV_EMB_INDEX and contribute nothing.
@@ -119,15 +124,21 @@ __global__ void __launch_bounds__(256) emb_tok_piece_kernel(const int64_t* __res
   }
 }
 
+// Pass 2: the warp of each run start (one warp per sorted position) adds the
+// pieces of its run, one per 32-row range it overlaps, in range order into
+// g_tok; each lane owns 4 consecutive columns per step (16-byte piece loads,
+// eight pieces in flight).
 __global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restrict__ skeys,
                                                           const float* __restrict__ piece, float* __restrict__ g_tok,
                                                           int64_t rows, int d, int64_t V, unsigned int* status) {
   pdl_wait();  // inputs are the previous kernel's outputs
-  const int64_t i = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int64_t i = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (i >= rows) return;
   const int64_t id = skeys[i];
   if (i > 0 && skeys[i - 1] == id) return;
   if (id < 0 || id >= V) {
-    if (threadIdx.x == 0) flag_error(status, RK_DEV_EMB_INDEX);
+    if (lane == 0) flag_error(status, RK_DEV_EMB_INDEX);
     return;
   }
   int64_t lo = i + 1, hi = rows;  // run end: first index with a different key
@@ -136,40 +147,72 @@ __global__ void __launch_bounds__(256) emb_tok_bwd_kernel(const int64_t* __restr
     if (skeys[mid] == id) lo = mid + 1; else hi = mid;
   }
   const int64_t end = lo;
-  // one piece per 32-row range of the run, summed in range order with eight
-  // loads in flight
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    float s = 0.f;
+  for (int c = lane * 4; c < d; c += 128) {
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
     int64_t p = i;
     while (p < end) {
-      float t[8];
+      float t[8][4];
       int cnt = 0;
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        t[u] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) t[u][e] = 0.f;
         if (p < end) {
-          t[u] = piece[p * d + c];
+          load_vec<float, 4>(piece + p * d + c, t[u]);
           p = (p / 32 + 1) * 32;
           ++cnt;
         }
       }
 #pragma unroll
       for (int u = 0; u < 8; ++u)
-        if (u < cnt) s += t[u];
+        if (u < cnt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) s[e] += t[u][e];
+        }
     }
-    g_tok[id * d + c] += s;
+    float* g = g_tok + id * d + c;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) g[e] += s[e];
   }
 }
 
+// g_pos[t] += sum over b of dx[b*T + t] (+ dx2), in b order; one thread per
+// (position, 4 columns), eight rows in flight.
 __global__ void __launch_bounds__(256) emb_pos_bwd_kernel(const float* __restrict__ dx, const float* __restrict__ dx2,
                                                           float* __restrict__ g_pos, int64_t rows, int T, int d) {
   pdl_wait();  // inputs are the previous kernel's outputs
-  const int t = blockIdx.x;
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    float s = 0.f;
-    for (int64_t r = t; r < rows; r += T) s += dx2 ? dx[r * d + c] + dx2[r * d + c] : dx[r * d + c];
-    g_pos[(int64_t)t * d + c] += s;
+  const int q = d / 4;
+  const int64_t item = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (item >= (int64_t)T * q) return;
+  const int t = (int)(item / q), c = (int)(item % q) * 4;
+  float s[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int64_t r0 = t; r0 < rows; r0 += 8 * (int64_t)T) {
+    float v[8][4];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t r = r0 + u * (int64_t)T;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[u][e] = 0.f;
+      if (r < rows) {
+        load_vec<float, 4>(dx + r * d + c, v[u]);
+        if (dx2) {
+          float v2[4];
+          load_vec<float, 4>(dx2 + r * d + c, v2);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) v[u][e] = v[u][e] + v2[e];
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u)
+      if (r0 + u * (int64_t)T < rows) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) s[e] += v[u][e];
+      }
   }
+  float* g = g_pos + (int64_t)t * d + c;
+#pragma unroll
+  for (int e = 0; e < 4; ++e) g[e] += s[e];
 }
 
 }  // namespace rk
@@ -204,10 +247,97 @@ extern "C" int rk_embedding_fwd(const int64_t* ids, const float* tok, const floa
   return rk_host::launch_status();
 }
 
+namespace {
+// The sort results lead the buffer (read by the second phase); the unsorted
+// keys, row indices and the sort's temporary storage follow.
+struct SortLayout {
+  int64_t* skeys;
+  int* srows;
+  int64_t* keys;
+  int* rows_in;
+  void* temp;
+  size_t temp_bytes;
+};
+size_t sort_bytes(int64_t rows, int64_t V) {
+  return 2 * align256(rows * sizeof(int64_t)) + 2 * align256(rows * sizeof(int)) + align256(cub_temp_bytes(rows, V));
+}
+SortLayout sort_layout(void* buf, int64_t rows, int64_t V) {
+  uint8_t* w = static_cast<uint8_t*>(buf);
+  SortLayout l;
+  l.skeys = reinterpret_cast<int64_t*>(w);
+  w += align256(rows * sizeof(int64_t));
+  l.srows = reinterpret_cast<int*>(w);
+  w += align256(rows * sizeof(int));
+  l.keys = reinterpret_cast<int64_t*>(w);
+  w += align256(rows * sizeof(int64_t));
+  l.rows_in = reinterpret_cast<int*>(w);
+  w += align256(rows * sizeof(int));
+  l.temp = w;
+  l.temp_bytes = cub_temp_bytes(rows, V);
+  return l;
+}
+}  // namespace
+
+extern "C" int64_t rk_embedding_bwd_sort_bytes(int64_t rows, int64_t V) {
+  if (rows <= 0 || V <= 0 || rows >= (1ll << 31)) return 0;
+  return (int64_t)sort_bytes(rows, V);
+}
+
+extern "C" int rk_embedding_bwd_sort(const int64_t* ids, int64_t rows, int64_t V, void* sorted, int64_t sorted_bytes,
+                                     void* stream) {
+  if (!ids || rows < 0 || V <= 0 || rows >= (1ll << 31)) return RK_ERR_ARG;
+  if (rows == 0) return RK_OK;
+  if (!sorted || sorted_bytes < rk_embedding_bwd_sort_bytes(rows, V)) return RK_ERR_WORKSPACE;
+  if (!rk_host::aligned(sorted, 16)) return RK_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SortLayout l = sort_layout(sorted, rows, V);
+  rk_host::launch_k(keys_kernel, (unsigned)((rows + 255) / 256), 256, 0, s, ids, l.keys, l.rows_in, rows, V);
+  int st = rk_host::launch_status();
+  if (st) return st;
+  size_t temp = l.temp_bytes;
+  if (cub::DeviceRadixSort::SortPairs(l.temp, temp, l.keys, l.skeys, l.rows_in, l.srows, (int)rows, 0,
+                                      key_bits(V + 1), s) != cudaSuccess)
+    return RK_ERR_LAUNCH;
+  rk_host::count_launch();
+  return RK_OK;
+}
+
+extern "C" int64_t rk_embedding_bwd_sorted_workspace(int64_t rows, int64_t d) {
+  if (rows <= 0 || d <= 0) return 0;
+  return (int64_t)align256(rows * 4 * (size_t)d);
+}
+
+extern "C" int rk_embedding_bwd_sorted(const void* sorted, int64_t sorted_bytes, const float* dx, const float* dx2,
+                                       float* g_tok, float* g_pos, int64_t rows, int64_t T, int64_t d, int64_t V,
+                                       void* workspace, int64_t workspace_bytes, void* stream) {
+  if (!dx || !g_tok || !g_pos || rows < 0 || T <= 0 || d <= 0 || V <= 0 || rows >= (1ll << 31)) return RK_ERR_ARG;
+  if (d > kMaxEmbWidth) return RK_ERR_UNSUPPORTED;
+  if (d % 4 || !rk_host::aligned(dx, 16) || (dx2 && !rk_host::aligned(dx2, 16))) return RK_ERR_ALIGN;
+  if (rows == 0) return RK_OK;
+  if (!sorted || sorted_bytes < rk_embedding_bwd_sort_bytes(rows, V)) return RK_ERR_WORKSPACE;
+  if (!workspace || workspace_bytes < rk_embedding_bwd_sorted_workspace(rows, d)) return RK_ERR_WORKSPACE;
+  if (!rk_host::aligned(sorted, 16) || !rk_host::aligned(workspace, 16)) return RK_ERR_ALIGN;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  SortLayout l = sort_layout(const_cast<void*>(sorted), rows, V);
+  float* piece = static_cast<float*>(workspace);
+  const int64_t piece_warps = (rows + 31) / 32 * ((d + 127) / 128);
+  rk_host::launch_k(emb_tok_piece_kernel, (unsigned)((piece_warps + 7) / 8), 256, 0, s, l.skeys, l.srows, dx, dx2,
+                    piece, rows, (int)d);
+  int st = rk_host::launch_status();
+  if (st) return st;
+  rk_host::launch_k(emb_tok_bwd_kernel, (unsigned)((rows + 7) / 8), 256, 0, s, l.skeys, piece, g_tok, rows, (int)d, V,
+                    rk_host::device_status_ptr());
+  st = rk_host::launch_status();
+  if (st) return st;
+  const int64_t items = T * (d / 4);
+  rk_host::launch_k(emb_pos_bwd_kernel, (unsigned)((items + 255) / 256), 256, 0, s, dx, dx2, g_pos, rows, (int)T,
+                    (int)d);
+  return rk_host::launch_status();
+}
+
 extern "C" int64_t rk_embedding_bwd_workspace(int64_t rows, int64_t V) {
-  if (rows <= 0 || V <= 0) return 0;
-  return (int64_t)(2 * align256(rows * sizeof(int64_t)) + 2 * align256(rows * sizeof(int)) +
-                   align256(cub_temp_bytes(rows, V)) + align256(rows * 4 * (size_t)kMaxEmbWidth));
+  if (rows <= 0 || V <= 0 || rows >= (1ll << 31)) return 0;
+  return (int64_t)(sort_bytes(rows, V) + align256(rows * 4 * (size_t)kMaxEmbWidth));
 }
 
 extern "C" int rk_embedding_bwd(const int64_t* ids, const float* dx, const float* dx2, float* g_tok, float* g_pos,
@@ -219,33 +349,10 @@ extern "C" int rk_embedding_bwd(const int64_t* ids, const float* dx, const float
   if (d % 4 || !rk_host::aligned(dx, 16) || (dx2 && !rk_host::aligned(dx2, 16))) return RK_ERR_ALIGN;
   if (rows == 0) return RK_OK;
   if (!workspace || workspace_bytes < rk_embedding_bwd_workspace(rows, V)) return RK_ERR_WORKSPACE;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  uint8_t* w = static_cast<uint8_t*>(workspace);
-  int64_t* keys = reinterpret_cast<int64_t*>(w);
-  w += align256(rows * sizeof(int64_t));
-  int64_t* skeys = reinterpret_cast<int64_t*>(w);
-  w += align256(rows * sizeof(int64_t));
-  int* rows_in = reinterpret_cast<int*>(w);
-  w += align256(rows * sizeof(int));
-  int* srows = reinterpret_cast<int*>(w);
-  w += align256(rows * sizeof(int));
-  size_t temp = cub_temp_bytes(rows, V);
-  float* piece = reinterpret_cast<float*>(w + align256(temp));
-  rk_host::launch_k(keys_kernel, (unsigned)((rows + 255) / 256), 256, 0, s, ids, keys, rows_in, rows, V);
-  int st = rk_host::launch_status();
+  if (!rk_host::aligned(workspace, 16)) return RK_ERR_ALIGN;
+  const int64_t sb = (int64_t)sort_bytes(rows, V);
+  int st = rk_embedding_bwd_sort(ids, rows, V, workspace, sb, stream);
   if (st) return st;
-  if (cub::DeviceRadixSort::SortPairs(w, temp, keys, skeys, rows_in, srows, (int)rows, 0, key_bits(V + 1), s) !=
-      cudaSuccess)
-    return RK_ERR_LAUNCH;
-  rk_host::count_launch();
-  const int64_t piece_warps = (rows + 31) / 32 * ((d + 127) / 128);
-  rk_host::launch_k(emb_tok_piece_kernel, (unsigned)((piece_warps + 7) / 8), 256, 0, s, skeys, srows, dx, dx2, piece,
-                    rows, (int)d);
-  st = rk_host::launch_status();
-  if (st) return st;
-  rk_host::launch_k(emb_tok_bwd_kernel, (unsigned)rows, 256, 0, s, skeys, piece, g_tok, rows, (int)d, V, rk_host::device_status_ptr());
-  st = rk_host::launch_status();
-  if (st) return st;
-  rk_host::launch_k(emb_pos_bwd_kernel, (unsigned)T, 256, 0, s, dx, dx2, g_pos, rows, (int)T, (int)d);
-  return rk_host::launch_status();
+  return rk_embedding_bwd_sorted(workspace, sb, dx, dx2, g_tok, g_pos, rows, T, d, V,
+                                 static_cast<uint8_t*>(workspace) + sb, workspace_bytes - sb, stream);
 }

@@ -405,6 +405,34 @@ def embedding_bwd(ids: torch.Tensor, dx: torch.Tensor, g_tok: torch.Tensor, g_po
               B * T, T, d, g_tok.shape[0], ws.data_ptr(), ws_bytes, _lib.stream_ptr())
 
 
+def embedding_bwd_sort(ids: torch.Tensor, vocab: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The first phase of embedding_bwd: the rows of ids [B, T] grouped by id,
+    into a uint8 buffer that embedding_bwd_sorted reads. It depends on the ids
+    alone, so it can be issued early, on another stream."""
+    require_cuda(ids)
+    rows = ids.numel()
+    nbytes = _lib.lib().rk_embedding_bwd_sort_bytes(rows, vocab)
+    if out is None:
+        out = torch.empty(max(nbytes, 1), device=ids.device, dtype=torch.uint8)
+    _lib.call("rk_embedding_bwd_sort", ids.contiguous().data_ptr(), rows, vocab, out.data_ptr(), out.numel(),
+              _lib.stream_ptr())
+    return out
+
+
+def embedding_bwd_sorted(sorted_rows: torch.Tensor, dx: torch.Tensor, g_tok: torch.Tensor, g_pos: torch.Tensor,
+                         T: int, dx2: torch.Tensor | None = None):
+    """The rest of embedding_bwd from embedding_bwd_sort's result (same ids):
+    accumulates dx (+ dx2) [B*T, d] into g_tok and g_pos, bit for bit as
+    embedding_bwd does."""
+    require_cuda(sorted_rows, dx, g_tok, g_pos)
+    rows, d = dx.shape
+    ws_bytes = _lib.lib().rk_embedding_bwd_sorted_workspace(rows, d)
+    ws = torch.empty(max(ws_bytes, 1), device=dx.device, dtype=torch.uint8)
+    _lib.call("rk_embedding_bwd_sorted", sorted_rows.data_ptr(), sorted_rows.numel(), dx.contiguous().data_ptr(),
+              None if dx2 is None else dx2.contiguous().data_ptr(), g_tok.data_ptr(), g_pos.data_ptr(), rows, T, d,
+              g_tok.shape[0], ws.data_ptr(), ws_bytes, _lib.stream_ptr())
+
+
 # ------------------------------------------------------------------ fused reversible-step helpers
 def add_rmsnorm_fwd(x: torch.Tensor, a: torch.Tensor, weight: torch.Tensor, eps: float, out_dtype: torch.dtype,
                     want_sum: bool = False, want_rstd: bool = True):

@@ -151,6 +151,12 @@ class ReversibleTrainer:
         self.loss_sum = torch.zeros((), device=dev, dtype=F32)
         side = torch.cuda.Stream(device=dev) if (dev.type == "cuda" and settings.overlap_wgrad) else None
         self.fwd_stream = torch.cuda.Stream(device=dev) if (dev.type == "cuda" and settings.overlap_forward) else None
+        # the last microstep's rows grouped by id (the first phase of its
+        # embedding backward), written on the forward stream after the later
+        # forward sweeps; _sorted_m names the microstep it holds, per update
+        self.emb_sorted = (torch.empty(max(_lib.lib().rk_embedding_bwd_sort_bytes(self.M, self.cfg.vocab_size), 1),
+                                       device=dev, dtype=torch.uint8) if self.fwd_stream is not None else None)
+        self._sorted_m = None
         self.kern = engine.LayerKernels(self.cfg.n_heads, B, T, self.cd, settings.mlp_tokens, wgrad_stream=side)
         # AdamW state (flat, fp32) and the device scalar block of rk_clip_adamw_prepare
         self.exp_avg = torch.zeros_like(self.flat)
@@ -385,7 +391,10 @@ class ReversibleTrainer:
         # boundary p = q = embedding: both cotangents reach it (summed inside the kernel)
         # (with the tied-gradient split, earlier microsteps scatter into g_head)
         g_emb = self.g_head if (self.g_head is not None and not last) else self.g_tok
-        if not last and kern.side is not None:
+        if self._sorted_m == m:
+            # the id grouping ran on the forward stream, joined before this microstep
+            fn.embedding_bwd_sorted(self.emb_sorted, dp, g_emb, self.g_pos, T, dx2=dq)
+        elif not last and kern.side is not None:
             # before the next microstep's head: on the weight-gradient stream,
             # ahead of that head's weight gradient (the other writer of g_tok)
             with kern.side_work():
@@ -407,6 +416,7 @@ class ReversibleTrainer:
         return len(self.layers) + 4
 
     def _update_body(self):
+        self._sorted_m = None
         self.gflat.zero_()
         if self.g_head is not None:
             self.g_head.zero_()
@@ -428,6 +438,8 @@ class ReversibleTrainer:
                 self.fwd_stream.wait_event(ready)
                 with torch.cuda.stream(self.fwd_stream):
                     later = [self._forward_states(m) for m in range(1, acc)]
+                    fn.embedding_bwd_sort(self.ids[acc - 1], self.cfg.vocab_size, out=self.emb_sorted)
+                    self._sorted_m = acc - 1
                 done = torch.cuda.Event()
                 done.record(self.fwd_stream)
                 states = self._forward_states(0)

@@ -345,6 +345,59 @@ def test_embedding_fwd_bwd_matches_torch_and_is_deterministic(B, T, V):
     assert torch.equal(g1, g2) and torch.equal(p1, p2)
 
 
+def _embedding_bwd_fixed_order(ids, dx, dx2, V, T):
+    """The backward's summation order restated in fp32 (numpy): rows stably
+    sorted by id; per 32-row range of the sorted rows, each run piece summed
+    in row order; a token's pieces summed in range order, then added to g_tok;
+    g_pos[t] the in-order sum over b of (dx + dx2)[b*T + t]."""
+    import numpy as np
+    v = (dx + dx2).cpu().numpy() if dx2 is not None else dx.cpu().numpy()
+    flat = ids.reshape(-1).cpu().numpy()
+    order = np.argsort(flat, kind="stable")
+    keys = flat[order]
+    g = np.zeros((V, v.shape[1]), dtype=np.float32)
+    sums = {}
+    for r0 in range(0, len(keys), 32):
+        j = r0
+        while j < min(r0 + 32, len(keys)):
+            acc = np.zeros(v.shape[1], dtype=np.float32)
+            k = keys[j]
+            while j < min(r0 + 32, len(keys)) and keys[j] == k:
+                acc = acc + v[order[j]]
+                j += 1
+            sums[k] = sums.get(k, np.zeros(v.shape[1], dtype=np.float32)) + acc
+    for k, sv in sums.items():
+        g[k] = g[k] + sv
+    pos = np.zeros((T, v.shape[1]), dtype=np.float32)
+    for b in range(len(flat) // T):
+        pos = pos + v[b * T:(b + 1) * T]
+    return torch.from_numpy(g), torch.from_numpy(pos)
+
+
+@pytest.mark.parametrize("B,T,V", [(29, 512, 50257), (3, 17, 101), (2, 64, 7)])
+def test_embedding_bwd_split_phases_and_fixed_order(B, T, V):
+    """rk_embedding_bwd_sort + rk_embedding_bwd_sorted equal rk_embedding_bwd
+    bit for bit (with both cotangents), and both equal the fixed summation
+    order restated in fp32; the sort buffer is reusable across calls."""
+    from reversability_b200 import functional as fn
+    import numpy as np
+    rng = np.random.default_rng(1)
+    ids = torch.from_numpy(np.minimum(rng.zipf(1.1, size=(B, T)) - 1, V - 1)).to(DEV)
+    d = 256
+    dx, dx2 = torch.randn(B * T, d, device=DEV), torch.randn(B * T, d, device=DEV)
+    g1, p1 = torch.zeros(V, d, device=DEV), torch.zeros(512, d, device=DEV)
+    fn.embedding_bwd(ids, dx, g1, p1, dx2=dx2)
+    srt = fn.embedding_bwd_sort(ids, V)
+    for _ in range(2):
+        g2, p2 = torch.zeros_like(g1), torch.zeros_like(p1)
+        fn.embedding_bwd_sorted(srt, dx, g2, p2, T, dx2=dx2)
+        assert torch.equal(g1, g2) and torch.equal(p1, p2)
+        srt = fn.embedding_bwd_sort(ids, V, out=srt)
+    g_ref, p_ref = _embedding_bwd_fixed_order(ids, dx, dx2, V, T)
+    assert torch.equal(p1[:T].cpu(), p_ref) and torch.count_nonzero(p1[T:]) == 0
+    assert torch.equal(g1.cpu(), g_ref)
+
+
 # ------------------------------------------------------------------ fused reversible-step kernels
 @pytest.mark.parametrize("cd", [torch.bfloat16, torch.float32])
 def test_add_rmsnorm_fwd_matches_unfused(cd):

@@ -341,18 +341,6 @@ __device__ __forceinline__ void swiglu_bwd_word(uint32_t& gw, uint32_t& vw, uint
   vw = pack2_rne_alu<T>(__fmul_rn(d0, unpack_half<T>(sw, 0)), __fmul_rn(d1, unpack_half<T>(sw, 1)));
 }
 
-// (m, s) += (m2, s2) for online log-sum-exp pairs (s = sum of exp(x - m)).
-__device__ __forceinline__ void lse_merge(float& m, float& s, float m2, float s2) {
-  const float mn = fmaxf(m, m2);
-  if (mn == -INFINITY) return;
-  // one exponential: the sum with the smaller max is scaled to the larger one
-  const bool first = m >= m2;
-  const float lo = first ? m2 : m, slo = first ? s2 : s, shi = first ? s : s2;
-  const float e = lo == -INFINITY ? 0.f : ex2_fast((lo - mn) * kLog2eF);
-  s = __fadd_rn(shi, __fmul_rn(slo, e));
-  m = mn;
-}
-
 // One 16-byte chunk (8 entries of one token, vocabulary v0..v0+7) of an A
 // tile, in place: e * f, and the entry at `label` (if in the chunk) set to gl.
 template <typename T>
@@ -2016,42 +2004,43 @@ __global__ void __launch_bounds__(256, 4) head_loss_kernel(const float2* __restr
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * 32;
   if (scale_dev) scale *= *scale_dev;
-  // the warp's four rows warp, warp + 8, .. are read together (16 loads in
-  // flight per lane); each row's entries lane, lane + 32, ... are merged in
-  // that order
-  float m4[4], s4[4];
-#pragma unroll
-  for (int r = 0; r < 4; ++r) {
-    m4[r] = -INFINITY;
-    s4[r] = 0.f;
-  }
-  for (int i0 = lane; i0 < width; i0 += 4 * 32) {
-    float2 p[4][4];
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-      const int row = row0 + warp + 8 * r;
-      const float2* st = stats + (int64_t)row * width;
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        p[r][k] = (row < rows && i0 + 32 * k < width) ? st[i0 + 32 * k] : make_float2(-INFINITY, 0.f);
-    }
-#pragma unroll
-    for (int r = 0; r < 4; ++r) {
-#pragma unroll
-      for (int k = 0; k < 4; ++k) lse_merge(m4[r], s4[r], p[r][k].x, p[r][k].y);
-    }
-  }
-#pragma unroll
+  // Per row (the warp's rows warp, warp + 8, ..), up to 512 entries at a
+  // time, 16 per lane loaded together (entries lane, lane + 32, ..): the
+  // chunk's max over the warp (exact in any order) raises the running max M
+  // (rescaling the lane's sum once when it rises), then each lane adds
+  // s_b * 2^((m_b - M) log2 e) in entry order, and the lanes' sums add in a
+  // fixed butterfly (every lane ends with the same sum).
+  constexpr int kPer = 16;
+#pragma unroll 1
   for (int r = 0; r < 4; ++r) {
     const int rr = warp + 8 * r;
     const int row = row0 + rr;
-    float m = m4[r], s = s4[r];
+    float m = -INFINITY, s = 0.f;
+    if (row < rows) {
+      const float2* st = stats + (int64_t)row * width;
+      for (int c0 = 0; c0 < width; c0 += 32 * kPer) {
+        float2 p[kPer];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
-      const float s2 = __shfl_xor_sync(0xffffffffu, s, o);
-      lse_merge(m, s, m2, s2);
+        for (int k = 0; k < kPer; ++k) {
+          const int i = c0 + lane + 32 * k;
+          p[k] = i < width ? st[i] : make_float2(-INFINITY, 0.f);
+        }
+        float mc = p[0].x;
+#pragma unroll
+        for (int k = 1; k < kPer; ++k) mc = fmaxf(mc, p[k].x);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) mc = fmaxf(mc, __shfl_xor_sync(0xffffffffu, mc, o));
+        const float mn = fmaxf(m, mc);
+        if (mn == -INFINITY) continue;  // warp-uniform: no block with a valid column yet
+        if (mn > m && m != -INFINITY) s = __fmul_rn(s, ex2_fast(__fmul_rn(__fsub_rn(m, mn), kLog2eF)));
+        m = mn;
+#pragma unroll
+        for (int k = 0; k < kPer; ++k)
+          s = __fmaf_rn(p[k].y, ex2_fast(__fmul_rn(__fsub_rn(p[k].x, mn), kLog2eF)), s);
+      }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
     if (row >= rows) {
       if (lane == 0) {
         s_nl[rr] = 0.f;

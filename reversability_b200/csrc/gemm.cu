@@ -2070,39 +2070,36 @@ __global__ void __launch_bounds__(256, 4) head_loss_kernel(const float2* __restr
     }
   }
   __syncthreads();
-  // 128 blocks x 32 rows at a time: row-contiguous reads of m_b (each thread
-  // four in flight), transposed through shared memory, block-contiguous writes
-  __shared__ float s_m[32][129];
+  // fcoef[b][row] for the CTA's rows: lane = row; each warp takes four
+  // consecutive blocks at a time (the row's four (m_b, s) entries are one
+  // 32-byte sector, read as two 16-byte loads) and stores each block's 32
+  // rows contiguously
   const int nrow = min(32, rows - row0);
-  for (int b0 = 0; b0 < width; b0 += 128) {
+  const bool live = lane < nrow;
+  const float nl = s_nl[lane], sc = s_sc[lane];
+  const float2* srow = stats + (int64_t)(row0 + lane) * width;
+  const bool vec = (reinterpret_cast<uintptr_t>(stats) & 15) == 0 && width % 2 == 0;
+  for (int b0 = warp * 4; b0 < width; b0 += 32) {
+    float mb[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    if (live) {
+      if (vec && b0 + 3 < width) {
+        const float4 lo = *reinterpret_cast<const float4*>(srow + b0);
+        const float4 hi = *reinterpret_cast<const float4*>(srow + b0 + 2);
+        mb[0] = lo.x;
+        mb[1] = lo.z;
+        mb[2] = hi.x;
+        mb[3] = hi.z;
+      } else {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int i = threadIdx.x + q * 256;  // 0..1023: (row rr, block pair) of the 32 x 128 tile
-      const int rr = i >> 5, bb = (i & 31) * 4;
-      float4 v = make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
-      if (rr < nrow) {
-        const float2* src = stats + (int64_t)(row0 + rr) * width + b0 + bb;
-        if (b0 + bb < width) v.x = src[0].x;
-        if (b0 + bb + 1 < width) v.y = src[1].x;
-        if (b0 + bb + 2 < width) v.z = src[2].x;
-        if (b0 + bb + 3 < width) v.w = src[3].x;
+        for (int k = 0; k < 4; ++k)
+          if (b0 + k < width) mb[k] = srow[b0 + k].x;
       }
-      s_m[rr][bb] = v.x;
-      s_m[rr][bb + 1] = v.y;
-      s_m[rr][bb + 2] = v.z;
-      s_m[rr][bb + 3] = v.w;
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (b0 + k < width)
+          fcoef[(int64_t)(b0 + k) * fcoef_ld + row0 + lane] =
+              (sc == 0.f || mb[k] == -INFINITY) ? 0.f : ex2_fast(fmaf(mb[k], kLog2eF, nl)) * sc;
     }
-    __syncthreads();
-    for (int i = threadIdx.x; i < 4096; i += blockDim.x) {
-      const int bb = i >> 5, rr = i & 31;
-      if (rr < nrow && b0 + bb < width) {
-        const float mb = s_m[rr][bb];
-        const float sc = s_sc[rr];
-        fcoef[(int64_t)(b0 + bb) * fcoef_ld + row0 + rr] =
-            (sc == 0.f || mb == -INFINITY) ? 0.f : ex2_fast(fmaf(mb, kLog2eF, s_nl[rr])) * sc;
-      }
-    }
-    __syncthreads();
   }
 }
 
